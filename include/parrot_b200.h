@@ -1,0 +1,178 @@
+/*
+ * parrot_b200.h — C ABI of libparrot_b200.so, the B200 (sm_100a) kernels for
+ * Parrot XL's MoE block and its companions (bf16 inference forward).
+ *
+ * Conventions
+ *   - Every tensor argument is a DEVICE pointer to a contiguous row-major
+ *     array, 16-byte aligned; bf16 unless the type says otherwise.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls only
+ *     enqueue work: they never synchronise and never allocate device memory.
+ *   - Return value: 0 on success, PARROT_EINVAL for a bad argument (nothing
+ *     launched), PARROT_ECUDA when a launch failed.  parrot_b200_last_error()
+ *     gives a message for the calling thread.  Device-side errors (a bounded
+ *     wait that ran out, an out-of-range expert id) are recorded in the
+ *     workspace status word; parrot_moe_read_status() reads it.
+ *
+ * Each entry point names the reference code it replaces
+ * (jkpdino/parrot-h200-worker, paths relative to the repository root).
+ */
+#ifndef PARROT_B200_H
+#define PARROT_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PARROT_OK 0
+#define PARROT_EINVAL (-1)
+#define PARROT_ECUDA (-2)
+#define PARROT_EUNSUPPORTED (-3)
+
+/* Version of this ABI (major * 100 + minor). */
+int parrot_b200_version(void);
+
+/* Message describing the last failed call on this thread ("" if none). */
+const char* parrot_b200_last_error(void);
+
+/* 1 if `device` is an sm_100 GPU these kernels run on, else 0. */
+int parrot_b200_device_supported(int device);
+
+/* ------------------------------------------------------------------------
+ * RMSNorm, y = bf16((x * rsqrt(mean(x^2) + eps)) * weight) over the last dim.
+ * Replaces parrot/model.py:116-127 (RMSNorm.forward) and the Metal kernels
+ * parrot/kernels/moe_bf16.metal:4-65 (rms_norm_bf16, rms_norm_decode_bf16)
+ * bound in parrot/metal_moe.py:37-55 (metal_rms_norm).
+ * x, out: [rows, dim]; weight: [dim].  dim % 8 == 0, dim <= 2048.
+ * ---------------------------------------------------------------------- */
+int parrot_rmsnorm_bf16(void* out, const void* x, const void* weight, int rows, int dim,
+                        float eps, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Block AttnRes depth mix over `n_sources` [rows, dim] tensors (1..16):
+ *   key_i = rms_norm(src_i; key_norm_weight, key_eps), s_i = <key_i, query>,
+ *   a = softmax_i(s), h = sum_i a_i * src_i,
+ * then, when out_norm_weight != NULL, the consumer RMSNorm of h.
+ * Replaces parrot/model.py:141-155 (DepthMix.forward) and :157-164
+ * (DepthMix.normalized -> output_norm(depth_mix(...))), and the Metal kernels
+ * moe_bf16.metal:249-435, 563-645 bound in metal_moe.py:419-477.
+ * mix_out (optional) receives h when a norm is fused.
+ * pending_base/pending_delta (optional, both or neither): the last source is
+ * bf16(pending_base + pending_delta) — the residual add of model.py:702 —
+ * and is also written to pending_out (cf. metal_moe.py:480-500).
+ * dim % 8 == 0, dim <= 1024.
+ * ---------------------------------------------------------------------- */
+int parrot_depthmix_bf16(void* out, const void* const* sources, int n_sources,
+                         const void* query, const void* key_norm_weight, float key_eps,
+                         const void* out_norm_weight, float out_eps, void* mix_out,
+                         const void* pending_base, const void* pending_delta,
+                         void* pending_out, int rows, int dim, void* stream);
+
+/* ------------------------------------------------------------------------
+ * MoE block: router + top-2 + capacity grouping + grouped SwiGLU experts +
+ * shared expert + weighted combine (+ residual add).
+ * ---------------------------------------------------------------------- */
+typedef struct parrot_moe_dims {
+  int tokens;      /* T, flattened tokens (0 allowed) */
+  int dim;         /* d, % 128 == 0, <= 1024 */
+  int n_experts;   /* E, 2..32 */
+  int top_k;       /* must be 2 */
+  int expert_dim;  /* H, % 64 == 0 */
+  int shared_dim;  /* Hs, % 64 == 0 */
+  int capacity;    /* slots per expert; 0 selects parrot_moe_capacity() */
+} parrot_moe_dims;
+
+/* Weights in torch.nn.Linear [out, in] layout.  gate_up / shared_gate_up are
+ * packed by parrot_pack_gate_up_bf16 (rows interleaved per 64-feature tile). */
+typedef struct parrot_moe_weights {
+  const void* router;          /* [E, d] */
+  const float* router_bias;    /* [E] fp32 logit offset or NULL (harness only) */
+  const void* gate_up;         /* [E, 2H, d] packed */
+  const void* down;            /* [E, d, H] */
+  const void* shared_gate_up;  /* [2Hs, d] packed */
+  const void* shared_down;     /* [d, Hs] */
+} parrot_moe_weights;
+
+typedef struct parrot_moe_outputs {
+  void* out;              /* [T, d] bf16, required */
+  const void* residual;   /* [T, d] or NULL: out = bf16(residual + moe(x)) */
+  float* probs;           /* [T, E] router softmax, or NULL */
+  long long* indices;     /* [T, 2] int64 expert ids, or NULL */
+  float* weights;         /* [T, 2] renormalised top-2 weights, or NULL */
+  int* positions;         /* [2T] grouped row of each assignment, or NULL */
+  int* counts;            /* [E] assignments per expert, or NULL */
+  float* stats;           /* [E + 1]: utilisation[E], aux loss; or NULL */
+} parrot_moe_outputs;
+
+/* Byte offsets of the buffers inside one MoE workspace (for inspection). */
+typedef struct parrot_moe_layout {
+  size_t indices, weights, positions, block_hist, block_prefix, block_probsum;
+  size_t counts, seg_rows, seg_base, done_counter, stats, status;
+  size_t grouped, hidden, y, shared_hidden, shared_y, total;
+  int capacity, grouped_rows, route_blocks, reserved;
+} parrot_moe_layout;
+
+/* Default capacity: max(8, ceil8(ceil(2 * 2T / E))), metal_moe.py:388-391. */
+int parrot_moe_capacity(int tokens, int n_experts);
+
+/* Fills `layout`; returns PARROT_EINVAL for unsupported dims. */
+int parrot_moe_workspace_layout(const parrot_moe_dims* dims, parrot_moe_layout* layout);
+
+/* Zeroes the control words of a fresh workspace (call once after allocating;
+ * a zero-filled allocation needs no call).  Enqueued on `stream`. */
+int parrot_moe_workspace_init(void* workspace, const parrot_moe_dims* dims, void* stream);
+
+/* Pack gate/up rows for the fused SwiGLU epilogue:
+ * dst[m, tile*128 + 2i + {0,1}, :] = {gate, up}[m, tile*64 + i, :].
+ * gate, up: [n_mats, hidden, dim]; dst: [n_mats, 2*hidden, dim]; hidden % 64 == 0.
+ * Replaces the weight packing of metal_moe.py:105-131 (pack_combined_weights). */
+int parrot_pack_gate_up_bf16(void* dst, const void* gate, const void* up, int n_mats, int hidden,
+                             int dim, void* stream);
+
+/* Whole MoE block.  Replaces parrot/model.py:505-569 (MoE.forward: router
+ * :521-527, per-expert dispatch loop :545-551, router statistics :554-569)
+ * and :571-585 (MoE.inference with addend), plus the Metal route/group/
+ * gather path metal_moe.py:58-81, 372-416 (moe_bf16.metal:67-134, 650-777).
+ * x: [T, d].  `workspace` holds parrot_moe_workspace_layout(dims).total bytes. */
+int parrot_moe_forward_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                            const void* x, const parrot_moe_outputs* outputs, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* Router + grouping only (metal_moe.py:58-81 metal_route, plus the slot
+ * scatter of moe_bf16.metal:678-696).  Leaves its results in the workspace
+ * and copies the optional outputs (probs, indices, weights, positions,
+ * counts, stats). */
+int parrot_moe_route_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                          const void* x, const parrot_moe_outputs* outputs, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* Expert GEMMs + shared expert + combine on a workspace filled by
+ * parrot_moe_route_bf16 for the same x (metal_moe.py:372-416 after routing). */
+int parrot_moe_experts_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                            const void* x, const parrot_moe_outputs* outputs, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* One grouped-GEMM stage on a workspace filled by parrot_moe_route_bf16
+ * (stage 0: gate_up + SwiGLU for routed and shared experts; stage 1: down).
+ * Used to time the tensor-core kernel on its own; the result is the same as
+ * the corresponding part of parrot_moe_experts_bf16 (cuda_training.py:26-30,
+ * the torch._grouped_mm pair it replaces). */
+int parrot_moe_gemm_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                         const void* x, void* workspace, size_t workspace_bytes, int stage,
+                         void* stream);
+
+/* Number of kernels this library has enqueued since it was loaded
+ * (instrumentation; no reference counterpart). */
+unsigned long long parrot_b200_launch_count(void);
+
+/* Copies the workspace status word {code, site, info, 0} to host memory
+ * (synchronises `stream`).  code 0 = ok. */
+int parrot_moe_read_status(const void* workspace, const parrot_moe_dims* dims, int* host_status4,
+                           void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PARROT_B200_H */

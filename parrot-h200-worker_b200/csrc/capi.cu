@@ -1,0 +1,521 @@
+// extern "C" entry points of libparrot_b200.so (declared in include/parrot_b200.h).
+//
+// This layer validates arguments, carves the caller's workspace, builds the
+// TMA tensor maps (host-side encode, cached per buffer) and enqueues the
+// kernels on the caller's stream.  It never allocates device memory and
+// never synchronises (except parrot_moe_read_status, a debugging read).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "kernels.h"
+#include "parrot_b200.h"
+
+using parrot::kGemmBlockK;
+using parrot::kGemmBlockN;
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<unsigned long long> g_launches{0};
+
+int fail(int code, const char* fmt, const char* detail = "") {
+  char buf[512];
+  std::snprintf(buf, sizeof(buf), fmt, detail);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(err);
+    return PARROT_ECUDA;
+  }
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return PARROT_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ---- TMA tensor maps ------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* ptr;
+  long long rows, cols;
+  int box_rows;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<const void*>()(k.ptr) ^ (size_t)(k.rows * 1315423911ll) ^
+           (size_t)(k.cols * 2654435761ll) ^ (size_t)k.box_rows;
+  }
+};
+
+std::mutex g_map_mutex;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// Row-major bf16 [rows, cols] matrix, box = 64 columns x box_rows rows, 128-B swizzle.
+bool tensor_map(CUtensorMap* out, const void* ptr, long long rows, long long cols, int box_rows) {
+  const MapKey key{ptr, rows, cols, box_rows};
+  {
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kGemmBlockK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUtensorMap map;
+  const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps.emplace(key, map);
+  *out = map;
+  return true;
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 148;
+  return n;
+}
+
+// ---- MoE workspace ----------------------------------------------------------
+int validate_dims(const parrot_moe_dims* d) {
+  if (d == nullptr) return fail(PARROT_EINVAL, "dims is NULL%s");
+  if (d->tokens < 0) return fail(PARROT_EINVAL, "tokens must be >= 0%s");
+  if (d->top_k != 2) return fail(PARROT_EINVAL, "top_k must be 2%s");
+  if (d->n_experts < 2 || d->n_experts > parrot::kMaxExperts)
+    return fail(PARROT_EINVAL, "n_experts must be in [2, 32]%s");
+  if (d->dim <= 0 || d->dim % 128 || d->dim > 1024)
+    return fail(PARROT_EINVAL, "dim must be a positive multiple of 128, <= 1024%s");
+  if (d->expert_dim <= 0 || d->expert_dim % 64)
+    return fail(PARROT_EINVAL, "expert_dim must be a positive multiple of 64%s");
+  if (d->shared_dim <= 0 || d->shared_dim % 64)
+    return fail(PARROT_EINVAL, "shared_dim must be a positive multiple of 64%s");
+  if (d->capacity < 0) return fail(PARROT_EINVAL, "capacity must be >= 0%s");
+  if ((size_t)d->n_experts * d->dim * 2 > 96 * 1024)
+    return fail(PARROT_EINVAL, "router weight exceeds 96 KB of shared memory%s");
+  return PARROT_OK;
+}
+
+int layout_of(const parrot_moe_dims* d, parrot_moe_layout* L) {
+  const int rc = validate_dims(d);
+  if (rc) return rc;
+  std::memset(L, 0, sizeof(*L));
+  const size_t T = d->tokens, D = d->dim, E = d->n_experts, H = d->expert_dim,
+               Hs = d->shared_dim;
+  const int C = d->capacity > 0 ? d->capacity : parrot_moe_capacity(d->tokens, d->n_experts);
+  const size_t A = 2 * T;
+  const size_t nb = (size_t)parrot::route_blocks(d->tokens);
+  const size_t R = E * (size_t)C + A;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align256(off + bytes);
+    return at;
+  };
+  // control words first: one region zeroed by parrot_moe_workspace_init
+  L->done_counter = take(16);
+  L->status = take(16);
+  L->indices = take(A * 4);
+  L->weights = take(A * 4);
+  L->positions = take(A * 4);
+  L->block_hist = take(nb * E * 4);
+  L->block_prefix = take(nb * E * 4);
+  L->block_probsum = take(nb * E * 4);
+  L->counts = take(E * 4);
+  L->seg_rows = take(2 * E * 4);
+  L->seg_base = take(2 * E * 4);
+  L->stats = take((E + 1) * 4);
+  L->grouped = take(R * D * 2);
+  L->hidden = take(R * H * 2);
+  L->y = take(R * D * 2);
+  L->shared_hidden = take(T * Hs * 2);
+  L->shared_y = take(T * D * 2);
+  L->total = off;
+  L->capacity = C;
+  L->grouped_rows = (int)R;
+  L->route_blocks = (int)nb;
+  return PARROT_OK;
+}
+
+template <typename T>
+T* at(void* ws, size_t off) {
+  return reinterpret_cast<T*>(static_cast<char*>(ws) + off);
+}
+
+int check_weights(const parrot_moe_weights* w) {
+  if (w == nullptr || w->router == nullptr || w->gate_up == nullptr || w->down == nullptr ||
+      w->shared_gate_up == nullptr || w->shared_down == nullptr)
+    return fail(PARROT_EINVAL, "missing weight pointer%s");
+  if (!aligned16(w->router) || !aligned16(w->gate_up) || !aligned16(w->down) ||
+      !aligned16(w->shared_gate_up) || !aligned16(w->shared_down))
+    return fail(PARROT_EINVAL, "weights must be 16-byte aligned%s");
+  return PARROT_OK;
+}
+
+parrot::MoeTables tables(void* ws, const parrot_moe_layout& L) {
+  parrot::MoeTables t;
+  t.block_prefix = at<int>(ws, L.block_prefix);
+  t.block_hist = at<int>(ws, L.block_hist);
+  t.block_probsum = at<float>(ws, L.block_probsum);
+  t.counts = at<int>(ws, L.counts);
+  t.seg_rows = at<int>(ws, L.seg_rows);
+  t.seg_base = at<int>(ws, L.seg_base);
+  t.done_counter = at<int>(ws, L.done_counter);
+  t.stats = at<float>(ws, L.stats);
+  return t;
+}
+
+int prepare(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
+            const parrot_moe_outputs* o, void* ws, size_t ws_bytes, parrot_moe_layout* L) {
+  int rc = layout_of(dims, L);
+  if (rc) return rc;
+  if ((rc = check_weights(w))) return rc;
+  if (o == nullptr || o->out == nullptr) return fail(PARROT_EINVAL, "outputs->out is required%s");
+  if (ws == nullptr || ws_bytes < L->total || !aligned16(ws))
+    return fail(PARROT_EINVAL, "workspace missing, misaligned or smaller than the layout total%s");
+  if (dims->tokens > 0 && (x == nullptr || !aligned16(x) || !aligned16(o->out) ||
+                           (o->residual && !aligned16(o->residual))))
+    return fail(PARROT_EINVAL, "x/out/residual must be non-null and 16-byte aligned%s");
+  return PARROT_OK;
+}
+
+int copy_out(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+  if (dst == nullptr || bytes == 0) return PARROT_OK;
+  if (cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return check_launch("output copy");
+  return PARROT_OK;
+}
+
+int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
+              const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L, cudaStream_t s) {
+  const int T = dims->tokens, E = dims->n_experts;
+  parrot::RouteArgs ra{};
+  ra.x = static_cast<const __nv_bfloat16*>(x);
+  ra.w = static_cast<const __nv_bfloat16*>(w->router);
+  ra.bias = w->router_bias;
+  ra.probs = o->probs;
+  ra.indices = at<int>(ws, L.indices);
+  ra.weights = at<float>(ws, L.weights);
+  ra.indices64 = o->indices;
+  ra.tab = tables(ws, L);
+  ra.tokens = T;
+  ra.dim = dims->dim;
+  ra.n_experts = E;
+  ra.capacity = L.capacity;
+  ra.status = at<int>(ws, L.status);
+  if (parrot::launch_route(ra, s)) return fail(PARROT_EINVAL, "route: unsupported dim%s");
+  int rc = check_launch("route_kernel");
+  if (rc) return rc;
+
+  parrot::GroupArgs ga{};
+  ga.x = static_cast<const __nv_bfloat16*>(x);
+  ga.indices = ra.indices;
+  ga.tab = ra.tab;
+  ga.positions = at<int>(ws, L.positions);
+  ga.grouped = at<__nv_bfloat16>(ws, L.grouped);
+  ga.tokens = T;
+  ga.dim = dims->dim;
+  ga.n_experts = E;
+  ga.capacity = L.capacity;
+  const int nb = L.route_blocks;
+  int split = (2 * sm_count() + nb - 1) / nb;
+  ga.copy_split = split < 1 ? 1 : (split > 8 ? 8 : split);
+  ga.status = ra.status;
+  parrot::launch_group(ga, s);
+  if ((rc = check_launch("group_kernel"))) return rc;
+
+  if ((rc = copy_out(o->weights, ra.weights, (size_t)2 * T * 4, s))) return rc;
+  if ((rc = copy_out(o->positions, ga.positions, (size_t)2 * T * 4, s))) return rc;
+  if ((rc = copy_out(o->counts, ra.tab.counts, (size_t)E * 4, s))) return rc;
+  if ((rc = copy_out(o->stats, ra.tab.stats, (size_t)(E + 1) * 4, s))) return rc;
+  return PARROT_OK;
+}
+
+int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights* w,
+             const void* x, void* ws, const parrot_moe_layout& L, cudaStream_t s) {
+  const int T = dims->tokens, D = dims->dim, E = dims->n_experts, H = dims->expert_dim,
+            Hs = dims->shared_dim, R = L.grouped_rows;
+  parrot::GemmArgs g{};
+  g.seg_rows = at<int>(ws, L.seg_rows);
+  g.seg_base = at<int>(ws, L.seg_base);
+  g.n_experts = E;
+  g.shared_rows = T;
+  g.status = at<int>(ws, L.status);
+  CUtensorMap mw, mx, msw, msx;
+  bool ok;
+  if (swiglu) {
+    g.m_tiles_routed = 2 * H / 128;
+    g.k_blocks_routed = D / kGemmBlockK;
+    g.weight_rows_per_expert = 2 * H;
+    g.out_routed = at<__nv_bfloat16>(ws, L.hidden);
+    g.ld_out_routed = H;
+    g.m_tiles_shared = 2 * Hs / 128;
+    g.k_blocks_shared = D / kGemmBlockK;
+    g.out_shared = at<__nv_bfloat16>(ws, L.shared_hidden);
+    g.ld_out_shared = Hs;
+    g.mode = parrot::kGemmSwiGLU;
+    ok = tensor_map(&mw, w->gate_up, (long long)E * 2 * H, D, 128) &&
+         tensor_map(&mx, at<void>(ws, L.grouped), R, D, kGemmBlockN) &&
+         tensor_map(&msw, w->shared_gate_up, 2LL * Hs, D, 128) &&
+         tensor_map(&msx, x, T, D, kGemmBlockN);
+  } else {
+    g.m_tiles_routed = D / 128;
+    g.k_blocks_routed = H / kGemmBlockK;
+    g.weight_rows_per_expert = D;
+    g.out_routed = at<__nv_bfloat16>(ws, L.y);
+    g.ld_out_routed = D;
+    g.m_tiles_shared = D / 128;
+    g.k_blocks_shared = Hs / kGemmBlockK;
+    g.out_shared = at<__nv_bfloat16>(ws, L.shared_y);
+    g.ld_out_shared = D;
+    g.mode = parrot::kGemmPlain;
+    ok = tensor_map(&mw, w->down, (long long)E * D, H, 128) &&
+         tensor_map(&mx, at<void>(ws, L.hidden), R, H, kGemmBlockN) &&
+         tensor_map(&msw, w->shared_down, D, Hs, 128) &&
+         tensor_map(&msx, at<void>(ws, L.shared_hidden), T, Hs, kGemmBlockN);
+  }
+  if (!ok) return fail(PARROT_ECUDA, "cuTensorMapEncodeTiled failed%s");
+  const int A = 2 * T;
+  const long long routed_units =
+      (long long)((A + kGemmBlockN - 1) / kGemmBlockN + 2 * E) * g.m_tiles_routed;
+  const long long shared_units = (long long)((T + kGemmBlockN - 1) / kGemmBlockN) * g.m_tiles_shared;
+  long long grid = routed_units + shared_units;
+  const int sms = sm_count();
+  if (grid > sms) grid = sms;
+  if (grid < 1) grid = 1;
+  if (parrot::launch_grouped_gemm(g, &mw, &mx, &msw, &msx, (int)grid, s))
+    return fail(PARROT_ECUDA, "grouped GEMM: could not set shared-memory size%s");
+  return check_launch(swiglu ? "grouped_gemm(gate_up)" : "grouped_gemm(down)");
+}
+
+int run_experts(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
+                const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L,
+                cudaStream_t s) {
+  int rc = run_gemm(true, dims, w, x, ws, L, s);
+  if (rc) return rc;
+  if ((rc = run_gemm(false, dims, w, x, ws, L, s))) return rc;
+  parrot::CombineArgs c{};
+  c.y = at<__nv_bfloat16>(ws, L.y);
+  c.shared_y = at<__nv_bfloat16>(ws, L.shared_y);
+  c.positions = at<int>(ws, L.positions);
+  c.indices = at<int>(ws, L.indices);
+  c.weights = at<float>(ws, L.weights);
+  c.residual = static_cast<const __nv_bfloat16*>(o->residual);
+  c.out = static_cast<__nv_bfloat16*>(o->out);
+  c.tokens = dims->tokens;
+  c.dim = dims->dim;
+  if (parrot::launch_combine(c, s)) return fail(PARROT_EINVAL, "combine: unsupported dim%s");
+  return check_launch("combine_kernel");
+}
+
+}  // namespace
+
+extern "C" {
+
+int parrot_b200_version(void) { return 100; }
+
+const char* parrot_b200_last_error(void) { return g_last_error.c_str(); }
+
+int parrot_b200_device_supported(int device) {
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return 0;
+  return prop.major == 10 ? 1 : 0;
+}
+
+int parrot_rmsnorm_bf16(void* out, const void* x, const void* weight, int rows, int dim,
+                        float eps, void* stream) {
+  if (rows < 0 || dim <= 0 || dim % 8 || dim > 2048)
+    return fail(PARROT_EINVAL, "rmsnorm: rows >= 0 and dim % 8 == 0, dim <= 2048 required%s");
+  if (rows == 0) return PARROT_OK;
+  if (!out || !x || !weight || !aligned16(out) || !aligned16(x) || !aligned16(weight))
+    return fail(PARROT_EINVAL, "rmsnorm: pointers must be non-null and 16-byte aligned%s");
+  parrot::launch_rmsnorm(static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(x),
+                         static_cast<const __nv_bfloat16*>(weight), rows, dim, eps,
+                         static_cast<cudaStream_t>(stream));
+  return check_launch("rmsnorm_kernel");
+}
+
+int parrot_depthmix_bf16(void* out, const void* const* sources, int n_sources,
+                         const void* query, const void* key_norm_weight, float key_eps,
+                         const void* out_norm_weight, float out_eps, void* mix_out,
+                         const void* pending_base, const void* pending_delta,
+                         void* pending_out, int rows, int dim, void* stream) {
+  if (n_sources < 1 || n_sources > parrot::kMaxDepthSources)
+    return fail(PARROT_EINVAL, "depthmix: n_sources must be in [1, 16]%s");
+  if (rows < 0 || dim <= 0 || dim % 8 || dim > 1024)
+    return fail(PARROT_EINVAL, "depthmix: dim % 8 == 0 and dim <= 1024 required%s");
+  if ((pending_delta == nullptr) != (pending_base == nullptr) ||
+      (pending_delta != nullptr && pending_out == nullptr))
+    return fail(PARROT_EINVAL, "depthmix: pending_base, pending_delta and pending_out go together%s");
+  if (rows == 0) return PARROT_OK;
+  if (!out || !query || !key_norm_weight || !sources)
+    return fail(PARROT_EINVAL, "depthmix: null pointer%s");
+  parrot::DepthMixArgs a{};
+  for (int i = 0; i < n_sources; ++i) {
+    const bool is_pending = pending_delta != nullptr && i == n_sources - 1;
+    const void* p = is_pending ? pending_out : sources[i];
+    if (p == nullptr || !aligned16(p))
+      return fail(PARROT_EINVAL, "depthmix: sources must be non-null and 16-byte aligned%s");
+    a.sources[i] = static_cast<const __nv_bfloat16*>(p);
+  }
+  a.n_sources = n_sources;
+  a.query = static_cast<const __nv_bfloat16*>(query);
+  a.key_w = static_cast<const __nv_bfloat16*>(key_norm_weight);
+  a.key_eps = key_eps;
+  a.out_w = static_cast<const __nv_bfloat16*>(out_norm_weight);
+  a.out_eps = out_eps;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.mix_out = static_cast<__nv_bfloat16*>(mix_out);
+  a.pending_base = static_cast<const __nv_bfloat16*>(pending_base);
+  a.pending_delta = static_cast<const __nv_bfloat16*>(pending_delta);
+  a.pending_out = static_cast<__nv_bfloat16*>(pending_out);
+  a.rows = rows;
+  a.dim = dim;
+  parrot::launch_depthmix(a, static_cast<cudaStream_t>(stream));
+  return check_launch("depthmix_kernel");
+}
+
+int parrot_moe_capacity(int tokens, int n_experts) {
+  if (n_experts <= 0 || tokens < 0) return 0;
+  const long long assignments = 2LL * tokens;
+  const long long balanced = (2 * assignments + n_experts - 1) / n_experts;
+  const long long c = (balanced + 7) / 8 * 8;
+  return (int)(c < 8 ? 8 : c);
+}
+
+int parrot_moe_workspace_layout(const parrot_moe_dims* dims, parrot_moe_layout* layout) {
+  if (layout == nullptr) return fail(PARROT_EINVAL, "layout is NULL%s");
+  return layout_of(dims, layout);
+}
+
+int parrot_moe_workspace_init(void* workspace, const parrot_moe_dims* dims, void* stream) {
+  parrot_moe_layout L;
+  int rc = layout_of(dims, &L);
+  if (rc) return rc;
+  if (workspace == nullptr) return fail(PARROT_EINVAL, "workspace is NULL%s");
+  if (cudaMemsetAsync(workspace, 0, L.indices, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return check_launch("workspace init");
+  return PARROT_OK;
+}
+
+int parrot_pack_gate_up_bf16(void* dst, const void* gate, const void* up, int n_mats, int hidden,
+                             int dim, void* stream) {
+  if (!dst || !gate || !up || n_mats <= 0 || hidden <= 0 || hidden % 64 || dim <= 0 || dim % 8)
+    return fail(PARROT_EINVAL, "pack_gate_up: bad arguments (hidden % 64, dim % 8)%s");
+  parrot::launch_pack_gate_up(static_cast<__nv_bfloat16*>(dst),
+                              static_cast<const __nv_bfloat16*>(gate),
+                              static_cast<const __nv_bfloat16*>(up), n_mats, hidden, dim,
+                              static_cast<cudaStream_t>(stream));
+  return check_launch("pack_gate_up_kernel");
+}
+
+int parrot_moe_route_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                          const void* x, const parrot_moe_outputs* outputs, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  int rc = prepare(dims, weights, x, outputs, workspace, workspace_bytes, &L);
+  if (rc) return rc;
+  if (dims->tokens == 0) return PARROT_OK;
+  return run_route(dims, weights, x, outputs, workspace, L, static_cast<cudaStream_t>(stream));
+}
+
+int parrot_moe_experts_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                            const void* x, const parrot_moe_outputs* outputs, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  int rc = prepare(dims, weights, x, outputs, workspace, workspace_bytes, &L);
+  if (rc) return rc;
+  if (dims->tokens == 0) return PARROT_OK;
+  return run_experts(dims, weights, x, outputs, workspace, L, static_cast<cudaStream_t>(stream));
+}
+
+int parrot_moe_forward_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                            const void* x, const parrot_moe_outputs* outputs, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  int rc = prepare(dims, weights, x, outputs, workspace, workspace_bytes, &L);
+  if (rc) return rc;
+  if (dims->tokens == 0) return PARROT_OK;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = run_route(dims, weights, x, outputs, workspace, L, s))) return rc;
+  return run_experts(dims, weights, x, outputs, workspace, L, s);
+}
+
+int parrot_moe_gemm_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                         const void* x, void* workspace, size_t workspace_bytes, int stage,
+                         void* stream) {
+  parrot_moe_layout L;
+  int rc = layout_of(dims, &L);
+  if (rc) return rc;
+  if ((rc = check_weights(weights))) return rc;
+  if (stage != 0 && stage != 1) return fail(PARROT_EINVAL, "stage must be 0 or 1%s");
+  if (workspace == nullptr || workspace_bytes < L.total || !aligned16(workspace))
+    return fail(PARROT_EINVAL, "workspace missing, misaligned or too small%s");
+  if (dims->tokens == 0) return PARROT_OK;
+  if (x == nullptr || !aligned16(x)) return fail(PARROT_EINVAL, "x must be 16-byte aligned%s");
+  return run_gemm(stage == 0, dims, weights, x, workspace, L, static_cast<cudaStream_t>(stream));
+}
+
+unsigned long long parrot_b200_launch_count(void) {
+  return g_launches.load(std::memory_order_relaxed);
+}
+
+int parrot_moe_read_status(const void* workspace, const parrot_moe_dims* dims, int* host_status4,
+                           void* stream) {
+  parrot_moe_layout L;
+  int rc = layout_of(dims, &L);
+  if (rc) return rc;
+  if (!workspace || !host_status4) return fail(PARROT_EINVAL, "null pointer%s");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(host_status4, static_cast<const char*>(workspace) + L.status, 16,
+                      cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return check_launch("read status");
+  return PARROT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,81 @@
+// Shared device helpers for the Parrot B200 kernels (sm_100a only).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "parrot_b200 targets sm_100a only"
+#endif
+
+namespace parrot {
+
+// ---------------------------------------------------------------------------
+// device status word: {code, site, info, unused}.  The first error wins.
+// Codes are >0 so the C-ABI can return them unchanged.
+// ---------------------------------------------------------------------------
+enum StatusCode : int {
+  kStatusOk = 0,
+  kStatusWaitTimeout = 1,   // a bounded mbarrier / flag wait ran out
+  kStatusBadIndex = 2,      // an expert id or row fell outside its range
+  kStatusBadShape = 3,      // launch shape inconsistent with the tables
+};
+
+__device__ __forceinline__ void report_status(int* status, int code, int site, int info) {
+  if (status == nullptr) return;
+  if (atomicCAS(status, 0, code) == 0) {
+    status[1] = site;
+    status[2] = info;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// bf16 <-> fp32 vector helpers (16-byte rows)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void bf16x8_to_float(const uint4& v, float f[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 float_to_bf16x8(const float f[8]) {
+  uint4 v;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+
+// Round an fp32 value to the nearest bf16 and back: models a tensor that the
+// reference materialises in bf16 between two torch ops.
+__device__ __forceinline__ float round_bf16(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Upper bound for every spin-wait in these kernels (nanoseconds).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+}  // namespace parrot

@@ -1,0 +1,490 @@
+// Grouped expert GEMMs on the 5th-generation tensor cores (N4).
+//
+// One persistent kernel computes, for every (segment, 128-row weight tile,
+// token tile) work unit,  D[128 x N] = W_tile[128 x K] * X_tile[N x K]^T
+// with tcgen05.mma (A and B from shared memory, fp32 accumulator in TMEM).
+// Weights are the MMA M side ("swap-AB"): a routed expert sees a few dozen
+// to a few thousand token rows, and putting tokens on N keeps every MMA
+// at M = 128 while N shrinks to the rows actually present (multiple of 16).
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: 128-byte-swizzled K slabs of W and X into a
+//               5-stage shared-memory ring (no multicast anywhere).
+//   warp 1      TMEM allocator + single-thread MMA issuer; tcgen05.commit
+//               frees ring stages and publishes finished accumulators.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, then
+//               SwiGLU mode:  weight rows are packed (gate_j, up_j) pairs, so
+//                             lanes 2i / 2i+1 hold gate / up of one feature;
+//                             h = bf16(bf16(silu(bf16 g)) * bf16 u)
+//               plain mode:   y = bf16(acc)
+//               staged through shared memory into row-major bf16 output.
+// Two TMEM accumulators (2 x 128 columns) let the epilogue of one unit run
+// under the MMAs of the next.  Every mbarrier wait is bounded; a timeout
+// records a status code, drains in-flight copies and MMAs, frees TMEM and
+// returns.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace parrot {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = kGemmBlockN;
+constexpr int BK = kGemmBlockK;
+constexpr int kStages = 5;
+constexpr int kTileA = BM * BK * 2;
+constexpr int kTileB = BN * BK * 2;
+constexpr int kChunk = 32;                   // TMEM columns per epilogue step
+constexpr int kStaging = kChunk * BM * 2;    // 32 tokens x 128 features bf16
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 2 * BN;
+constexpr int kSegMax = 2 * kMaxExperts;
+
+struct __align__(8) SmemTail {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int prefix[kSegMax + 2];
+  int seg_rows[kSegMax];
+  int seg_base[kSegMax];
+};
+
+constexpr size_t kSmemBytes =
+    1024 + (size_t)kStages * (kTileA + kTileB) + 2 * kStaging + sizeof(SmemTail);
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false if the CTA is aborting or the limit ran out.
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                       int* status, int site) {
+  for (int i = 0; i < 128; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      report_status(status, kStatusWaitTimeout, site, (int)blockIdx.x);
+      return false;
+    }
+  }
+}
+
+// Drain wait used on the way out: ignores the abort flag, still bounded.
+__device__ __noinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > kWaitLimitNs) return;
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+  const uint64_t addr = smem_u32(tile);
+  return ((addr >> 4) & 0x3FFFull)      // start address
+         | (1ull << 16)                 // leading byte offset (16 B, unused for SW128 K-major)
+         | (64ull << 32)                // stride byte offset: 1024 B between 8-row groups
+         | (1ull << 46)                 // descriptor version (sm_100)
+         | (2ull << 61);                // 128-byte swizzle
+}
+
+__device__ __forceinline__ uint32_t make_idesc(int n) {
+  return (1u << 4)                          // D = f32
+         | (1u << 7)                        // A = bf16
+         | (1u << 10)                       // B = bf16
+         | ((uint32_t)(n >> 3) << 17)       // N
+         | ((uint32_t)(BM >> 4) << 24);     // M
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(addr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+struct Unit {
+  bool routed;
+  int w_row;      // first weight row of the 128-row tile
+  int x_row;      // first token row of the tile
+  int valid;      // token rows present (<= BN)
+  int k_blocks;
+  int out_col;    // first output feature
+  __nv_bfloat16* out;
+  int ld;
+};
+
+__device__ __forceinline__ Unit decode_unit(int u, const GemmArgs& g, const SmemTail& t) {
+  Unit r;
+  const int n_seg = 2 * g.n_experts;
+  const int feat_per_tile = g.mode == kGemmSwiGLU ? BM / 2 : BM;
+  if (u < t.prefix[n_seg]) {
+    int s = 0;
+    while (t.prefix[s + 1] <= u) ++s;
+    const int local = u - t.prefix[s];
+    const int n_tiles = (t.seg_rows[s] + BN - 1) / BN;
+    const int mt = local / n_tiles, nt = local - mt * n_tiles;
+    const int e = s % g.n_experts;
+    r.routed = true;
+    r.w_row = e * g.weight_rows_per_expert + mt * BM;
+    r.x_row = t.seg_base[s] + nt * BN;
+    r.valid = min(BN, t.seg_rows[s] - nt * BN);
+    r.k_blocks = g.k_blocks_routed;
+    r.out_col = mt * feat_per_tile;
+    r.out = g.out_routed;
+    r.ld = g.ld_out_routed;
+  } else {
+    const int local = u - t.prefix[n_seg];
+    const int n_tiles = (g.shared_rows + BN - 1) / BN;
+    const int mt = local / n_tiles, nt = local - mt * n_tiles;
+    r.routed = false;
+    r.w_row = mt * BM;
+    r.x_row = nt * BN;
+    r.valid = min(BN, g.shared_rows - nt * BN);
+    r.k_blocks = g.k_blocks_shared;
+    r.out_col = mt * feat_per_tile;
+    r.out = g.out_shared;
+    r.ld = g.ld_out_shared;
+  }
+  return r;
+}
+
+__device__ __forceinline__ float silu_bf16(float g) {
+  const float gb = round_bf16(g);
+  return round_bf16(gb / (1.0f + expf(-gb)));
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w_routed,
+                        const __grid_constant__ CUtensorMap tm_x_routed,
+                        const __grid_constant__ CUtensorMap tm_w_shared,
+                        const __grid_constant__ CUtensorMap tm_x_shared, const GemmArgs g) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* tiles_a = base;
+  unsigned char* tiles_b = base + kStages * kTileA;
+  unsigned char* staging = tiles_b + kStages * kTileB;
+  SmemTail& t = *reinterpret_cast<SmemTail*>(staging + 2 * kStaging);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_seg = 2 * g.n_experts;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&t.full[s], 1);
+      mbar_init(&t.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&t.tfull[a], 1);
+      mbar_init(&t.tempty[a], 4);
+    }
+    mbar_init(&t.drain, 1);
+    t.abort = 0;
+    // work-unit prefix over segments (routed), shared units follow
+    int acc = 0;
+    t.prefix[0] = 0;
+    const int m_routed = g.m_tiles_routed;
+    for (int s = 0; s < n_seg; ++s) {
+      const int rows = g.seg_rows[s];
+      const int sb = g.seg_base[s];
+      t.seg_rows[s] = rows;
+      t.seg_base[s] = sb;
+      acc += ((rows + BN - 1) / BN) * m_routed;
+      t.prefix[s + 1] = acc;
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile(
+        "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+            smem_u32(&t.tmem_base)),
+        "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem = t.tmem_base;
+  const int shared_units =
+      g.shared_rows > 0 ? ((g.shared_rows + BN - 1) / BN) * g.m_tiles_shared : 0;
+  const int total = t.prefix[n_seg] + shared_units;
+  volatile int* abort_flag = &t.abort;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued[kStages] = {};
+      uint32_t issued_phase[kStages] = {};
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const Unit un = decode_unit(u, g, t);
+        const CUtensorMap* mw = un.routed ? &tm_w_routed : &tm_w_shared;
+        const CUtensorMap* mx = un.routed ? &tm_x_routed : &tm_x_shared;
+        for (int kb = 0; kb < un.k_blocks; ++kb) {
+          if (!mbar_wait(&t.empty[stage], phase ^ 1, abort_flag, g.status, 10)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&t.full[stage], kTileA + kTileB);
+          tma_load_2d(tiles_a + stage * kTileA, mw, kb * BK, un.w_row, &t.full[stage]);
+          tma_load_2d(tiles_b + stage * kTileB, mx, kb * BK, un.x_row, &t.full[stage]);
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // every issued copy has landed before the CTA can exit
+      for (int s = 0; s < kStages; ++s)
+        if (issued[s]) mbar_drain(&t.full[s], issued_phase[s]);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const Unit un = decode_unit(u, g, t);
+        if (!mbar_wait(&t.tempty[acc], acc_phase ^ 1, abort_flag, g.status, 20)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * BN;
+        const int n = (un.valid + 15) & ~15;
+        const uint32_t idesc = make_idesc(n);
+        for (int kb = 0; kb < un.k_blocks; ++kb) {
+          if (!mbar_wait(&t.full[stage], phase, abort_flag, g.status, 21)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sw128_desc(tiles_a + stage * kTileA);
+          const uint64_t db = sw128_desc(tiles_b + stage * kTileB);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          mma_commit(&t.empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&t.tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // all MMAs issued by this thread have finished before TMEM is freed
+      mma_commit(&t.drain);
+      mbar_drain(&t.drain, 0);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;                 // TMEM lane quarter of this warp
+    const int et = threadIdx.x - 64;        // 0..127
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int chunk_iter = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x) {
+      const Unit un = decode_unit(u, g, t);
+      if (!mbar_wait(&t.tfull[acc], acc_phase, abort_flag, g.status, 30)) break;
+      tc_fence_after();
+      const int chunks = (un.valid + kChunk - 1) / kChunk;
+      for (int c = 0; c < chunks; ++c, ++chunk_iter) {
+        uint32_t r[32];
+        tmem_ld32(tmem + acc * BN + c * kChunk + ((uint32_t)(q * 32) << 16), r);
+        __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging + (chunk_iter & 1) * kStaging);
+        const int rows_here = min(kChunk, un.valid - c * kChunk);
+        __nv_bfloat16* out_base = un.out + (size_t)(un.x_row + c * kChunk) * un.ld + un.out_col;
+        if (g.mode == kGemmSwiGLU) {
+          const bool is_up = lane & 1;
+          const int f = q * 16 + (lane >> 1);
+          const int tok0 = is_up ? 16 : 0;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float mine_other = __uint_as_float(is_up ? r[j] : r[16 + j]);
+            const float recv = __shfl_xor_sync(0xffffffffu, mine_other, 1);
+            const float gate = is_up ? recv : __uint_as_float(r[j]);
+            const float up = is_up ? __uint_as_float(r[16 + j]) : recv;
+            const float h = silu_bf16(gate) * round_bf16(up);
+            st[(tok0 + j) * (BM / 2) + f] = __float2bfloat16_rn(h);
+          }
+          epi_bar();
+          // 32 tokens x 64 features: 256 16-byte pieces
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int idx = et + 128 * i;
+            const int tok = idx >> 3, part = idx & 7;
+            if (tok < rows_here)
+              *reinterpret_cast<uint4*>(out_base + (size_t)tok * un.ld + part * 8) =
+                  reinterpret_cast<const uint4*>(st)[idx];
+          }
+        } else {
+          const int m = q * 32 + lane;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) st[j * BM + m] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          epi_bar();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int idx = et + 128 * i;
+            const int tok = idx >> 4, part = idx & 15;
+            if (tok < rows_here)
+              *reinterpret_cast<uint4*>(out_base + (size_t)tok * un.ld + part * 8) =
+                  reinterpret_cast<const uint4*>(st)[idx];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&t.tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+// gate/up interleave: dst[m][tile*128 + 2i + {0,1}] = {gate, up}[m][tile*64 + i]
+__global__ void pack_gate_up_kernel(__nv_bfloat16* __restrict__ dst,
+                                    const __nv_bfloat16* __restrict__ gate,
+                                    const __nv_bfloat16* __restrict__ up, int n_mats, int hidden,
+                                    int dim) {
+  const int nvec = dim >> 3;
+  const size_t total = (size_t)n_mats * 2 * hidden * nvec;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % nvec);
+    const size_t row = i / nvec;                 // packed row over all matrices
+    const int m = (int)(row / (2 * hidden));
+    const int r = (int)(row % (2 * hidden));
+    const int tile = r / BM, within = r % BM;
+    const int feat = tile * (BM / 2) + (within >> 1);
+    const __nv_bfloat16* src = (within & 1) ? up : gate;
+    reinterpret_cast<uint4*>(dst)[i] =
+        reinterpret_cast<const uint4*>(src + ((size_t)m * hidden + feat) * dim)[c];
+  }
+}
+
+}  // namespace
+
+size_t grouped_gemm_smem_bytes() { return kSmemBytes; }
+
+int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
+                        const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
+                        const CUtensorMap* tm_x_shared, int grid, cudaStream_t stream) {
+  // the attribute belongs to each device's context: set it once per device
+  static unsigned long long configured = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
+  if (!(configured & (1ull << dev))) {
+    cudaError_t err = cudaFuncSetAttribute(grouped_gemm_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kSmemBytes);
+    if (err != cudaSuccess) return -2;
+    configured |= 1ull << dev;
+  }
+  grouped_gemm_kernel<<<grid, kThreads, kSmemBytes, stream>>>(*tm_w_routed, *tm_x_routed,
+                                                              *tm_w_shared, *tm_x_shared, args);
+  return 0;
+}
+
+int launch_pack_gate_up(__nv_bfloat16* dst, const __nv_bfloat16* gate, const __nv_bfloat16* up,
+                        int n_mats, int hidden, int dim, cudaStream_t stream) {
+  const size_t total = (size_t)n_mats * 2 * hidden * (dim / 8);
+  const int threads = 256;
+  const int blocks = (int)((total + threads - 1) / threads < 4096 ? (total + threads - 1) / threads : 4096);
+  pack_gate_up_kernel<<<blocks, threads, 0, stream>>>(dst, gate, up, n_mats, hidden, dim);
+  return 0;
+}
+
+}  // namespace parrot

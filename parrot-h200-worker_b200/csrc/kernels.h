@@ -1,0 +1,122 @@
+// Internal launcher declarations shared by the .cu files and the C-ABI layer.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace parrot {
+
+constexpr int kMaxDepthSources = 16;
+constexpr int kMaxExperts = 32;
+constexpr int kRouteTokensPerBlock = 32;   // router/grouping block: 64 assignments
+constexpr int kGemmBlockN = 128;           // token rows per grouped-GEMM tile
+constexpr int kGemmBlockK = 64;            // 128-byte swizzled K slab
+
+struct DepthMixArgs {
+  const __nv_bfloat16* sources[kMaxDepthSources];
+  int n_sources;
+  const __nv_bfloat16* query;
+  const __nv_bfloat16* key_w;
+  float key_eps;
+  const __nv_bfloat16* out_w;     // consumer RMSNorm weight, or null
+  float out_eps;
+  __nv_bfloat16* out;
+  __nv_bfloat16* mix_out;         // optional un-normalised mix
+  const __nv_bfloat16* pending_base;   // optional deferred residual
+  const __nv_bfloat16* pending_delta;
+  __nv_bfloat16* pending_out;
+  int rows;
+  int dim;
+};
+
+// Device-side MoE bookkeeping written by the router's last block and read by
+// the grouping, GEMM and combine kernels.  All int32.
+struct MoeTables {
+  int* block_prefix;   // [n_blocks, E] exclusive prefix of per-block counts
+  int* block_hist;     // [n_blocks, E]
+  float* block_probsum;  // [n_blocks, E]
+  int* counts;         // [E]
+  int* seg_rows;       // [2E] rows in capacity segment e, overflow segment e
+  int* seg_base;       // [2E] first grouped row of each segment
+  int* done_counter;   // [1] last-block ticket (self-resetting)
+  float* stats;        // [E + 1]: utilisation[E], aux
+};
+
+struct RouteArgs {
+  const __nv_bfloat16* x;     // [T, d]
+  const __nv_bfloat16* w;     // [E, d]
+  const float* bias;          // [E] or null (harness-only logit offset)
+  float* probs;               // [T, E] or null
+  int* indices;               // [T, 2]
+  float* weights;             // [T, 2]
+  long long* indices64;       // [T, 2] or null (reference dtype)
+  MoeTables tab;
+  int tokens, dim, n_experts, capacity;
+  int* status;
+};
+
+struct GroupArgs {
+  const __nv_bfloat16* x;     // [T, d]
+  const int* indices;         // [T, 2]
+  MoeTables tab;
+  int* positions;             // [2T] grouped row of each assignment
+  __nv_bfloat16* grouped;     // [E*C + 2T, d]
+  int tokens, dim, n_experts, capacity;
+  int copy_split;
+  int* status;
+};
+
+struct CombineArgs {
+  const __nv_bfloat16* y;         // [R, d] routed expert outputs by grouped row
+  const __nv_bfloat16* shared_y;  // [T, d]
+  const int* positions;           // [2T]
+  const int* indices;             // [T, 2]
+  const float* weights;           // [T, 2]
+  const __nv_bfloat16* residual;  // [T, d] or null
+  __nv_bfloat16* out;             // [T, d]
+  int tokens, dim;
+};
+
+enum GemmMode : int { kGemmSwiGLU = 0, kGemmPlain = 1 };
+
+struct GemmArgs {
+  // routed part: 2E segments (capacity, overflow) per expert
+  const int* seg_rows;
+  const int* seg_base;
+  int n_experts;
+  int m_tiles_routed;     // output features / 128
+  int k_blocks_routed;    // K / 64
+  int weight_rows_per_expert;
+  __nv_bfloat16* out_routed;
+  int ld_out_routed;      // elements per output row
+  // shared part
+  int shared_rows;        // tokens (0 disables)
+  int m_tiles_shared;
+  int k_blocks_shared;
+  __nv_bfloat16* out_shared;
+  int ld_out_shared;
+  int mode;
+  int* status;
+};
+
+int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat16* w,
+                   int rows, int dim, float eps, cudaStream_t stream);
+int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream);
+int launch_route(const RouteArgs& args, cudaStream_t stream);
+int launch_group(const GroupArgs& args, cudaStream_t stream);
+int launch_combine(const CombineArgs& args, cudaStream_t stream);
+int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
+                        const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
+                        const CUtensorMap* tm_x_shared, int grid, cudaStream_t stream);
+int launch_pack_gate_up(__nv_bfloat16* dst, const __nv_bfloat16* gate, const __nv_bfloat16* up,
+                        int n_mats, int hidden, int dim, cudaStream_t stream);
+size_t grouped_gemm_smem_bytes();
+
+inline int route_blocks(int tokens) {
+  return (tokens + kRouteTokensPerBlock - 1) / kRouteTokensPerBlock;
+}
+
+}  // namespace parrot

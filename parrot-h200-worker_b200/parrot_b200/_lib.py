@@ -1,0 +1,99 @@
+"""ctypes binding of ``libparrot_b200.so`` (the C ABI in ``include/parrot_b200.h``).
+
+There is no fallback: if the library is missing or the device is not an
+sm_100 GPU, calls raise ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_float, c_int, c_size_t, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).with_name("libparrot_b200.so")
+
+PARROT_OK = 0
+PARROT_EINVAL = -1
+PARROT_ECUDA = -2
+
+
+class MoeDims(ctypes.Structure):
+    _fields_ = [("tokens", c_int), ("dim", c_int), ("n_experts", c_int), ("top_k", c_int),
+                ("expert_dim", c_int), ("shared_dim", c_int), ("capacity", c_int)]
+
+
+class MoeWeights(ctypes.Structure):
+    _fields_ = [("router", c_void_p), ("router_bias", c_void_p), ("gate_up", c_void_p),
+                ("down", c_void_p), ("shared_gate_up", c_void_p), ("shared_down", c_void_p)]
+
+
+class MoeOutputs(ctypes.Structure):
+    _fields_ = [("out", c_void_p), ("residual", c_void_p), ("probs", c_void_p),
+                ("indices", c_void_p), ("weights", c_void_p), ("positions", c_void_p),
+                ("counts", c_void_p), ("stats", c_void_p)]
+
+
+LAYOUT_OFFSETS = ("indices", "weights", "positions", "block_hist", "block_prefix",
+                  "block_probsum", "counts", "seg_rows", "seg_base", "done_counter", "stats",
+                  "status", "grouped", "hidden", "y", "shared_hidden", "shared_y", "total")
+
+
+class MoeLayout(ctypes.Structure):
+    _fields_ = [(name, c_size_t) for name in LAYOUT_OFFSETS] + [
+        ("capacity", c_int), ("grouped_rows", c_int), ("route_blocks", c_int),
+        ("reserved", c_int)]
+
+
+_SIGNATURES = {
+    "parrot_b200_version": (c_int, []),
+    "parrot_b200_last_error": (ctypes.c_char_p, []),
+    "parrot_b200_device_supported": (c_int, [c_int]),
+    "parrot_rmsnorm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
+    "parrot_depthmix_bf16": (c_int, [c_void_p, POINTER(c_void_p), c_int, c_void_p, c_void_p,
+                                     c_float, c_void_p, c_float, c_void_p, c_void_p, c_void_p,
+                                     c_void_p, c_int, c_int, c_void_p]),
+    "parrot_moe_capacity": (c_int, [c_int, c_int]),
+    "parrot_moe_workspace_layout": (c_int, [POINTER(MoeDims), POINTER(MoeLayout)]),
+    "parrot_moe_workspace_init": (c_int, [c_void_p, POINTER(MoeDims), c_void_p]),
+    "parrot_pack_gate_up_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                         c_void_p]),
+    "parrot_moe_forward_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
+                                        POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
+    "parrot_moe_route_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
+                                      POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
+    "parrot_moe_experts_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
+                                        POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
+    "parrot_moe_gemm_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p, c_void_p,
+                                     c_size_t, c_int, c_void_p]),
+    "parrot_b200_launch_count": (ctypes.c_ulonglong, []),
+    "parrot_moe_read_status": (c_int, [c_void_p, POINTER(MoeDims), POINTER(c_int), c_void_p]),
+}
+
+_LIB: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the in-tree library (once) and declare every entry point's signature."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH.name} is not built; run `python -m parrot_b200.build` "
+                "(nvcc 12.9, sm_100a). The B200 backend has no fallback.")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = lib
+    return _LIB
+
+
+def check(rc: int, what: str) -> None:
+    """Turn a non-zero C status into ``RuntimeError`` naming the kernel."""
+    if rc != PARROT_OK:
+        msg = load().parrot_b200_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed (status {rc}): {msg}")
+
+
+def exported_names() -> list[str]:
+    return list(_SIGNATURES)

@@ -1,0 +1,324 @@
+"""PyTorch <-> libparrot_b200 bridge for the B200 MoE / depth backends.
+
+Each function mirrors one function of the reference's inference bridge
+(``parrot/metal_moe.py``) with the same argument meaning, but calls the
+sm_100a kernels through the C ABI.  Tensors stay on the caller's CUDA device
+and every launch goes on ``torch.cuda.current_stream()``; outputs are fresh
+``torch.empty`` tensors owned by the caller.  There is no CPU or eager-PyTorch
+fallback: a CPU tensor, a non-bf16 dtype, autograd, or a missing library all
+raise.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Sequence
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+_SUPPORTED: dict[int, bool] = {}
+_WORKSPACES: dict[tuple, Tensor] = {}
+
+
+# ---------------------------------------------------------------------------
+# argument checks (the reference raises the same way, metal_moe.py:154-157)
+# ---------------------------------------------------------------------------
+def _require_device(t: Tensor, what: str) -> None:
+    if t.device.type != "cuda":
+        raise RuntimeError(f"The B200 {what} backend requires CUDA tensors, got {t.device}")
+    if t.dtype != torch.bfloat16:
+        raise RuntimeError(f"The B200 {what} backend requires bfloat16, got {t.dtype}")
+    idx = t.device.index if t.device.index is not None else torch.cuda.current_device()
+    ok = _SUPPORTED.get(idx)
+    if ok is None:
+        ok = bool(_lib.load().parrot_b200_device_supported(idx))
+        _SUPPORTED[idx] = ok
+    if not ok:
+        raise RuntimeError(f"The B200 {what} backend requires an sm_100 GPU (device {idx})")
+
+
+def _require_inference(what: str) -> None:
+    if torch.is_grad_enabled():
+        raise RuntimeError(
+            f"The B200 {what} backend is inference-only; call it under "
+            "torch.inference_mode() or torch.no_grad()")
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _p(t: Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _rows(x: Tensor) -> tuple[Tensor, int, int]:
+    x = x.contiguous()
+    dim = x.shape[-1]
+    return x, x.numel() // dim, dim
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm  (metal_moe.py:37-55)
+# ---------------------------------------------------------------------------
+def b200_rms_norm(module, x: Tensor) -> Tensor:
+    """``module.weight``-scaled RMSNorm of ``x`` over its last dimension."""
+    _require_device(x, "RMSNorm")
+    _require_inference("RMSNorm")
+    x, rows, dim = _rows(x)
+    out = torch.empty_like(x)
+    lib = _lib.load()
+    w = module.weight
+    _lib.check(lib.parrot_rmsnorm_bf16(_p(out), _p(x), _p(w), rows, dim, float(module.eps),
+                                       _stream()), "parrot_rmsnorm_bf16")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Block AttnRes depth mixing  (metal_moe.py:419-500)
+# ---------------------------------------------------------------------------
+def _depth_call(module, sources: Sequence[Tensor], output_norm, pending_delta: Tensor | None):
+    first = sources[0]
+    _require_device(first, "depth")
+    _require_inference("depth")
+    n = len(sources)
+    if not 1 <= n <= 16:
+        raise RuntimeError("B200 depth mixing supports one to sixteen sources")
+    flat = [s.reshape(-1, s.shape[-1]).contiguous() for s in sources]
+    rows, dim = flat[0].shape
+    out = torch.empty((rows, dim), device=first.device, dtype=first.dtype)
+    pending_out = None
+    base = None
+    if pending_delta is not None:
+        base = flat[-1]
+        pending_delta = pending_delta.reshape(rows, dim).contiguous()
+        pending_out = torch.empty_like(out)
+    ptrs = (ctypes.c_void_p * n)(*[s.data_ptr() for s in flat])
+    lib = _lib.load()
+    ow = None if output_norm is None else output_norm.weight
+    oe = 0.0 if output_norm is None else float(output_norm.eps)
+    _lib.check(lib.parrot_depthmix_bf16(
+        _p(out), ptrs, n, _p(module.query), _p(module.norm.weight), float(module.norm.eps),
+        _p(ow), oe, None, _p(base), _p(pending_delta), _p(pending_out), rows, dim, _stream()),
+        "parrot_depthmix_bf16")
+    out = out.view_as(first)
+    if pending_delta is None:
+        return out, None
+    return out, pending_out.view_as(first)
+
+
+def b200_depth_mix(module, sources: Sequence[Tensor]) -> Tensor:
+    """``DepthMix.forward``: softmax-weighted sum of the raw sources."""
+    return _depth_call(module, sources, None, None)[0]
+
+
+def b200_depth_mix_norm(module, sources: Sequence[Tensor], output_norm,
+                        pending_delta: Tensor | None = None):
+    """``output_norm(DepthMix(sources))`` in one kernel.
+
+    With ``pending_delta``, the last source is ``sources[-1] + pending_delta``
+    (a residual add the caller deferred) and the call returns
+    ``(normalized, resolved_last_source)``; otherwise it returns ``normalized``.
+    """
+    out, resolved = _depth_call(module, sources, output_norm, pending_delta)
+    return out if pending_delta is None else (out, resolved)
+
+
+# ---------------------------------------------------------------------------
+# MoE  (metal_moe.py:58-131, 372-416)
+# ---------------------------------------------------------------------------
+def pack_weights(module) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Pack the routed and shared experts once per parameter version.
+
+    Returns ``(router [E,d], gate_up [E,2H,d], down [E,d,H], shared_gate_up
+    [2Hs,d], shared_down [d,Hs])``; gate/up rows are interleaved per 64-row
+    tile for the fused SwiGLU epilogue.  Like ``metal_moe.py:84-131`` the
+    packed copy is reused without re-checking versions while the module is in
+    eval mode with gradients disabled; ``invalidate_packed_weights`` forces a
+    repack after in-place weight edits made in that state.
+    """
+    cached = module.__dict__.get("_b200_pack")
+    if cached is not None and not torch.is_grad_enabled() and not module.training:
+        return cached[1]
+    params = [module.router.weight]
+    for e in module.experts:
+        params += [e.gate.weight, e.up.weight, e.down.weight]
+    params += [module.shared.gate.weight, module.shared.up.weight, module.shared.down.weight]
+    version = tuple((p._version, p.device, p.dtype, p.data_ptr()) for p in params)
+    if cached is not None and cached[0] == version:
+        return cached[1]
+    for p in params:
+        _require_device(p, "MoE")
+    lib = _lib.load()
+    with torch.no_grad():
+        cfg = module.cfg
+        E, H, Hs, d = cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim, cfg.dim
+        gate = torch.stack([e.gate.weight.detach() for e in module.experts]).contiguous()
+        up = torch.stack([e.up.weight.detach() for e in module.experts]).contiguous()
+        gate_up = torch.empty((E, 2 * H, d), device=gate.device, dtype=gate.dtype)
+        _lib.check(lib.parrot_pack_gate_up_bf16(_p(gate_up), _p(gate), _p(up), E, H, d,
+                                                _stream()), "parrot_pack_gate_up_bf16")
+        down = torch.stack([e.down.weight.detach() for e in module.experts]).contiguous()
+        sg = module.shared.gate.weight.detach().contiguous()
+        su = module.shared.up.weight.detach().contiguous()
+        shared_gate_up = torch.empty((2 * Hs, d), device=sg.device, dtype=sg.dtype)
+        _lib.check(lib.parrot_pack_gate_up_bf16(_p(shared_gate_up), _p(sg), _p(su), 1, Hs, d,
+                                                _stream()), "parrot_pack_gate_up_bf16")
+        packed = (module.router.weight.detach().contiguous(), gate_up, down, shared_gate_up,
+                  module.shared.down.weight.detach().contiguous())
+    module.__dict__["_b200_pack"] = (version, packed)
+    return packed
+
+
+def invalidate_packed_weights(module) -> None:
+    module.__dict__.pop("_b200_pack", None)
+
+
+def moe_dims(cfg, tokens: int, capacity: int = 0) -> _lib.MoeDims:
+    return _lib.MoeDims(tokens, cfg.dim, cfg.n_experts, cfg.top_k, cfg.expert_dim,
+                        cfg.shared_expert_dim, capacity)
+
+
+def workspace_layout(dims: _lib.MoeDims) -> _lib.MoeLayout:
+    layout = _lib.MoeLayout()
+    _lib.check(_lib.load().parrot_moe_workspace_layout(ctypes.byref(dims), ctypes.byref(layout)),
+               "parrot_moe_workspace_layout")
+    return layout
+
+
+def workspace(device: torch.device, dims: _lib.MoeDims) -> Tensor:
+    """Zero-initialised workspace shared by all MoE layers of one shape on ``device``.
+
+    Calls that share a workspace must be ordered on one stream.
+    """
+    key = (device.index if device.index is not None else torch.cuda.current_device(),
+           dims.tokens, dims.dim, dims.n_experts, dims.expert_dim, dims.shared_dim,
+           dims.capacity)
+    ws = _WORKSPACES.get(key)
+    if ws is None:
+        layout = workspace_layout(dims)
+        ws = torch.zeros(int(layout.total), device=device, dtype=torch.uint8)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def _weights_struct(packed, bias: Tensor | None) -> _lib.MoeWeights:
+    router, gate_up, down, sgu, sd = packed
+    return _lib.MoeWeights(router.data_ptr(), None if bias is None else bias.data_ptr(),
+                           gate_up.data_ptr(), down.data_ptr(), sgu.data_ptr(), sd.data_ptr())
+
+
+def _router_bias(module) -> Tensor | None:
+    bias = getattr(module, "router_bias", None)
+    if bias is None:
+        return None
+    return bias.to(device=module.router.weight.device, dtype=torch.float32).contiguous()
+
+
+def b200_moe(module, flat: Tensor, collect_stats: bool, addend: Tensor | None = None):
+    """Whole MoE block on ``flat`` [T, d]: returns ``(out, aux, utilization)``.
+
+    ``out = addend + moe(flat)`` when ``addend`` is given (the residual add of
+    ``model.py:585`` / ``:702`` fused into the combine).  ``aux`` and
+    ``utilization`` are ``None`` unless ``collect_stats``.
+    """
+    _require_device(flat, "MoE")
+    _require_inference("MoE")
+    flat = flat.contiguous()
+    T, d = flat.shape
+    cfg = module.cfg
+    packed = pack_weights(module)
+    dims = moe_dims(cfg, T)
+    ws = workspace(flat.device, dims)
+    out = torch.empty_like(flat)
+    if addend is not None:
+        addend = addend.reshape(T, d).contiguous()
+        _require_device(addend, "MoE")
+    stats = torch.empty(cfg.n_experts + 1, device=flat.device, dtype=torch.float32) \
+        if collect_stats else None
+    bias = _router_bias(module)
+    outputs = _lib.MoeOutputs(out.data_ptr(), None if addend is None else addend.data_ptr(),
+                              None, None, None, None, None,
+                              None if stats is None else stats.data_ptr())
+    weights = _weights_struct(packed, bias)
+    _lib.check(_lib.load().parrot_moe_forward_bf16(
+        ctypes.byref(dims), ctypes.byref(weights), _p(flat), ctypes.byref(outputs),
+        _p(ws), ws.numel(), _stream()), "parrot_moe_forward_bf16")
+    if stats is None:
+        return out, None, None
+    return out, stats[cfg.n_experts], stats[:cfg.n_experts]
+
+
+def b200_route(module, flat: Tensor, collect_stats: bool):
+    """Router + grouping: ``(probs|None, weights, indices, positions, counts)``.
+
+    Same outputs as ``metal_route`` (``metal_moe.py:58-81``): fp32 softmax
+    probabilities (when ``collect_stats``), renormalised top-2 weights
+    [T, 2] fp32, expert ids [T, 2] int64, grouped row of each assignment
+    [2T] int32 and per-expert counts [E] int32.  The grouped token rows stay in
+    the shared workspace for ``b200_experts``.
+    """
+    _require_device(flat, "MoE")
+    _require_inference("MoE")
+    flat = flat.contiguous()
+    T, d = flat.shape
+    cfg = module.cfg
+    packed = pack_weights(module)
+    dims = moe_dims(cfg, T)
+    ws = workspace(flat.device, dims)
+    dev = flat.device
+    probs = torch.empty((T, cfg.n_experts), device=dev, dtype=torch.float32) \
+        if collect_stats else None
+    weights = torch.empty((T, 2), device=dev, dtype=torch.float32)
+    indices = torch.empty((T, 2), device=dev, dtype=torch.int64)
+    positions = torch.empty(2 * T, device=dev, dtype=torch.int32)
+    counts = torch.empty(cfg.n_experts, device=dev, dtype=torch.int32)
+    placeholder = torch.empty_like(flat[:1]) if T else flat
+    outputs = _lib.MoeOutputs(placeholder.data_ptr(), None, _p(probs), indices.data_ptr(),
+                              weights.data_ptr(), positions.data_ptr(), counts.data_ptr(), None)
+    wst = _weights_struct(packed, _router_bias(module))
+    _lib.check(_lib.load().parrot_moe_route_bf16(
+        ctypes.byref(dims), ctypes.byref(wst), _p(flat), ctypes.byref(outputs), _p(ws),
+        ws.numel(), _stream()), "parrot_moe_route_bf16")
+    ws.__dict__["_b200_routed"] = (flat.data_ptr(), positions.data_ptr())
+    return probs, weights, indices, positions, counts
+
+
+def b200_experts(module, flat: Tensor, indices: Tensor, weights: Tensor,
+                 positions: Tensor, counts: Tensor, addend: Tensor | None = None) -> Tensor:
+    """Experts + shared expert + combine after ``b200_route`` (``metal_moe.py:372-416``).
+
+    ``positions`` must be the tensor ``b200_route`` returned for this ``flat``:
+    the grouped rows it refers to live in the shared workspace.
+    """
+    _require_device(flat, "MoE")
+    _require_inference("MoE")
+    flat = flat.contiguous()
+    T, d = flat.shape
+    packed = pack_weights(module)
+    dims = moe_dims(module.cfg, T)
+    ws = workspace(flat.device, dims)
+    if ws.__dict__.get("_b200_routed") != (flat.data_ptr(), positions.data_ptr()):
+        raise ValueError("b200_experts needs the positions returned by b200_route for this input")
+    out = torch.empty_like(flat)
+    if addend is not None:
+        addend = addend.reshape(T, d).contiguous()
+    outputs = _lib.MoeOutputs(out.data_ptr(), None if addend is None else addend.data_ptr(),
+                              None, None, None, None, None, None)
+    wst = _weights_struct(packed, _router_bias(module))
+    _lib.check(_lib.load().parrot_moe_experts_bf16(
+        ctypes.byref(dims), ctypes.byref(wst), _p(flat), ctypes.byref(outputs), _p(ws),
+        ws.numel(), _stream()), "parrot_moe_experts_bf16")
+    return out
+
+
+def read_status(flat_tokens: int, cfg, device: torch.device) -> list[int]:
+    """Device status word of the workspace used for ``flat_tokens`` (synchronises)."""
+    dims = moe_dims(cfg, flat_tokens)
+    ws = workspace(device, dims)
+    buf = (ctypes.c_int * 4)()
+    _lib.check(_lib.load().parrot_moe_read_status(_p(ws), ctypes.byref(dims), buf, _stream()),
+               "parrot_moe_read_status")
+    return list(buf)

@@ -1,0 +1,103 @@
+"""Shared helpers for the GPU parity tests (the oracle is the checker)."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from oracle import parrot_oracle as po
+from parrot_b200 import _lib, bridge
+from parrot_b200 import model as pm
+from parrot_b200.workloads import make_hidden_states, make_moe_layer_weights
+
+
+def bf16_round(t: torch.Tensor) -> torch.Tensor:
+    return t.to(torch.bfloat16).float()
+
+
+def rel_max_err(actual: torch.Tensor, expected: torch.Tensor) -> float:
+    """max |a - e| / rms(e) — the north-star tolerance metric."""
+    a, e = actual.float().cpu(), expected.float().cpu()
+    rms = e.pow(2).mean().sqrt().clamp_min(1e-30)
+    return float((a - e).abs().max() / rms)
+
+
+def cosine(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.double().flatten().cpu(), b.double().flatten().cpu()
+    return float(a @ b / (a.norm() * b.norm()))
+
+
+def moe_config(dim=768, n_experts=16, expert_dim=512, shared_dim=256, **kw) -> pm.ModelConfig:
+    return pm.ModelConfig(dim=dim, n_experts=n_experts, expert_dim=expert_dim,
+                          shared_expert_dim=shared_dim, n_heads=max(1, dim // 96),
+                          n_kv_heads=1, head_dim=96 if dim % 96 == 0 else 32, **kw)
+
+
+def build_moe_pair(cfg: pm.ModelConfig, seed: int, std: float = 0.02):
+    """(product MoE on cuda bf16, oracle MoE on cpu fp32) with identical bf16 weights."""
+    w = make_moe_layer_weights(cfg.dim, cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim,
+                               seed=seed, std=std)
+    w = {k: bf16_round(v) for k, v in w.items()}
+    prod = pm.MoE(cfg)
+    prod.load_state_dict(w)
+    prod = prod.to("cuda", torch.bfloat16).eval()
+    ocfg = po.OracleConfig(dim=cfg.dim, n_experts=cfg.n_experts, expert_dim=cfg.expert_dim,
+                           shared_expert_dim=cfg.shared_expert_dim,
+                           collect_router_stats=True)
+    orc = po.MoE(ocfg)
+    orc.load_state_dict(w)
+    orc.eval()
+    return prod, orc
+
+
+def hidden_states(tokens: int, dim: int, seed: int) -> torch.Tensor:
+    return make_hidden_states(tokens, dim, seed).to(torch.bfloat16)
+
+
+def workspace_view(ws: torch.Tensor, layout, name: str, dtype, shape) -> torch.Tensor:
+    off = getattr(layout, name)
+    n = 1
+    for s in shape:
+        n *= s
+    nbytes = n * torch.tensor([], dtype=dtype).element_size()
+    return ws[off:off + nbytes].view(dtype).view(*shape)
+
+
+def call_moe_forward(module, x: torch.Tensor, capacity: int = 0, residual=None,
+                     want_probs=True):
+    """Direct C-ABI call with an explicit capacity; returns (out, extras dict, ws, layout)."""
+    cfg = module.cfg
+    T = x.shape[0]
+    dims = _lib.MoeDims(T, cfg.dim, cfg.n_experts, 2, cfg.expert_dim, cfg.shared_expert_dim,
+                        capacity)
+    layout = bridge.workspace_layout(dims)
+    ws = torch.zeros(int(layout.total), device="cuda", dtype=torch.uint8)
+    packed = bridge.pack_weights(module)
+    bias = bridge._router_bias(module)
+    w = bridge._weights_struct(packed, bias)
+    dev = x.device
+    out = torch.empty_like(x)
+    ex = {
+        "probs": torch.full((T, cfg.n_experts), float("nan"), device=dev) if want_probs else None,
+        "indices": torch.full((T, 2), -7, device=dev, dtype=torch.int64),
+        "weights": torch.full((T, 2), float("nan"), device=dev),
+        "positions": torch.full((2 * T,), -7, device=dev, dtype=torch.int32),
+        "counts": torch.full((cfg.n_experts,), -7, device=dev, dtype=torch.int32),
+        "stats": torch.full((cfg.n_experts + 1,), float("nan"), device=dev),
+    }
+    o = _lib.MoeOutputs(out.data_ptr(), None if residual is None else residual.data_ptr(),
+                        *[None if ex[k] is None else ex[k].data_ptr()
+                          for k in ("probs", "indices", "weights", "positions", "counts",
+                                    "stats")])
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = _lib.load().parrot_moe_forward_bf16(ctypes.byref(dims), ctypes.byref(w),
+                                             ctypes.c_void_p(x.data_ptr()), ctypes.byref(o),
+                                             ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream)
+    _lib.check(rc, "parrot_moe_forward_bf16")
+    torch.cuda.synchronize()
+    status = (ctypes.c_int * 4)()
+    _lib.check(_lib.load().parrot_moe_read_status(ctypes.c_void_p(ws.data_ptr()),
+                                                  ctypes.byref(dims), status, stream),
+               "parrot_moe_read_status")
+    ex["status"] = list(status)
+    return out, ex, ws, layout

@@ -1,0 +1,144 @@
+"""Host-side checks that need no GPU: the C ABI loads and exports every
+declared symbol, the pure-host queries agree with the oracle, and the
+product's config/module tree matches the reference's."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import parrot_oracle as po
+from parrot_b200 import ModelConfig, Parrot, _lib
+from parrot_b200 import build as pbuild
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "parrot_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(parrot_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    pbuild.build()
+    return _lib.load()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = declared_functions()
+    assert len(names) >= 12
+    for name in names:
+        assert hasattr(lib, name), name
+    assert sorted(_lib.exported_names()) == names
+
+
+def test_version_and_error_string(lib):
+    assert lib.parrot_b200_version() == 100
+    assert isinstance(lib.parrot_b200_last_error(), bytes)
+
+
+@pytest.mark.parametrize("tokens,experts", [(0, 16), (1, 16), (256, 16), (512, 16), (16384, 16),
+                                            (7, 4), (33, 2), (100, 32)])
+def test_capacity_matches_oracle(lib, tokens, experts):
+    assert lib.parrot_moe_capacity(tokens, experts) == po.expert_capacity(2 * tokens, experts)
+
+
+def test_workspace_layout_is_aligned_and_ordered(lib):
+    dims = _lib.MoeDims(512, 768, 16, 2, 512, 256, 0)
+    lay = _lib.MoeLayout()
+    assert lib.parrot_moe_workspace_layout(ctypes.byref(dims), ctypes.byref(lay)) == 0
+    offsets = [getattr(lay, n) for n in _lib.LAYOUT_OFFSETS]
+    assert all(o % 256 == 0 for o in offsets)
+    assert lay.capacity == 128
+    assert lay.grouped_rows == 16 * 128 + 1024
+    assert lay.route_blocks == 16
+    assert lay.shared_y + 512 * 768 * 2 <= lay.total
+
+
+@pytest.mark.parametrize("field,value", [("top_k", 1), ("dim", 96), ("n_experts", 33),
+                                         ("expert_dim", 100), ("shared_dim", 0)])
+def test_layout_rejects_unsupported_dims(lib, field, value):
+    d = dict(tokens=8, dim=768, n_experts=16, top_k=2, expert_dim=512, shared_dim=256, capacity=0)
+    d[field] = value
+    dims = _lib.MoeDims(**d)
+    lay = _lib.MoeLayout()
+    assert lib.parrot_moe_workspace_layout(ctypes.byref(dims), ctypes.byref(lay)) == _lib.PARROT_EINVAL
+    assert lib.parrot_b200_last_error()
+
+
+def test_entry_points_reject_bad_arguments_before_launch(lib):
+    # argument errors are detected on the host, so these need no GPU
+    assert lib.parrot_rmsnorm_bf16(None, None, None, 4, 100, 1e-6, None) == _lib.PARROT_EINVAL
+    assert lib.parrot_depthmix_bf16(None, None, 0, None, None, 1e-6, None, 1e-6, None, None,
+                                    None, None, 4, 768, None) == _lib.PARROT_EINVAL
+    assert lib.parrot_pack_gate_up_bf16(None, None, None, 1, 100, 768, None) == _lib.PARROT_EINVAL
+    dims = _lib.MoeDims(4, 768, 16, 2, 512, 256, 0)
+    w = _lib.MoeWeights()
+    o = _lib.MoeOutputs()
+    assert lib.parrot_moe_forward_bf16(ctypes.byref(dims), ctypes.byref(w), None, ctypes.byref(o),
+                                       None, 0, None) == _lib.PARROT_EINVAL
+
+
+def tiny_b200(**kw):
+    base = dict(vocab_size=32768, dim=128, n_layers=4, n_heads=4, n_kv_heads=2, head_dim=32,
+                kv_latent_dim=32, n_experts=8, expert_dim=128, shared_expert_dim=64,
+                window_size=128, max_seq_len=512)
+    base.update(kw)
+    return ModelConfig(**base)
+
+
+def test_seeded_init_and_state_dict_match_reference_layout():
+    torch.manual_seed(0)
+    model = Parrot(tiny_b200())
+    torch.manual_seed(0)
+    oracle = po.OracleParrot(po.tiny_config())
+    a, b = model.state_dict(), oracle.state_dict()
+    assert list(a) == list(b)
+    for k in a:
+        assert torch.equal(a[k], b[k]), k
+
+
+def test_default_config_is_parrot_xl():
+    cfg = ModelConfig()
+    assert (cfg.dim, cfg.n_layers, cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim) == \
+        (768, 16, 16, 512, 256)
+    assert cfg.depth_sources == 9
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(moe_backend="pytorch"), "moe_backend"),
+    (dict(depth_backend="metal"), "depth_backend"),
+    (dict(top_k=1), "top_k"),
+    (dict(n_experts=33), "experts"),
+    (dict(dim=96, n_heads=1, n_kv_heads=1), "dim"),
+    (dict(expert_dim=500), "expert widths"),
+    (dict(n_heads=3), "n_heads"),
+    (dict(norm_eps=0.0), "norm_eps"),
+    (dict(vocab_size=0), "vocab_size"),
+])
+def test_config_validation(kw, msg):
+    with pytest.raises(ValueError, match=msg):
+        ModelConfig(**kw)
+
+
+def test_parameter_counts_match_reference_formula():
+    cfg = tiny_b200()
+    torch.manual_seed(0)
+    counts = Parrot(cfg).parameter_counts()
+    torch.manual_seed(0)
+    o = po.OracleParrot(po.tiny_config())
+    total = sum(p.numel() for p in o.parameters())
+    assert counts["total"] == total
+    assert counts["active_per_token"] == total - cfg.n_layers * (cfg.n_experts - 2) * 3 * \
+        cfg.dim * cfg.expert_dim
+
+
+def test_bridge_refuses_cpu_tensors():
+    from parrot_b200 import bridge
+    cfg = tiny_b200()
+    norm = Parrot(cfg).final_norm
+    with torch.inference_mode(), pytest.raises(RuntimeError, match="CUDA"):
+        bridge.b200_rms_norm(norm, torch.zeros(2, 128, dtype=torch.bfloat16))

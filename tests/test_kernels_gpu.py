@@ -1,0 +1,314 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle, through the C ABI.
+
+Contract: expert assignment and grouping permutation are
+bit-exact given identical router probabilities; floating-point outputs match
+within  max|out - oracle| <= 2e-2 * rms(oracle).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import parrot_oracle as po
+from parrot_b200 import _lib, bridge
+from parrot_b200 import model as pm
+from parrot_b200.workloads import tune_zipf_router_bias
+from tests.gpu_helpers import (bf16_round, build_moe_pair, call_moe_forward, hidden_states,
+                               moe_config, rel_max_err, workspace_view)
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2  # max-abs error relative to the oracle output RMS
+
+
+@pytest.fixture(autouse=True)
+def _inference():
+    with torch.inference_mode():
+        yield
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("rows,dim", [(1, 768), (7, 768), (512, 768), (33, 128), (5, 64),
+                                      (16, 2048)])
+def test_rmsnorm_matches_oracle(rows, dim):
+    g = torch.Generator().manual_seed(rows * 1000 + dim)
+    x = (torch.randn(rows, dim, generator=g) * 3).to(torch.bfloat16)
+    w = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16)
+    norm = pm.RMSNorm(dim, 1e-6)
+    norm.weight.data.copy_(w.float())
+    norm = norm.to("cuda", torch.bfloat16)
+    out = norm(x.cuda()).cpu()
+    ref = po.RMSNorm(dim, 1e-6)
+    ref.weight.data.copy_(w.float())
+    exp = ref(x.float())
+    assert rel_max_err(out, exp) < TOL
+    # bf16 reference semantics: one rounding of the fp32 result
+    diff = (out.float() - exp.to(torch.bfloat16).float()).abs()
+    assert float(diff.max()) <= float(exp.abs().max()) * 2 ** -7
+
+
+# ---------------------------------------------------------------------------
+# Block AttnRes depth mix (+ consumer RMSNorm, + deferred residual)
+# ---------------------------------------------------------------------------
+def _depth_modules(dim, seed):
+    g = torch.Generator().manual_seed(seed)
+    q = (0.5 * torch.randn(dim, generator=g)).to(torch.bfloat16).float()
+    kw = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16).float()
+    ow = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16).float()
+    cfg = moe_config(dim=dim if dim % 128 == 0 else 128)
+    prod = pm.DepthMix(cfg) if dim == cfg.dim else None
+    ocfg = po.OracleConfig(dim=dim)
+    orc = po.DepthMix(ocfg)
+    orc.query.data.copy_(q)
+    orc.norm.weight.data.copy_(kw)
+    onorm = po.RMSNorm(dim, 1e-6)
+    onorm.weight.data.copy_(ow)
+    return prod, orc, onorm, (q, kw, ow)
+
+
+def _sources(n, rows, dim, seed):
+    g = torch.Generator().manual_seed(seed)
+    return [(torch.randn(rows, dim, generator=g) * (1 + i)).to(torch.bfloat16) for i in range(n)]
+
+
+@pytest.mark.parametrize("n_sources", [1, 2, 5, 9, 16])
+@pytest.mark.parametrize("rows", [1, 7, 512])
+def test_depth_mix_norm_matches_oracle(n_sources, rows):
+    dim = 768
+    prod, orc, onorm, (q, kw, ow) = _depth_modules(dim, n_sources + rows)
+    prod.query.data.copy_(q)
+    prod.norm.weight.data.copy_(kw)
+    prod = prod.to("cuda", torch.bfloat16)
+    pnorm = pm.RMSNorm(dim, 1e-6)
+    pnorm.weight.data.copy_(ow)
+    pnorm = pnorm.to("cuda", torch.bfloat16)
+    srcs = _sources(n_sources, rows, dim, 7 * rows + n_sources)
+    got_mix = prod([s.cuda() for s in srcs]).cpu()
+    got = prod.normalized([s.cuda() for s in srcs], pnorm).cpu()
+    exp_mix = orc([s.float() for s in srcs])
+    exp = onorm(exp_mix)
+    assert rel_max_err(got_mix, exp_mix) < TOL
+    assert rel_max_err(got, exp) < TOL
+    # the oracle evaluated in bf16 (the reference's CUDA dtype) agrees more tightly
+    orc_b = orc.to(torch.bfloat16)
+    onorm_b = onorm.to(torch.bfloat16)
+    exp_b = onorm_b(orc_b(srcs))
+    assert rel_max_err(got, exp_b) < 1e-2
+
+
+def test_depth_mix_pending_residual_resolves_the_add():
+    dim, rows = 768, 64
+    prod, orc, onorm, (q, kw, ow) = _depth_modules(dim, 3)
+    prod.query.data.copy_(q)
+    prod.norm.weight.data.copy_(kw)
+    prod = prod.to("cuda", torch.bfloat16)
+    pnorm = pm.RMSNorm(dim, 1e-6)
+    pnorm.weight.data.copy_(ow)
+    pnorm = pnorm.to("cuda", torch.bfloat16)
+    srcs = _sources(4, rows, dim, 11)
+    delta = _sources(1, rows, dim, 12)[0]
+    resolved_ref = (srcs[-1].cuda() + delta.cuda())
+    got, resolved = prod.normalized([s.cuda() for s in srcs], pnorm, delta.cuda())
+    assert torch.equal(resolved, resolved_ref)
+    plain = prod.normalized([s.cuda() for s in srcs[:-1]] + [resolved_ref], pnorm)
+    assert torch.equal(got, plain)
+
+
+# ---------------------------------------------------------------------------
+# Router, grouping and the whole MoE block
+# ---------------------------------------------------------------------------
+def _check_routing(ex, module_cfg, oracle_trace, T):
+    probs = ex["probs"].float().cpu()
+    idx = ex["indices"].cpu()
+    # bit-exact selection given the kernel's own probabilities (ties flagged)
+    top3 = probs.topk(min(3, module_cfg.n_experts), dim=-1)
+    ties = (top3.values[:, 0] == top3.values[:, 1]).sum()
+    if module_cfg.n_experts > 2:
+        ties += (top3.values[:, 1] == top3.values[:, 2]).sum()
+    assert int(ties) == 0, "exact ties in the test inputs"
+    np.testing.assert_array_equal(idx.numpy(), probs.topk(2, dim=-1).indices.numpy())
+    w = ex["weights"].cpu()
+    sel = probs.gather(1, idx)
+    torch.testing.assert_close(w, sel / sel.sum(-1, keepdim=True), rtol=0, atol=0)
+    # against the oracle's own routing: equal wherever its decision margin is resolvable
+    op = oracle_trace.probabilities
+    torch.testing.assert_close(probs, op, rtol=1e-4, atol=1e-6)
+    margin = torch.minimum(op.topk(3, dim=-1).values[:, 1] - op.topk(3, dim=-1).values[:, 2],
+                           op.topk(2, dim=-1).values[:, 0] - op.topk(2, dim=-1).values[:, 1]) \
+        if module_cfg.n_experts > 2 else torch.ones(T)
+    clear = margin > 1e-5
+    np.testing.assert_array_equal(idx[clear].numpy(), oracle_trace.indices[clear].numpy())
+    # grouping: stable counting sort of the kernel's indices, exactly
+    grouping = po.group_assignments(idx.numpy(), module_cfg.n_experts)
+    rows = po.grouped_rows(grouping, idx.numpy())
+    np.testing.assert_array_equal(ex["positions"].cpu().numpy(), np.array(rows, dtype=np.int32))
+    np.testing.assert_array_equal(ex["counts"].cpu().numpy(), np.array(grouping.counts))
+    return grouping
+
+
+@pytest.mark.parametrize("tokens", [256, 512])
+def test_xl_moe_layer_matches_oracle(tokens):
+    cfg = moe_config()
+    prod, orc = build_moe_pair(cfg, seed=1)
+    x = hidden_states(tokens, cfg.dim, seed=0)
+    out, ex, ws, layout = call_moe_forward(prod, x.cuda())
+    assert ex["status"][0] == 0, ex["status"]
+    exp, aux, util = orc(x.float())
+    _check_routing(ex, cfg, orc.last_trace, tokens)
+    assert rel_max_err(out, exp) < TOL
+    stats = ex["stats"].cpu()
+    own = torch.bincount(ex["indices"].cpu().flatten(), minlength=cfg.n_experts).float() / (2 * tokens)
+    torch.testing.assert_close(stats[:-1], own, rtol=0, atol=0)
+    torch.testing.assert_close(stats[:-1], util, rtol=0, atol=2.0 / (2 * tokens))
+    torch.testing.assert_close(stats[-1], aux, rtol=2e-3, atol=1e-6)
+    # every assignment's token row was scattered to its grouped row
+    grouped = workspace_view(ws, layout, "grouped", torch.bfloat16,
+                             (layout.grouped_rows, cfg.dim)).cpu()
+    pos = ex["positions"].cpu().long()
+    tok = torch.arange(2 * tokens) // 2
+    assert torch.equal(grouped[pos], x[tok])
+
+
+def test_xl_moe_layer_intermediates_match_oracle_experts():
+    """gate_up+SwiGLU and down GEMM outputs, per grouped row, vs the oracle experts."""
+    cfg = moe_config()
+    T = 256
+    prod, orc = build_moe_pair(cfg, seed=1)
+    x = hidden_states(T, cfg.dim, seed=0)
+    out, ex, ws, layout = call_moe_forward(prod, x.cuda())
+    R = layout.grouped_rows
+    hidden = workspace_view(ws, layout, "hidden", torch.bfloat16, (R, cfg.expert_dim)).cpu()
+    y = workspace_view(ws, layout, "y", torch.bfloat16, (R, cfg.dim)).cpu()
+    sh = workspace_view(ws, layout, "shared_hidden", torch.bfloat16, (T, cfg.shared_expert_dim)).cpu()
+    sy = workspace_view(ws, layout, "shared_y", torch.bfloat16, (T, cfg.dim)).cpu()
+    idx = ex["indices"].cpu()
+    pos = ex["positions"].cpu().long()
+    xf = x.float()
+    for e in range(cfg.n_experts):
+        a = torch.nonzero(idx.flatten() == e).flatten()
+        if a.numel() == 0:
+            continue
+        tokens = a // 2
+        ex_mod = orc.experts[e]
+        g = ex_mod.gate(xf[tokens])
+        u = ex_mod.up(xf[tokens])
+        h_ref = torch.nn.functional.silu(g) * u
+        assert rel_max_err(hidden[pos[a]], h_ref) < TOL, e
+        y_ref = ex_mod.down(hidden[pos[a]].float())
+        assert rel_max_err(y[pos[a]], y_ref) < TOL, e
+    hs_ref = torch.nn.functional.silu(orc.shared.gate(xf)) * orc.shared.up(xf)
+    assert rel_max_err(sh, hs_ref) < TOL
+    assert rel_max_err(sy, orc.shared.down(sh.float())) < TOL
+
+
+@pytest.mark.parametrize("tokens,experts,dim,hidden,shared", [
+    (1, 16, 768, 512, 256), (2, 16, 768, 512, 256), (7, 4, 128, 64, 64),
+    (33, 2, 128, 128, 64), (100, 32, 256, 128, 128), (130, 8, 128, 192, 64),
+])
+def test_moe_edge_shapes(tokens, experts, dim, hidden, shared):
+    cfg = moe_config(dim=dim, n_experts=experts, expert_dim=hidden, shared_dim=shared)
+    prod, orc = build_moe_pair(cfg, seed=tokens + experts)
+    x = hidden_states(tokens, dim, seed=tokens)
+    out, ex, _, _ = call_moe_forward(prod, x.cuda())
+    assert ex["status"][0] == 0, ex["status"]
+    exp, _, _ = orc(x.float())
+    _check_routing(ex, cfg, orc.last_trace, tokens)
+    assert rel_max_err(out, exp) < TOL
+
+
+@pytest.mark.parametrize("capacity", [8, 16, 40])
+def test_forced_overflow_is_exact(capacity):
+    """Tiny capacities push most assignments through the overflow segments."""
+    cfg = moe_config(dim=256, n_experts=8, expert_dim=128, shared_dim=64)
+    prod, orc = build_moe_pair(cfg, seed=5)
+    T = 300
+    x = hidden_states(T, cfg.dim, seed=9)
+    out, ex, ws, layout = call_moe_forward(prod, x.cuda(), capacity=capacity)
+    assert ex["status"][0] == 0, ex["status"]
+    counts = ex["counts"].cpu()
+    assert int((counts - capacity).clamp_min(0).sum()) > 0
+    exp, _, _ = orc(x.float())
+    idx = ex["indices"].cpu()
+    grouping = po.group_assignments(idx.numpy(), cfg.n_experts, capacity=capacity)
+    rows = po.grouped_rows(grouping, idx.numpy())
+    np.testing.assert_array_equal(ex["positions"].cpu().numpy(), np.array(rows, dtype=np.int32))
+    assert rel_max_err(out, exp) < TOL
+
+
+def test_zipf_skew_overflow_matches_oracle():
+    """BASELINE config-4 routing skew (Zipf 1.2 over 16 experts) at 2048 tokens."""
+    cfg = moe_config()
+    prod, orc = build_moe_pair(cfg, seed=1)
+    T = 2048
+    x = hidden_states(T, cfg.dim, seed=0)
+    bias = tune_zipf_router_bias(x.float(), orc.router.weight.detach())
+    prod.router_bias = bias
+    orc.router_bias = bias
+    out, ex, _, layout = call_moe_forward(prod, x.cuda())
+    assert ex["status"][0] == 0, ex["status"]
+    counts = ex["counts"].cpu()
+    assert int(counts.max()) > layout.capacity  # the overflow path ran
+    exp, _, _ = orc(x.float())
+    _check_routing(ex, cfg, orc.last_trace, T)
+    assert rel_max_err(out, exp) < TOL
+
+
+def test_residual_is_fused_into_combine():
+    cfg = moe_config()
+    prod, orc = build_moe_pair(cfg, seed=2)
+    x = hidden_states(64, cfg.dim, seed=4).cuda()
+    r = hidden_states(64, cfg.dim, seed=5).cuda()
+    plain, _, _, _ = call_moe_forward(prod, x)
+    fused, _, _, _ = call_moe_forward(prod, x, residual=r)
+    assert torch.equal(fused, (r + plain))
+
+
+def test_moe_is_deterministic():
+    cfg = moe_config()
+    prod, _ = build_moe_pair(cfg, seed=3)
+    x = hidden_states(512, cfg.dim, seed=1).cuda()
+    a, ea, _, _ = call_moe_forward(prod, x)
+    b, eb, _, _ = call_moe_forward(prod, x)
+    assert torch.equal(a, b)
+    for k in ("indices", "positions", "counts", "weights"):
+        assert torch.equal(ea[k], eb[k]), k
+
+
+def test_zero_tokens_is_a_no_op():
+    cfg = moe_config()
+    prod, _ = build_moe_pair(cfg, seed=3)
+    x = torch.empty(0, cfg.dim, device="cuda", dtype=torch.bfloat16)
+    out, _, _ = bridge.b200_moe(prod, x, True)
+    assert out.shape == (0, cfg.dim)
+
+
+def test_route_then_experts_equals_fused():
+    cfg = moe_config()
+    prod, orc = build_moe_pair(cfg, seed=6)
+    x = hidden_states(200, cfg.dim, seed=2).cuda()
+    probs, w, idx, pos, counts = bridge.b200_route(prod, x, True)
+    staged = bridge.b200_experts(prod, x, idx, w, pos, counts)
+    fused, _, _ = bridge.b200_moe(prod, x, False)
+    assert torch.equal(staged, fused)
+    assert idx.dtype == torch.int64 and pos.dtype == torch.int32
+    with pytest.raises(ValueError):
+        bridge.b200_experts(prod, x.clone(), idx, w, pos, counts)
+
+
+def test_large_token_count_tensor_core_path():
+    """T = 4096: many token tiles per expert; checked through size-independent
+    properties plus sampled rows against the oracle."""
+    cfg = moe_config()
+    prod, orc = build_moe_pair(cfg, seed=7)
+    T = 4096
+    x = hidden_states(T, cfg.dim, seed=3)
+    out, ex, ws, layout = call_moe_forward(prod, x.cuda(), want_probs=True)
+    assert ex["status"][0] == 0
+    counts = ex["counts"].cpu()
+    assert int(counts.sum()) == 2 * T
+    sample = torch.arange(0, T, 61)
+    exp, _, _ = orc(x.float()[sample])
+    assert rel_max_err(out.cpu()[sample], exp) < TOL

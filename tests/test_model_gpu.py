@@ -1,0 +1,128 @@
+"""End-to-end parity of the B200 Parrot model against the CPU oracle.
+
+The product model (bf16 on the GPU, hot path on sm_100a kernels) and the
+oracle (fp32 on the CPU) load identical bf16-representable weights; logits
+must agree to cosine >= 0.9999.
+"""
+import pytest
+import torch
+
+from oracle import parrot_oracle as po
+from parrot_b200 import ModelConfig, Parrot
+from tests.gpu_helpers import cosine, rel_max_err
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(vocab_size=32768, dim=128, n_layers=4, n_heads=4, n_kv_heads=2, head_dim=32,
+            kv_latent_dim=32, n_experts=8, expert_dim=128, shared_expert_dim=64,
+            window_size=128, max_seq_len=512)
+
+
+def _pair(kw: dict, seed: int = 0, randomize: bool = False, **cfg_extra):
+    cfg = ModelConfig(**kw, **cfg_extra)
+    torch.manual_seed(seed)
+    prod = Parrot(cfg)
+    if randomize:
+        g = torch.Generator().manual_seed(seed + 100)
+        with torch.no_grad():
+            for name, p in prod.named_parameters():
+                if name.endswith("query"):
+                    p.copy_(0.5 * torch.randn(p.shape, generator=g))
+                elif p.ndim == 1:
+                    p.copy_(1 + 0.2 * torch.randn(p.shape, generator=g))
+    prod = prod.to("cuda", torch.bfloat16).eval()
+    okw = {k: v for k, v in cfg.__dict__.items()
+           if k in po.OracleConfig.__dataclass_fields__}
+    orc = po.OracleParrot(po.OracleConfig(**okw)).eval()
+    orc.load_state_dict({k: v.float().cpu() for k, v in prod.state_dict().items()})
+    return prod, orc
+
+
+@pytest.mark.parametrize("randomize", [False, True])
+def test_tiny_forward_logits(randomize):
+    prod, orc = _pair(TINY, randomize=randomize)
+    ids = torch.randint(0, 32768, (1, 512), generator=torch.Generator().manual_seed(0))
+    with torch.inference_mode():
+        got = prod(ids.cuda())
+    with torch.no_grad():
+        exp = orc(ids)
+    assert cosine(got.logits, exp.logits) >= 0.9999
+    agree = (got.logits.float().cpu().argmax(-1) == exp.logits.argmax(-1)).float().mean()
+    assert float(agree) >= 0.97
+    assert abs(float(got.aux_loss) - float(exp.aux_loss)) < 2e-2 * float(exp.aux_loss)
+    assert got.expert_utilization.shape == exp.expert_utilization.shape
+
+
+def test_tiny_forward_matches_golden_reference_argmax(golden_dir):
+    """Config 1 against the reference's own frozen outputs (seed-0 weights)."""
+    import numpy as np
+    g = np.load(golden_dir / "tiny_forward.npz")
+    cfg = ModelConfig(**TINY)
+    torch.manual_seed(0)
+    prod = Parrot(cfg).to("cuda", torch.bfloat16).eval()
+    ids = torch.from_numpy(g["ids"].astype(np.int64)).cuda()
+    with torch.inference_mode():
+        logits = prod(ids).logits[0].float().cpu()
+    rows = torch.from_numpy(g["rows"])
+    pos = torch.from_numpy(g["rows_pos"].astype(np.int64))
+    assert cosine(logits[pos], rows) >= 0.999
+    lse = torch.logsumexp(logits, -1)
+    assert float((lse - torch.from_numpy(g["lse"])).abs().max()) < 5e-2
+
+
+def test_forward_with_labels_bag4_and_supervised_only():
+    prod, orc = _pair(TINY, seed=3, randomize=True)
+    ids = torch.randint(0, 32768, (2, 128), generator=torch.Generator().manual_seed(4))
+    with torch.inference_mode():
+        got = prod(ids.cuda(), labels=ids.cuda(), bag_size=4, supervised_logits_only=True)
+    with torch.no_grad():
+        exp = orc(ids, labels=ids, bag_size=4, supervised_logits_only=True)
+    assert got.logits.shape == exp.logits.shape == (2, 31, 32768)
+    assert cosine(got.logits, exp.logits) >= 0.9999
+    assert abs(float(got.loss) - float(exp.loss)) < 2e-2
+
+
+def test_standard_residual_variant():
+    prod, orc = _pair(TINY, seed=5, residual="standard")
+    ids = torch.randint(0, 32768, (1, 96), generator=torch.Generator().manual_seed(6))
+    with torch.inference_mode():
+        got = prod(ids.cuda())
+    with torch.no_grad():
+        exp = orc(ids)
+    assert cosine(got.logits, exp.logits) >= 0.9999
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_prefill_and_decode(batch):
+    prod, orc = _pair(TINY, seed=7, randomize=True)
+    ids = torch.randint(0, 32768, (batch, 150), generator=torch.Generator().manual_seed(8))
+    lp, state = prod.prefill(ids[:, :140].cuda())
+    le, ostate = orc.prefill(ids[:, :140])
+    assert cosine(lp, le) >= 0.9999
+    for step in range(4):
+        nxt = ids[:, 140 + step:141 + step]
+        lp, state = prod.decode_step(nxt.cuda(), state)
+        le, ostate = orc.decode_step(nxt, ostate)
+        assert cosine(lp, le) >= 0.9999, step
+    assert state.position == 144
+    tok, state = prod.decode_next(ids[:, 144:145].cuda(), state)
+    assert tok.shape == (batch, 1)
+
+
+def test_xl_forward_1x512():
+    """Parrot XL default, seed 0, bf16 forward on 1x512 ids."""
+    prod, orc = _pair({}, seed=0)
+    ids = torch.randint(0, 32768, (1, 512), generator=torch.Generator().manual_seed(0))
+    with torch.inference_mode():
+        got = prod(ids.cuda())
+    with torch.no_grad():
+        exp = orc(ids)
+    assert cosine(got.logits, exp.logits) >= 0.9999
+    assert rel_max_err(got.logits, exp.logits) < 0.1
+
+
+def test_forward_requires_inference_mode():
+    prod, _ = _pair(TINY)
+    ids = torch.randint(0, 32768, (1, 16)).cuda()
+    with pytest.raises(RuntimeError, match="inference-only"):
+        prod(ids)
