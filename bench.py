@@ -113,7 +113,6 @@ def cpu_reference_forward(steps: int, warmup: int) -> dict:
     cores = po.oracle_threads()
     torch.manual_seed(0)
     model = po.OracleParrot(po.OracleConfig()).eval()
-    model.config.__class__  # frozen config; router stats stay on, like the reference default
     ids = random_token_ids(1, SEQ, 32768, seed=0)
     with torch.no_grad():
         for _ in range(warmup):
@@ -152,11 +151,16 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def time_moe_kernels(model, steps: int, tokens: int) -> dict:
-    """Per-launch CUDA-event timing of the gate_up grouped GEMM and of the whole
-    MoE block, cycling through the model's 16 MoE layers so each launch streams
-    its weights from HBM (16 x 26 MB > L2)."""
+def time_moe_kernels(model, tokens: int, replays: int = 20) -> dict:
+    """CUDA-event timing of the gate_up grouped GEMM and of the whole MoE block.
+
+    Each is captured as one CUDA graph of 16 back-to-back launches that cycle
+    through the model's 16 MoE layers, so every launch streams its own 26 MB
+    of expert weights from HBM (16 x 26 MB > the 126 MB L2); the graph is
+    replayed ``replays`` times between two events on the launching stream.
+    """
     from parrot_b200 import _lib, bridge
+    from parrot_b200.graphs import capture_calls
     lib = _lib.load()
     cfg = model.config
     layers = [b.moe for b in model.blocks]
@@ -166,39 +170,38 @@ def time_moe_kernels(model, steps: int, tokens: int) -> dict:
         bridge.b200_route(layers[0], x, False)
         dims = bridge.moe_dims(cfg, tokens)
         ws = bridge.workspace(x.device, dims)
-        stream = torch.cuda.current_stream()
-        sp = ctypes.c_void_p(stream.cuda_stream)
         structs = [bridge._weights_struct(bridge.pack_weights(m), None) for m in layers]
-        gemm_ms, moe_ms = [], []
-        n = max(steps, 2 * len(layers))
-        for i in range(n + len(layers)):
-            w = structs[i % len(layers)]
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
+
+        def gemm_cycle():
+            sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for w in structs:
+                _lib.check(lib.parrot_moe_gemm_bf16(
+                    ctypes.byref(dims), ctypes.byref(w), ctypes.c_void_p(x.data_ptr()),
+                    ctypes.c_void_p(ws.data_ptr()), ws.numel(), 0, sp), "parrot_moe_gemm_bf16")
+
+        def moe_cycle():
+            for m in layers:
+                bridge.b200_moe(m, x, False)
+
+        out = {}
+        for name, fn in (("gemm", gemm_cycle), ("moe", moe_cycle)):
+            graph = capture_calls(fn)
+            graph.replay()
+            torch.cuda.synchronize()
+            stream = torch.cuda.current_stream()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            _lib.check(lib.parrot_moe_gemm_bf16(ctypes.byref(dims), ctypes.byref(w),
-                                                ctypes.c_void_p(x.data_ptr()),
-                                                ctypes.c_void_p(ws.data_ptr()), ws.numel(), 0, sp),
-                       "parrot_moe_gemm_bf16")
+            for _ in range(replays):
+                graph.replay()
             b.record(stream)
-            if i >= len(layers):
-                gemm_ms.append((a, b))
-        for i in range(n + len(layers)):
-            m = layers[i % len(layers)]
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            bridge.b200_moe(m, x, False)
-            b.record(stream)
-            if i >= len(layers):
-                moe_ms.append((a, b))
-        torch.cuda.synchronize()
-    gemm = statistics.mean(a.elapsed_time(b) for a, b in gemm_ms)
-    moe = statistics.mean(a.elapsed_time(b) for a, b in moe_ms)
+            torch.cuda.synchronize()
+            out[f"{name}_ms"] = a.elapsed_time(b) / (replays * len(layers))
+            del graph
     E, H, Hs, d = cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim, cfg.dim
     A = 2 * tokens
-    algo_bytes = 2 * (E * 2 * H * d + 2 * Hs * d + A * d + tokens * d + A * H + tokens * Hs)
-    return {"gemm_ms": gemm, "moe_ms": moe, "gemm_bytes": algo_bytes, "launches": len(gemm_ms)}
+    out["gemm_bytes"] = 2 * (E * 2 * H * d + 2 * Hs * d + A * d + tokens * d + A * H + tokens * Hs)
+    out["launches"] = replays * len(layers)
+    return out
 
 
 def run_b200(args):
@@ -233,34 +236,47 @@ def run_b200(args):
         torch.cuda.synchronize()
 
     with torch.inference_mode():
-        for _ in range(max(3, args.warmup)):
+        # eager forward: warm-up, launch count per forward, eager time (context only)
+        model(ids)
+        l0 = lib.parrot_b200_launch_count()
+        model(ids)
+        launches_per_forward = lib.parrot_b200_launch_count() - l0
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(3):
             model(ids)
+        torch.cuda.synchronize()
+        eager_ms = (time.perf_counter() - t0) * 1000 / 3
+
+        graphed = model.capture(1, SEQ)
+        graphed(ids)
+        for _ in range(max(3, args.warmup)):
+            graphed.graph.replay()
         barrier()
         sampler = ClockSampler(local)
         sampler.start()
-        launches0 = lib.parrot_b200_launch_count()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(args.steps):
-            out = model(ids)
+            graphed.graph.replay()
         end.record(stream)
         barrier()
-        launches = lib.parrot_b200_launch_count() - launches0
         ms = start.elapsed_time(end)
 
-        # end to end: pinned H2D ids + forward + D2H logits, every step
+        # end to end through the public call: pinned H2D ids, replay, D2H logits
+        out = graphed.output
         logits_host = torch.empty(out.logits.shape, dtype=out.logits.dtype, pin_memory=True)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
-            ids.copy_(ids_host, non_blocking=True)
-            o = model(ids)
+            o = graphed(ids_host)
             logits_host.copy_(o.logits, non_blocking=True)
         e1.record(stream)
         barrier()
         clocks = sampler.stop()
         e2e_ms = e0.elapsed_time(e1)
+        launches = launches_per_forward * args.steps
 
     def max_over_ranks(v: float) -> float:
         if dist is None:
@@ -271,8 +287,8 @@ def run_b200(args):
 
     ms = max_over_ranks(ms)
     e2e_ms = max_over_ranks(e2e_ms)
-    kern = time_moe_kernels(model, args.steps, SEQ) if rank == 0 else None
-    kern256 = time_moe_kernels(model, args.steps, 256) if rank == 0 else None
+    kern = time_moe_kernels(model, SEQ) if rank == 0 else None
+    kern256 = time_moe_kernels(model, 256) if rank == 0 else None
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -288,6 +304,7 @@ def run_b200(args):
         "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (uniform token ids, random-init Parrot XL, seed 0)",
+        "timing": "CUDA-graph replay of Parrot.forward (Parrot.capture); events on the replay stream",
         "config": {"workload": "Parrot XL forward 1x512 incl. full logits (BASELINE config 3)",
                    "model": "Parrot XL (16 layers, 16 experts top-2, d=768)",
                    "global_batch": world, "seq_len": SEQ,
@@ -298,6 +315,8 @@ def run_b200(args):
                 "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(),
                 "d2h_bytes_per_step": logits_host.numel() * logits_host.element_size()},
         "gpu_launches": int(launches),
+        "launches_per_forward": int(launches_per_forward),
+        "eager_ms_per_step": eager_ms,
         "roofline": {"kernel": "grouped_gemm_kernel (gate_up + SwiGLU, routed + shared), T=512",
                      "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_source": peak_kind,

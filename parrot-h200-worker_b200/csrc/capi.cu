@@ -214,7 +214,8 @@ int prepare(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void
   int rc = layout_of(dims, L);
   if (rc) return rc;
   if ((rc = check_weights(w))) return rc;
-  if (o == nullptr || o->out == nullptr) return fail(PARROT_EINVAL, "outputs->out is required%s");
+  if (o == nullptr || (dims->tokens > 0 && o->out == nullptr))
+    return fail(PARROT_EINVAL, "outputs->out is required%s");
   if (ws == nullptr || ws_bytes < L->total || !aligned16(ws))
     return fail(PARROT_EINVAL, "workspace missing, misaligned or smaller than the layout total%s");
   if (dims->tokens > 0 && (x == nullptr || !aligned16(x) || !aligned16(o->out) ||

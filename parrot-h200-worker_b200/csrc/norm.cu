@@ -73,13 +73,15 @@ int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat
 // Depth mix (model.py:149-155) with optional consumer RMSNorm (model.py:157-164)
 // and optional deferred residual (model.py:702: partial = partial + delta).
 //
-// Per token row t and source i:
-//   key_i  = bf16(v_i * rsqrt(mean(v_i^2) + key_eps) * key_w)      (F.rms_norm)
-//   s_i    = sum_d key_i[d] * q[d]                                 (fp32)
-//   a_i    = bf16(softmax_i(s)_i)
-//   h      = bf16(sum_i bf16(a_i * v_i))
+// Per token row t and source i, all in fp32:
+//   key_i  = v_i * rsqrt(mean(v_i^2) + key_eps) * key_w            (F.rms_norm)
+//   s_i    = sum_d key_i[d] * q[d]
+//   a      = softmax_i(s)
+//   h      = bf16(sum_i a_i * v_i)                                 (the mixed tensor)
 //   out    = out_w ? bf16((h * rsqrt(mean(h^2) + out_eps)) * out_w) : h
-// Rounding points follow the bf16 tensors the reference materialises.
+// Scores and weights stay fp32 (as the reference's fused Metal kernel keeps
+// them, moe_bf16.metal:331-435): with a peaked softmax over sources, rounding
+// the keys to bf16 first would move the weights by percents.
 // When `pending_delta` is set, the last source is bf16(pending_base + delta)
 // and is written to `pending_out` (the resolved partial block sum).
 // ---------------------------------------------------------------------------
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(128) depthmix_kernel(DepthMixArgs a) {
         float f[8];
         bf16x8_to_float(v[i], f);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) dot = fmaf(round_bf16((f[j] * inv) * kw[i][j]), q[i][j], dot);
+        for (int j = 0; j < 8; ++j) dot = fmaf((f[j] * inv) * kw[i][j], q[i][j], dot);
       }
     }
     dot = warp_sum(dot);
@@ -162,7 +164,7 @@ __global__ void __launch_bounds__(128) depthmix_kernel(DepthMixArgs a) {
     score[s] = expf(score[s] - smax);
     den += score[s];
   }
-  for (int s = 0; s < S; ++s) score[s] = round_bf16(score[s] / den);
+  for (int s = 0; s < S; ++s) score[s] = score[s] / den;
 
   float h[V][8];
 #pragma unroll
@@ -180,7 +182,7 @@ __global__ void __launch_bounds__(128) depthmix_kernel(DepthMixArgs a) {
         float f[8];
         bf16x8_to_float(is_pend ? pend[i] : __ldg(src + c), f);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) h[i][j] += round_bf16(alpha * f[j]);
+        for (int j = 0; j < 8; ++j) h[i][j] = fmaf(alpha, f[j], h[i][j]);
       }
     }
   }

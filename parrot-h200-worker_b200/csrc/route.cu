@@ -133,14 +133,19 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
   if (!last_s) return;
   __threadfence();
 
-  // ---- last block: per-expert exclusive prefix over blocks (one warp per expert)
+  // ---- last block: one warp per expert builds the exclusive prefix over
+  // blocks (warp scan, 32 blocks per step) and the probability column sum
+  // (lane partials in block order, then a fixed-order tree: deterministic).
   const int nb = gridDim.x;
   __shared__ int count_s[kMaxExperts];
+  __shared__ float psum_e[kMaxExperts];
   for (int e = warp; e < E; e += kRouteWarps) {
     int carry = 0;
+    float ps = 0.f;
     for (int base = 0; base < nb; base += 32) {
       const int b = base + lane;
       const int v = (b < nb) ? __ldcg(a.tab.block_hist + b * E + e) : 0;
+      if (b < nb) ps += __ldcg(a.tab.block_probsum + b * E + e);
       int incl = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -150,7 +155,11 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
       if (b < nb) a.tab.block_prefix[b * E + e] = carry + incl - v;
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (lane == 0) count_s[e] = carry;
+    ps = warp_sum(ps);
+    if (lane == 0) {
+      count_s[e] = carry;
+      psum_e[e] = ps;
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -167,11 +176,9 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
       a.tab.seg_rows[E + e] = ov;
       a.tab.seg_base[E + e] = overflow_base;
       overflow_base += ov;
-      float ps = 0.f;
-      for (int b = 0; b < nb; ++b) ps += __ldcg(a.tab.block_probsum + b * E + e);
       const float util = (float)c / (float)A;
       a.tab.stats[e] = util;
-      aux += util * (ps / (float)T);
+      aux += util * (psum_e[e] / (float)T);
     }
     a.tab.stats[E] = (float)E * aux;
     *a.tab.done_counter = 0;  // ready for the next launch

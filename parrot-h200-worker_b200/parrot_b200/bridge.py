@@ -46,6 +46,19 @@ def _require_inference(what: str) -> None:
             "torch.inference_mode() or torch.no_grad()")
 
 
+def param_key(p: Tensor) -> tuple:
+    """Cache key of a parameter: its version counter when it has one.
+
+    Tensors created under ``torch.inference_mode`` carry no version counter;
+    for those the key is the storage identity alone.
+    """
+    try:
+        version = p._version
+    except RuntimeError:
+        version = -1
+    return (version, p.device, p.dtype, p.data_ptr())
+
+
 def _stream() -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
@@ -146,7 +159,7 @@ def pack_weights(module) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
     for e in module.experts:
         params += [e.gate.weight, e.up.weight, e.down.weight]
     params += [module.shared.gate.weight, module.shared.up.weight, module.shared.down.weight]
-    version = tuple((p._version, p.device, p.dtype, p.data_ptr()) for p in params)
+    version = tuple(param_key(p) for p in params)
     if cached is not None and cached[0] == version:
         return cached[1]
     for p in params:

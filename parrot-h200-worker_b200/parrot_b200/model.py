@@ -179,7 +179,7 @@ def _rotate(cfg: ModelConfig, x: Tensor, start: int) -> Tensor:
 
 def _packed(module: nn.Module, attr: str, params: tuple[Tensor, ...]) -> Tensor:
     """Concatenated projection weights, rebuilt when any parameter changes."""
-    version = tuple((p._version, p.device, p.dtype, p.data_ptr()) for p in params)
+    version = tuple(bridge.param_key(p) for p in params)
     hit = module.__dict__.get(attr)
     if hit is None or hit[0] != version:
         hit = (version, torch.cat([p.detach() for p in params], 0).contiguous())
@@ -291,7 +291,7 @@ class GlobalMLA(nn.Module):
         """Latent-space query / output weights (``model.py:362-397``)."""
         c = self.cfg
         params = (self.q.weight, self.k_up.weight, self.v_up.weight, self.out.weight)
-        version = tuple((p._version, p.device, p.dtype, p.data_ptr()) for p in params)
+        version = tuple(bridge.param_key(p) for p in params)
         hit = self.__dict__.get("_absorbed_cache")
         if hit is None or hit[0] != version:
             wq = self.q.weight.detach().float().view(c.n_heads, c.head_dim, c.dim)
@@ -317,7 +317,8 @@ class GlobalMLA(nn.Module):
         cache.latent[:, position:position + 1].copy_(self.kv_down(x))
         seen = cache.latent[:, :position + 1]
         q = F.linear(x.float(), aq.float()).view(b, 1, c.n_heads, c.kv_latent_dim).transpose(1, 2)
-        kv = seen[:, None].expand(-1, c.n_heads, -1, -1)
+        # the absorbed query is fp32 (model.py:420); attend over the latents in fp32 too
+        kv = seen[:, None].expand(-1, c.n_heads, -1, -1).float()
         ctx = F.scaled_dot_product_attention(q, kv, kv, scale=c.head_dim ** -0.5)
         ctx = ctx.transpose(1, 2).reshape(b, 1, c.n_heads * c.kv_latent_dim)
         out = F.linear(ctx, ao.float()).to(x.dtype)
@@ -622,6 +623,15 @@ class Parrot(nn.Module):
     def decode_next(self, input_ids: Tensor, state: GenerationState):
         """Append one token and return the next greedy token (``model.py:927-931``)."""
         return self.decode_step(input_ids, state, _next_token_only=True)
+
+    def capture(self, batch: int, source_len: int, **forward_kwargs):
+        """CUDA-graph replay of ``forward`` for one input shape.
+
+        Returns a ``graphs.GraphedForward``; calling it with ``[batch,
+        source_len]`` ids (host or device) runs the captured forward.
+        """
+        from .graphs import GraphedForward
+        return GraphedForward(self, batch, source_len, **forward_kwargs)
 
     def parameter_counts(self) -> dict[str, int]:
         total = sum(p.numel() for p in self.parameters())
