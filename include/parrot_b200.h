@@ -83,15 +83,16 @@ typedef struct parrot_moe_dims {
   int capacity;    /* slots per expert; 0 selects parrot_moe_capacity() */
 } parrot_moe_dims;
 
-/* Weights in torch.nn.Linear [out, in] layout.  gate_up / shared_gate_up are
- * packed by parrot_pack_gate_up_bf16 (rows interleaved per 64-feature tile). */
+/* Expert weights start in torch.nn.Linear [out, in] layout and are packed
+ * once into the tiled layout the GEMMs stream: gate_up / shared_gate_up by
+ * parrot_pack_gate_up_bf16, down / shared_down by parrot_pack_down_bf16. */
 typedef struct parrot_moe_weights {
-  const void* router;          /* [E, d] */
+  const void* router;          /* [E, d], nn.Linear layout */
   const float* router_bias;    /* [E] fp32 logit offset or NULL (harness only) */
-  const void* gate_up;         /* [E, 2H, d] packed */
-  const void* down;            /* [E, d, H] */
-  const void* shared_gate_up;  /* [2Hs, d] packed */
-  const void* shared_down;     /* [d, Hs] */
+  const void* gate_up;         /* E * 2H * d elements, parrot_pack_gate_up_bf16 */
+  const void* down;            /* E * d * H elements, parrot_pack_down_bf16 */
+  const void* shared_gate_up;  /* 2Hs * d elements, parrot_pack_gate_up_bf16 */
+  const void* shared_down;     /* d * Hs elements, parrot_pack_down_bf16 */
 } parrot_moe_weights;
 
 typedef struct parrot_moe_outputs {
@@ -109,7 +110,11 @@ typedef struct parrot_moe_outputs {
 typedef struct parrot_moe_layout {
   size_t indices, weights, positions, block_hist, block_prefix, block_probsum;
   size_t counts, seg_rows, seg_base, done_counter, stats, status;
-  size_t grouped, hidden, y, shared_hidden, shared_y, total;
+  size_t row_dst, row_w;  /* per grouped row: token-major slot, route weight */
+  size_t grouped;         /* [E*C + 2T, d] token rows grouped by expert */
+  size_t hidden;          /* [E*C + 2T, H] SwiGLU hidden, same row order */
+  size_t contrib;         /* [2T, d] bf16(bf16(y) * bf16(w)), slot 2t + (lower expert id first) */
+  size_t shared_hidden, shared_y, total;
   int capacity, grouped_rows, route_blocks, reserved;
 } parrot_moe_layout;
 
@@ -123,12 +128,21 @@ int parrot_moe_workspace_layout(const parrot_moe_dims* dims, parrot_moe_layout* 
  * a zero-filled allocation needs no call).  Enqueued on `stream`. */
 int parrot_moe_workspace_init(void* workspace, const parrot_moe_dims* dims, void* stream);
 
-/* Pack gate/up rows for the fused SwiGLU epilogue:
- * dst[m, tile*128 + 2i + {0,1}, :] = {gate, up}[m, tile*64 + i, :].
- * gate, up: [n_mats, hidden, dim]; dst: [n_mats, 2*hidden, dim]; hidden % 64 == 0.
+/* Pack gate/up for the fused SwiGLU GEMM.  Logical packed row p of matrix m
+ * is gate (p even) or up (p odd) of feature (p / 128) * 64 + (p % 128) / 2;
+ * rows are stored as 128-row x 64-column tiles, each a contiguous 16 KB block,
+ * ordered (m, row tile, column slab).  gate, up: [n_mats, hidden, dim];
+ * dst: n_mats * 2 * hidden * dim elements; hidden % 64 == 0, dim % 64 == 0.
  * Replaces the weight packing of metal_moe.py:105-131 (pack_combined_weights). */
 int parrot_pack_gate_up_bf16(void* dst, const void* gate, const void* up, int n_mats, int hidden,
                              int dim, void* stream);
+
+/* Pack [n_mats, rows, cols] (down projections, [d, H]) into the same tiled
+ * layout: 128 x 64 tiles ordered (m, row tile, column slab).
+ * rows % 128 == 0, cols % 64 == 0.  Replaces metal_moe.py:97-99 (torch.stack of
+ * the expert down weights). */
+int parrot_pack_down_bf16(void* dst, const void* src, int n_mats, int rows, int cols,
+                          void* stream);
 
 /* Whole MoE block.  Replaces parrot/model.py:505-569 (MoE.forward: router
  * :521-527, per-expert dispatch loop :545-551, router statistics :554-569)

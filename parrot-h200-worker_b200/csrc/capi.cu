@@ -135,8 +135,6 @@ int validate_dims(const parrot_moe_dims* d) {
   if (d->shared_dim <= 0 || d->shared_dim % 64)
     return fail(PARROT_EINVAL, "shared_dim must be a positive multiple of 64%s");
   if (d->capacity < 0) return fail(PARROT_EINVAL, "capacity must be >= 0%s");
-  if ((size_t)d->n_experts * d->dim * 2 > 96 * 1024)
-    return fail(PARROT_EINVAL, "router weight exceeds 96 KB of shared memory%s");
   return PARROT_OK;
 }
 
@@ -169,9 +167,11 @@ int layout_of(const parrot_moe_dims* d, parrot_moe_layout* L) {
   L->seg_rows = take(2 * E * 4);
   L->seg_base = take(2 * E * 4);
   L->stats = take((E + 1) * 4);
+  L->row_dst = take(R * 4);
+  L->row_w = take(R * 4);
   L->grouped = take(R * D * 2);
   L->hidden = take(R * H * 2);
-  L->y = take(R * D * 2);
+  L->contrib = take(A * D * 2);
   L->shared_hidden = take(T * Hs * 2);
   L->shared_y = take(T * D * 2);
   L->total = off;
@@ -248,7 +248,7 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ra.n_experts = E;
   ra.capacity = L.capacity;
   ra.status = at<int>(ws, L.status);
-  if (parrot::launch_route(ra, s)) return fail(PARROT_EINVAL, "route: unsupported dim%s");
+  if (parrot::launch_route(ra, s)) return fail(PARROT_ECUDA, "route: unsupported dim or smem%s");
   int rc = check_launch("route_kernel");
   if (rc) return rc;
 
@@ -256,17 +256,22 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ga.x = static_cast<const __nv_bfloat16*>(x);
   ga.indices = ra.indices;
   ga.tab = ra.tab;
+  ga.weights = ra.weights;
   ga.positions = at<int>(ws, L.positions);
+  ga.row_dst = at<int>(ws, L.row_dst);
+  ga.row_w = at<float>(ws, L.row_w);
   ga.grouped = at<__nv_bfloat16>(ws, L.grouped);
   ga.tokens = T;
   ga.dim = dims->dim;
   ga.n_experts = E;
   ga.capacity = L.capacity;
   const int nb = L.route_blocks;
-  int split = (2 * sm_count() + nb - 1) / nb;
-  ga.copy_split = split < 1 ? 1 : (split > 8 ? 8 : split);
+  const int want = (2 * sm_count() + nb - 1) / nb;  // about two blocks per SM
+  int split = 1;
+  while (split * 2 <= want && split < 8) split *= 2;
+  ga.copy_split = split;
   ga.status = ra.status;
-  parrot::launch_group(ga, s);
+  if (parrot::launch_group(ga, s)) return fail(PARROT_ECUDA, "group: shared-memory setup failed%s");
   if ((rc = check_launch("group_kernel"))) return rc;
 
   if ((rc = copy_out(o->weights, ra.weights, (size_t)2 * T * 4, s))) return rc;
@@ -291,7 +296,6 @@ int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights*
   if (swiglu) {
     g.m_tiles_routed = 2 * H / 128;
     g.k_blocks_routed = D / kGemmBlockK;
-    g.weight_rows_per_expert = 2 * H;
     g.out_routed = at<__nv_bfloat16>(ws, L.hidden);
     g.ld_out_routed = H;
     g.m_tiles_shared = 2 * Hs / 128;
@@ -299,24 +303,26 @@ int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights*
     g.out_shared = at<__nv_bfloat16>(ws, L.shared_hidden);
     g.ld_out_shared = Hs;
     g.mode = parrot::kGemmSwiGLU;
-    ok = tensor_map(&mw, w->gate_up, (long long)E * 2 * H, D, 128) &&
+    // weights are tiled (parrot_pack_*): a [tiles * 128, 64] view, one box per tile
+    ok = tensor_map(&mw, w->gate_up, (long long)E * 2 * H * D / kGemmBlockK, kGemmBlockK, 128) &&
          tensor_map(&mx, at<void>(ws, L.grouped), R, D, kGemmBlockN) &&
-         tensor_map(&msw, w->shared_gate_up, 2LL * Hs, D, 128) &&
+         tensor_map(&msw, w->shared_gate_up, 2LL * Hs * D / kGemmBlockK, kGemmBlockK, 128) &&
          tensor_map(&msx, x, T, D, kGemmBlockN);
   } else {
     g.m_tiles_routed = D / 128;
     g.k_blocks_routed = H / kGemmBlockK;
-    g.weight_rows_per_expert = D;
-    g.out_routed = at<__nv_bfloat16>(ws, L.y);
+    g.out_routed = at<__nv_bfloat16>(ws, L.contrib);
     g.ld_out_routed = D;
+    g.row_dst = at<int>(ws, L.row_dst);
+    g.row_w = at<float>(ws, L.row_w);
     g.m_tiles_shared = D / 128;
     g.k_blocks_shared = Hs / kGemmBlockK;
     g.out_shared = at<__nv_bfloat16>(ws, L.shared_y);
     g.ld_out_shared = D;
     g.mode = parrot::kGemmPlain;
-    ok = tensor_map(&mw, w->down, (long long)E * D, H, 128) &&
+    ok = tensor_map(&mw, w->down, (long long)E * D * H / kGemmBlockK, kGemmBlockK, 128) &&
          tensor_map(&mx, at<void>(ws, L.hidden), R, H, kGemmBlockN) &&
-         tensor_map(&msw, w->shared_down, D, Hs, 128) &&
+         tensor_map(&msw, w->shared_down, (long long)D * Hs / kGemmBlockK, kGemmBlockK, 128) &&
          tensor_map(&msx, at<void>(ws, L.shared_hidden), T, Hs, kGemmBlockN);
   }
   if (!ok) return fail(PARROT_ECUDA, "cuTensorMapEncodeTiled failed%s");
@@ -340,11 +346,8 @@ int run_experts(const parrot_moe_dims* dims, const parrot_moe_weights* w, const 
   if (rc) return rc;
   if ((rc = run_gemm(false, dims, w, x, ws, L, s))) return rc;
   parrot::CombineArgs c{};
-  c.y = at<__nv_bfloat16>(ws, L.y);
+  c.contrib = at<__nv_bfloat16>(ws, L.contrib);
   c.shared_y = at<__nv_bfloat16>(ws, L.shared_y);
-  c.positions = at<int>(ws, L.positions);
-  c.indices = at<int>(ws, L.indices);
-  c.weights = at<float>(ws, L.weights);
   c.residual = static_cast<const __nv_bfloat16*>(o->residual);
   c.out = static_cast<__nv_bfloat16*>(o->out);
   c.tokens = dims->tokens;
@@ -416,7 +419,8 @@ int parrot_depthmix_bf16(void* out, const void* const* sources, int n_sources,
   a.pending_out = static_cast<__nv_bfloat16*>(pending_out);
   a.rows = rows;
   a.dim = dim;
-  parrot::launch_depthmix(a, static_cast<cudaStream_t>(stream));
+  if (parrot::launch_depthmix(a, static_cast<cudaStream_t>(stream)))
+    return fail(PARROT_ECUDA, "depthmix: could not configure shared memory%s");
   return check_launch("depthmix_kernel");
 }
 
@@ -445,13 +449,22 @@ int parrot_moe_workspace_init(void* workspace, const parrot_moe_dims* dims, void
 
 int parrot_pack_gate_up_bf16(void* dst, const void* gate, const void* up, int n_mats, int hidden,
                              int dim, void* stream) {
-  if (!dst || !gate || !up || n_mats <= 0 || hidden <= 0 || hidden % 64 || dim <= 0 || dim % 8)
-    return fail(PARROT_EINVAL, "pack_gate_up: bad arguments (hidden % 64, dim % 8)%s");
+  if (!dst || !gate || !up || n_mats <= 0 || hidden <= 0 || hidden % 64 || dim <= 0 || dim % 64)
+    return fail(PARROT_EINVAL, "pack_gate_up: bad arguments (hidden % 64, dim % 64)%s");
   parrot::launch_pack_gate_up(static_cast<__nv_bfloat16*>(dst),
                               static_cast<const __nv_bfloat16*>(gate),
                               static_cast<const __nv_bfloat16*>(up), n_mats, hidden, dim,
                               static_cast<cudaStream_t>(stream));
   return check_launch("pack_gate_up_kernel");
+}
+
+int parrot_pack_down_bf16(void* dst, const void* src, int n_mats, int rows, int cols,
+                          void* stream) {
+  if (!dst || !src || n_mats <= 0 || rows <= 0 || rows % 128 || cols <= 0 || cols % 64)
+    return fail(PARROT_EINVAL, "pack_down: bad arguments (rows % 128, cols % 64)%s");
+  parrot::launch_pack_tiles(static_cast<__nv_bfloat16*>(dst), static_cast<const __nv_bfloat16*>(src),
+                            n_mats, rows, cols, static_cast<cudaStream_t>(stream));
+  return check_launch("pack_tiles_kernel");
 }
 
 int parrot_moe_route_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,

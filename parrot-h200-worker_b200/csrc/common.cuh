@@ -69,6 +69,36 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Reduce N per-lane partial values across the warp at once (N a power of two,
+// N <= 32).  Halving exchanges move half of the remaining values per step, so
+// N values cost N - 1 + log2(32 / N) shuffles instead of 5 N.  On return,
+// lane l holds the warp-wide total of value index (l % N) in v[0].
+template <int N>
+__device__ __forceinline__ float warp_reduce_many(float (&v)[N], int lane) {
+#pragma unroll
+  for (int o = N / 2; o >= 1; o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int j = 0; j < o; ++j) {
+      const float send = upper ? v[j] : v[j + o];
+      const float keep = upper ? v[j + o] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+#pragma unroll
+  for (int o = N; o < 32; o <<= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+  return v[0];
+}
+
+// 16-byte global -> shared asynchronous copy (bypasses L1), and its fences.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -15,7 +15,7 @@
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, then
 //               SwiGLU mode:  weight rows are packed (gate_j, up_j) pairs, so
 //                             lanes 2i / 2i+1 hold gate / up of one feature;
-//                             h = bf16(bf16(silu(bf16 g)) * bf16 u)
+//                             h = bf16(silu_lut[bf16 g] * bf16 u)
 //               plain mode:   y = bf16(acc)
 //               staged through shared memory into row-major bf16 output.
 // Two TMEM accumulators (2 x 128 columns) let the epilogue of one unit run
@@ -31,9 +31,15 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = kGemmBlockN;
 constexpr int BK = kGemmBlockK;
-constexpr int kStages = 5;
-constexpr int kTileA = BM * BK * 2;
-constexpr int kTileB = BN * BK * 2;
+#ifndef PARROT_GEMM_SLABS
+#define PARROT_GEMM_SLABS 1
+#endif
+constexpr int kSlabs = PARROT_GEMM_SLABS;            // 64-wide K slabs per pipeline stage
+constexpr int kStages = kSlabs == 1 ? 5 : 3;
+constexpr int kSlabA = BM * BK * 2;
+constexpr int kSlabB = BN * BK * 2;
+constexpr int kTileA = kSlabs * kSlabA;
+constexpr int kTileB = kSlabs * kSlabB;
 constexpr int kChunk = 32;                   // TMEM columns per epilogue step
 constexpr int kStaging = kChunk * BM * 2;    // 32 tokens x 128 features bf16
 constexpr int kThreads = 192;
@@ -48,6 +54,9 @@ struct __align__(8) SmemTail {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  int scan_carry;
+  int unit_dst[BN];     // plain-mode scatter: destination row of each token row
+  float unit_w[BN];     // and its route weight
   int prefix[kSegMax + 2];
   int seg_rows[kSegMax];
   int seg_base[kSegMax];
@@ -179,7 +188,7 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 
 struct Unit {
   bool routed;
-  int w_row;      // first weight row of the 128-row tile
+  int w_row;      // row of the unit's first weight tile in the tiled weight view
   int x_row;      // first token row of the tile
   int valid;      // token rows present (<= BN)
   int k_blocks;
@@ -200,7 +209,7 @@ __device__ __forceinline__ Unit decode_unit(int u, const GemmArgs& g, const Smem
     const int mt = local / n_tiles, nt = local - mt * n_tiles;
     const int e = s % g.n_experts;
     r.routed = true;
-    r.w_row = e * g.weight_rows_per_expert + mt * BM;
+    r.w_row = (e * g.m_tiles_routed + mt) * g.k_blocks_routed * BM;
     r.x_row = t.seg_base[s] + nt * BN;
     r.valid = min(BN, t.seg_rows[s] - nt * BN);
     r.k_blocks = g.k_blocks_routed;
@@ -212,7 +221,7 @@ __device__ __forceinline__ Unit decode_unit(int u, const GemmArgs& g, const Smem
     const int n_tiles = (g.shared_rows + BN - 1) / BN;
     const int mt = local / n_tiles, nt = local - mt * n_tiles;
     r.routed = false;
-    r.w_row = mt * BM;
+    r.w_row = mt * g.k_blocks_shared * BM;
     r.x_row = nt * BN;
     r.valid = min(BN, g.shared_rows - nt * BN);
     r.k_blocks = g.k_blocks_shared;
@@ -223,10 +232,21 @@ __device__ __forceinline__ Unit decode_unit(int u, const GemmArgs& g, const Smem
   return r;
 }
 
-__device__ __forceinline__ float silu_bf16(float g) {
-  const float gb = round_bf16(g);
-  return round_bf16(gb / (1.0f + expf(-gb)));
+// SiLU of every bf16 value, rounded to bf16: silu_lut[bits(x)] =
+// bf16(x / (1 + expf(-x))), the expression PyTorch evaluates in fp32 for a
+// bf16 tensor.  The gate projection is rounded to bf16 before SiLU (the
+// reference materialises it as a bf16 tensor), so the epilogue looks its
+// SiLU up instead of spending an exp and an IEEE divide per element.
+__device__ __nv_bfloat16 silu_lut[1 << 16];
+
+__global__ void build_silu_lut_kernel() {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (1 << 16)) return;
+  const float x = __uint_as_float((uint32_t)i << 16);
+  silu_lut[i] = __float2bfloat16_rn(x / (1.0f + expf(-x)));
 }
+
+
 
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w_routed,
@@ -255,19 +275,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&t.drain, 1);
     t.abort = 0;
-    // work-unit prefix over segments (routed), shared units follow
-    int acc = 0;
-    t.prefix[0] = 0;
-    const int m_routed = g.m_tiles_routed;
-    for (int s = 0; s < n_seg; ++s) {
-      const int rows = g.seg_rows[s];
-      const int sb = g.seg_base[s];
-      t.seg_rows[s] = rows;
-      t.seg_base[s] = sb;
-      acc += ((rows + BN - 1) / BN) * m_routed;
-      t.prefix[s + 1] = acc;
-    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2 || warp == 3) {
+    // work-unit prefix over the 2E segments: one thread per segment loads its
+    // row count, then a two-warp inclusive scan (shared units follow)
+    const int s = threadIdx.x - 64;
+    int rows = 0;
+    if (s < n_seg) {
+      rows = g.seg_rows[s];
+      t.seg_rows[s] = rows;
+      t.seg_base[s] = g.seg_base[s];
+    }
+    int incl = ((rows + BN - 1) / BN) * g.m_tiles_routed;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (warp == 2 && lane == 31) t.scan_carry = incl;
+    asm volatile("bar.sync 2, 64;" ::: "memory");
+    if (warp == 3) incl += t.scan_carry;
+    if (s < n_seg) t.prefix[s + 1] = incl;
+    if (s == 0) t.prefix[0] = 0;
   }
   if (warp == 1) {
     asm volatile(
@@ -298,14 +328,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Unit un = decode_unit(u, g, t);
         const CUtensorMap* mw = un.routed ? &tm_w_routed : &tm_w_shared;
         const CUtensorMap* mx = un.routed ? &tm_x_routed : &tm_x_shared;
-        for (int kb = 0; kb < un.k_blocks; ++kb) {
+        for (int kb = 0; kb < un.k_blocks; kb += kSlabs) {
           if (!mbar_wait(&t.empty[stage], phase ^ 1, abort_flag, g.status, 10)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&t.full[stage], kTileA + kTileB);
-          tma_load_2d(tiles_a + stage * kTileA, mw, kb * BK, un.w_row, &t.full[stage]);
-          tma_load_2d(tiles_b + stage * kTileB, mx, kb * BK, un.x_row, &t.full[stage]);
+          const int slabs = min(kSlabs, un.k_blocks - kb);
+          mbar_arrive_expect_tx(&t.full[stage], slabs * (kSlabA + kSlabB));
+          for (int sl = 0; sl < slabs; ++sl) {
+            tma_load_2d(tiles_a + stage * kTileA + sl * kSlabA, mw, 0, un.w_row + (kb + sl) * BM,
+                        &t.full[stage]);
+            tma_load_2d(tiles_b + stage * kTileB + sl * kSlabB, mx, (kb + sl) * BK, un.x_row,
+                        &t.full[stage]);
+          }
           issued[stage] = true;
           issued_phase[stage] = phase;
           if (++stage == kStages) {
@@ -334,17 +369,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem + acc * BN;
         const int n = (un.valid + 15) & ~15;
         const uint32_t idesc = make_idesc(n);
-        for (int kb = 0; kb < un.k_blocks; ++kb) {
+        for (int kb = 0; kb < un.k_blocks; kb += kSlabs) {
           if (!mbar_wait(&t.full[stage], phase, abort_flag, g.status, 21)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t da = sw128_desc(tiles_a + stage * kTileA);
-          const uint64_t db = sw128_desc(tiles_b + stage * kTileB);
+          const int slabs = min(kSlabs, un.k_blocks - kb);
+          for (int sl = 0; sl < slabs; ++sl) {
+            const uint64_t da = sw128_desc(tiles_a + stage * kTileA + sl * kSlabA);
+            const uint64_t db = sw128_desc(tiles_b + stage * kTileB + sl * kSlabB);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+            for (int k = 0; k < BK / 16; ++k)
+              mma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, ((kb + sl) | k) != 0);
+          }
           mma_commit(&t.empty[stage]);
           if (++stage == kStages) {
             stage = 0;
@@ -370,6 +408,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     int chunk_iter = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
       const Unit un = decode_unit(u, g, t);
+      const bool scatter = g.mode == kGemmPlain && un.routed && g.row_dst != nullptr;
+      if (scatter) {
+        // per-row destination and weight, fetched while the MMAs run
+        epi_bar();  // the previous unit's stores are done with these arrays
+        if (et < un.valid) {
+          t.unit_dst[et] = __ldg(g.row_dst + un.x_row + et);
+          t.unit_w[et] = round_bf16(__ldg(g.row_w + un.x_row + et));
+        }
+        epi_bar();
+      }
       if (!mbar_wait(&t.tfull[acc], acc_phase, abort_flag, g.status, 30)) break;
       tc_fence_after();
       const int chunks = (un.valid + kChunk - 1) / kChunk;
@@ -383,15 +431,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool is_up = lane & 1;
           const int f = q * 16 + (lane >> 1);
           const int tok0 = is_up ? 16 : 0;
+          // 1. pair exchange: even lanes keep tokens 0-15, odd lanes 16-31
+          uint16_t gbits[16];
+          float up[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float mine_other = __uint_as_float(is_up ? r[j] : r[16 + j]);
             const float recv = __shfl_xor_sync(0xffffffffu, mine_other, 1);
             const float gate = is_up ? recv : __uint_as_float(r[j]);
-            const float up = is_up ? __uint_as_float(r[16 + j]) : recv;
-            const float h = silu_bf16(gate) * round_bf16(up);
-            st[(tok0 + j) * (BM / 2) + f] = __float2bfloat16_rn(h);
+            gbits[j] = __bfloat16_as_ushort(__float2bfloat16_rn(gate));
+            up[j] = round_bf16(is_up ? __uint_as_float(r[16 + j]) : recv);
           }
+          // 2. all SiLU lookups in flight together, 3. h = bf16(silu * up)
+          __nv_bfloat16 sv[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) sv[j] = silu_lut[gbits[j]];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            st[(tok0 + j) * (BM / 2) + f] = __float2bfloat16_rn(__bfloat162float(sv[j]) * up[j]);
           epi_bar();
           // 32 tokens x 64 features: 256 16-byte pieces
 #pragma unroll
@@ -400,6 +457,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int tok = idx >> 3, part = idx & 7;
             if (tok < rows_here)
               *reinterpret_cast<uint4*>(out_base + (size_t)tok * un.ld + part * 8) =
+                  reinterpret_cast<const uint4*>(st)[idx];
+          }
+        } else if (scatter) {
+          // routed contribution bf16(bf16(y) * bf16(w)) to its token-major slot
+          const int m = q * 32 + lane;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            st[j * BM + m] = __float2bfloat16_rn(
+                round_bf16(__uint_as_float(r[j])) * t.unit_w[c * kChunk + j]);
+          epi_bar();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int idx = et + 128 * i;
+            const int tok = idx >> 4, part = idx & 15;
+            if (tok < rows_here)
+              *reinterpret_cast<uint4*>(un.out + (size_t)t.unit_dst[c * kChunk + tok] * un.ld +
+                                        un.out_col + part * 8) =
                   reinterpret_cast<const uint4*>(st)[idx];
           }
         } else {
@@ -434,24 +508,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// gate/up interleave: dst[m][tile*128 + 2i + {0,1}] = {gate, up}[m][tile*64 + i]
+// Weight tiles are stored in the order the GEMM streams them: tile (m, rt, kb)
+// is rows [rt*128, rt*128 + 128) x columns [kb*64, kb*64 + 64) of matrix m,
+// 128 rows of 64 bf16 (16 KB) back to back, so every TMA box is one
+// contiguous 16 KB block of HBM.
+constexpr int kTileVecs = BM * BK / 8;   // 16-byte vectors per tile
+
+// gate/up: packed row p of a tile holds gate (p even) or up (p odd) of
+// feature rt*64 + p/2, so an M tile carries 64 features' gate and up rows.
 __global__ void pack_gate_up_kernel(__nv_bfloat16* __restrict__ dst,
                                     const __nv_bfloat16* __restrict__ gate,
                                     const __nv_bfloat16* __restrict__ up, int n_mats, int hidden,
                                     int dim) {
-  const int nvec = dim >> 3;
-  const size_t total = (size_t)n_mats * 2 * hidden * nvec;
+  const int kb_count = dim / BK, rt_count = 2 * hidden / BM;
+  const size_t total = (size_t)n_mats * rt_count * kb_count * kTileVecs;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
        i += (size_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % nvec);
-    const size_t row = i / nvec;                 // packed row over all matrices
-    const int m = (int)(row / (2 * hidden));
-    const int r = (int)(row % (2 * hidden));
-    const int tile = r / BM, within = r % BM;
-    const int feat = tile * (BM / 2) + (within >> 1);
-    const __nv_bfloat16* src = (within & 1) ? up : gate;
-    reinterpret_cast<uint4*>(dst)[i] =
-        reinterpret_cast<const uint4*>(src + ((size_t)m * hidden + feat) * dim)[c];
+    const size_t tile = i / kTileVecs;
+    const int w = (int)(i % kTileVecs), r = w >> 3, cv = w & 7;
+    const int kb = (int)(tile % kb_count);
+    const int rt = (int)((tile / kb_count) % rt_count);
+    const int m = (int)(tile / ((size_t)kb_count * rt_count));
+    const int feat = rt * (BM / 2) + (r >> 1);
+    const __nv_bfloat16* src = (r & 1) ? up : gate;
+    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(
+        src + ((size_t)m * hidden + feat) * dim + kb * BK)[cv];
+  }
+}
+
+// plain [n_mats, rows, cols] -> tiles
+__global__ void pack_tiles_kernel(__nv_bfloat16* __restrict__ dst,
+                                  const __nv_bfloat16* __restrict__ src, int n_mats, int rows,
+                                  int cols) {
+  const int kb_count = cols / BK, rt_count = rows / BM;
+  const size_t total = (size_t)n_mats * rt_count * kb_count * kTileVecs;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t tile = i / kTileVecs;
+    const int w = (int)(i % kTileVecs), r = w >> 3, cv = w & 7;
+    const int kb = (int)(tile % kb_count);
+    const int rt = (int)((tile / kb_count) % rt_count);
+    const int m = (int)(tile / ((size_t)kb_count * rt_count));
+    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(
+        src + ((size_t)m * rows + rt * BM + r) * cols + kb * BK)[cv];
   }
 }
 
@@ -471,6 +570,10 @@ int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)kSmemBytes);
     if (err != cudaSuccess) return -2;
+    // the SiLU table of this device, built once on the caller's stream ahead
+    // of the first GEMM (which is why the first call should not be captured)
+    build_silu_lut_kernel<<<(1 << 16) / 256, 256, 0, stream>>>();
+    if (cudaGetLastError() != cudaSuccess) return -2;
     configured |= 1ull << dev;
   }
   grouped_gemm_kernel<<<grid, kThreads, kSmemBytes, stream>>>(*tm_w_routed, *tm_x_routed,
@@ -478,12 +581,22 @@ int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
   return 0;
 }
 
+static int pack_blocks(size_t vecs) {
+  const size_t b = (vecs + 255) / 256;
+  return (int)(b < 4096 ? b : 4096);
+}
+
 int launch_pack_gate_up(__nv_bfloat16* dst, const __nv_bfloat16* gate, const __nv_bfloat16* up,
                         int n_mats, int hidden, int dim, cudaStream_t stream) {
-  const size_t total = (size_t)n_mats * 2 * hidden * (dim / 8);
-  const int threads = 256;
-  const int blocks = (int)((total + threads - 1) / threads < 4096 ? (total + threads - 1) / threads : 4096);
-  pack_gate_up_kernel<<<blocks, threads, 0, stream>>>(dst, gate, up, n_mats, hidden, dim);
+  const size_t vecs = (size_t)n_mats * 2 * hidden * (dim / 8);
+  pack_gate_up_kernel<<<pack_blocks(vecs), 256, 0, stream>>>(dst, gate, up, n_mats, hidden, dim);
+  return 0;
+}
+
+int launch_pack_tiles(__nv_bfloat16* dst, const __nv_bfloat16* src, int n_mats, int rows,
+                      int cols, cudaStream_t stream) {
+  const size_t vecs = (size_t)n_mats * rows * (cols / 8);
+  pack_tiles_kernel<<<pack_blocks(vecs), 256, 0, stream>>>(dst, src, n_mats, rows, cols);
   return 0;
 }
 

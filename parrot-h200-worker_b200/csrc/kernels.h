@@ -61,8 +61,11 @@ struct RouteArgs {
 struct GroupArgs {
   const __nv_bfloat16* x;     // [T, d]
   const int* indices;         // [T, 2]
+  const float* weights;       // [T, 2] route weights
   MoeTables tab;
   int* positions;             // [2T] grouped row of each assignment
+  int* row_dst;               // [R] token-major contribution slot of each grouped row
+  float* row_w;               // [R] route weight of each grouped row
   __nv_bfloat16* grouped;     // [E*C + 2T, d]
   int tokens, dim, n_experts, capacity;
   int copy_split;
@@ -70,11 +73,8 @@ struct GroupArgs {
 };
 
 struct CombineArgs {
-  const __nv_bfloat16* y;         // [R, d] routed expert outputs by grouped row
+  const __nv_bfloat16* contrib;   // [2T, d] weighted routed outputs, token-major
   const __nv_bfloat16* shared_y;  // [T, d]
-  const int* positions;           // [2T]
-  const int* indices;             // [T, 2]
-  const float* weights;           // [T, 2]
   const __nv_bfloat16* residual;  // [T, d] or null
   __nv_bfloat16* out;             // [T, d]
   int tokens, dim;
@@ -89,9 +89,12 @@ struct GemmArgs {
   int n_experts;
   int m_tiles_routed;     // output features / 128
   int k_blocks_routed;    // K / 64
-  int weight_rows_per_expert;
   __nv_bfloat16* out_routed;
   int ld_out_routed;      // elements per output row
+  // plain mode, routed units: when set, grouped row r is written scaled by
+  // bf16(row_w[r]) to out_routed row row_dst[r] instead of row r
+  const int* row_dst;
+  const float* row_w;
   // shared part
   int shared_rows;        // tokens (0 disables)
   int m_tiles_shared;
@@ -113,6 +116,8 @@ int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
                         const CUtensorMap* tm_x_shared, int grid, cudaStream_t stream);
 int launch_pack_gate_up(__nv_bfloat16* dst, const __nv_bfloat16* gate, const __nv_bfloat16* up,
                         int n_mats, int hidden, int dim, cudaStream_t stream);
+int launch_pack_tiles(__nv_bfloat16* dst, const __nv_bfloat16* src, int n_mats, int rows,
+                      int cols, cudaStream_t stream);
 size_t grouped_gemm_smem_bytes();
 
 inline int route_blocks(int tokens) {

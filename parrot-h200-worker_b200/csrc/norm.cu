@@ -82,20 +82,36 @@ int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat
 // Scores and weights stay fp32 (as the reference's fused Metal kernel keeps
 // them, moe_bf16.metal:331-435): with a peaked softmax over sources, rounding
 // the keys to bf16 first would move the weights by percents.
-// When `pending_delta` is set, the last source is bf16(pending_base + delta)
-// and is written to `pending_out` (the resolved partial block sum).
+//
+// One warp per row.  The warp first issues 16-byte async copies of every
+// source row into its shared-memory slab (all loads in flight at once: one
+// memory round trip), then makes one pass for the S sums of squares and the S
+// raw key.query dots (s_i = rsqrt(...) * sum_d v kw q), reduced together with
+// warp_reduce_many, a lane-parallel softmax, and a second pass for the mix.
 // ---------------------------------------------------------------------------
-template <int V>
-__global__ void __launch_bounds__(128) depthmix_kernel(DepthMixArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= a.rows) return;
-  const int dim = a.dim;
-  const int nvec = dim >> 3;
-  const size_t off = (size_t)row * dim;
-  const int S = a.n_sources;
-  const bool pending = a.pending_delta != nullptr;
+constexpr int kDepthWarps = 4;
 
+template <int V>
+__global__ void __launch_bounds__(32 * kDepthWarps) depthmix_kernel(DepthMixArgs a) {
+  extern __shared__ __align__(16) unsigned char depth_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int row = blockIdx.x * kDepthWarps + warp;
+  if (row >= a.rows) return;
+  const int dim = a.dim, nvec = dim >> 3, S = a.n_sources;
+  const size_t off = (size_t)row * dim;
+  const bool pending = a.pending_delta != nullptr;
+  uint4* slab = reinterpret_cast<uint4*>(depth_smem) + (size_t)warp * S * nvec;
+
+  // 1. every source slice of this row in flight at once
+  for (int s = 0; s < S; ++s) {
+    if (pending && s == S - 1) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(a.sources[s] + off);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) cp_async16(slab + s * nvec + c, src + c);
+    }
+  }
   float q[V][8], kw[V][8];
 #pragma unroll
   for (int i = 0; i < V; ++i) {
@@ -105,94 +121,83 @@ __global__ void __launch_bounds__(128) depthmix_kernel(DepthMixArgs a) {
       bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.key_w) + c), kw[i]);
     }
   }
-
-  // The pending (last) source lives in registers for both passes.
-  uint4 pend[V];
-  if (pending) {
+  if (pending) {  // the deferred residual add, resolved in registers
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       const int c = lane + 32 * i;
       if (c < nvec) {
-        float b[8], d[8];
+        float b[8], dl[8];
         bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.pending_base + off) + c), b);
-        bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.pending_delta + off) + c), d);
+        bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.pending_delta + off) + c), dl);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) b[j] = b[j] + d[j];
-        pend[i] = float_to_bf16x8(b);
-        reinterpret_cast<uint4*>(a.pending_out + off)[c] = pend[i];
+        for (int j = 0; j < 8; ++j) b[j] = b[j] + dl[j];
+        const uint4 r = float_to_bf16x8(b);
+        reinterpret_cast<uint4*>(a.pending_out + off)[c] = r;
+        slab[(S - 1) * nvec + c] = r;
       }
     }
   }
+  cp_async_wait_all();  // each lane reads back only the slices it copied
 
-  float score[kMaxDepthSources];
-  float smax = -INFINITY;
-  for (int s = 0; s < S; ++s) {
-    const bool is_pend = pending && s == S - 1;
-    const uint4* src = reinterpret_cast<const uint4*>(a.sources[s] + off);
-    uint4 v[V];
-    float ss = 0.f;
+  // 2. sums of squares and raw key.query dots of all sources, reduced together
+  float ss[kMaxDepthSources], raw[kMaxDepthSources];
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) {
-        v[i] = is_pend ? pend[i] : __ldg(src + c);
-        float f[8];
-        bf16x8_to_float(v[i], f);
+  for (int s = 0; s < kMaxDepthSources; ++s) {
+    ss[s] = 0.f;
+    raw[s] = 0.f;
+    if (s < S) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+      for (int i = 0; i < V; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nvec) {
+          float f[8];
+          bf16x8_to_float(slab[s * nvec + c], f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            ss[s] = fmaf(f[j], f[j], ss[s]);
+            raw[s] = fmaf(f[j] * kw[i][j], q[i][j], raw[s]);
+          }
+        }
       }
     }
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss / (float)dim + a.key_eps);
-    float dot = 0.f;
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) {
-        float f[8];
-        bf16x8_to_float(v[i], f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) dot = fmaf((f[j] * inv) * kw[i][j], q[i][j], dot);
-      }
-    }
-    dot = warp_sum(dot);
-    score[s] = dot;
-    smax = fmaxf(smax, dot);
   }
-  float den = 0.f;
-  for (int s = 0; s < S; ++s) {
-    score[s] = expf(score[s] - smax);
-    den += score[s];
-  }
-  for (int s = 0; s < S; ++s) score[s] = score[s] / den;
+  const float ss_l = warp_reduce_many<kMaxDepthSources>(ss, lane);
+  const float raw_l = warp_reduce_many<kMaxDepthSources>(raw, lane);
+  // lane l now owns source l % 16
+  const int src_l = lane & (kMaxDepthSources - 1);
+  const bool valid = src_l < S;
+  const float score = valid ? rsqrtf(ss_l / (float)dim + a.key_eps) * raw_l : -INFINITY;
+  const float m = warp_max(score);
+  const float e = valid ? expf(score - m) : 0.f;
+  const float den = warp_sum(lane < kMaxDepthSources ? e : 0.f);
+  const float alpha_l = e / den;
 
+  // 3. mix, then the consumer RMSNorm
   float h[V][8];
 #pragma unroll
   for (int i = 0; i < V; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) h[i][j] = 0.f;
   for (int s = 0; s < S; ++s) {
-    const bool is_pend = pending && s == S - 1;
-    const uint4* src = reinterpret_cast<const uint4*>(a.sources[s] + off);
-    const float alpha = score[s];
+    const float alpha = __shfl_sync(0xffffffffu, alpha_l, s);
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       const int c = lane + 32 * i;
       if (c < nvec) {
         float f[8];
-        bf16x8_to_float(is_pend ? pend[i] : __ldg(src + c), f);
+        bf16x8_to_float(slab[s * nvec + c], f);
 #pragma unroll
         for (int j = 0; j < 8; ++j) h[i][j] = fmaf(alpha, f[j], h[i][j]);
       }
     }
   }
-  float ss = 0.f;
+  float sq = 0.f;
 #pragma unroll
   for (int i = 0; i < V; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       h[i][j] = round_bf16(h[i][j]);
-      ss = fmaf(h[i][j], h[i][j], ss);
+      sq = fmaf(h[i][j], h[i][j], sq);
     }
   uint4* orow = reinterpret_cast<uint4*>(a.out + off);
   if (a.mix_out != nullptr) {
@@ -211,8 +216,8 @@ __global__ void __launch_bounds__(128) depthmix_kernel(DepthMixArgs a) {
     }
     return;
   }
-  ss = warp_sum(ss);
-  const float inv = rsqrtf(ss / (float)dim + a.out_eps);
+  sq = warp_sum(sq);
+  const float inv = rsqrtf(sq / (float)dim + a.out_eps);
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     const int c = lane + 32 * i;
@@ -226,19 +231,34 @@ __global__ void __launch_bounds__(128) depthmix_kernel(DepthMixArgs a) {
   }
 }
 
+template <int V>
+static int launch_depthmix_v(const DepthMixArgs& args, cudaStream_t stream) {
+  const size_t smem = (size_t)kDepthWarps * args.n_sources * (args.dim / 8) * sizeof(uint4);
+  static unsigned long long configured = 0;  // per device: the attribute lives in its context
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
+  if (!(configured & (1ull << dev))) {
+    const int max_smem = kDepthWarps * kMaxDepthSources * (1024 / 8) * (int)sizeof(uint4);
+    if (cudaFuncSetAttribute(depthmix_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             max_smem) != cudaSuccess)
+      return -2;
+    configured |= 1ull << dev;
+  }
+  dim3 grid((args.rows + kDepthWarps - 1) / kDepthWarps), block(32 * kDepthWarps);
+  depthmix_kernel<V><<<grid, block, smem, stream>>>(args);
+  return 0;
+}
+
 int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream) {
   if (args.rows == 0) return 0;
-  const int warps = 4;
-  dim3 grid((args.rows + warps - 1) / warps), block(32 * warps);
   const int v = (args.dim / 8 + 31) / 32;
   switch (v) {
-    case 1: depthmix_kernel<1><<<grid, block, 0, stream>>>(args); break;
-    case 2: depthmix_kernel<2><<<grid, block, 0, stream>>>(args); break;
-    case 3: depthmix_kernel<3><<<grid, block, 0, stream>>>(args); break;
-    case 4: depthmix_kernel<4><<<grid, block, 0, stream>>>(args); break;
+    case 1: return launch_depthmix_v<1>(args, stream);
+    case 2: return launch_depthmix_v<2>(args, stream);
+    case 3: return launch_depthmix_v<3>(args, stream);
+    case 4: return launch_depthmix_v<4>(args, stream);
     default: return -1;
   }
-  return 0;
 }
 
 }  // namespace parrot

@@ -34,7 +34,8 @@ class MoeOutputs(ctypes.Structure):
 
 LAYOUT_OFFSETS = ("indices", "weights", "positions", "block_hist", "block_prefix",
                   "block_probsum", "counts", "seg_rows", "seg_base", "done_counter", "stats",
-                  "status", "grouped", "hidden", "y", "shared_hidden", "shared_y", "total")
+                  "status", "row_dst", "row_w", "grouped", "hidden", "contrib",
+                  "shared_hidden", "shared_y", "total")
 
 
 class MoeLayout(ctypes.Structure):
@@ -56,6 +57,7 @@ _SIGNATURES = {
     "parrot_moe_workspace_init": (c_int, [c_void_p, POINTER(MoeDims), c_void_p]),
     "parrot_pack_gate_up_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_void_p]),
+    "parrot_pack_down_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "parrot_moe_forward_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                         POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
     "parrot_moe_route_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,

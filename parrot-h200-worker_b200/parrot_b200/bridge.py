@@ -145,9 +145,9 @@ def b200_depth_mix_norm(module, sources: Sequence[Tensor], output_norm,
 def pack_weights(module) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
     """Pack the routed and shared experts once per parameter version.
 
-    Returns ``(router [E,d], gate_up [E,2H,d], down [E,d,H], shared_gate_up
-    [2Hs,d], shared_down [d,Hs])``; gate/up rows are interleaved per 64-row
-    tile for the fused SwiGLU epilogue.  Like ``metal_moe.py:84-131`` the
+    Returns ``(router [E,d], gate_up, down, shared_gate_up, shared_down)``;
+    the expert matrices are in the C ABI's tiled layout (contiguous 16 KB
+    128 x 64 tiles; gate/up rows interleaved for the fused SwiGLU epilogue).  Like ``metal_moe.py:84-131`` the
     packed copy is reused without re-checking versions while the module is in
     eval mode with gradients disabled; ``invalidate_packed_weights`` forces a
     repack after in-place weight edits made in that state.
@@ -173,14 +173,21 @@ def pack_weights(module) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
         gate_up = torch.empty((E, 2 * H, d), device=gate.device, dtype=gate.dtype)
         _lib.check(lib.parrot_pack_gate_up_bf16(_p(gate_up), _p(gate), _p(up), E, H, d,
                                                 _stream()), "parrot_pack_gate_up_bf16")
-        down = torch.stack([e.down.weight.detach() for e in module.experts]).contiguous()
+        stacked = torch.stack([e.down.weight.detach() for e in module.experts]).contiguous()
+        down = torch.empty_like(stacked)
+        _lib.check(lib.parrot_pack_down_bf16(_p(down), _p(stacked), E, d, H, _stream()),
+                   "parrot_pack_down_bf16")
         sg = module.shared.gate.weight.detach().contiguous()
         su = module.shared.up.weight.detach().contiguous()
         shared_gate_up = torch.empty((2 * Hs, d), device=sg.device, dtype=sg.dtype)
         _lib.check(lib.parrot_pack_gate_up_bf16(_p(shared_gate_up), _p(sg), _p(su), 1, Hs, d,
                                                 _stream()), "parrot_pack_gate_up_bf16")
+        sd = module.shared.down.weight.detach().contiguous()
+        shared_down = torch.empty_like(sd)
+        _lib.check(lib.parrot_pack_down_bf16(_p(shared_down), _p(sd), 1, d, Hs, _stream()),
+                   "parrot_pack_down_bf16")
         packed = (module.router.weight.detach().contiguous(), gate_up, down, shared_gate_up,
-                  module.shared.down.weight.detach().contiguous())
+                  shared_down)
     module.__dict__["_b200_pack"] = (version, packed)
     return packed
 

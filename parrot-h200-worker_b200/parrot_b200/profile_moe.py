@@ -1,0 +1,70 @@
+"""Small, fixed workloads for profiling the B200 kernels under Nsight Compute.
+
+    python parrot-h200-worker_b200/parrot_b200/profile_moe.py --tokens 512 --iters 3
+    python parrot-h200-worker_b200/parrot_b200/profile_moe.py --forward --iters 2
+
+``--tokens T`` runs ``iters`` eager calls of one Parrot XL MoE block (seeded
+weights ~N(0, 0.02), x ~ N(0, 1)); each call launches route, group,
+gate_up GEMM, down GEMM and combine, in that order.  ``--forward`` runs
+``iters`` eager Parrot XL forwards on 1 x 512 ids.  Device memory stays under
+2 GB, so ``ncu`` captures of these commands end in seconds.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+from pathlib import Path
+
+if __package__ in (None, ""):
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+
+import torch  # noqa: E402
+
+from parrot_b200 import ModelConfig, Parrot  # noqa: E402
+from parrot_b200.model import MoE  # noqa: E402
+from parrot_b200.workloads import (make_hidden_states, make_moe_layer_weights,  # noqa: E402
+                                   random_token_ids, tune_zipf_router_bias)
+
+
+def moe_block(tokens: int, iters: int, zipf: bool) -> None:
+    cfg = ModelConfig()
+    moe = MoE(cfg)
+    w = make_moe_layer_weights(cfg.dim, cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim, 1)
+    moe.load_state_dict(w)
+    x = make_hidden_states(tokens, cfg.dim, 0)
+    if zipf:
+        moe.router_bias = tune_zipf_router_bias(x, w["router.weight"])
+    moe = moe.to("cuda", torch.bfloat16).eval()
+    xd = x.to("cuda", torch.bfloat16)
+    with torch.inference_mode():
+        for _ in range(iters):
+            moe(xd)
+    torch.cuda.synchronize()
+
+
+def forward(iters: int) -> None:
+    torch.manual_seed(0)
+    model = Parrot(ModelConfig()).to("cuda", torch.bfloat16).eval()
+    ids = random_token_ids(1, 512, 32768, 0).cuda()
+    with torch.inference_mode():
+        for _ in range(iters):
+            model(ids)
+    torch.cuda.synchronize()
+
+
+def main() -> None:
+    p = argparse.ArgumentParser()
+    p.add_argument("--tokens", type=int, default=512)
+    p.add_argument("--iters", type=int, default=3)
+    p.add_argument("--forward", action="store_true")
+    p.add_argument("--zipf", action="store_true", help="Zipf(1.2) router bias (overflow path)")
+    a = p.parse_args()
+    if a.forward:
+        forward(a.iters)
+    else:
+        moe_block(a.tokens, a.iters, a.zipf)
+    print("profile workload done")
+
+
+if __name__ == "__main__":
+    main()

@@ -191,12 +191,16 @@ def test_xl_moe_layer_intermediates_match_oracle_experts():
     out, ex, ws, layout = call_moe_forward(prod, x.cuda())
     R = layout.grouped_rows
     hidden = workspace_view(ws, layout, "hidden", torch.bfloat16, (R, cfg.expert_dim)).cpu()
-    y = workspace_view(ws, layout, "y", torch.bfloat16, (R, cfg.dim)).cpu()
+    contrib = workspace_view(ws, layout, "contrib", torch.bfloat16, (2 * T, cfg.dim)).cpu()
     sh = workspace_view(ws, layout, "shared_hidden", torch.bfloat16, (T, cfg.shared_expert_dim)).cpu()
     sy = workspace_view(ws, layout, "shared_y", torch.bfloat16, (T, cfg.dim)).cpu()
     idx = ex["indices"].cpu()
     pos = ex["positions"].cpu().long()
+    w = ex["weights"].cpu()
     xf = x.float()
+    # contribution slot of assignment a = 2t + (0 if its expert is the token's lower id)
+    other = idx.flip(-1).flatten()
+    slot = (torch.arange(2 * T) & ~1) + (idx.flatten() > other).long()
     for e in range(cfg.n_experts):
         a = torch.nonzero(idx.flatten() == e).flatten()
         if a.numel() == 0:
@@ -207,8 +211,8 @@ def test_xl_moe_layer_intermediates_match_oracle_experts():
         u = ex_mod.up(xf[tokens])
         h_ref = torch.nn.functional.silu(g) * u
         assert_bf16_close(hidden[pos[a]], h_ref, f"hidden e{e}")
-        y_ref = ex_mod.down(hidden[pos[a]].float())
-        assert_bf16_close(y[pos[a]], y_ref, f"y e{e}")
+        y_ref = ex_mod.down(hidden[pos[a]].float()) * w.flatten()[a, None]
+        assert_bf16_close(contrib[slot[a]], y_ref, f"contribution e{e}")
     hs_ref = torch.nn.functional.silu(orc.shared.gate(xf)) * orc.shared.up(xf)
     assert_bf16_close(sh, hs_ref, "shared hidden")
     assert_bf16_close(sy, orc.shared.down(sh.float()), "shared y")
