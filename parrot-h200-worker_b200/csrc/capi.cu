@@ -224,13 +224,6 @@ int prepare(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void
   return PARROT_OK;
 }
 
-int copy_out(void* dst, const void* src, size_t bytes, cudaStream_t s) {
-  if (dst == nullptr || bytes == 0) return PARROT_OK;
-  if (cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
-    return check_launch("output copy");
-  return PARROT_OK;
-}
-
 int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
               const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L, cudaStream_t s) {
   const int T = dims->tokens, E = dims->n_experts;
@@ -242,6 +235,9 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ra.indices = at<int>(ws, L.indices);
   ra.weights = at<float>(ws, L.weights);
   ra.indices64 = o->indices;
+  ra.weights_out = o->weights;
+  ra.counts_out = o->counts;
+  ra.stats_out = o->stats;
   ra.tab = tables(ws, L);
   ra.tokens = T;
   ra.dim = dims->dim;
@@ -258,6 +254,7 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ga.tab = ra.tab;
   ga.weights = ra.weights;
   ga.positions = at<int>(ws, L.positions);
+  ga.positions_out = o->positions;
   ga.row_dst = at<int>(ws, L.row_dst);
   ga.row_w = at<float>(ws, L.row_w);
   ga.grouped = at<__nv_bfloat16>(ws, L.grouped);
@@ -272,13 +269,7 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ga.copy_split = split;
   ga.status = ra.status;
   if (parrot::launch_group(ga, s)) return fail(PARROT_ECUDA, "group: shared-memory setup failed%s");
-  if ((rc = check_launch("group_kernel"))) return rc;
-
-  if ((rc = copy_out(o->weights, ra.weights, (size_t)2 * T * 4, s))) return rc;
-  if ((rc = copy_out(o->positions, ga.positions, (size_t)2 * T * 4, s))) return rc;
-  if ((rc = copy_out(o->counts, ra.tab.counts, (size_t)E * 4, s))) return rc;
-  if ((rc = copy_out(o->stats, ra.tab.stats, (size_t)(E + 1) * 4, s))) return rc;
-  return PARROT_OK;
+  return check_launch("group_kernel");
 }
 
 int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights* w,

@@ -19,7 +19,9 @@
 //               plain mode:   y = bf16(acc)
 //               staged through shared memory into row-major bf16 output.
 // Two TMEM accumulators (2 x 128 columns) let the epilogue of one unit run
-// under the MMAs of the next.  Every mbarrier wait is bounded; a timeout
+// under the MMAs of the next.  Launched with programmatic dependent launch:
+// a CTA whose first unit is static streams that unit's weight slabs before
+// waiting for the kernel that produced its activations.  Every mbarrier wait is bounded; a timeout
 // records a status code, drains in-flight copies and MMAs, frees TMEM and
 // returns.
 #include "common.cuh"
@@ -31,15 +33,9 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = kGemmBlockN;
 constexpr int BK = kGemmBlockK;
-#ifndef PARROT_GEMM_SLABS
-#define PARROT_GEMM_SLABS 1
-#endif
-constexpr int kSlabs = PARROT_GEMM_SLABS;            // 64-wide K slabs per pipeline stage
-constexpr int kStages = kSlabs == 1 ? 5 : 3;
-constexpr int kSlabA = BM * BK * 2;
-constexpr int kSlabB = BN * BK * 2;
-constexpr int kTileA = kSlabs * kSlabA;
-constexpr int kTileB = kSlabs * kSlabB;
+constexpr int kStages = 5;
+constexpr int kTileA = BM * BK * 2;
+constexpr int kTileB = BN * BK * 2;
 constexpr int kChunk = 32;                   // TMEM columns per epilogue step
 constexpr int kStaging = kChunk * BM * 2;    // 32 tokens x 128 features bf16
 constexpr int kThreads = 192;
@@ -197,38 +193,65 @@ struct Unit {
   int ld;
 };
 
+// Work units, in this order:
+//   static routed  u < E*MT:        capacity segment e = u / MT, M tile u % MT, token tile 0
+//   static shared  next SU units:   shared expert, M tile x token tile
+//   dynamic        the rest:        further token tiles of capacity segments,
+//                                   then every token tile of the overflow segments
+// The static units' weight tiles are known before the routing results exist,
+// so a CTA starts streaming them before its grid-dependency wait.
+__device__ __forceinline__ int extra_tiles(int s, int rows, int n_experts) {
+  const int tiles = (rows + BN - 1) / BN;
+  return s < n_experts ? max(tiles - 1, 0) : tiles;
+}
+
+__device__ __forceinline__ int static_units(const GemmArgs& g) {
+  const int shared_tiles = (g.shared_rows + BN - 1) / BN;
+  return g.n_experts * g.m_tiles_routed + shared_tiles * g.m_tiles_shared;
+}
+
 __device__ __forceinline__ Unit decode_unit(int u, const GemmArgs& g, const SmemTail& t) {
   Unit r;
-  const int n_seg = 2 * g.n_experts;
+  const int E = g.n_experts, MT = g.m_tiles_routed;
   const int feat_per_tile = g.mode == kGemmSwiGLU ? BM / 2 : BM;
-  if (u < t.prefix[n_seg]) {
-    int s = 0;
-    while (t.prefix[s + 1] <= u) ++s;
-    const int local = u - t.prefix[s];
-    const int n_tiles = (t.seg_rows[s] + BN - 1) / BN;
-    const int mt = local / n_tiles, nt = local - mt * n_tiles;
-    const int e = s % g.n_experts;
+  const int s0 = E * MT;
+  const int shared_tiles = (g.shared_rows + BN - 1) / BN;
+  const int su = shared_tiles * g.m_tiles_shared;
+  int s = -1, mt = 0, nt = 0;
+  if (u < s0) {
+    s = u / MT;
+    mt = u - s * MT;
+  } else if (u >= s0 + su) {
+    const int v = u - s0 - su;
+    s = 0;
+    while (t.prefix[s + 1] <= v) ++s;
+    const int local = v - t.prefix[s];
+    const int n_extra = extra_tiles(s, t.seg_rows[s], E);
+    mt = local / n_extra;
+    nt = local - mt * n_extra + (s < E ? 1 : 0);
+  }
+  if (s >= 0) {
+    const int e = s % E;
     r.routed = true;
-    r.w_row = (e * g.m_tiles_routed + mt) * g.k_blocks_routed * BM;
+    r.w_row = (e * MT + mt) * g.k_blocks_routed * BM;
     r.x_row = t.seg_base[s] + nt * BN;
-    r.valid = min(BN, t.seg_rows[s] - nt * BN);
+    r.valid = max(0, min(BN, t.seg_rows[s] - nt * BN));
     r.k_blocks = g.k_blocks_routed;
-    r.out_col = mt * feat_per_tile;
     r.out = g.out_routed;
     r.ld = g.ld_out_routed;
   } else {
-    const int local = u - t.prefix[n_seg];
-    const int n_tiles = (g.shared_rows + BN - 1) / BN;
-    const int mt = local / n_tiles, nt = local - mt * n_tiles;
+    const int local = u - s0;
+    mt = local / shared_tiles;
+    nt = local - mt * shared_tiles;
     r.routed = false;
     r.w_row = mt * g.k_blocks_shared * BM;
     r.x_row = nt * BN;
     r.valid = min(BN, g.shared_rows - nt * BN);
     r.k_blocks = g.k_blocks_shared;
-    r.out_col = mt * feat_per_tile;
     r.out = g.out_shared;
     r.ld = g.ld_out_shared;
   }
+  r.out_col = mt * feat_per_tile;
   return r;
 }
 
@@ -277,28 +300,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     t.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 2 || warp == 3) {
-    // work-unit prefix over the 2E segments: one thread per segment loads its
-    // row count, then a two-warp inclusive scan (shared units follow)
-    const int s = threadIdx.x - 64;
-    int rows = 0;
-    if (s < n_seg) {
-      rows = g.seg_rows[s];
-      t.seg_rows[s] = rows;
-      t.seg_base[s] = g.seg_base[s];
-    }
-    int incl = ((rows + BN - 1) / BN) * g.m_tiles_routed;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int n = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += n;
-    }
-    if (warp == 2 && lane == 31) t.scan_carry = incl;
-    asm volatile("bar.sync 2, 64;" ::: "memory");
-    if (warp == 3) incl += t.scan_carry;
-    if (s < n_seg) t.prefix[s + 1] = incl;
-    if (s == 0) t.prefix[0] = 0;
-  }
   if (warp == 1) {
     asm volatile(
         "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -310,37 +311,89 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
 
+  // Weight slabs of a static first unit stream in before the upstream kernel
+  // has finished: they depend on nothing it writes.
+  const int n_static = static_units(g);
+  int prefetched = 0;
+  if (warp == 0 && lane == 0 && (int)blockIdx.x < n_static) {
+    const int u = blockIdx.x;
+    const int s0 = g.n_experts * g.m_tiles_routed;
+    const bool routed = u < s0;
+    const CUtensorMap* mw = routed ? &tm_w_routed : &tm_w_shared;
+    int w_row, kbs;
+    if (routed) {
+      w_row = u * g.k_blocks_routed * BM;  // (e * MT + mt) == u
+      kbs = g.k_blocks_routed;
+    } else {
+      const int shared_tiles = (g.shared_rows + BN - 1) / BN;
+      w_row = ((u - s0) / shared_tiles) * g.k_blocks_shared * BM;
+      kbs = g.k_blocks_shared;
+    }
+    prefetched = min(kStages, kbs);
+    for (int kb = 0; kb < prefetched; ++kb) {
+      mbar_arrive_expect_tx(&t.full[kb], kTileA + kTileB);  // B follows after the wait
+      tma_load_2d(tiles_a + kb * kTileA, mw, 0, w_row + kb * BM, &t.full[kb]);
+    }
+  }
+  griddep_wait();
+
+  if (warp == 2 || warp == 3) {
+    // prefix of the dynamic units over the 2E segments: one thread per
+    // segment loads its row count, then a two-warp inclusive scan
+    const int s = threadIdx.x - 64;
+    int rows = 0;
+    if (s < n_seg) {
+      rows = g.seg_rows[s];
+      t.seg_rows[s] = rows;
+      t.seg_base[s] = g.seg_base[s];
+    }
+    int incl = s < n_seg ? extra_tiles(s, rows, g.n_experts) * g.m_tiles_routed : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (warp == 2 && lane == 31) t.scan_carry = incl;
+    asm volatile("bar.sync 2, 64;" ::: "memory");
+    if (warp == 3) incl += t.scan_carry;
+    if (s < n_seg) t.prefix[s + 1] = incl;
+    if (s == 0) t.prefix[0] = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) griddep_launch();
+
   const uint32_t tmem = t.tmem_base;
-  const int shared_units =
-      g.shared_rows > 0 ? ((g.shared_rows + BN - 1) / BN) * g.m_tiles_shared : 0;
-  const int total = t.prefix[n_seg] + shared_units;
+  const int total = n_static + t.prefix[n_seg];
   volatile int* abort_flag = &t.abort;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
+      int stage = prefetched % kStages;
+      uint32_t phase = prefetched == kStages ? 1u : 0u;
       bool issued[kStages] = {};
       uint32_t issued_phase[kStages] = {};
+      for (int kb = 0; kb < prefetched; ++kb) issued[kb] = true;  // phase 0
       bool ok = true;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         const Unit un = decode_unit(u, g, t);
         const CUtensorMap* mw = un.routed ? &tm_w_routed : &tm_w_shared;
         const CUtensorMap* mx = un.routed ? &tm_x_routed : &tm_x_shared;
-        for (int kb = 0; kb < un.k_blocks; kb += kSlabs) {
+        int kb = 0;
+        if (u == (int)blockIdx.x) {
+          // activation slabs of the prefetched stages (their barriers already
+          // expect A and B bytes)
+          for (; kb < prefetched; ++kb)
+            tma_load_2d(tiles_b + kb * kTileB, mx, kb * BK, un.x_row, &t.full[kb]);
+        }
+        for (; kb < un.k_blocks; ++kb) {
           if (!mbar_wait(&t.empty[stage], phase ^ 1, abort_flag, g.status, 10)) {
             ok = false;
             break;
           }
-          const int slabs = min(kSlabs, un.k_blocks - kb);
-          mbar_arrive_expect_tx(&t.full[stage], slabs * (kSlabA + kSlabB));
-          for (int sl = 0; sl < slabs; ++sl) {
-            tma_load_2d(tiles_a + stage * kTileA + sl * kSlabA, mw, 0, un.w_row + (kb + sl) * BM,
-                        &t.full[stage]);
-            tma_load_2d(tiles_b + stage * kTileB + sl * kSlabB, mx, (kb + sl) * BK, un.x_row,
-                        &t.full[stage]);
-          }
+          mbar_arrive_expect_tx(&t.full[stage], kTileA + kTileB);
+          tma_load_2d(tiles_a + stage * kTileA, mw, 0, un.w_row + kb * BM, &t.full[stage]);
+          tma_load_2d(tiles_b + stage * kTileB, mx, kb * BK, un.x_row, &t.full[stage]);
           issued[stage] = true;
           issued_phase[stage] = phase;
           if (++stage == kStages) {
@@ -367,22 +420,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&t.tempty[acc], acc_phase ^ 1, abort_flag, g.status, 20)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * BN;
-        const int n = (un.valid + 15) & ~15;
+        const int n = max(16, (un.valid + 15) & ~15);  // an empty expert still drains its slabs
         const uint32_t idesc = make_idesc(n);
-        for (int kb = 0; kb < un.k_blocks; kb += kSlabs) {
+        for (int kb = 0; kb < un.k_blocks; ++kb) {
           if (!mbar_wait(&t.full[stage], phase, abort_flag, g.status, 21)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const int slabs = min(kSlabs, un.k_blocks - kb);
-          for (int sl = 0; sl < slabs; ++sl) {
-            const uint64_t da = sw128_desc(tiles_a + stage * kTileA + sl * kSlabA);
-            const uint64_t db = sw128_desc(tiles_b + stage * kTileB + sl * kSlabB);
+          const uint64_t da = sw128_desc(tiles_a + stage * kTileA);
+          const uint64_t db = sw128_desc(tiles_b + stage * kTileB);
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k)
-              mma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, ((kb + sl) | k) != 0);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
           mma_commit(&t.empty[stage]);
           if (++stage == kStages) {
             stage = 0;
@@ -576,9 +626,10 @@ int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
     if (cudaGetLastError() != cudaSuccess) return -2;
     configured |= 1ull << dev;
   }
-  grouped_gemm_kernel<<<grid, kThreads, kSmemBytes, stream>>>(*tm_w_routed, *tm_x_routed,
-                                                              *tm_w_shared, *tm_x_shared, args);
-  return 0;
+  return launch_pdl(grouped_gemm_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream,
+                    *tm_w_routed, *tm_x_routed, *tm_w_shared, *tm_x_shared, args) == cudaSuccess
+             ? 0
+             : -2;
 }
 
 static int pack_blocks(size_t vecs) {

@@ -53,6 +53,9 @@ struct RouteArgs {
   int* indices;               // [T, 2]
   float* weights;             // [T, 2]
   long long* indices64;       // [T, 2] or null (reference dtype)
+  float* weights_out;         // [T, 2] or null: caller's copy of weights
+  int* counts_out;            // [E] or null
+  float* stats_out;           // [E + 1] or null
   MoeTables tab;
   int tokens, dim, n_experts, capacity;
   int* status;
@@ -64,6 +67,7 @@ struct GroupArgs {
   const float* weights;       // [T, 2] route weights
   MoeTables tab;
   int* positions;             // [2T] grouped row of each assignment
+  int* positions_out;         // [2T] or null: caller's copy
   int* row_dst;               // [R] token-major contribution slot of each grouped row
   float* row_w;               // [R] route weight of each grouped row
   __nv_bfloat16* grouped;     // [E*C + 2T, d]

@@ -17,6 +17,8 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(__nv_bfloat16* __restrict_
                                                       int rows, int dim, float eps) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  griddep_wait();
+  griddep_launch();
   if (row >= rows) return;
   const int nvec = dim >> 3;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * dim);
@@ -58,12 +60,12 @@ int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat
   dim3 grid((rows + warps - 1) / warps), block(32 * warps);
   const int v = (dim / 8 + 31) / 32;
   switch (v) {
-    case 1: rmsnorm_kernel<1><<<grid, block, 0, stream>>>(out, x, w, rows, dim, eps); break;
-    case 2: rmsnorm_kernel<2><<<grid, block, 0, stream>>>(out, x, w, rows, dim, eps); break;
-    case 3: rmsnorm_kernel<3><<<grid, block, 0, stream>>>(out, x, w, rows, dim, eps); break;
-    case 4: rmsnorm_kernel<4><<<grid, block, 0, stream>>>(out, x, w, rows, dim, eps); break;
+    case 1: launch_pdl(rmsnorm_kernel<1>, grid, block, 0, stream, out, x, w, rows, dim, eps); break;
+    case 2: launch_pdl(rmsnorm_kernel<2>, grid, block, 0, stream, out, x, w, rows, dim, eps); break;
+    case 3: launch_pdl(rmsnorm_kernel<3>, grid, block, 0, stream, out, x, w, rows, dim, eps); break;
+    case 4: launch_pdl(rmsnorm_kernel<4>, grid, block, 0, stream, out, x, w, rows, dim, eps); break;
     case 5: case 6: case 7: case 8:
-      rmsnorm_kernel<8><<<grid, block, 0, stream>>>(out, x, w, rows, dim, eps); break;
+      launch_pdl(rmsnorm_kernel<8>, grid, block, 0, stream, out, x, w, rows, dim, eps); break;
     default: return -1;
   }
   return 0;
@@ -96,6 +98,8 @@ __global__ void __launch_bounds__(32 * kDepthWarps) depthmix_kernel(DepthMixArgs
   extern __shared__ __align__(16) unsigned char depth_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int row = blockIdx.x * kDepthWarps + warp;
+  griddep_wait();
+  griddep_launch();
   if (row >= a.rows) return;
   const int dim = a.dim, nvec = dim >> 3, S = a.n_sources;
   const size_t off = (size_t)row * dim;
@@ -245,8 +249,7 @@ static int launch_depthmix_v(const DepthMixArgs& args, cudaStream_t stream) {
     configured |= 1ull << dev;
   }
   dim3 grid((args.rows + kDepthWarps - 1) / kDepthWarps), block(32 * kDepthWarps);
-  depthmix_kernel<V><<<grid, block, smem, stream>>>(args);
-  return 0;
+  return launch_pdl(depthmix_kernel<V>, grid, block, smem, stream, args) == cudaSuccess ? 0 : -2;
 }
 
 int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream) {

@@ -39,8 +39,11 @@ __global__ void __launch_bounds__(32 * kRouteWarps) route_kernel(RouteArgs a) {
   uint4* w_s = reinterpret_cast<uint4*>(route_smem);            // [E][nvec]
   uint4* x_s = w_s + (size_t)E * nvec;                          // [32][nvec]
   {
+    // the router weight is a parameter: fetch it before the upstream kernel ends
     const uint4* wg = reinterpret_cast<const uint4*>(a.w);
     for (int i = threadIdx.x; i < E * nvec; i += blockDim.x) cp_async16(w_s + i, wg + i);
+    griddep_wait();
+    griddep_launch();
     const int first = blk * kRouteTokensPerBlock;
     const int rows = min(kRouteTokensPerBlock, T - first);
     const uint4* xg = reinterpret_cast<const uint4*>(a.x + (size_t)first * d);
@@ -126,6 +129,10 @@ __global__ void __launch_bounds__(32 * kRouteWarps) route_kernel(RouteArgs a) {
       a.indices[2 * t + 1] = i2;
       a.weights[2 * t] = v1 / sel;
       a.weights[2 * t + 1] = v2 / sel;
+      if (a.weights_out != nullptr) {
+        a.weights_out[2 * t] = v1 / sel;
+        a.weights_out[2 * t + 1] = v2 / sel;
+      }
       if (a.indices64 != nullptr) {
         a.indices64[2 * t] = i1;
         a.indices64[2 * t + 1] = i2;
@@ -189,6 +196,7 @@ __global__ void __launch_bounds__(32 * kRouteWarps) route_kernel(RouteArgs a) {
     for (int e = 0; e < E; ++e) {
       const int c = count_s[e];
       a.tab.counts[e] = c;
+      if (a.counts_out != nullptr) a.counts_out[e] = c;
       a.tab.seg_rows[e] = c < C ? c : C;
       a.tab.seg_base[e] = e * C;
       const int ov = c > C ? c - C : 0;
@@ -197,9 +205,11 @@ __global__ void __launch_bounds__(32 * kRouteWarps) route_kernel(RouteArgs a) {
       overflow_base += ov;
       const float util = (float)c / (float)A;
       a.tab.stats[e] = util;
+      if (a.stats_out != nullptr) a.stats_out[e] = util;
       aux += util * (psum_e[e] / (float)T);
     }
     a.tab.stats[E] = (float)E * aux;
+    if (a.stats_out != nullptr) a.stats_out[E] = (float)E * aux;
     *a.tab.done_counter = 0;  // ready for the next launch
   }
 }
@@ -217,8 +227,8 @@ static int launch_route_ve(const RouteArgs& args, int nb, cudaStream_t stream) {
       return -2;
     configured |= 1ull << dev;
   }
-  route_kernel<V, EP><<<nb, 32 * kRouteWarps, smem, stream>>>(args);
-  return 0;
+  return launch_pdl(route_kernel<V, EP>, dim3(nb), dim3(32 * kRouteWarps), smem, stream, args) ==
+                 cudaSuccess ? 0 : -2;
 }
 
 template <int V>
@@ -261,6 +271,8 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
   const int blk = blockIdx.x, split = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nvec = d >> 3;
+  griddep_wait();
+  griddep_launch();
 
   // this split's assignments [lo, hi) cover tokens [lo/2, hi/2) of the block
   const int per = (kAssign + a.copy_split - 1) / a.copy_split;
@@ -300,6 +312,7 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
       row = slot < C ? e * C + slot : obase_s[e] + (slot - C);
       if (split == 0) {
         a.positions[a_idx] = row;
+        if (a.positions_out != nullptr) a.positions_out[a_idx] = row;
         a.row_dst[row] = (a_idx & ~1) + (e < partner ? 0 : 1);
         a.row_w[row] = __ldg(a.weights + a_idx);
       }
@@ -333,8 +346,7 @@ int launch_group(const GroupArgs& args, cudaStream_t stream) {
       return -2;
     configured |= 1ull << dev;
   }
-  group_kernel<<<grid, 128, smem, stream>>>(args);
-  return 0;
+  return launch_pdl(group_kernel, grid, dim3(128), smem, stream, args) == cudaSuccess ? 0 : -2;
 }
 
 // ---------------------------------------------------------------------------
@@ -349,6 +361,8 @@ template <int V>
 __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  griddep_wait();
+  griddep_launch();
   if (t >= a.tokens) return;
   const int d = a.dim, nvec = d >> 3;
   const uint4* c0 = reinterpret_cast<const uint4*>(a.contrib + (size_t)(2 * t) * d);
@@ -394,10 +408,10 @@ int launch_combine(const CombineArgs& args, cudaStream_t stream) {
   dim3 grid((args.tokens + warps - 1) / warps), block(32 * warps);
   const int v = (args.dim / 8 + 31) / 32;
   switch (v) {
-    case 1: combine_kernel<1><<<grid, block, 0, stream>>>(args); break;
-    case 2: combine_kernel<2><<<grid, block, 0, stream>>>(args); break;
-    case 3: combine_kernel<3><<<grid, block, 0, stream>>>(args); break;
-    case 4: combine_kernel<4><<<grid, block, 0, stream>>>(args); break;
+    case 1: launch_pdl(combine_kernel<1>, grid, block, 0, stream, args); break;
+    case 2: launch_pdl(combine_kernel<2>, grid, block, 0, stream, args); break;
+    case 3: launch_pdl(combine_kernel<3>, grid, block, 0, stream, args); break;
+    case 4: launch_pdl(combine_kernel<4>, grid, block, 0, stream, args); break;
     default: return -1;
   }
   return 0;
