@@ -153,6 +153,24 @@ int parrot_moe_forward_bf16(const parrot_moe_dims* dims, const parrot_moe_weight
                             const void* x, const parrot_moe_outputs* outputs, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* Whole MoE block without a caller-provided workspace, for callers that
+ * cannot allocate device memory at the point of the call (a runtime that owns
+ * all device memory and forbids allocation on its hot path, or code that must
+ * not enter an allocator).  Same computation and arguments as
+ * parrot_moe_forward_bf16; the workspace is a 4 MiB array compiled into this
+ * library, one per device that loads it, kept until the process exits —
+ * enough for Parrot XL widths (d 768, 16 experts of 512, shared 256) up to 192
+ * tokens.  Dims whose workspace (parrot_moe_workspace_layout) exceeds 4 MiB are
+ * rejected with PARROT_EINVAL.  It calls no allocator.  The first call on a
+ * device looks up the array's device address (and, like any first MoE call,
+ * builds the SiLU table there); make it before any stream capture.  All calls
+ * share the one array: calls whose GPU work overlaps (other streams, other
+ * threads) race and must be serialised by the caller.
+ * No counterpart in the reference. */
+int parrot_moe_forward_static_bf16(const parrot_moe_dims* dims,
+                                   const parrot_moe_weights* weights, const void* x,
+                                   const parrot_moe_outputs* outputs, void* stream);
+
 /* Router + grouping only (metal_moe.py:58-81 metal_route, plus the slot
  * scatter of moe_bf16.metal:678-696).  Leaves its results in the workspace
  * and copies the optional outputs (probs, indices, weights, positions,

@@ -347,6 +347,40 @@ int run_experts(const parrot_moe_dims* dims, const parrot_moe_weights* w, const 
   return check_launch("combine_kernel");
 }
 
+// ---- allocation-free MoE entry point --------------------------------------
+// Some callers cannot allocate device memory when they call the MoE block: a
+// runtime that hands out all device memory up front and forbids allocation on
+// its hot path, or code running where the allocator must not be entered.
+// parrot_moe_forward_static_bf16 serves them from a fixed workspace compiled
+// into this library instead of one the caller passes in.
+constexpr size_t kStaticWorkspaceBytes = size_t(4) << 20;  // 4 MiB per device
+
+// Device-side workspace.  In host code this name is only a stand-in for the
+// symbol, never a device address: its address on a device comes from
+// cudaGetSymbolAddress with that device current.
+static __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
+
+std::mutex g_static_mutex;
+void* g_static_address[64] = {};
+
+// Address of g_static_workspace on the current device, looked up once per device.
+int static_workspace_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(PARROT_ECUDA, "static workspace: no current CUDA device%s");
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (g_static_address[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_static_workspace);
+    if (err != cudaSuccess || p == nullptr)
+      return fail(PARROT_ECUDA, "static workspace: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(err));
+    g_static_address[dev] = p;
+  }
+  *out = g_static_address[dev];
+  return PARROT_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -507,6 +541,31 @@ int parrot_moe_gemm_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* 
 
 unsigned long long parrot_b200_launch_count(void) {
   return g_launches.load(std::memory_order_relaxed);
+}
+
+int parrot_moe_forward_static_bf16(const parrot_moe_dims* dims,
+                                   const parrot_moe_weights* weights, const void* x,
+                                   const parrot_moe_outputs* outputs, void* stream) {
+  parrot_moe_layout L;
+  int rc = layout_of(dims, &L);
+  if (rc) return rc;
+  if (L.total > kStaticWorkspaceBytes) {
+    char msg[160];
+    std::snprintf(msg, sizeof(msg), "%zu bytes, more than the %zu-byte static workspace",
+                  L.total, kStaticWorkspaceBytes);
+    return fail(PARROT_EINVAL, "moe_forward_static: these dims need a workspace of %s", msg);
+  }
+  void* ws = nullptr;
+  if ((rc = static_workspace_address(&ws))) return rc;
+  if ((rc = prepare(dims, weights, x, outputs, ws, kStaticWorkspaceBytes, &L))) return rc;
+  if (dims->tokens == 0) return PARROT_OK;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The array keeps whatever the previous call left: the last-block ticket and
+  // the status word must start at zero, so clear the control region first.
+  if (cudaMemsetAsync(ws, 0, L.indices, s) != cudaSuccess)
+    return check_launch("static workspace clear");
+  if ((rc = run_route(dims, weights, x, outputs, ws, L, s))) return rc;
+  return run_experts(dims, weights, x, outputs, ws, L, s);
 }
 
 int parrot_moe_read_status(const void* workspace, const parrot_moe_dims* dims, int* host_status4,

@@ -60,6 +60,8 @@ _SIGNATURES = {
     "parrot_pack_down_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "parrot_moe_forward_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                         POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
+    "parrot_moe_forward_static_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
+                                               POINTER(MoeOutputs), c_void_p]),
     "parrot_moe_route_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                       POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
     "parrot_moe_experts_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
