@@ -49,6 +49,18 @@ def parse_args():
     return p.parse_args()
 
 
+def ncu_traffic(kernel: str) -> float | None:
+    """Per-launch DRAM bytes of ``kernel`` from the committed ncu summary."""
+    path = ROOT / "profiles" / "traffic.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        parts = line.split()
+        if len(parts) == 2 and parts[0] == kernel:
+            return float(parts[1])
+    return None
+
+
 def measured_peaks() -> tuple[dict, str]:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -71,7 +83,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={','.join(self.FIELDS)}", "--format=csv,noheader,nounits",
-                 "-i", str(self.index), "-lms", "200"],
+                 "-i", str(self.index), "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -321,7 +333,8 @@ def run_b200(args):
                      "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_source": peak_kind,
                      "algorithmic_bytes": kern["gemm_bytes"], "launch_us": 1000 * kern["gemm_ms"],
-                     "traffic": None},
+                     "traffic": ncu_traffic("grouped_gemm_gate_up_T512"),
+                     "traffic_source": "ncu --set full capture, profiles/traffic.txt"},
         "moe_layer_us": {"T512": 1000 * kern["moe_ms"], "T256": 1000 * kern256["moe_ms"],
                          "gate_up_gemm_T256_us": 1000 * kern256["gemm_ms"]},
         "clocks": clocks,
