@@ -70,6 +70,22 @@ int parrot_depthmix_bf16(void* out, const void* const* sources, int n_sources,
                          void* pending_out, int rows, int dim, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Rotary position embedding, in place, for the packed q/k/v projection of
+ * local attention.  Replaces parrot/model.py:206-216 (LocalGQA._rope) applied
+ * to q and k in :218-230 / :232-262.  x: [rows, row_stride] bf16, rows in
+ * (batch, position) order with seq_len positions per batch row, position of
+ * row r = start + r % seq_len.  The first rot_cols columns (the q and k heads,
+ * rot_cols = (n_heads + n_kv_heads) * head_dim) are rotated as heads of
+ * head_dim interleaved (even, odd) pairs; the bf16 products and sums are
+ * rounded exactly as the reference's bf16 expression.  cos/sin tables:
+ * [max_positions, head_dim / 2] bf16.  head_dim % 8 == 0.
+ * Outside the MoE block: part of the forward this library accelerates.
+ * ---------------------------------------------------------------------- */
+int parrot_rope_inplace_bf16(void* x, const void* cos_table, const void* sin_table, int rows,
+                             int row_stride, int rot_cols, int head_dim, int seq_len, int start,
+                             int max_positions, void* stream);
+
+/* ------------------------------------------------------------------------
  * MoE block: router + top-2 + capacity grouping + grouped SwiGLU experts +
  * shared expert + weighted combine (+ residual add).
  * ---------------------------------------------------------------------- */

@@ -147,6 +147,7 @@ int layout_of(const parrot_moe_dims* d, parrot_moe_layout* L) {
   const int C = d->capacity > 0 ? d->capacity : parrot_moe_capacity(d->tokens, d->n_experts);
   const size_t A = 2 * T;
   const size_t nb = (size_t)parrot::route_blocks(d->tokens);
+  const size_t ng = (size_t)parrot::group_blocks(d->tokens);
   const size_t R = E * (size_t)C + A;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -161,7 +162,7 @@ int layout_of(const parrot_moe_dims* d, parrot_moe_layout* L) {
   L->weights = take(A * 4);
   L->positions = take(A * 4);
   L->block_hist = take(nb * E * 4);
-  L->block_prefix = take(nb * E * 4);
+  L->block_prefix = take(ng * E * 4);
   L->block_probsum = take(nb * E * 4);
   L->counts = take(E * 4);
   L->seg_rows = take(2 * E * 4);
@@ -262,8 +263,8 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ga.dim = dims->dim;
   ga.n_experts = E;
   ga.capacity = L.capacity;
-  const int nb = L.route_blocks;
-  const int want = (2 * sm_count() + nb - 1) / nb;  // about two blocks per SM
+  const int ng = parrot::group_blocks(T);
+  const int want = (2 * sm_count() + ng - 1) / ng;  // about two blocks per SM
   int split = 1;
   while (split * 2 <= want && split < 8) split *= 2;
   ga.copy_split = split;
@@ -447,6 +448,26 @@ int parrot_depthmix_bf16(void* out, const void* const* sources, int n_sources,
   if (parrot::launch_depthmix(a, static_cast<cudaStream_t>(stream)))
     return fail(PARROT_ECUDA, "depthmix: could not configure shared memory%s");
   return check_launch("depthmix_kernel");
+}
+
+int parrot_rope_inplace_bf16(void* x, const void* cos_table, const void* sin_table, int rows,
+                             int row_stride, int rot_cols, int head_dim, int seq_len, int start,
+                             int max_positions, void* stream) {
+  if (rows < 0 || head_dim <= 0 || head_dim % 8 || rot_cols < 0 || rot_cols % head_dim ||
+      row_stride < rot_cols || row_stride % 8 || seq_len <= 0 || start < 0)
+    return fail(PARROT_EINVAL, "rope: need head_dim %% 8 == 0, rot_cols a multiple of head_dim, "
+                               "row_stride %% 8 == 0 and >= rot_cols%s");
+  if (start + seq_len > max_positions)
+    return fail(PARROT_EINVAL, "rope: position exceeds the cos/sin tables%s");
+  if (rows == 0 || rot_cols == 0) return PARROT_OK;
+  if (!x || !cos_table || !sin_table || !aligned16(x))
+    return fail(PARROT_EINVAL, "rope: null or misaligned pointer%s");
+  if (parrot::launch_rope(static_cast<__nv_bfloat16*>(x),
+                          static_cast<const __nv_bfloat16*>(cos_table),
+                          static_cast<const __nv_bfloat16*>(sin_table), rows, row_stride,
+                          rot_cols, head_dim, seq_len, start, static_cast<cudaStream_t>(stream)))
+    return fail(PARROT_ECUDA, "rope: launch failed%s");
+  return check_launch("rope_kernel");
 }
 
 int parrot_moe_capacity(int tokens, int n_experts) {

@@ -11,7 +11,8 @@ namespace parrot {
 
 constexpr int kMaxDepthSources = 16;
 constexpr int kMaxExperts = 32;
-constexpr int kRouteTokensPerBlock = 32;   // router/grouping block: 64 assignments
+constexpr int kRouteTokensPerBlock = 8;    // router block: histogram granularity
+constexpr int kGroupTokensPerBlock = 32;   // grouping block: 64 assignments, 4 router blocks
 constexpr int kGemmBlockN = 128;           // token rows per grouped-GEMM tile
 constexpr int kGemmBlockK = 64;            // 128-byte swizzled K slab
 
@@ -35,9 +36,9 @@ struct DepthMixArgs {
 // Device-side MoE bookkeeping written by the router's last block and read by
 // the grouping, GEMM and combine kernels.  All int32.
 struct MoeTables {
-  int* block_prefix;   // [n_blocks, E] exclusive prefix of per-block counts
-  int* block_hist;     // [n_blocks, E]
-  float* block_probsum;  // [n_blocks, E]
+  int* block_prefix;   // [group blocks, E] exclusive prefix of counts at each grouping block
+  int* block_hist;     // [router blocks, E]
+  float* block_probsum;  // [router blocks, E]
   int* counts;         // [E]
   int* seg_rows;       // [2E] rows in capacity segment e, overflow segment e
   int* seg_base;       // [2E] first grouped row of each segment
@@ -112,6 +113,9 @@ struct GemmArgs {
 int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat16* w,
                    int rows, int dim, float eps, cudaStream_t stream);
 int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream);
+int launch_rope(__nv_bfloat16* x, const __nv_bfloat16* cos_t, const __nv_bfloat16* sin_t,
+                int rows, int row_stride, int rot_cols, int head_dim, int seq_len, int start,
+                cudaStream_t stream);
 int launch_route(const RouteArgs& args, cudaStream_t stream);
 int launch_group(const GroupArgs& args, cudaStream_t stream);
 int launch_combine(const CombineArgs& args, cudaStream_t stream);
@@ -126,6 +130,9 @@ size_t grouped_gemm_smem_bytes();
 
 inline int route_blocks(int tokens) {
   return (tokens + kRouteTokensPerBlock - 1) / kRouteTokensPerBlock;
+}
+inline int group_blocks(int tokens) {
+  return (tokens + kGroupTokensPerBlock - 1) / kGroupTokensPerBlock;
 }
 
 }  // namespace parrot

@@ -116,13 +116,24 @@ __global__ void __launch_bounds__(32 * kDepthWarps) depthmix_kernel(DepthMixArgs
       if (c < nvec) cp_async16(slab + s * nvec + c, src + c);
     }
   }
+  // every small vector this warp needs, requested together
+  uint4 qv[V], kwv[V], owv[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nvec) {
+      qv[i] = __ldg(reinterpret_cast<const uint4*>(a.query) + c);
+      kwv[i] = __ldg(reinterpret_cast<const uint4*>(a.key_w) + c);
+      if (a.out_w != nullptr) owv[i] = __ldg(reinterpret_cast<const uint4*>(a.out_w) + c);
+    }
+  }
   float q[V][8], kw[V][8];
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     const int c = lane + 32 * i;
     if (c < nvec) {
-      bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.query) + c), q[i]);
-      bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.key_w) + c), kw[i]);
+      bf16x8_to_float(qv[i], q[i]);
+      bf16x8_to_float(kwv[i], kw[i]);
     }
   }
   if (pending) {  // the deferred residual add, resolved in registers
@@ -227,7 +238,7 @@ __global__ void __launch_bounds__(32 * kDepthWarps) depthmix_kernel(DepthMixArgs
     const int c = lane + 32 * i;
     if (c < nvec) {
       float g[8];
-      bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.out_w) + c), g);
+      bf16x8_to_float(owv[i], g);
 #pragma unroll
       for (int j = 0; j < 8; ++j) g[j] = (h[i][j] * inv) * g[j];
       orow[c] = float_to_bf16x8(g);
@@ -262,6 +273,56 @@ int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream) {
     case 4: return launch_depthmix_v<4>(args, stream);
     default: return -1;
   }
+}
+
+// ---------------------------------------------------------------------------
+// Rotary embedding in place (model.py:206-216), for the packed projection
+// output of local attention: the first n_heads * head_dim columns of each row
+// hold the q and k heads; pair (x[2j], x[2j+1]) of a head at position p becomes
+//   (bf16(bf16(x0 c) - bf16(x1 s)), bf16(bf16(x0 s) + bf16(x1 c))),
+// c = cos[p][j], s = sin[p][j] (bf16 tables): every product and sum rounded
+// like the reference's bf16 tensor expression.  One thread per 8 columns.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rope_kernel(__nv_bfloat16* __restrict__ x,
+                                                   const __nv_bfloat16* __restrict__ cos_t,
+                                                   const __nv_bfloat16* __restrict__ sin_t,
+                                                   int rows, int row_stride, int rot_cols,
+                                                   int head_dim, int seq_len, int start) {
+  griddep_wait();
+  griddep_launch();
+  const int vec_per_row = rot_cols >> 3;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)rows * vec_per_row) return;
+  const int r = (int)(i / vec_per_row), v = (int)(i % vec_per_row);
+  const int col = v * 8;
+  const int pos = start + r % seq_len;
+  const int j0 = (col % head_dim) >> 1;
+  uint4* px = reinterpret_cast<uint4*>(x + (size_t)r * row_stride + col);
+  float f[8];
+  bf16x8_to_float(*px, f);
+  const uint2 cv = *reinterpret_cast<const uint2*>(cos_t + (size_t)pos * (head_dim >> 1) + j0);
+  const uint2 sv = *reinterpret_cast<const uint2*>(sin_t + (size_t)pos * (head_dim >> 1) + j0);
+  const __nv_bfloat16* cb = reinterpret_cast<const __nv_bfloat16*>(&cv);
+  const __nv_bfloat16* sb = reinterpret_cast<const __nv_bfloat16*>(&sv);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float c = __bfloat162float(cb[k]), s = __bfloat162float(sb[k]);
+    const float e = f[2 * k], o = f[2 * k + 1];
+    f[2 * k] = round_bf16(e * c) - round_bf16(o * s);
+    f[2 * k + 1] = round_bf16(e * s) + round_bf16(o * c);
+  }
+  *px = float_to_bf16x8(f);
+}
+
+int launch_rope(__nv_bfloat16* x, const __nv_bfloat16* cos_t, const __nv_bfloat16* sin_t,
+                int rows, int row_stride, int rot_cols, int head_dim, int seq_len, int start,
+                cudaStream_t stream) {
+  const long long total = (long long)rows * (rot_cols / 8);
+  if (total == 0) return 0;
+  const int threads = 256;
+  return launch_pdl(rope_kernel, dim3((unsigned)((total + threads - 1) / threads)),
+                    dim3(threads), 0, stream, x, cos_t, sin_t, rows, row_stride, rot_cols,
+                    head_dim, seq_len, start) == cudaSuccess ? 0 : -2;
 }
 
 }  // namespace parrot

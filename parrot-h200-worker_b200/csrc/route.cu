@@ -17,8 +17,9 @@
 
 namespace parrot {
 
-constexpr int kRouteWarps = 16;
+constexpr int kRouteWarps = 4;
 constexpr int kTokensPerWarp = kRouteTokensPerBlock / kRouteWarps;  // 2
+constexpr int kRouteBlocksPerGroup = kGroupTokensPerBlock / kRouteTokensPerBlock;  // 4
 
 // One warp routes kTokensPerWarp tokens.  The block first stages the router
 // weight [E, d] and its 32 token rows in shared memory with 16-byte async
@@ -160,25 +161,34 @@ __global__ void __launch_bounds__(32 * kRouteWarps) route_kernel(RouteArgs a) {
   __threadfence();
 
   // ---- last block: one warp per expert builds the exclusive prefix over
-  // blocks (warp scan, 32 blocks per step) and the probability column sum
-  // (lane partials in block order, then a fixed-order tree: deterministic).
+  // grouping blocks (each the sum of 4 router blocks; warp scan, 32 grouping
+  // blocks per step) and the probability column sum (lane partials in block
+  // order, then a fixed-order tree: deterministic).
   const int nb = gridDim.x;
+  const int ng = (nb + kRouteBlocksPerGroup - 1) / kRouteBlocksPerGroup;
   __shared__ int count_s[kMaxExperts];
   __shared__ float psum_e[kMaxExperts];
   for (int e = warp; e < E; e += kRouteWarps) {
     int carry = 0;
     float ps = 0.f;
-    for (int base = 0; base < nb; base += 32) {
-      const int b = base + lane;
-      const int v = (b < nb) ? __ldcg(a.tab.block_hist + b * E + e) : 0;
-      if (b < nb) ps += __ldcg(a.tab.block_probsum + b * E + e);
+    for (int base = 0; base < ng; base += 32) {
+      const int gb = base + lane;
+      int v = 0;
+#pragma unroll
+      for (int r = 0; r < kRouteBlocksPerGroup; ++r) {
+        const int b = gb * kRouteBlocksPerGroup + r;
+        if (gb < ng && b < nb) {
+          v += __ldcg(a.tab.block_hist + b * E + e);
+          ps += __ldcg(a.tab.block_probsum + b * E + e);
+        }
+      }
       int incl = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int n = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += n;
       }
-      if (b < nb) a.tab.block_prefix[b * E + e] = carry + incl - v;
+      if (gb < ng) a.tab.block_prefix[gb * E + e] = carry + incl - v;
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
     ps = warp_sum(ps);
@@ -252,7 +262,8 @@ int launch_route(const RouteArgs& args, cudaStream_t stream) {
 // ---------------------------------------------------------------------------
 // grouping: stable slots and the 16-byte row scatter
 //
-// Block b owns assignments [64 b, 64 b + 64) (tokens [32 b, 32 b + 32)).
+// Block b owns assignments [64 b, 64 b + 64) (tokens [32 b, 32 b + 32)); its
+// exclusive per-expert prefix comes from the router's last block.
 // Everything independent is requested up front: the assignment expert ids,
 // this block's exclusive prefix and the overflow bases, and (async copies)
 // the token rows this split copies.  Then ranks come from warp match, and
@@ -261,7 +272,7 @@ int launch_route(const RouteArgs& args, cudaStream_t stream) {
 // the token's pair, the order the reference adds them) and its route weight.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
-  constexpr int kAssign = 2 * kRouteTokensPerBlock;  // 64 per block
+  constexpr int kAssign = 2 * kGroupTokensPerBlock;  // 64 per block
   extern __shared__ __align__(16) unsigned char group_smem[];
   __shared__ int warp_cnt[2][kMaxExperts];
   __shared__ int prefix_s[kMaxExperts];
@@ -277,7 +288,7 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
   // this split's assignments [lo, hi) cover tokens [lo/2, hi/2) of the block
   const int per = (kAssign + a.copy_split - 1) / a.copy_split;
   const int lo = min(kAssign, split * per) & ~1, hi = min(kAssign, lo + per + (per & 1));
-  const int tok_lo = blk * kRouteTokensPerBlock + lo / 2;
+  const int tok_lo = blk * kGroupTokensPerBlock + lo / 2;
   const int n_tok = max(0, min(T - tok_lo, (hi - lo) / 2));
   uint4* x_s = reinterpret_cast<uint4*>(group_smem);
   {
@@ -334,15 +345,15 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
 
 int launch_group(const GroupArgs& args, cudaStream_t stream) {
   if (args.tokens == 0) return 0;
-  dim3 grid(route_blocks(args.tokens), args.copy_split);
-  const int per = (2 * kRouteTokensPerBlock + args.copy_split - 1) / args.copy_split;
+  dim3 grid(group_blocks(args.tokens), args.copy_split);
+  const int per = (2 * kGroupTokensPerBlock + args.copy_split - 1) / args.copy_split;
   const size_t smem = (size_t)((per + (per & 1)) / 2) * (args.dim / 8) * 16;
   static unsigned long long configured = 0;  // per device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
   if (!(configured & (1ull << dev))) {
     if (cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kRouteTokensPerBlock * (1024 / 8) * 16) != cudaSuccess)
+                             kGroupTokensPerBlock * (1024 / 8) * 16) != cudaSuccess)
       return -2;
     configured |= 1ull << dev;
   }

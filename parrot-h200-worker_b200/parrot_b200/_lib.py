@@ -52,6 +52,8 @@ _SIGNATURES = {
     "parrot_depthmix_bf16": (c_int, [c_void_p, POINTER(c_void_p), c_int, c_void_p, c_void_p,
                                      c_float, c_void_p, c_float, c_void_p, c_void_p, c_void_p,
                                      c_void_p, c_int, c_int, c_void_p]),
+    "parrot_rope_inplace_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                         c_int, c_int, c_int, c_int, c_void_p]),
     "parrot_moe_capacity": (c_int, [c_int, c_int]),
     "parrot_moe_workspace_layout": (c_int, [POINTER(MoeDims), POINTER(MoeLayout)]),
     "parrot_moe_workspace_init": (c_int, [c_void_p, POINTER(MoeDims), c_void_p]),

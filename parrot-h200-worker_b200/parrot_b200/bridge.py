@@ -90,6 +90,23 @@ def b200_rms_norm(module, x: Tensor) -> Tensor:
 
 
 # ---------------------------------------------------------------------------
+# Rotary embedding, in place on the packed q/k/v projection (model.py:206-216)
+# ---------------------------------------------------------------------------
+def b200_rope_(qkv: Tensor, cos: Tensor, sin: Tensor, rot_heads: int, head_dim: int,
+               start: int) -> Tensor:
+    """Rotate the first ``rot_heads`` heads of every row of ``qkv`` [b, t, width] in place."""
+    _require_device(qkv, "RoPE")
+    b, t, width = qkv.shape
+    if not qkv.is_contiguous():
+        raise RuntimeError("b200_rope_ needs a contiguous projection output")
+    lib = _lib.load()
+    _lib.check(lib.parrot_rope_inplace_bf16(
+        _p(qkv), _p(cos), _p(sin), b * t, width, rot_heads * head_dim, head_dim, t, start,
+        cos.shape[0], _stream()), "parrot_rope_inplace_bf16")
+    return qkv
+
+
+# ---------------------------------------------------------------------------
 # Block AttnRes depth mixing  (metal_moe.py:419-500)
 # ---------------------------------------------------------------------------
 def _depth_call(module, sources: Sequence[Tensor], output_norm, pending_delta: Tensor | None):

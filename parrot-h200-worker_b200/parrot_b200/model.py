@@ -166,17 +166,6 @@ def _rope_tables(cfg: ModelConfig, device, dtype) -> tuple[Tensor, Tensor]:
     return hit
 
 
-def _rotate(cfg: ModelConfig, x: Tensor, start: int) -> Tensor:
-    """RoPE on interleaved (even, odd) pairs at positions start.. (``model.py:206-216``)."""
-    stop = start + x.shape[-2]
-    if stop > cfg.max_seq_len:
-        raise ValueError("RoPE position exceeds max_seq_len")
-    cos, sin = _rope_tables(cfg, x.device, x.dtype)
-    cos, sin = cos[start:stop], sin[start:stop]
-    even, odd = x[..., 0::2], x[..., 1::2]
-    return torch.stack((even * cos - odd * sin, even * sin + odd * cos), -1).flatten(-2)
-
-
 def _packed(module: nn.Module, attr: str, params: tuple[Tensor, ...]) -> Tensor:
     """Concatenated projection weights, rebuilt when any parameter changes."""
     version = tuple(bridge.param_key(p) for p in params)
@@ -199,14 +188,19 @@ class LocalGQA(nn.Module):
         self.out = nn.Linear(cfg.n_heads * cfg.head_dim, cfg.dim, bias=False)
 
     def _qkv(self, x: Tensor, start: int):
+        """q, k (rotated) and v as [b, heads, t, head_dim] views of one projection."""
         c = self.cfg
         b, t, _ = x.shape
+        if start + t > c.max_seq_len:
+            raise ValueError("RoPE position exceeds max_seq_len")
         w = _packed(self, "_qkv_weight", (self.q.weight, self.k.weight, self.v.weight))
+        qkv = F.linear(x, w)
+        cos, sin = _rope_tables(c, x.device, x.dtype)
+        bridge.b200_rope_(qkv, cos, sin, c.n_heads + c.n_kv_heads, c.head_dim, start)
         qw, kw = c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim
-        q, k, v = F.linear(x, w).split((qw, kw, kw), -1)
-        q = _rotate(c, q.view(b, t, c.n_heads, c.head_dim).transpose(1, 2), start)
-        k = _rotate(c, k.view(b, t, c.n_kv_heads, c.head_dim).transpose(1, 2), start)
-        v = v.view(b, t, c.n_kv_heads, c.head_dim).transpose(1, 2)
+        q = qkv[..., :qw].view(b, t, c.n_heads, c.head_dim).transpose(1, 2)
+        k = qkv[..., qw:qw + kw].view(b, t, c.n_kv_heads, c.head_dim).transpose(1, 2)
+        v = qkv[..., qw + kw:].view(b, t, c.n_kv_heads, c.head_dim).transpose(1, 2)
         return q, k, v
 
     def prefill(self, x: Tensor):

@@ -326,3 +326,26 @@ def test_large_token_count_tensor_core_path():
     sample = torch.arange(0, T, 61)
     exp, _, _ = orc(x.float()[sample])
     assert_bf16_close(out.cpu()[sample], exp, "T=4096 sample")
+
+
+# ---------------------------------------------------------------------------
+# Rotary embedding (local attention q/k)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("batch,seq,start", [(1, 512, 0), (3, 37, 0), (2, 1, 700)])
+def test_rope_inplace_is_bit_exact_to_reference_bf16(batch, seq, start):
+    from parrot_b200.model import _rope_tables
+    cfg = po.OracleConfig()
+    H, KV, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    g = torch.Generator().manual_seed(seq + start)
+    qkv = torch.randn(batch, seq, (H + 2 * KV) * hd, generator=g).to("cuda", torch.bfloat16)
+    qw, kw = H * hd, KV * hd
+    # the oracle's rotation evaluated in bf16 (the reference's expression)
+    q_ref = po._apply_rope(cfg, qkv[..., :qw].view(batch, seq, H, hd).transpose(1, 2), start)
+    k_ref = po._apply_rope(cfg, qkv[..., qw:qw + kw].view(batch, seq, KV, hd).transpose(1, 2),
+                           start)
+    v_ref = qkv[..., qw + kw:].clone()
+    cos, sin = _rope_tables(moe_config(), qkv.device, qkv.dtype)
+    bridge.b200_rope_(qkv, cos, sin, H + KV, hd, start)
+    assert torch.equal(qkv[..., :qw].view(batch, seq, H, hd).transpose(1, 2), q_ref)
+    assert torch.equal(qkv[..., qw:qw + kw].view(batch, seq, KV, hd).transpose(1, 2), k_ref)
+    assert torch.equal(qkv[..., qw + kw:], v_ref)
