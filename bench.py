@@ -216,6 +216,112 @@ def time_moe_kernels(model, tokens: int, replays: int = 20) -> dict:
     return out
 
 
+def time_zipf_layer(tokens: int = 16384, replays: int = 10) -> dict:
+    """BASELINE config 4 on one GPU: one XL MoE layer, Zipf(1.2)-skewed routing
+    (harness router bias), CUDA-graph replays of the whole block."""
+    from parrot_b200 import ModelConfig, bridge
+    from parrot_b200.graphs import capture_calls
+    from parrot_b200.model import MoE
+    from parrot_b200.workloads import (make_hidden_states, make_moe_layer_weights,
+                                       tune_zipf_router_bias)
+    cfg = ModelConfig()
+    w = make_moe_layer_weights(cfg.dim, cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim, 1)
+    moe = MoE(cfg)
+    moe.load_state_dict(w)
+    x = make_hidden_states(tokens, cfg.dim, 0)
+    moe = moe.to("cuda", torch.bfloat16).eval()
+    moe.router_bias = tune_zipf_router_bias(x, w["router.weight"]).to("cuda", torch.float32)
+    xd = x.to("cuda", torch.bfloat16)
+    with torch.inference_mode():
+        _, _, util = bridge.b200_moe(moe, xd, True)
+        graph = capture_calls(lambda: bridge.b200_moe(moe, xd, False))
+        graph.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(replays):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+    us = 1000 * a.elapsed_time(b) / replays
+    flops = 2 * (2 * tokens * cfg.dim * 3 * cfg.expert_dim + tokens * cfg.dim * 3 *
+                 cfg.shared_expert_dim + tokens * cfg.dim * cfg.n_experts)
+    capacity = max(8, ((4 * tokens + cfg.n_experts - 1) // cfg.n_experts + 7) // 8 * 8)
+    counts = (util.float() * 2 * tokens).round().int().tolist()
+    return {"us": us, "tflops": flops / (us * 1e-6) / 1e12, "tokens": tokens,
+            "expert_counts": counts, "capacity": capacity,
+            "overflow_rows": sum(max(0, c - capacity) for c in counts)}
+
+
+def time_decode(model, batches=(1, 8, 64), prompt: int = 128, new_tokens: int = 16) -> dict:
+    """prefill 128 ids, then 16 greedy decode_step calls (eager)."""
+    from parrot_b200.workloads import random_token_ids
+    out = {}
+    with torch.inference_mode():
+        for b in batches:
+            ids = random_token_ids(b, prompt, model.config.vocab_size, seed=b).cuda()
+            logits, state = model.prefill(ids)
+            nxt = logits.argmax(-1)
+            model.decode_step(nxt, state)  # warm the decode path once
+            logits, state = model.prefill(ids)
+            nxt = logits.argmax(-1)
+            torch.cuda.synchronize()
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(new_tokens):
+                logits, state = model.decode_step(nxt, state)
+                nxt = logits.argmax(-1)
+            e.record()
+            torch.cuda.synchronize()
+            out[f"B{b}"] = b * new_tokens / (a.elapsed_time(e) * 1e-3)
+    return out
+
+
+def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 10,
+                  warmup: int = 3) -> dict:
+    """BASELINE config 4 expert-parallel: the Zipf-skewed XL MoE layer with its
+    16384 tokens split evenly over the ranks and the experts round-robin over
+    them; NCCL all-to-all of counts, rows and outputs.  Every rank runs it;
+    the time is the max over ranks."""
+    from parrot_b200 import ModelConfig, ep
+    from parrot_b200.model import MoE
+    from parrot_b200.workloads import (make_hidden_states, make_moe_layer_weights,
+                                       tune_zipf_router_bias)
+    cfg = ModelConfig()
+    w = make_moe_layer_weights(cfg.dim, cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim, 1)
+    moe = MoE(cfg)
+    moe.load_state_dict(w)
+    x = make_hidden_states(total, cfg.dim, 0)
+    moe = moe.to("cuda", torch.bfloat16).eval()
+    moe.router_bias = tune_zipf_router_bias(x, w["router.weight"]).to("cuda", torch.float32)
+    per = total // world
+    xs = x[rank * per:(rank + 1) * per].to("cuda", torch.bfloat16)
+    with torch.inference_mode():
+        layer = ep.ExpertParallelMoE(ep.B200EpOps(moe, rank, world), ep.TorchComm(),
+                                     cfg.n_experts)
+        for _ in range(warmup):
+            layer(xs)
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            layer(xs)
+        b.record()
+        dist.barrier()
+        torch.cuda.synchronize()
+    us = torch.tensor([1000 * a.elapsed_time(b) / iters], device="cuda", dtype=torch.float64)
+    dist.all_reduce(us, op=dist.ReduceOp.MAX)
+    recv = torch.tensor([layer.last_recv_rows], device="cuda", dtype=torch.int64)
+    recv_all = [torch.zeros_like(recv) for _ in range(world)]
+    dist.all_gather(recv_all, recv)
+    t_us = float(us.item())
+    return {"us": t_us, "tokens_total": per * world, "tokens_per_s": per * world / (t_us * 1e-6),
+            "ranks": world, "placement": "round-robin (expert e on rank e % ranks)",
+            "received_rows_per_rank": [int(r.item()) for r in recv_all],
+            "timing": "CUDA events, max over ranks; one host read of the counts per call"}
+
+
 def run_b200(args):
     from parrot_b200 import ModelConfig, Parrot, _lib
     from parrot_b200 import build as pbuild
@@ -254,11 +360,13 @@ def run_b200(args):
         model(ids)
         launches_per_forward = lib.parrot_b200_launch_count() - l0
         barrier()
-        t0 = time.perf_counter()
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        q0.record(stream)
         for _ in range(3):
             model(ids)
+        q1.record(stream)
         torch.cuda.synchronize()
-        eager_ms = (time.perf_counter() - t0) * 1000 / 3
+        eager_ms = q0.elapsed_time(q1) / 3
 
         graphed = model.capture(1, SEQ)
         graphed(ids)
@@ -301,6 +409,9 @@ def run_b200(args):
     e2e_ms = max_over_ranks(e2e_ms)
     kern = time_moe_kernels(model, SEQ) if rank == 0 else None
     kern256 = time_moe_kernels(model, 256) if rank == 0 else None
+    decode = time_decode(model) if rank == 0 else None
+    zipf = time_zipf_layer() if rank == 0 else None
+    ep_zipf = time_ep_layer(dist, rank, world) if dist is not None else None
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -338,6 +449,9 @@ def run_b200(args):
         "moe_layer_us": {"T512": 1000 * kern["moe_ms"], "T256": 1000 * kern256["moe_ms"],
                          "gate_up_gemm_T256_us": 1000 * kern256["gemm_ms"]},
         "clocks": clocks,
+        "config4_zipf_moe_layer": zipf,
+        "config4_ep_zipf_moe_layer": ep_zipf,
+        "config5_decode_tokens_per_s": decode,
     }
     if world == 1 and not args.skip_cpu_baseline:
         base = cpu_reference_forward(steps=2, warmup=1)

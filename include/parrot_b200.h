@@ -96,7 +96,9 @@ typedef struct parrot_moe_dims {
   int top_k;       /* must be 2 */
   int expert_dim;  /* H, % 64 == 0 */
   int shared_dim;  /* Hs, % 64 == 0 */
-  int capacity;    /* slots per expert; 0 selects parrot_moe_capacity() */
+  int capacity;    /* slots per expert; 0 selects parrot_moe_capacity();
+                      -1 packs all rows per expert, experts in id order (no capacity
+                      region: the expert-parallel send layout) */
 } parrot_moe_dims;
 
 /* Expert weights start in torch.nn.Linear [out, in] layout and are packed
@@ -218,6 +220,50 @@ unsigned long long parrot_b200_launch_count(void);
  * (synchronises `stream`).  code 0 = ok. */
 int parrot_moe_read_status(const void* workspace, const parrot_moe_dims* dims, int* host_status4,
                            void* stream);
+
+/* ---- expert parallelism ----------------------------------------------------
+ * The reference runs every expert on one device; these four calls split the
+ * same computation (model.py:521-551) across ep_ranks devices that each own
+ * n_experts / ep_ranks experts, round-robin: expert e lives on rank
+ * e % ep_ranks as local expert e / ep_ranks.  The exchange between them (an
+ * all-to-all of row counts, of token rows, and back of expert outputs) is the
+ * caller's, over NCCL; these calls only touch local memory.  The result equals
+ * parrot_moe_forward_bf16 on the same tokens bit for bit.
+ *
+ * Router + grouping for expert parallelism.  dims->capacity must be -1: the
+ * workspace's grouped rows [2T, d] then hold every assignment packed by
+ * destination rank, then local expert, then ascending token (the reference's
+ * torch.where order, model.py:548).  outputs->counts (optional) receives the
+ * per-expert row counts; out/residual are unused. */
+int parrot_moe_ep_dispatch_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                                const void* x, const parrot_moe_outputs* outputs, int ep_ranks,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* The shared expert (model.py:546, `self.shared(flat)`) on this rank's own
+ * tokens, into the workspace; only weights->shared_gate_up/shared_down are read. */
+int parrot_moe_shared_ffn_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                               const void* x, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/* Grouped SwiGLU experts over received rows (model.py:443-448 per expert):
+ * x [rows, dim] is cut into n_segments contiguous segments (device int arrays
+ * seg_rows, seg_base: first row; seg_expert: which of the n_mats packed
+ * matrices, parrot_pack_gate_up_bf16 / parrot_pack_down_bf16 layout).
+ * hidden [rows, expert_dim] is scratch; y [rows, dim] receives the unweighted
+ * expert outputs in the order of x.  status: device int[4], or NULL. */
+int parrot_moe_expert_ffn_bf16(int rows, int dim, int expert_dim, int n_mats, int n_segments,
+                               const int* seg_rows, const int* seg_base, const int* seg_expert,
+                               const void* gate_up, const void* down, const void* x,
+                               void* hidden, void* y, int* status, void* stream);
+
+/* Combine for expert parallelism (model.py:551): y [2T, d] holds the expert
+ * outputs returned in the dispatch's grouped-row order; out = shared output +
+ * route-weighted outputs in ascending expert order (+ residual when non-NULL).
+ * Reads indices, weights, positions and the shared output from the workspace
+ * of parrot_moe_ep_dispatch_bf16 / parrot_moe_shared_ffn_bf16. */
+int parrot_moe_ep_combine_bf16(const parrot_moe_dims* dims, const void* y, const void* workspace,
+                               size_t workspace_bytes, const void* residual, void* out,
+                               void* stream);
 
 #ifdef __cplusplus
 }

@@ -134,7 +134,7 @@ int validate_dims(const parrot_moe_dims* d) {
     return fail(PARROT_EINVAL, "expert_dim must be a positive multiple of 64%s");
   if (d->shared_dim <= 0 || d->shared_dim % 64)
     return fail(PARROT_EINVAL, "shared_dim must be a positive multiple of 64%s");
-  if (d->capacity < 0) return fail(PARROT_EINVAL, "capacity must be >= 0%s");
+  if (d->capacity < -1) return fail(PARROT_EINVAL, "capacity must be >= -1%s");
   return PARROT_OK;
 }
 
@@ -144,7 +144,10 @@ int layout_of(const parrot_moe_dims* d, parrot_moe_layout* L) {
   std::memset(L, 0, sizeof(*L));
   const size_t T = d->tokens, D = d->dim, E = d->n_experts, H = d->expert_dim,
                Hs = d->shared_dim;
-  const int C = d->capacity > 0 ? d->capacity : parrot_moe_capacity(d->tokens, d->n_experts);
+  // capacity 0 selects the default; -1 packs every row per expert (no capacity region)
+  const int C = d->capacity > 0    ? d->capacity
+                : d->capacity == 0 ? parrot_moe_capacity(d->tokens, d->n_experts)
+                                   : 0;
   const size_t A = 2 * T;
   const size_t nb = (size_t)parrot::route_blocks(d->tokens);
   const size_t ng = (size_t)parrot::group_blocks(d->tokens);
@@ -226,7 +229,8 @@ int prepare(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void
 }
 
 int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
-              const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L, cudaStream_t s) {
+              const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L, cudaStream_t s,
+              int ep_ranks = 1) {
   const int T = dims->tokens, E = dims->n_experts;
   parrot::RouteArgs ra{};
   ra.x = static_cast<const __nv_bfloat16*>(x);
@@ -244,6 +248,7 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ra.dim = dims->dim;
   ra.n_experts = E;
   ra.capacity = L.capacity;
+  ra.ep_ranks = ep_ranks;
   ra.status = at<int>(ws, L.status);
   if (parrot::launch_route(ra, s)) return fail(PARROT_ECUDA, "route: unsupported dim or smem%s");
   int rc = check_launch("route_kernel");
@@ -274,12 +279,16 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
 }
 
 int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights* w,
-             const void* x, void* ws, const parrot_moe_layout& L, cudaStream_t s) {
+             const void* x, void* ws, const parrot_moe_layout& L, cudaStream_t s,
+             bool shared_only = false) {
   const int T = dims->tokens, D = dims->dim, E = dims->n_experts, H = dims->expert_dim,
             Hs = dims->shared_dim, R = L.grouped_rows;
   parrot::GemmArgs g{};
   g.seg_rows = at<int>(ws, L.seg_rows);
   g.seg_base = at<int>(ws, L.seg_base);
+  g.seg_expert = nullptr;
+  g.n_seg = shared_only ? 0 : 2 * E;
+  g.static_routed = (L.capacity > 0 && !shared_only) ? 1 : 0;
   g.n_experts = E;
   g.shared_rows = T;
   g.status = at<int>(ws, L.status);
@@ -296,10 +305,16 @@ int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights*
     g.ld_out_shared = Hs;
     g.mode = parrot::kGemmSwiGLU;
     // weights are tiled (parrot_pack_*): a [tiles * 128, 64] view, one box per tile
-    ok = tensor_map(&mw, w->gate_up, (long long)E * 2 * H * D / kGemmBlockK, kGemmBlockK, 128) &&
-         tensor_map(&mx, at<void>(ws, L.grouped), R, D, kGemmBlockN) &&
-         tensor_map(&msw, w->shared_gate_up, 2LL * Hs * D / kGemmBlockK, kGemmBlockK, 128) &&
+    ok = tensor_map(&msw, w->shared_gate_up, 2LL * Hs * D / kGemmBlockK, kGemmBlockK, 128) &&
          tensor_map(&msx, x, T, D, kGemmBlockN);
+    if (shared_only) {  // no routed units: the routed maps are never read
+      mw = msw;
+      mx = msx;
+    } else {
+      ok = ok &&
+           tensor_map(&mw, w->gate_up, (long long)E * 2 * H * D / kGemmBlockK, kGemmBlockK, 128) &&
+           tensor_map(&mx, at<void>(ws, L.grouped), R, D, kGemmBlockN);
+    }
   } else {
     g.m_tiles_routed = D / 128;
     g.k_blocks_routed = H / kGemmBlockK;
@@ -312,15 +327,22 @@ int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights*
     g.out_shared = at<__nv_bfloat16>(ws, L.shared_y);
     g.ld_out_shared = D;
     g.mode = parrot::kGemmPlain;
-    ok = tensor_map(&mw, w->down, (long long)E * D * H / kGemmBlockK, kGemmBlockK, 128) &&
-         tensor_map(&mx, at<void>(ws, L.hidden), R, H, kGemmBlockN) &&
-         tensor_map(&msw, w->shared_down, (long long)D * Hs / kGemmBlockK, kGemmBlockK, 128) &&
+    ok = tensor_map(&msw, w->shared_down, (long long)D * Hs / kGemmBlockK, kGemmBlockK, 128) &&
          tensor_map(&msx, at<void>(ws, L.shared_hidden), T, Hs, kGemmBlockN);
+    if (shared_only) {
+      mw = msw;
+      mx = msx;
+    } else {
+      ok = ok &&
+           tensor_map(&mw, w->down, (long long)E * D * H / kGemmBlockK, kGemmBlockK, 128) &&
+           tensor_map(&mx, at<void>(ws, L.hidden), R, H, kGemmBlockN);
+    }
   }
   if (!ok) return fail(PARROT_ECUDA, "cuTensorMapEncodeTiled failed%s");
   const int A = 2 * T;
   const long long routed_units =
-      (long long)((A + kGemmBlockN - 1) / kGemmBlockN + 2 * E) * g.m_tiles_routed;
+      shared_only ? 0
+                  : (long long)((A + kGemmBlockN - 1) / kGemmBlockN + 2 * E) * g.m_tiles_routed;
   const long long shared_units = (long long)((T + kGemmBlockN - 1) / kGemmBlockN) * g.m_tiles_shared;
   long long grid = routed_units + shared_units;
   const int sms = sm_count();
@@ -346,6 +368,77 @@ int run_experts(const parrot_moe_dims* dims, const parrot_moe_weights* w, const 
   c.dim = dims->dim;
   if (parrot::launch_combine(c, s)) return fail(PARROT_EINVAL, "combine: unsupported dim%s");
   return check_launch("combine_kernel");
+}
+
+// ---- expert-parallel pieces -------------------------------------------------
+int check_router(const parrot_moe_weights* w) {
+  if (w == nullptr || w->router == nullptr || !aligned16(w->router))
+    return fail(PARROT_EINVAL, "router weight missing or not 16-byte aligned%s");
+  return PARROT_OK;
+}
+
+int check_shared(const parrot_moe_weights* w) {
+  if (w == nullptr || w->shared_gate_up == nullptr || w->shared_down == nullptr ||
+      !aligned16(w->shared_gate_up) || !aligned16(w->shared_down))
+    return fail(PARROT_EINVAL, "shared expert weights missing or not 16-byte aligned%s");
+  return PARROT_OK;
+}
+
+int ws_ok(const void* ws, size_t ws_bytes, const parrot_moe_layout& L) {
+  if (ws == nullptr || ws_bytes < L.total || !aligned16(ws))
+    return fail(PARROT_EINVAL, "workspace missing, misaligned or smaller than the layout total%s");
+  return PARROT_OK;
+}
+
+// Grouped SwiGLU FFN over caller-described row segments: hidden = SwiGLU
+// halves of x @ gate_up, y = hidden @ down, rows in the order of x.
+int run_ffn(int rows, int dim, int expert_dim, int n_mats, int n_seg, const int* seg_rows,
+            const int* seg_base, const int* seg_expert, const void* gate_up, const void* down,
+            const void* x, void* hidden, void* y, int* status, cudaStream_t s) {
+  CUtensorMap mw, mx;
+  const int sms = sm_count();
+  for (int stage = 0; stage < 2; ++stage) {
+    const bool swiglu = stage == 0;
+    parrot::GemmArgs g{};
+    g.seg_rows = seg_rows;
+    g.seg_base = seg_base;
+    g.seg_expert = seg_expert;
+    g.n_seg = n_seg;
+    g.static_routed = 0;
+    g.n_experts = n_mats;
+    g.shared_rows = 0;
+    g.status = status;
+    bool ok;
+    if (swiglu) {
+      g.m_tiles_routed = 2 * expert_dim / 128;
+      g.k_blocks_routed = dim / kGemmBlockK;
+      g.out_routed = static_cast<__nv_bfloat16*>(hidden);
+      g.ld_out_routed = expert_dim;
+      g.mode = parrot::kGemmSwiGLU;
+      ok = tensor_map(&mw, gate_up, (long long)n_mats * 2 * expert_dim * dim / kGemmBlockK,
+                      kGemmBlockK, 128) &&
+           tensor_map(&mx, x, rows, dim, kGemmBlockN);
+    } else {
+      g.m_tiles_routed = dim / 128;
+      g.k_blocks_routed = expert_dim / kGemmBlockK;
+      g.out_routed = static_cast<__nv_bfloat16*>(y);
+      g.ld_out_routed = dim;
+      g.mode = parrot::kGemmPlain;
+      ok = tensor_map(&mw, down, (long long)n_mats * dim * expert_dim / kGemmBlockK, kGemmBlockK,
+                      128) &&
+           tensor_map(&mx, hidden, rows, expert_dim, kGemmBlockN);
+    }
+    if (!ok) return fail(PARROT_ECUDA, "cuTensorMapEncodeTiled failed%s");
+    // the shared maps are never read (shared_rows == 0)
+    long long grid = (long long)((rows + kGemmBlockN - 1) / kGemmBlockN + n_seg) * g.m_tiles_routed;
+    if (grid > sms) grid = sms;
+    if (grid < 1) grid = 1;
+    if (parrot::launch_grouped_gemm(g, &mw, &mx, &mw, &mx, (int)grid, s))
+      return fail(PARROT_ECUDA, "grouped GEMM: could not set shared-memory size%s");
+    const int rc = check_launch(swiglu ? "grouped_gemm(ffn gate_up)" : "grouped_gemm(ffn down)");
+    if (rc) return rc;
+  }
+  return PARROT_OK;
 }
 
 // ---- allocation-free MoE entry point --------------------------------------
@@ -587,6 +680,84 @@ int parrot_moe_forward_static_bf16(const parrot_moe_dims* dims,
     return check_launch("static workspace clear");
   if ((rc = run_route(dims, weights, x, outputs, ws, L, s))) return rc;
   return run_experts(dims, weights, x, outputs, ws, L, s);
+}
+
+int parrot_moe_ep_dispatch_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                                const void* x, const parrot_moe_outputs* outputs, int ep_ranks,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  int rc = layout_of(dims, &L);
+  if (rc) return rc;
+  if (dims->capacity != -1)
+    return fail(PARROT_EINVAL, "ep_dispatch: dims->capacity must be -1 (packed rows)%s");
+  if (ep_ranks < 1 || dims->n_experts % ep_ranks)
+    return fail(PARROT_EINVAL, "ep_dispatch: ep_ranks must divide n_experts%s");
+  if ((rc = check_router(weights)) || (rc = ws_ok(workspace, workspace_bytes, L))) return rc;
+  if (outputs == nullptr) return fail(PARROT_EINVAL, "ep_dispatch: outputs is NULL%s");
+  if (dims->tokens == 0) return PARROT_OK;
+  if (x == nullptr || !aligned16(x)) return fail(PARROT_EINVAL, "x must be 16-byte aligned%s");
+  return run_route(dims, weights, x, outputs, workspace, L, static_cast<cudaStream_t>(stream),
+                   ep_ranks);
+}
+
+int parrot_moe_shared_ffn_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                               const void* x, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  parrot_moe_layout L;
+  int rc = layout_of(dims, &L);
+  if (rc) return rc;
+  if ((rc = check_shared(weights)) || (rc = ws_ok(workspace, workspace_bytes, L))) return rc;
+  if (dims->tokens == 0) return PARROT_OK;
+  if (x == nullptr || !aligned16(x)) return fail(PARROT_EINVAL, "x must be 16-byte aligned%s");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = run_gemm(true, dims, weights, x, workspace, L, s, true))) return rc;
+  return run_gemm(false, dims, weights, x, workspace, L, s, true);
+}
+
+int parrot_moe_expert_ffn_bf16(int rows, int dim, int expert_dim, int n_mats, int n_segments,
+                               const int* seg_rows, const int* seg_base, const int* seg_expert,
+                               const void* gate_up, const void* down, const void* x,
+                               void* hidden, void* y, int* status, void* stream) {
+  if (rows < 0 || n_segments < 0 || n_segments > 2 * parrot::kMaxExperts)
+    return fail(PARROT_EINVAL, "expert_ffn: rows >= 0 and 0 <= n_segments <= 64 required%s");
+  if (dim <= 0 || dim % 128 || dim > 1024 || expert_dim <= 0 || expert_dim % 64 || n_mats < 1)
+    return fail(PARROT_EINVAL, "expert_ffn: dim % 128 == 0 (<= 1024), expert_dim % 64 == 0%s");
+  if (rows == 0 || n_segments == 0) return PARROT_OK;
+  if (!seg_rows || !seg_base || !seg_expert || !gate_up || !down || !x || !hidden || !y)
+    return fail(PARROT_EINVAL, "expert_ffn: null pointer%s");
+  if (!aligned16(gate_up) || !aligned16(down) || !aligned16(x) || !aligned16(hidden) ||
+      !aligned16(y))
+    return fail(PARROT_EINVAL, "expert_ffn: buffers must be 16-byte aligned%s");
+  return run_ffn(rows, dim, expert_dim, n_mats, n_segments, seg_rows, seg_base, seg_expert,
+                 gate_up, down, x, hidden, y, status, static_cast<cudaStream_t>(stream));
+}
+
+int parrot_moe_ep_combine_bf16(const parrot_moe_dims* dims, const void* y, const void* workspace,
+                               size_t workspace_bytes, const void* residual, void* out,
+                               void* stream) {
+  parrot_moe_layout L;
+  int rc = layout_of(dims, &L);
+  if (rc) return rc;
+  if ((rc = ws_ok(workspace, workspace_bytes, L))) return rc;
+  if (dims->tokens == 0) return PARROT_OK;
+  if (!y || !out || !aligned16(y) || !aligned16(out) || (residual && !aligned16(residual)))
+    return fail(PARROT_EINVAL, "ep_combine: y/out/residual must be 16-byte aligned%s");
+  void* ws = const_cast<void*>(workspace);
+  parrot::EpCombineArgs c{};
+  c.y = static_cast<const __nv_bfloat16*>(y);
+  c.indices = at<int>(ws, L.indices);
+  c.weights = at<float>(ws, L.weights);
+  c.positions = at<int>(ws, L.positions);
+  c.shared_y = at<__nv_bfloat16>(ws, L.shared_y);
+  c.residual = static_cast<const __nv_bfloat16*>(residual);
+  c.out = static_cast<__nv_bfloat16*>(out);
+  c.tokens = dims->tokens;
+  c.dim = dims->dim;
+  c.rows = L.grouped_rows;
+  c.status = at<int>(ws, L.status);
+  if (parrot::launch_ep_combine(c, static_cast<cudaStream_t>(stream)))
+    return fail(PARROT_EINVAL, "ep_combine: unsupported dim%s");
+  return check_launch("ep_combine_kernel");
 }
 
 int parrot_moe_read_status(const void* workspace, const parrot_moe_dims* dims, int* host_status4,

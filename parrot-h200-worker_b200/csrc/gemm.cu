@@ -56,6 +56,7 @@ struct __align__(8) SmemTail {
   int prefix[kSegMax + 2];
   int seg_rows[kSegMax];
   int seg_base[kSegMax];
+  int seg_expert[kSegMax];
 };
 
 constexpr size_t kSmemBytes =
@@ -200,21 +201,25 @@ struct Unit {
 //                                   then every token tile of the overflow segments
 // The static units' weight tiles are known before the routing results exist,
 // so a CTA starts streaming them before its grid-dependency wait.
-__device__ __forceinline__ int extra_tiles(int s, int rows, int n_experts) {
+__device__ __forceinline__ int extra_tiles(int s, int rows, const GemmArgs& g) {
   const int tiles = (rows + BN - 1) / BN;
-  return s < n_experts ? max(tiles - 1, 0) : tiles;
+  return (g.static_routed && s < g.n_experts) ? max(tiles - 1, 0) : tiles;
+}
+
+__device__ __forceinline__ int static_routed_units(const GemmArgs& g) {
+  return g.static_routed ? g.n_experts * g.m_tiles_routed : 0;
 }
 
 __device__ __forceinline__ int static_units(const GemmArgs& g) {
   const int shared_tiles = (g.shared_rows + BN - 1) / BN;
-  return g.n_experts * g.m_tiles_routed + shared_tiles * g.m_tiles_shared;
+  return static_routed_units(g) + shared_tiles * g.m_tiles_shared;
 }
 
 __device__ __forceinline__ Unit decode_unit(int u, const GemmArgs& g, const SmemTail& t) {
   Unit r;
   const int E = g.n_experts, MT = g.m_tiles_routed;
   const int feat_per_tile = g.mode == kGemmSwiGLU ? BM / 2 : BM;
-  const int s0 = E * MT;
+  const int s0 = static_routed_units(g);
   const int shared_tiles = (g.shared_rows + BN - 1) / BN;
   const int su = shared_tiles * g.m_tiles_shared;
   int s = -1, mt = 0, nt = 0;
@@ -226,12 +231,12 @@ __device__ __forceinline__ Unit decode_unit(int u, const GemmArgs& g, const Smem
     s = 0;
     while (t.prefix[s + 1] <= v) ++s;
     const int local = v - t.prefix[s];
-    const int n_extra = extra_tiles(s, t.seg_rows[s], E);
+    const int n_extra = extra_tiles(s, t.seg_rows[s], g);
     mt = local / n_extra;
-    nt = local - mt * n_extra + (s < E ? 1 : 0);
+    nt = local - mt * n_extra + ((g.static_routed && s < E) ? 1 : 0);
   }
   if (s >= 0) {
-    const int e = s % E;
+    const int e = t.seg_expert[s];
     r.routed = true;
     r.w_row = (e * MT + mt) * g.k_blocks_routed * BM;
     r.x_row = t.seg_base[s] + nt * BN;
@@ -285,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   SmemTail& t = *reinterpret_cast<SmemTail*>(staging + 2 * kStaging);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_seg = 2 * g.n_experts;
+  const int n_seg = g.n_seg;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -317,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int prefetched = 0;
   if (warp == 0 && lane == 0 && (int)blockIdx.x < n_static) {
     const int u = blockIdx.x;
-    const int s0 = g.n_experts * g.m_tiles_routed;
+    const int s0 = static_routed_units(g);
     const bool routed = u < s0;
     const CUtensorMap* mw = routed ? &tm_w_routed : &tm_w_shared;
     int w_row, kbs;
@@ -346,8 +351,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       rows = g.seg_rows[s];
       t.seg_rows[s] = rows;
       t.seg_base[s] = g.seg_base[s];
+      t.seg_expert[s] = g.seg_expert != nullptr ? g.seg_expert[s] : s % g.n_experts;
     }
-    int incl = s < n_seg ? extra_tiles(s, rows, g.n_experts) * g.m_tiles_routed : 0;
+    int incl = s < n_seg ? extra_tiles(s, rows, g) * g.m_tiles_routed : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int n = __shfl_up_sync(0xffffffffu, incl, o);

@@ -59,6 +59,10 @@ struct RouteArgs {
   float* stats_out;           // [E + 1] or null
   MoeTables tab;
   int tokens, dim, n_experts, capacity;
+  // overflow segments are laid out destination-major for ep_ranks expert-
+  // parallel ranks: expert e lives on rank e % ep_ranks as local expert
+  // e / ep_ranks, so rank r's rows form one contiguous block (1: id order)
+  int ep_ranks;
   int* status;
 };
 
@@ -85,12 +89,31 @@ struct CombineArgs {
   int tokens, dim;
 };
 
+// Expert-parallel combine: the routed outputs come back in grouped-row order
+// (unweighted, bf16); each token gathers its two rows through positions.
+struct EpCombineArgs {
+  const __nv_bfloat16* y;         // [rows, d] expert outputs in grouped-row order
+  const int* indices;             // [T, 2]
+  const float* weights;           // [T, 2]
+  const int* positions;           // [2T] grouped row of each assignment
+  const __nv_bfloat16* shared_y;  // [T, d]
+  const __nv_bfloat16* residual;  // [T, d] or null
+  __nv_bfloat16* out;             // [T, d]
+  int tokens, dim, rows;
+  int* status;
+};
+
 enum GemmMode : int { kGemmSwiGLU = 0, kGemmPlain = 1 };
 
 struct GemmArgs {
-  // routed part: 2E segments (capacity, overflow) per expert
+  // routed part: n_seg segments of contiguous rows, each multiplied by one
+  // expert's weights (capacity layout: 2E segments, capacity then overflow)
   const int* seg_rows;
   const int* seg_base;
+  const int* seg_expert;  // [n_seg] expert of each segment, or null: segment s is expert s % E
+  int n_seg;
+  int static_routed;      // 1: segments e < E are capacity segments whose first token tile is
+                          // a static unit (weights streamed before the grid dependency)
   int n_experts;
   int m_tiles_routed;     // output features / 128
   int k_blocks_routed;    // K / 64
@@ -119,6 +142,7 @@ int launch_rope(__nv_bfloat16* x, const __nv_bfloat16* cos_t, const __nv_bfloat1
 int launch_route(const RouteArgs& args, cudaStream_t stream);
 int launch_group(const GroupArgs& args, cudaStream_t stream);
 int launch_combine(const CombineArgs& args, cudaStream_t stream);
+int launch_ep_combine(const EpCombineArgs& args, cudaStream_t stream);
 int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
                         const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
                         const CUtensorMap* tm_x_shared, int grid, cudaStream_t stream);

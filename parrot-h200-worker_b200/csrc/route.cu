@@ -201,7 +201,15 @@ __global__ void __launch_bounds__(32 * kRouteWarps) route_kernel(RouteArgs a) {
   if (threadIdx.x == 0) {
     const int C = a.capacity;
     const int A = 2 * T;
+    const int G = a.ep_ranks, El = E / G;
     int overflow_base = E * C;
+    for (int q = 0; q < E; ++q) {
+      const int e = (q % El) * G + q / El;  // rank q / El, local expert q % El
+      const int ov = count_s[e] > C ? count_s[e] - C : 0;
+      a.tab.seg_rows[E + e] = ov;
+      a.tab.seg_base[E + e] = overflow_base;
+      overflow_base += ov;
+    }
     float aux = 0.f;
     for (int e = 0; e < E; ++e) {
       const int c = count_s[e];
@@ -209,10 +217,6 @@ __global__ void __launch_bounds__(32 * kRouteWarps) route_kernel(RouteArgs a) {
       if (a.counts_out != nullptr) a.counts_out[e] = c;
       a.tab.seg_rows[e] = c < C ? c : C;
       a.tab.seg_base[e] = e * C;
-      const int ov = c > C ? c - C : 0;
-      a.tab.seg_rows[E + e] = ov;
-      a.tab.seg_base[E + e] = overflow_base;
-      overflow_base += ov;
       const float util = (float)c / (float)A;
       a.tab.stats[e] = util;
       if (a.stats_out != nullptr) a.stats_out[e] = util;
@@ -411,6 +415,80 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
       o[c] = float_to_bf16x8(s);
     }
   }
+}
+
+// One warp per token: gathers the token's two expert rows through positions,
+// weights them exactly as the down GEMM's scatter epilogue does
+// (bf16(bf16(y) * bf16(w))) and adds them to the shared output in ascending
+// expert order, so the result is bit-identical to the single-GPU block.
+template <int V>
+__global__ void __launch_bounds__(128) ep_combine_kernel(EpCombineArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  griddep_wait();
+  griddep_launch();
+  if (t >= a.tokens) return;
+  const int d = a.dim, nvec = d >> 3;
+  const int e0 = __ldg(a.indices + 2 * t), e1 = __ldg(a.indices + 2 * t + 1);
+  int p0 = __ldg(a.positions + 2 * t), p1 = __ldg(a.positions + 2 * t + 1);
+  if (p0 < 0 || p0 >= a.rows || p1 < 0 || p1 >= a.rows) {
+    if (lane == 0) report_status(a.status, kStatusBadIndex, 4, t);
+    return;
+  }
+  float w0 = round_bf16(__ldg(a.weights + 2 * t)), w1 = round_bf16(__ldg(a.weights + 2 * t + 1));
+  if (e1 < e0) {  // lower expert id first
+    const int tp = p0; p0 = p1; p1 = tp;
+    const float tw = w0; w0 = w1; w1 = tw;
+  }
+  const uint4* y0 = reinterpret_cast<const uint4*>(a.y + (size_t)p0 * d);
+  const uint4* y1 = reinterpret_cast<const uint4*>(a.y + (size_t)p1 * d);
+  const uint4* sh = reinterpret_cast<const uint4*>(a.shared_y + (size_t)t * d);
+  const uint4* rs = a.residual ? reinterpret_cast<const uint4*>(a.residual + (size_t)t * d) : nullptr;
+  uint4* o = reinterpret_cast<uint4*>(a.out + (size_t)t * d);
+  uint4 vs[V], v0[V], v1[V], vr[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nvec) {
+      vs[i] = __ldg(sh + c);
+      v0[i] = __ldg(y0 + c);
+      v1[i] = __ldg(y1 + c);
+      if (rs != nullptr) vr[i] = __ldg(rs + c);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nvec) {
+      float s[8], p[8], q[8];
+      bf16x8_to_float(vs[i], s);
+      bf16x8_to_float(v0[i], p);
+      bf16x8_to_float(v1[i], q);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        s[k] = round_bf16(round_bf16(s[k] + round_bf16(p[k] * w0)) + round_bf16(q[k] * w1));
+      if (rs != nullptr) {
+        float b[8];
+        bf16x8_to_float(vr[i], b);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s[k] = b[k] + s[k];
+      }
+      o[c] = float_to_bf16x8(s);
+    }
+  }
+}
+
+int launch_ep_combine(const EpCombineArgs& args, cudaStream_t stream) {
+  if (args.tokens == 0) return 0;
+  const dim3 grid((args.tokens + 3) / 4), block(128);
+  switch ((args.dim / 8 + 31) / 32) {
+    case 1: launch_pdl(ep_combine_kernel<1>, grid, block, 0, stream, args); break;
+    case 2: launch_pdl(ep_combine_kernel<2>, grid, block, 0, stream, args); break;
+    case 3: launch_pdl(ep_combine_kernel<3>, grid, block, 0, stream, args); break;
+    case 4: launch_pdl(ep_combine_kernel<4>, grid, block, 0, stream, args); break;
+    default: return -1;
+  }
+  return 0;
 }
 
 int launch_combine(const CombineArgs& args, cudaStream_t stream) {

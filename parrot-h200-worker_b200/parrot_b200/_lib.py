@@ -72,6 +72,16 @@ _SIGNATURES = {
                                      c_size_t, c_int, c_void_p]),
     "parrot_b200_launch_count": (ctypes.c_ulonglong, []),
     "parrot_moe_read_status": (c_int, [c_void_p, POINTER(MoeDims), POINTER(c_int), c_void_p]),
+    "parrot_moe_ep_dispatch_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
+                                            POINTER(MoeOutputs), c_int, c_void_p, c_size_t,
+                                            c_void_p]),
+    "parrot_moe_shared_ffn_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
+                                           c_void_p, c_size_t, c_void_p]),
+    "parrot_moe_expert_ffn_bf16": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                           c_void_p, c_void_p, c_void_p]),
+    "parrot_moe_ep_combine_bf16": (c_int, [POINTER(MoeDims), c_void_p, c_void_p, c_size_t,
+                                           c_void_p, c_void_p, c_void_p]),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -1,0 +1,153 @@
+"""Expert-parallel MoE on the GPU, through the C ABI.
+
+Ranks that share one GPU run as threads (the exchange is a device copy);
+with two or more GPUs one NCCL process per GPU runs the same orchestration.
+Each rank's output must equal the single-device MoE block on that rank's
+tokens bit for bit, and the packed grouping mode must equal the capacity
+layout bit for bit.
+"""
+import ctypes
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from parrot_b200 import _lib, bridge, ep
+from parrot_b200.workloads import tune_zipf_router_bias
+from tests.ep_support import ThreadComm, ThreadGroup, run_threads
+from tests.gpu_helpers import build_moe_pair, hidden_states, moe_config
+
+pytestmark = pytest.mark.gpu
+
+
+def zipf_module(seed: int, tokens: int):
+    cfg = moe_config()
+    module, oracle = build_moe_pair(cfg, seed=seed)
+    x = hidden_states(tokens, cfg.dim, seed=seed + 100)
+    bias = tune_zipf_router_bias(x.float(), oracle.router.weight)
+    module.router_bias = bias.cuda()
+    return module, x.cuda()
+
+
+def shard_sizes(total: int, ranks: int) -> list[int]:
+    gen = torch.Generator().manual_seed(total + ranks)
+    inner = sorted(int(v) for v in torch.randint(0, total + 1, (ranks - 1,), generator=gen))
+    cuts = [0] + inner + [total]
+    sizes = [b - a for a, b in zip(cuts, cuts[1:])]
+    if ranks >= 4:
+        sizes[-2] += sizes[-1]
+        sizes[-1] = 0
+    return sizes
+
+
+def _forward_packed(module, x, capacity):
+    cfg = module.cfg
+    dims = bridge.moe_dims(cfg, x.shape[0], capacity=capacity)
+    lay = bridge.workspace_layout(dims)
+    ws = torch.zeros(int(lay.total), device="cuda", dtype=torch.uint8)
+    out = torch.empty_like(x)
+    outputs = _lib.MoeOutputs(out.data_ptr(), None, None, None, None, None, None, None)
+    w = bridge._weights_struct(bridge.pack_weights(module), bridge._router_bias(module))
+    _lib.check(_lib.load().parrot_moe_forward_bf16(
+        ctypes.byref(dims), ctypes.byref(w), bridge._p(x), ctypes.byref(outputs), bridge._p(ws),
+        ws.numel(), bridge._stream()), "parrot_moe_forward_bf16")
+    status = (ctypes.c_int * 4)()
+    _lib.check(_lib.load().parrot_moe_read_status(bridge._p(ws), ctypes.byref(dims), status,
+                                                  bridge._stream()), "read status")
+    assert list(status) == [0, 0, 0, 0]
+    return out
+
+
+@pytest.mark.parametrize("tokens,zipf", [(512, False), (2048, True), (37, False)])
+def test_packed_grouping_equals_capacity_layout(tokens, zipf):
+    with torch.inference_mode():
+        if zipf:
+            module, x = zipf_module(seed=8, tokens=tokens)
+        else:
+            cfg = moe_config()
+            module, _ = build_moe_pair(cfg, seed=8)
+            x = hidden_states(tokens, cfg.dim, seed=9).cuda()
+        want = _forward_packed(module, x, 0)
+        got = _forward_packed(module, x, -1)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+
+
+def _ep_threads(module, x, ranks, residual):
+    sizes = shard_sizes(x.shape[0], ranks)
+    starts = [sum(sizes[:r]) for r in range(ranks)]
+    group = ThreadGroup(ranks)
+    ops = [ep.B200EpOps(module, r, ranks) for r in range(ranks)]
+
+    def rank_fn(r):
+        xs = x[starts[r]:starts[r] + sizes[r]]
+        rs = residual[starts[r]:starts[r] + sizes[r]]
+        layer = ep.ExpertParallelMoE(ops[r], ThreadComm(group, r), module.cfg.n_experts)
+        with torch.inference_mode():
+            return layer(xs, rs), layer.last_recv_rows
+
+    results = run_threads(group, rank_fn)
+    torch.cuda.synchronize()
+    return sizes, starts, results
+
+
+@pytest.mark.parametrize("ranks,zipf", [(2, False), (4, True), (8, True), (16, False)])
+def test_expert_parallel_threads_equal_single_device_block(ranks, zipf):
+    tokens = 3000
+    with torch.inference_mode():
+        if zipf:
+            module, x = zipf_module(seed=12, tokens=tokens)
+        else:
+            cfg = moe_config()
+            module, _ = build_moe_pair(cfg, seed=12)
+            x = hidden_states(tokens, cfg.dim, seed=13).cuda()
+        residual = hidden_states(tokens, module.cfg.dim, seed=14).cuda()
+        sizes, starts, results = _ep_threads(module, x, ranks, residual)
+        assert sum(n for _, n in results) == 2 * tokens
+        for r in range(ranks):
+            xs = x[starts[r]:starts[r] + sizes[r]]
+            if sizes[r] == 0:
+                assert results[r][0].shape[0] == 0
+                continue
+            want, _, _ = bridge.b200_moe(module, xs, False,
+                                         residual[starts[r]:starts[r] + sizes[r]])
+            torch.cuda.synchronize()
+            assert torch.equal(results[r][0], want), f"rank {r}"
+
+
+def _nccl_rank(rank, ranks, port, seed, tokens):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=ranks,
+                            device_id=torch.device("cuda", rank))
+    try:
+        with torch.inference_mode():
+            module, x = zipf_module(seed=seed, tokens=tokens)
+            sizes = shard_sizes(tokens, ranks)
+            start = sum(sizes[:rank])
+            xs = x[start:start + sizes[rank]]
+            layer = ep.ExpertParallelMoE(ep.B200EpOps(module, rank, ranks), ep.TorchComm(),
+                                         module.cfg.n_experts)
+            got = layer(xs)
+            want, _, _ = bridge.b200_moe(module, xs, False) if sizes[rank] else (got, 0, 0)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), f"rank {rank}"
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_expert_parallel_over_nccl_equals_single_device_block():
+    ranks = min(torch.cuda.device_count(), 8)
+    mp.spawn(_nccl_rank, args=(ranks, _free_port(), 21, 4096), nprocs=ranks, join=True)
