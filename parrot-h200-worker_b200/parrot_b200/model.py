@@ -22,8 +22,14 @@ from typing import Literal
 import torch
 from torch import Tensor, nn
 from torch.nn import functional as F
+from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from . import bridge
+
+# Decode attends over a key length that grows by one every step.  The cuDNN
+# SDPA backend builds an execution plan per new shape, so decode keeps to the
+# shape-generic backends.
+_DECODE_SDPA = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
 
 _ROPE: dict[tuple, tuple[Tensor, Tensor]] = {}
 _WINDOW_MASKS: dict[tuple, list[Tensor]] = {}
@@ -245,8 +251,10 @@ class LocalGQA(nn.Module):
         cache.key[:, :, position:position + 1].copy_(k)
         cache.value[:, :, position:position + 1].copy_(v)
         lo = max(0, position - self.cfg.window_size + 1)
-        y = F.scaled_dot_product_attention(q, cache.key[:, :, lo:position + 1],
-                                           cache.value[:, :, lo:position + 1], enable_gqa=True)
+        with sdpa_kernel(_DECODE_SDPA):
+            y = F.scaled_dot_product_attention(q, cache.key[:, :, lo:position + 1],
+                                               cache.value[:, :, lo:position + 1],
+                                               enable_gqa=True)
         out = self.out(y.transpose(1, 2).reshape(x.shape[0], 1, -1))
         return out if addend is None else addend + out
 
@@ -313,7 +321,8 @@ class GlobalMLA(nn.Module):
         q = F.linear(x.float(), aq.float()).view(b, 1, c.n_heads, c.kv_latent_dim).transpose(1, 2)
         # the absorbed query is fp32 (model.py:420); attend over the latents in fp32 too
         kv = seen[:, None].expand(-1, c.n_heads, -1, -1).float()
-        ctx = F.scaled_dot_product_attention(q, kv, kv, scale=c.head_dim ** -0.5)
+        with sdpa_kernel(_DECODE_SDPA):
+            ctx = F.scaled_dot_product_attention(q, kv, kv, scale=c.head_dim ** -0.5)
         ctx = ctx.transpose(1, 2).reshape(b, 1, c.n_heads * c.kv_latent_dim)
         out = F.linear(ctx, ao.float()).to(x.dtype)
         return out if addend is None else addend + out

@@ -44,24 +44,30 @@ def make_hidden_states(tokens: int, dim: int, seed: int) -> Tensor:
 
 
 def tune_zipf_router_bias(x: Tensor, router_weight: Tensor,
-                          target=ZIPF_16, iterations: int = 40) -> Tensor:
+                          target=ZIPF_16, iterations: int = 300) -> Tensor:
     """Per-expert router logit offsets whose top-2 assignment shares follow ``target``.
 
     The reference router has no bias (``parrot/model.py:467``).  The skewed
     stress workload adds a harness-only offset ``b[e]`` to the fp32 router
     logits before the softmax, identically on every path.  The offsets are
-    fitted by fixed-point iteration ``b += log(target / achieved)`` on the
-    given sample, so the same (x, weights) always gives the same bias.
+    fitted on the given sample by damped fixed-point steps
+    ``b += clamp(log(target / achieved) / 2, -s, s)`` with a shrinking step
+    limit ``s`` (undamped steps oscillate: a share of 0 makes the log step
+    huge).  Deterministic: the same (x, weights) always gives the same bias.
+    The top-2 of the logits equals the top-2 of the softmax, so the fit
+    works on logits.
     """
     logits = (x.float() @ router_weight.float().t()).double()
     target_t = torch.tensor(target, dtype=torch.float64)
     target_t = target_t / target_t.sum()
     bias = torch.log(target_t)
     n = logits.shape[1]
-    for _ in range(iterations):
-        idx = (logits + bias).softmax(-1).topk(2, dim=-1).indices
+    for it in range(iterations):
+        idx = (logits + bias).topk(2, dim=-1).indices
         share = torch.bincount(idx.flatten(), minlength=n).double() / idx.numel()
-        bias = bias + 0.7 * torch.log(target_t.clamp_min(1e-9) / share.clamp_min(1e-6))
+        limit = 0.25 * 0.985 ** it
+        step = 0.5 * torch.log(target_t.clamp_min(1e-9) / share.clamp_min(1e-4))
+        bias = bias + step.clamp(-limit, limit)
         bias = bias - bias.max()
     return bias.float()
 
