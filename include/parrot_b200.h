@@ -126,14 +126,19 @@ typedef struct parrot_moe_outputs {
 
 /* Byte offsets of the buffers inside one MoE workspace (for inspection). */
 typedef struct parrot_moe_layout {
-  size_t indices, weights, positions, block_hist, block_prefix, block_probsum;
-  size_t counts, seg_rows, seg_base, done_counter, stats, status;
+  size_t indices, weights, positions;
+  size_t chunk_hist;      /* [ceil(T/32), E] int32 expert histogram per 32-token chunk */
+  size_t tile_hist;       /* [ceil(T/128), E] int32 per 128-token router tile */
+  size_t tile_probsum;    /* [ceil(T/128), E] f32 router probability sums per tile */
+  size_t counts, seg_rows, seg_base, stats, status;
   size_t row_dst, row_w;  /* per grouped row: token-major slot, route weight */
   size_t grouped;         /* [E*C + 2T, d] token rows grouped by expert */
   size_t hidden;          /* [E*C + 2T, H] SwiGLU hidden, same row order */
   size_t contrib;         /* [2T, d] bf16(bf16(y) * bf16(w)), slot 2t + (lower expert id first) */
   size_t shared_hidden, shared_y, total;
-  int capacity, grouped_rows, route_blocks, reserved;
+  int capacity, grouped_rows;
+  int route_blocks;       /* router CTAs: ceil(T / 128) */
+  int reserved;
 } parrot_moe_layout;
 
 /* Default capacity: max(8, ceil8(ceil(2 * 2T / E))), metal_moe.py:388-391. */
@@ -142,7 +147,7 @@ int parrot_moe_capacity(int tokens, int n_experts);
 /* Fills `layout`; returns PARROT_EINVAL for unsupported dims. */
 int parrot_moe_workspace_layout(const parrot_moe_dims* dims, parrot_moe_layout* layout);
 
-/* Zeroes the control words of a fresh workspace (call once after allocating;
+/* Zeroes the status word of a fresh workspace (call once after allocating;
  * a zero-filled allocation needs no call).  Enqueued on `stream`. */
 int parrot_moe_workspace_init(void* workspace, const parrot_moe_dims* dims, void* stream);
 

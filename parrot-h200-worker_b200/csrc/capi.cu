@@ -149,8 +149,8 @@ int layout_of(const parrot_moe_dims* d, parrot_moe_layout* L) {
                 : d->capacity == 0 ? parrot_moe_capacity(d->tokens, d->n_experts)
                                    : 0;
   const size_t A = 2 * T;
-  const size_t nb = (size_t)parrot::route_blocks(d->tokens);
-  const size_t ng = (size_t)parrot::group_blocks(d->tokens);
+  const size_t n_tiles = (size_t)parrot::route_blocks(d->tokens);
+  const size_t n_chunks = (size_t)parrot::group_blocks(d->tokens);
   const size_t R = E * (size_t)C + A;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -158,15 +158,14 @@ int layout_of(const parrot_moe_dims* d, parrot_moe_layout* L) {
     off = align256(off + bytes);
     return at;
   };
-  // control words first: one region zeroed by parrot_moe_workspace_init
-  L->done_counter = take(16);
+  // the status word first: the region parrot_moe_workspace_init zeroes
   L->status = take(16);
   L->indices = take(A * 4);
   L->weights = take(A * 4);
   L->positions = take(A * 4);
-  L->block_hist = take(nb * E * 4);
-  L->block_prefix = take(ng * E * 4);
-  L->block_probsum = take(nb * E * 4);
+  L->chunk_hist = take(n_chunks * E * 4);
+  L->tile_hist = take(n_tiles * E * 4);
+  L->tile_probsum = take(n_tiles * E * 4);
   L->counts = take(E * 4);
   L->seg_rows = take(2 * E * 4);
   L->seg_base = take(2 * E * 4);
@@ -181,7 +180,7 @@ int layout_of(const parrot_moe_dims* d, parrot_moe_layout* L) {
   L->total = off;
   L->capacity = C;
   L->grouped_rows = (int)R;
-  L->route_blocks = (int)nb;
+  L->route_blocks = (int)n_tiles;
   return PARROT_OK;
 }
 
@@ -202,13 +201,12 @@ int check_weights(const parrot_moe_weights* w) {
 
 parrot::MoeTables tables(void* ws, const parrot_moe_layout& L) {
   parrot::MoeTables t;
-  t.block_prefix = at<int>(ws, L.block_prefix);
-  t.block_hist = at<int>(ws, L.block_hist);
-  t.block_probsum = at<float>(ws, L.block_probsum);
+  t.chunk_hist = at<int>(ws, L.chunk_hist);
+  t.tile_hist = at<int>(ws, L.tile_hist);
+  t.tile_probsum = at<float>(ws, L.tile_probsum);
   t.counts = at<int>(ws, L.counts);
   t.seg_rows = at<int>(ws, L.seg_rows);
   t.seg_base = at<int>(ws, L.seg_base);
-  t.done_counter = at<int>(ws, L.done_counter);
   t.stats = at<float>(ws, L.stats);
   return t;
 }
@@ -233,24 +231,23 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
               int ep_ranks = 1) {
   const int T = dims->tokens, E = dims->n_experts;
   parrot::RouteArgs ra{};
-  ra.x = static_cast<const __nv_bfloat16*>(x);
-  ra.w = static_cast<const __nv_bfloat16*>(w->router);
   ra.bias = w->router_bias;
   ra.probs = o->probs;
   ra.indices = at<int>(ws, L.indices);
   ra.weights = at<float>(ws, L.weights);
   ra.indices64 = o->indices;
   ra.weights_out = o->weights;
-  ra.counts_out = o->counts;
-  ra.stats_out = o->stats;
   ra.tab = tables(ws, L);
   ra.tokens = T;
   ra.dim = dims->dim;
   ra.n_experts = E;
-  ra.capacity = L.capacity;
-  ra.ep_ranks = ep_ranks;
   ra.status = at<int>(ws, L.status);
-  if (parrot::launch_route(ra, s)) return fail(PARROT_ECUDA, "route: unsupported dim or smem%s");
+  CUtensorMap mx, mw;
+  if (!tensor_map(&mx, x, T, dims->dim, parrot::kRouteTile) ||
+      !tensor_map(&mw, w->router, E, dims->dim, parrot::route_experts_padded(E)))
+    return fail(PARROT_ECUDA, "route: cuTensorMapEncodeTiled failed%s");
+  if (parrot::launch_route(ra, &mx, &mw, s))
+    return fail(PARROT_ECUDA, "route: unsupported dim or shared-memory setup failed%s");
   int rc = check_launch("route_kernel");
   if (rc) return rc;
 
@@ -264,10 +261,13 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ga.row_dst = at<int>(ws, L.row_dst);
   ga.row_w = at<float>(ws, L.row_w);
   ga.grouped = at<__nv_bfloat16>(ws, L.grouped);
+  ga.counts_out = o->counts;
+  ga.stats_out = o->stats;
   ga.tokens = T;
   ga.dim = dims->dim;
   ga.n_experts = E;
   ga.capacity = L.capacity;
+  ga.ep_ranks = ep_ranks;
   const int ng = parrot::group_blocks(T);
   const int want = (2 * sm_count() + ng - 1) / ng;  // about two blocks per SM
   int split = 1;
@@ -674,8 +674,8 @@ int parrot_moe_forward_static_bf16(const parrot_moe_dims* dims,
   if ((rc = prepare(dims, weights, x, outputs, ws, kStaticWorkspaceBytes, &L))) return rc;
   if (dims->tokens == 0) return PARROT_OK;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The array keeps whatever the previous call left: the last-block ticket and
-  // the status word must start at zero, so clear the control region first.
+  // The array keeps whatever the previous call left: the status word must
+  // start at zero, so clear it first.
   if (cudaMemsetAsync(ws, 0, L.indices, s) != cudaSuccess)
     return check_launch("static workspace clear");
   if ((rc = run_route(dims, weights, x, outputs, ws, L, s))) return rc;

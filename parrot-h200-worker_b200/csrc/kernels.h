@@ -11,8 +11,9 @@ namespace parrot {
 
 constexpr int kMaxDepthSources = 16;
 constexpr int kMaxExperts = 32;
-constexpr int kRouteTokensPerBlock = 8;    // router block: histogram granularity
-constexpr int kGroupTokensPerBlock = 32;   // grouping block: 64 assignments, 4 router blocks
+constexpr int kRouteTile = 128;            // tokens per router CTA (the MMA M side)
+constexpr int kGroupTokensPerBlock = 32;   // grouping block / histogram chunk: 64 assignments
+constexpr int kChunksPerTile = kRouteTile / kGroupTokensPerBlock;  // 4
 constexpr int kGemmBlockN = 128;           // token rows per grouped-GEMM tile
 constexpr int kGemmBlockK = 64;            // 128-byte swizzled K slab
 
@@ -33,36 +34,29 @@ struct DepthMixArgs {
   int dim;
 };
 
-// Device-side MoE bookkeeping written by the router's last block and read by
-// the grouping, GEMM and combine kernels.  All int32.
+// Device-side MoE bookkeeping.  The router writes per-chunk (32 tokens) and
+// per-tile (128 tokens) expert histograms and per-tile probability sums; the
+// grouping kernel turns them into slots and writes the segment tables, counts
+// and statistics that the GEMMs and the caller read.
 struct MoeTables {
-  int* block_prefix;   // [group blocks, E] exclusive prefix of counts at each grouping block
-  int* block_hist;     // [router blocks, E]
-  float* block_probsum;  // [router blocks, E]
+  int* chunk_hist;     // [chunks, E]  assignments per expert in each 32-token chunk
+  int* tile_hist;      // [tiles, E]   the same per 128-token router tile
+  float* tile_probsum;  // [tiles, E]  sum of router probabilities per expert
   int* counts;         // [E]
   int* seg_rows;       // [2E] rows in capacity segment e, overflow segment e
   int* seg_base;       // [2E] first grouped row of each segment
-  int* done_counter;   // [1] last-block ticket (self-resetting)
   float* stats;        // [E + 1]: utilisation[E], aux
 };
 
 struct RouteArgs {
-  const __nv_bfloat16* x;     // [T, d]
-  const __nv_bfloat16* w;     // [E, d]
   const float* bias;          // [E] or null (harness-only logit offset)
   float* probs;               // [T, E] or null
   int* indices;               // [T, 2]
   float* weights;             // [T, 2]
   long long* indices64;       // [T, 2] or null (reference dtype)
   float* weights_out;         // [T, 2] or null: caller's copy of weights
-  int* counts_out;            // [E] or null
-  float* stats_out;           // [E + 1] or null
   MoeTables tab;
-  int tokens, dim, n_experts, capacity;
-  // overflow segments are laid out destination-major for ep_ranks expert-
-  // parallel ranks: expert e lives on rank e % ep_ranks as local expert
-  // e / ep_ranks, so rank r's rows form one contiguous block (1: id order)
-  int ep_ranks;
+  int tokens, dim, n_experts;
   int* status;
 };
 
@@ -76,7 +70,13 @@ struct GroupArgs {
   int* row_dst;               // [R] token-major contribution slot of each grouped row
   float* row_w;               // [R] route weight of each grouped row
   __nv_bfloat16* grouped;     // [E*C + 2T, d]
+  int* counts_out;            // [E] or null
+  float* stats_out;           // [E + 1] or null
   int tokens, dim, n_experts, capacity;
+  // overflow segments are laid out destination-major for ep_ranks expert-
+  // parallel ranks: expert e lives on rank e % ep_ranks as local expert
+  // e / ep_ranks, so rank r's rows form one contiguous block (1: id order)
+  int ep_ranks;
   int copy_split;
   int* status;
 };
@@ -139,7 +139,10 @@ int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream);
 int launch_rope(__nv_bfloat16* x, const __nv_bfloat16* cos_t, const __nv_bfloat16* sin_t,
                 int rows, int row_stride, int rot_cols, int head_dim, int seq_len, int start,
                 cudaStream_t stream);
-int launch_route(const RouteArgs& args, cudaStream_t stream);
+// x_map: [T, d] bf16, box 128 rows x 64; w_map: [E, d] bf16, box
+// route_experts_padded(E) rows x 64 (rows past E read as zero).
+int launch_route(const RouteArgs& args, const CUtensorMap* x_map, const CUtensorMap* w_map,
+                 cudaStream_t stream);
 int launch_group(const GroupArgs& args, cudaStream_t stream);
 int launch_combine(const CombineArgs& args, cudaStream_t stream);
 int launch_ep_combine(const EpCombineArgs& args, cudaStream_t stream);
@@ -152,10 +155,13 @@ int launch_pack_tiles(__nv_bfloat16* dst, const __nv_bfloat16* src, int n_mats, 
                       int cols, cudaStream_t stream);
 size_t grouped_gemm_smem_bytes();
 
-inline int route_blocks(int tokens) {
-  return (tokens + kRouteTokensPerBlock - 1) / kRouteTokensPerBlock;
+__host__ __device__ inline int route_blocks(int tokens) {
+  return (tokens + kRouteTile - 1) / kRouteTile;
 }
-inline int group_blocks(int tokens) {
+__host__ __device__ inline int route_experts_padded(int n_experts) {
+  return n_experts <= 16 ? 16 : 32;
+}
+__host__ __device__ inline int group_blocks(int tokens) {
   return (tokens + kGroupTokensPerBlock - 1) / kGroupTokensPerBlock;
 }
 

@@ -1,293 +1,291 @@
 // Router (N1) and deterministic capacity grouping (N2).
 //
-// route_kernel:  fp32 router logits + softmax + top-2 + renormalised weights,
-//                one warp per two tokens from shared-memory staged inputs,
-//                lane-parallel over experts.
-//                Each block also counts its assignments per expert and sums
-//                its probabilities per expert; the last block to finish (a
-//                ticket counter, no spinning) turns those into exclusive
-//                per-block prefixes, segment tables and router statistics.
-// group_kernel:  ranks each assignment inside its block with warp match,
-//                adds the block prefix -> a stable slot (ascending token order
-//                within each expert, the reference's torch.where order), maps
-//                slot -> grouped row (capacity region, else the overflow
-//                region), and copies the token rows with 16-byte vectors.
+// route_kernel:  one CTA per 128 tokens.  The router logits are a skinny GEMM
+//                [128 x d] x [d x E]: TMA streams 64-column slabs of the token
+//                tile and of the router weight through a shared-memory ring,
+//                one thread issues tcgen05.mma (M = 128 tokens, N = E rounded
+//                up to 16/32, fp32 accumulator in TMEM).  Each of the 128
+//                threads then reads its token's E logits from TMEM with one
+//                tcgen05.ld and does the softmax, top-2 and renormalisation
+//                in registers (no cross-lane reductions).  Each warp (32
+//                tokens) records its expert histogram; the CTA records its
+//                tile histogram and probability sums.
+// group_kernel:  every block derives its exclusive per-expert prefix from the
+//                tile and chunk histograms (no serial pass, no spinning),
+//                ranks each assignment inside its block with warp match -> a
+//                stable slot (ascending token order within each expert, the
+//                reference's torch.where order), maps slot -> grouped row
+//                (capacity region, else the overflow region), and copies the
+//                token rows with 16-byte vectors.  Block 0 also writes the
+//                segment tables, counts and router statistics.
 #include "common.cuh"
 #include "kernels.h"
+#include "tc.cuh"
 
 namespace parrot {
 
-constexpr int kRouteWarps = 4;
-constexpr int kTokensPerWarp = kRouteTokensPerBlock / kRouteWarps;  // 2
-constexpr int kRouteBlocksPerGroup = kGroupTokensPerBlock / kRouteTokensPerBlock;  // 4
+using namespace tc;
 
-// One warp routes kTokensPerWarp tokens.  The block first stages the router
-// weight [E, d] and its 32 token rows in shared memory with 16-byte async
-// copies (every load in flight at once), then lanes split d and accumulate
-// all E partial dot products, reduced together (warp_reduce_many); after that
-// lane l owns expert l % EP for the softmax and the top-2 search.
-template <int V, int EP>
-__global__ void __launch_bounds__(32 * kRouteWarps) route_kernel(RouteArgs a) {
-  extern __shared__ __align__(16) unsigned char route_smem[];
-  __shared__ int hist_s[kMaxExperts];
-  __shared__ float psum_s[kRouteWarps][kMaxExperts];
-  __shared__ int last_s;
+constexpr int kRouteStages = 6;
+constexpr int kRouteXTile = kRouteTile * 64 * 2;  // 16 KB slab of 128 tokens x 64 columns
 
-  const int E = a.n_experts, d = a.dim, T = a.tokens;
-  const int nvec = d >> 3;
+struct __align__(8) RouteSmem {
+  uint64_t full[kRouteStages];
+  uint64_t empty[kRouteStages];
+  uint64_t done;
+  uint32_t tmem;
+  int abort;
+  int hist[4][kMaxExperts];
+  float psum[4][kMaxExperts];
+};
+
+template <int NP>
+constexpr size_t route_smem_bytes() {
+  return 1024 + (size_t)kRouteStages * (kRouteXTile + NP * 128) + sizeof(RouteSmem);
+}
+
+template <int NP>
+__global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUtensorMap x_map,
+                                                    const __grid_constant__ CUtensorMap w_map,
+                                                    RouteArgs a) {
+  constexpr int kWTile = NP * 128;  // NP experts x 64 columns
+  extern __shared__ unsigned char route_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(route_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* x_tiles = base;
+  unsigned char* w_tiles = base + kRouteStages * kRouteXTile;
+  RouteSmem& sm = *reinterpret_cast<RouteSmem*>(w_tiles + kRouteStages * kWTile);
+
+  const int E = a.n_experts, T = a.tokens;
+  const int kb_count = a.dim / 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int blk = blockIdx.x;
-  uint4* w_s = reinterpret_cast<uint4*>(route_smem);            // [E][nvec]
-  uint4* x_s = w_s + (size_t)E * nvec;                          // [32][nvec]
+  const int tile = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRouteStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    mbar_init(&sm.done, 1);
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  (&sm.hist[0][0])[threadIdx.x] = 0;
+  if (warp == 1) tmem_alloc(&sm.tmem, 32);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  volatile int* abort_flag = &sm.abort;
+
+  // the router weight is a parameter: its slabs stream in before the
+  // upstream kernel (which writes x) has finished
+  const int pre = min(kRouteStages, kb_count);
+  if (threadIdx.x == 0) {
+    for (int kb = 0; kb < pre; ++kb) {
+      mbar_arrive_expect_tx(&sm.full[kb], kRouteXTile + kWTile);
+      tma_load_2d(w_tiles + kb * kWTile, &w_map, kb * 64, 0, &sm.full[kb]);
+    }
+  }
+  griddep_wait();
+  griddep_launch();
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      bool issued[kRouteStages] = {};
+      uint32_t issued_phase[kRouteStages] = {};
+      for (int kb = 0; kb < pre; ++kb) {
+        tma_load_2d(x_tiles + kb * kRouteXTile, &x_map, kb * 64, tile * kRouteTile, &sm.full[kb]);
+        issued[kb] = true;
+      }
+      for (int kb = pre; kb < kb_count; ++kb) {
+        const int stage = kb % kRouteStages;
+        const uint32_t phase = (uint32_t)(kb / kRouteStages) & 1u;
+        if (!mbar_wait(&sm.empty[stage], phase ^ 1u, abort_flag, a.status, 20)) break;
+        mbar_arrive_expect_tx(&sm.full[stage], kRouteXTile + kWTile);
+        tma_load_2d(w_tiles + stage * kWTile, &w_map, kb * 64, 0, &sm.full[stage]);
+        tma_load_2d(x_tiles + stage * kRouteXTile, &x_map, kb * 64, tile * kRouteTile,
+                    &sm.full[stage]);
+        issued[stage] = true;
+        issued_phase[stage] = phase;
+      }
+      // every issued copy has landed before the CTA can exit
+      for (int s = 0; s < kRouteStages; ++s)
+        if (issued[s]) mbar_drain(&sm.full[s], issued_phase[s]);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(kRouteTile, NP);
+      for (int kb = 0; kb < kb_count; ++kb) {
+        const int stage = kb % kRouteStages;
+        const uint32_t phase = (uint32_t)(kb / kRouteStages) & 1u;
+        if (!mbar_wait(&sm.full[stage], phase, abort_flag, a.status, 21)) break;
+        tc_fence_after();
+        const uint64_t da = sw128_desc(x_tiles + stage * kRouteXTile);
+        const uint64_t db = sw128_desc(w_tiles + stage * kWTile);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mma_bf16(sm.tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+        mma_commit(&sm.empty[stage]);
+      }
+      mma_commit(&sm.done);  // also fires when the loop stopped early: in-flight MMAs drain
+    }
+    __syncwarp();
+  }
+
+  // ---------------- epilogue: one thread per token ----------------
+  mbar_wait(&sm.done, 0, abort_flag, a.status, 22);
+  __syncwarp();
+  tc_fence_after();
+  const bool ok = *abort_flag == 0;
+  float p[NP];
+  const int t = tile * kRouteTile + (int)threadIdx.x;
+  const bool valid_tok = ok && t < T;
   {
-    // the router weight is a parameter: fetch it before the upstream kernel ends
-    const uint4* wg = reinterpret_cast<const uint4*>(a.w);
-    for (int i = threadIdx.x; i < E * nvec; i += blockDim.x) cp_async16(w_s + i, wg + i);
-    griddep_wait();
-    griddep_launch();
-    const int first = blk * kRouteTokensPerBlock;
-    const int rows = min(kRouteTokensPerBlock, T - first);
-    const uint4* xg = reinterpret_cast<const uint4*>(a.x + (size_t)first * d);
-    for (int i = threadIdx.x; i < rows * nvec; i += blockDim.x) cp_async16(x_s + i, xg + i);
-    if (threadIdx.x < kMaxExperts) hist_s[threadIdx.x] = 0;
-    cp_async_wait_all();
-  }
-  __syncthreads();
-
-  const int t0 = blk * kRouteTokensPerBlock + warp * kTokensPerWarp;
-  float xf[kTokensPerWarp][V][8];
-#pragma unroll
-  for (int j = 0; j < kTokensPerWarp; ++j)
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const int c = lane + 32 * i;
-      if (t0 + j < T && c < nvec)
-        bf16x8_to_float(x_s[(warp * kTokensPerWarp + j) * nvec + c], xf[j][i]);
-      else
-#pragma unroll
-        for (int k = 0; k < 8; ++k) xf[j][i][k] = 0.f;
+    uint32_t r[NP];
+    const uint32_t addr = sm.tmem + ((uint32_t)(warp * 32) << 16);
+    if constexpr (NP == 16) {
+      tmem_ld16(addr, r);
+    } else {
+      uint32_t (&r32)[32] = reinterpret_cast<uint32_t (&)[32]>(r);
+      tmem_ld32(addr, r32);
     }
-  float part[kTokensPerWarp][EP];
+    float m = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < kTokensPerWarp; ++j)
+    for (int e = 0; e < NP; ++e) {
+      float l = __uint_as_float(r[e]);
+      if (e < E && a.bias != nullptr) l += __ldg(a.bias + e);
+      p[e] = e < E ? l : -INFINITY;
+      m = fmaxf(m, p[e]);
+    }
+    float den = 0.f;
 #pragma unroll
-    for (int e = 0; e < EP; ++e) part[j][e] = 0.f;
+    for (int e = 0; e < NP; ++e) {
+      p[e] = e < E ? expf(p[e] - m) : 0.f;
+      den += p[e];
+    }
 #pragma unroll
-  for (int e = 0; e < EP; ++e) {
-    if (e < E) {
+    for (int e = 0; e < NP; ++e) p[e] = valid_tok ? p[e] / den : 0.f;
+  }
+  if (valid_tok) {
+    // top-2; equal probabilities resolve to the lower expert id
+    int i1 = 0;
+    float v1 = p[0];
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
-        const int c = lane + 32 * i;
-        if (c < nvec) {
-          float wf[8];
-          bf16x8_to_float(w_s[e * nvec + c], wf);
-#pragma unroll
-          for (int j = 0; j < kTokensPerWarp; ++j)
-#pragma unroll
-            for (int k = 0; k < 8; ++k) part[j][e] = fmaf(xf[j][i][k], wf[k], part[j][e]);
-        }
+    for (int e = 1; e < NP; ++e)
+      if (e < E && p[e] > v1) {
+        v1 = p[e];
+        i1 = e;
       }
-    }
-  }
-
-  const int my_e = lane & (EP - 1);
-  const bool valid = my_e < E;
-  float psum_lane = 0.f;
+    int i2 = -1;
+    float v2 = -1.f;  // every probability is >= 0
 #pragma unroll
-  for (int j = 0; j < kTokensPerWarp; ++j) {
-    const int t = t0 + j;
-    float logit = warp_reduce_many<EP>(part[j], lane);
-    if (t >= T) continue;  // warp-uniform
-    if (a.bias != nullptr && valid) logit += __ldg(a.bias + my_e);
-    const float m = warp_max(valid ? logit : -INFINITY);
-    const float ex = valid ? expf(logit - m) : 0.f;
-    const float den = warp_sum(lane < EP ? ex : 0.f);
-    const float p = ex / den;
-    // top-2 on the probabilities; equal values resolve to the lower expert id
-    float v1 = valid ? p : -1.f;
-    int i1 = my_e;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, v1, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, i1, o);
-      if (ov > v1 || (ov == v1 && oi < i1)) { v1 = ov; i1 = oi; }
-    }
-    float v2 = (valid && my_e != i1) ? p : -1.f;
-    int i2 = my_e;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, v2, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, i2, o);
-      if (ov > v2 || (ov == v2 && oi < i2)) { v2 = ov; i2 = oi; }
-    }
-    if (lane < E) {
-      psum_lane += p;
-      if (a.probs != nullptr) a.probs[(size_t)t * E + lane] = p;
-    }
-    if (lane == 0) {
-      const float sel = v1 + v2;
-      a.indices[2 * t] = i1;
-      a.indices[2 * t + 1] = i2;
-      a.weights[2 * t] = v1 / sel;
-      a.weights[2 * t + 1] = v2 / sel;
-      if (a.weights_out != nullptr) {
-        a.weights_out[2 * t] = v1 / sel;
-        a.weights_out[2 * t + 1] = v2 / sel;
+    for (int e = 0; e < NP; ++e)
+      if (e < E && e != i1 && p[e] > v2) {
+        v2 = p[e];
+        i2 = e;
       }
-      if (a.indices64 != nullptr) {
-        a.indices64[2 * t] = i1;
-        a.indices64[2 * t + 1] = i2;
-      }
-      atomicAdd(&hist_s[i1], 1);
-      atomicAdd(&hist_s[i2], 1);
+    const float sel = v1 + v2;
+    const float w1 = v1 / sel, w2 = v2 / sel;
+    reinterpret_cast<int2*>(a.indices)[t] = make_int2(i1, i2);
+    reinterpret_cast<float2*>(a.weights)[t] = make_float2(w1, w2);
+    if (a.weights_out != nullptr) reinterpret_cast<float2*>(a.weights_out)[t] = make_float2(w1, w2);
+    if (a.indices64 != nullptr) {
+      a.indices64[2 * t] = i1;
+      a.indices64[2 * t + 1] = i2;
     }
-  }
-  psum_s[warp][lane] = psum_lane;
-  __syncthreads();
-  if (threadIdx.x < E) {
-    float s = 0.f;
-    for (int w = 0; w < kRouteWarps; ++w) s += psum_s[w][threadIdx.x];
-    a.tab.block_hist[blk * E + threadIdx.x] = hist_s[threadIdx.x];
-    a.tab.block_probsum[blk * E + threadIdx.x] = s;
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int ticket = atomicAdd(a.tab.done_counter, 1);
-    last_s = (ticket == (int)gridDim.x - 1);
-  }
-  __syncthreads();
-  if (!last_s) return;
-  __threadfence();
-
-  // ---- last block: one warp per expert builds the exclusive prefix over
-  // grouping blocks (each the sum of 4 router blocks; warp scan, 32 grouping
-  // blocks per step) and the probability column sum (lane partials in block
-  // order, then a fixed-order tree: deterministic).
-  const int nb = gridDim.x;
-  const int ng = (nb + kRouteBlocksPerGroup - 1) / kRouteBlocksPerGroup;
-  __shared__ int count_s[kMaxExperts];
-  __shared__ float psum_e[kMaxExperts];
-  for (int e = warp; e < E; e += kRouteWarps) {
-    int carry = 0;
-    float ps = 0.f;
-    for (int base = 0; base < ng; base += 32) {
-      const int gb = base + lane;
-      int v = 0;
+    if (a.probs != nullptr) {
 #pragma unroll
-      for (int r = 0; r < kRouteBlocksPerGroup; ++r) {
-        const int b = gb * kRouteBlocksPerGroup + r;
-        if (gb < ng && b < nb) {
-          v += __ldcg(a.tab.block_hist + b * E + e);
-          ps += __ldcg(a.tab.block_probsum + b * E + e);
-        }
-      }
-      int incl = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += n;
-      }
-      if (gb < ng) a.tab.block_prefix[gb * E + e] = carry + incl - v;
-      carry += __shfl_sync(0xffffffffu, incl, 31);
+      for (int e = 0; e < NP; ++e)
+        if (e < E) a.probs[(size_t)t * E + e] = p[e];
     }
-    ps = warp_sum(ps);
-    if (lane == 0) {
-      count_s[e] = carry;
-      psum_e[e] = ps;
+    atomicAdd(&sm.hist[warp][i1], 1);
+    atomicAdd(&sm.hist[warp][i2], 1);
+  }
+  // per-warp probability sums in a fixed shuffle order (deterministic)
+  const float ps = warp_reduce_many<NP>(p, lane);
+  if (lane < E) sm.psum[warp][lane] = ps;
+  __syncthreads();
+  if (ok) {
+    const int chunk0 = tile * kChunksPerTile;
+    const int n_chunks = (T + kGroupTokensPerBlock - 1) / kGroupTokensPerBlock;
+    if (lane < E && chunk0 + warp < n_chunks)
+      a.tab.chunk_hist[(size_t)(chunk0 + warp) * E + lane] = sm.hist[warp][lane];
+    if (threadIdx.x < E) {
+      const int e = threadIdx.x;
+      a.tab.tile_hist[(size_t)tile * E + e] =
+          sm.hist[0][e] + sm.hist[1][e] + sm.hist[2][e] + sm.hist[3][e];
+      a.tab.tile_probsum[(size_t)tile * E + e] =
+          ((sm.psum[0][e] + sm.psum[1][e]) + sm.psum[2][e]) + sm.psum[3][e];
     }
   }
+  tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int C = a.capacity;
-    const int A = 2 * T;
-    const int G = a.ep_ranks, El = E / G;
-    int overflow_base = E * C;
-    for (int q = 0; q < E; ++q) {
-      const int e = (q % El) * G + q / El;  // rank q / El, local expert q % El
-      const int ov = count_s[e] > C ? count_s[e] - C : 0;
-      a.tab.seg_rows[E + e] = ov;
-      a.tab.seg_base[E + e] = overflow_base;
-      overflow_base += ov;
-    }
-    float aux = 0.f;
-    for (int e = 0; e < E; ++e) {
-      const int c = count_s[e];
-      a.tab.counts[e] = c;
-      if (a.counts_out != nullptr) a.counts_out[e] = c;
-      a.tab.seg_rows[e] = c < C ? c : C;
-      a.tab.seg_base[e] = e * C;
-      const float util = (float)c / (float)A;
-      a.tab.stats[e] = util;
-      if (a.stats_out != nullptr) a.stats_out[e] = util;
-      aux += util * (psum_e[e] / (float)T);
-    }
-    a.tab.stats[E] = (float)E * aux;
-    if (a.stats_out != nullptr) a.stats_out[E] = (float)E * aux;
-    *a.tab.done_counter = 0;  // ready for the next launch
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(sm.tmem, 32);
   }
 }
 
-template <int V, int EP>
-static int launch_route_ve(const RouteArgs& args, int nb, cudaStream_t stream) {
-  const size_t smem = (size_t)(args.n_experts + kRouteTokensPerBlock) * (args.dim / 8) * 16;
+template <int NP>
+static int launch_route_np(const RouteArgs& args, const CUtensorMap* x_map,
+                           const CUtensorMap* w_map, cudaStream_t stream) {
+  constexpr size_t smem = route_smem_bytes<NP>();
   static unsigned long long configured = 0;  // per device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
   if (!(configured & (1ull << dev))) {
-    const int max_smem = (kMaxExperts + kRouteTokensPerBlock) * (1024 / 8) * 16;
-    if (cudaFuncSetAttribute(route_kernel<V, EP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             max_smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(route_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
       return -2;
     configured |= 1ull << dev;
   }
-  return launch_pdl(route_kernel<V, EP>, dim3(nb), dim3(32 * kRouteWarps), smem, stream, args) ==
-                 cudaSuccess ? 0 : -2;
+  return launch_pdl(route_kernel<NP>, dim3(route_blocks(args.tokens)), dim3(128), smem, stream,
+                    *x_map, *w_map, args) == cudaSuccess
+             ? 0
+             : -2;
 }
 
-template <int V>
-static int launch_route_v(const RouteArgs& args, int nb, cudaStream_t stream) {
-  return args.n_experts <= 16 ? launch_route_ve<V, 16>(args, nb, stream)
-                              : launch_route_ve<V, 32>(args, nb, stream);
-}
-
-int launch_route(const RouteArgs& args, cudaStream_t stream) {
+int launch_route(const RouteArgs& args, const CUtensorMap* x_map, const CUtensorMap* w_map,
+                 cudaStream_t stream) {
   if (args.tokens == 0) return 0;
-  const int nb = route_blocks(args.tokens);
-  switch ((args.dim / 8 + 31) / 32) {
-    case 1: return launch_route_v<1>(args, nb, stream);
-    case 2: return launch_route_v<2>(args, nb, stream);
-    case 3: return launch_route_v<3>(args, nb, stream);
-    case 4: return launch_route_v<4>(args, nb, stream);
-    default: return -1;
-  }
+  if (args.dim % 64 || args.dim > 1024) return -1;
+  return route_experts_padded(args.n_experts) == 16
+             ? launch_route_np<16>(args, x_map, w_map, stream)
+             : launch_route_np<32>(args, x_map, w_map, stream);
 }
 
 // ---------------------------------------------------------------------------
 // grouping: stable slots and the 16-byte row scatter
 //
-// Block b owns assignments [64 b, 64 b + 64) (tokens [32 b, 32 b + 32)); its
-// exclusive per-expert prefix comes from the router's last block.
-// Everything independent is requested up front: the assignment expert ids,
-// this block's exclusive prefix and the overflow bases, and (async copies)
-// the token rows this split copies.  Then ranks come from warp match, and
-// every assignment's grouped row is written along with where its expert
-// output goes (token-major slot 2 t + j, j = 0 for the lower expert id of
-// the token's pair, the order the reference adds them) and its route weight.
+// Block b owns assignments [64 b, 64 b + 64) (tokens [32 b, 32 b + 32), the
+// router's chunk b).  Its exclusive per-expert prefix is the sum of the tile
+// histograms before its router tile plus the chunk histograms before it in
+// that tile; the per-expert totals (for the overflow bases) are the sum of all
+// tile histograms.  Every block computes both itself from a few KB in L2, so
+// no block waits for another.  Everything independent is requested up front:
+// the assignment expert ids and (async copies) the token rows this split
+// copies.  Then ranks come from warp match, and every assignment's grouped row
+// is written along with where its expert output goes (token-major slot
+// 2 t + j, j = 0 for the lower expert id of the token's pair, the order the
+// reference adds them) and its route weight.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
   constexpr int kAssign = 2 * kGroupTokensPerBlock;  // 64 per block
   extern __shared__ __align__(16) unsigned char group_smem[];
   __shared__ int warp_cnt[2][kMaxExperts];
   __shared__ int prefix_s[kMaxExperts];
+  __shared__ int count_s[kMaxExperts];
   __shared__ int obase_s[kMaxExperts];
   __shared__ int row_s[kAssign];
+  __shared__ int red_before[128], red_total[128];
+  __shared__ float red_psum[128];
   const int E = a.n_experts, C = a.capacity, T = a.tokens, d = a.dim;
   const int blk = blockIdx.x, split = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nvec = d >> 3;
-  griddep_wait();
-  griddep_launch();
+  const bool writer = blk == 0 && split == 0;  // writes tables, counts and statistics
 
   // this split's assignments [lo, hi) cover tokens [lo/2, hi/2) of the block
   const int per = (kAssign + a.copy_split - 1) / a.copy_split;
@@ -296,17 +294,86 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
   const int n_tok = max(0, min(T - tok_lo, (hi - lo) / 2));
   uint4* x_s = reinterpret_cast<uint4*>(group_smem);
   {
+    // the token rows are the router's input, not its output
     const uint4* xg = reinterpret_cast<const uint4*>(a.x + (size_t)tok_lo * d);
     for (int i = tid; i < n_tok * nvec; i += blockDim.x) cp_async16(x_s + i, xg + i);
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
+  griddep_wait();
+  griddep_launch();
+
   const int a_idx = blk * kAssign + tid;
   int e = -1;
   if (warp < 2 && a_idx < 2 * T) e = __ldg(a.indices + a_idx);
-  if (tid >= 64 && tid < 64 + E) prefix_s[tid - 64] = __ldg(a.tab.block_prefix + blk * E + tid - 64);
-  if (tid >= 96 && tid < 96 + E) obase_s[tid - 96] = __ldg(a.tab.seg_base + E + tid - 96);
-  if (tid < 2 * kMaxExperts) (&warp_cnt[0][0])[tid] = 0;
+  {
+    // prefix and totals: thread (phase, expert) sums every P-th tile row
+    const int P = blockDim.x / E;
+    const int n_tiles = route_blocks(T), my_tile = blk / kChunksPerTile;
+    int before = 0, total = 0;
+    float ps = 0.f;
+    if (tid < P * E) {
+      const int ex = tid % E;
+      for (int r = tid / E; r < n_tiles; r += P) {
+        const int v = __ldcg(a.tab.tile_hist + (size_t)r * E + ex);
+        total += v;
+        if (r < my_tile) before += v;
+        if (writer) ps += __ldcg(a.tab.tile_probsum + (size_t)r * E + ex);
+      }
+    }
+    red_before[tid] = before;
+    red_total[tid] = total;
+    red_psum[tid] = ps;
+    if (tid < 2 * kMaxExperts) (&warp_cnt[0][0])[tid] = 0;
+    __syncthreads();
+    if (tid < E) {
+      int b = 0, c = 0;
+      float s = 0.f;
+      for (int ph = 0; ph < P; ++ph) {
+        b += red_before[ph * E + tid];
+        c += red_total[ph * E + tid];
+        s += red_psum[ph * E + tid];
+      }
+      for (int ch = my_tile * kChunksPerTile; ch < blk; ++ch)
+        b += __ldcg(a.tab.chunk_hist + (size_t)ch * E + tid);
+      prefix_s[tid] = b;
+      count_s[tid] = c;
+      red_psum[tid] = s;  // slot tid is only read by this thread from here on
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    // overflow bases, destination-major for expert parallelism (id order when ep_ranks == 1)
+    const int G = a.ep_ranks, El = E / G;
+    int base = E * C;
+    for (int q = 0; q < E; ++q) {
+      const int ex = (q % El) * G + q / El;
+      obase_s[ex] = base;
+      base += max(count_s[ex] - C, 0);
+    }
+  }
   __syncthreads();
+  if (writer && tid < E) {
+    const int c = count_s[tid];
+    a.tab.counts[tid] = c;
+    if (a.counts_out != nullptr) a.counts_out[tid] = c;
+    a.tab.seg_rows[tid] = min(c, C);
+    a.tab.seg_base[tid] = tid * C;
+    a.tab.seg_rows[E + tid] = max(c - C, 0);
+    a.tab.seg_base[E + tid] = obase_s[tid];
+    const float util = (float)c / (float)(2 * T);
+    a.tab.stats[tid] = util;
+    if (a.stats_out != nullptr) a.stats_out[tid] = util;
+  }
+  if (writer && warp == 1) {
+    // aux = E * sum_e util_e * mean_t p_te, summed in expert order by one lane
+    if (lane == 0) {
+      float aux = 0.f;
+      for (int x = 0; x < E; ++x)
+        aux += ((float)count_s[x] / (float)(2 * T)) * (red_psum[x] / (float)T);
+      a.tab.stats[E] = (float)E * aux;
+      if (a.stats_out != nullptr) a.stats_out[E] = (float)E * aux;
+    }
+  }
 
   int rank = 0;
   if (warp < 2) {

@@ -32,8 +32,8 @@ class MoeOutputs(ctypes.Structure):
                 ("counts", c_void_p), ("stats", c_void_p)]
 
 
-LAYOUT_OFFSETS = ("indices", "weights", "positions", "block_hist", "block_prefix",
-                  "block_probsum", "counts", "seg_rows", "seg_base", "done_counter", "stats",
+LAYOUT_OFFSETS = ("indices", "weights", "positions", "chunk_hist", "tile_hist",
+                  "tile_probsum", "counts", "seg_rows", "seg_base", "stats",
                   "status", "row_dst", "row_w", "grouped", "hidden", "contrib",
                   "shared_hidden", "shared_y", "total")
 

@@ -32,9 +32,9 @@ def moe_block(tokens: int, iters: int, zipf: bool) -> None:
     w = make_moe_layer_weights(cfg.dim, cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim, 1)
     moe.load_state_dict(w)
     x = make_hidden_states(tokens, cfg.dim, 0)
-    if zipf:
-        moe.router_bias = tune_zipf_router_bias(x, w["router.weight"])
     moe = moe.to("cuda", torch.bfloat16).eval()
+    if zipf:
+        moe.router_bias = tune_zipf_router_bias(x, w["router.weight"]).to("cuda", torch.float32)
     xd = x.to("cuda", torch.bfloat16)
     with torch.inference_mode():
         for _ in range(iters):
