@@ -18,7 +18,7 @@
 #include "parrot_b200.h"
 
 using parrot::kGemmBlockK;
-using parrot::kGemmBlockN;
+using parrot::kGemmSubRows;
 
 namespace {
 
@@ -288,7 +288,7 @@ int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights*
   g.seg_base = at<int>(ws, L.seg_base);
   g.seg_expert = nullptr;
   g.n_seg = shared_only ? 0 : 2 * E;
-  g.static_routed = (L.capacity > 0 && !shared_only) ? 1 : 0;
+  g.static_routed = shared_only ? 0 : 1;
   g.n_experts = E;
   g.shared_rows = T;
   g.status = at<int>(ws, L.status);
@@ -304,16 +304,17 @@ int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights*
     g.out_shared = at<__nv_bfloat16>(ws, L.shared_hidden);
     g.ld_out_shared = Hs;
     g.mode = parrot::kGemmSwiGLU;
+    g.w_routed = shared_only ? nullptr : w->gate_up;
     // weights are tiled (parrot_pack_*): a [tiles * 128, 64] view, one box per tile
     ok = tensor_map(&msw, w->shared_gate_up, 2LL * Hs * D / kGemmBlockK, kGemmBlockK, 128) &&
-         tensor_map(&msx, x, T, D, kGemmBlockN);
+         tensor_map(&msx, x, T, D, kGemmSubRows);
     if (shared_only) {  // no routed units: the routed maps are never read
       mw = msw;
       mx = msx;
     } else {
       ok = ok &&
            tensor_map(&mw, w->gate_up, (long long)E * 2 * H * D / kGemmBlockK, kGemmBlockK, 128) &&
-           tensor_map(&mx, at<void>(ws, L.grouped), R, D, kGemmBlockN);
+           tensor_map(&mx, at<void>(ws, L.grouped), R, D, kGemmSubRows);
     }
   } else {
     g.m_tiles_routed = D / 128;
@@ -327,28 +328,29 @@ int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights*
     g.out_shared = at<__nv_bfloat16>(ws, L.shared_y);
     g.ld_out_shared = D;
     g.mode = parrot::kGemmPlain;
+    g.w_routed = shared_only ? nullptr : w->down;
     ok = tensor_map(&msw, w->shared_down, (long long)D * Hs / kGemmBlockK, kGemmBlockK, 128) &&
-         tensor_map(&msx, at<void>(ws, L.shared_hidden), T, Hs, kGemmBlockN);
+         tensor_map(&msx, at<void>(ws, L.shared_hidden), T, Hs, kGemmSubRows);
     if (shared_only) {
       mw = msw;
       mx = msx;
     } else {
       ok = ok &&
            tensor_map(&mw, w->down, (long long)E * D * H / kGemmBlockK, kGemmBlockK, 128) &&
-           tensor_map(&mx, at<void>(ws, L.hidden), R, H, kGemmBlockN);
+           tensor_map(&mx, at<void>(ws, L.hidden), R, H, kGemmSubRows);
     }
   }
   if (!ok) return fail(PARROT_ECUDA, "cuTensorMapEncodeTiled failed%s");
   const int A = 2 * T;
+  const int bn = parrot::gemm_token_tile(A);
   const long long routed_units =
-      shared_only ? 0
-                  : (long long)((A + kGemmBlockN - 1) / kGemmBlockN + 2 * E) * g.m_tiles_routed;
-  const long long shared_units = (long long)((T + kGemmBlockN - 1) / kGemmBlockN) * g.m_tiles_shared;
+      shared_only ? 0 : (long long)((A + bn - 1) / bn + 2 * E) * g.m_tiles_routed;
+  const long long shared_units = (long long)((T + bn - 1) / bn) * g.m_tiles_shared;
   long long grid = routed_units + shared_units;
   const int sms = sm_count();
   if (grid > sms) grid = sms;
   if (grid < 1) grid = 1;
-  if (parrot::launch_grouped_gemm(g, &mw, &mx, &msw, &msx, (int)grid, s))
+  if (parrot::launch_grouped_gemm(g, &mw, &mx, &msw, &msx, (int)grid, bn, s))
     return fail(PARROT_ECUDA, "grouped GEMM: could not set shared-memory size%s");
   return check_launch(swiglu ? "grouped_gemm(gate_up)" : "grouped_gemm(down)");
 }
@@ -417,7 +419,7 @@ int run_ffn(int rows, int dim, int expert_dim, int n_mats, int n_seg, const int*
       g.mode = parrot::kGemmSwiGLU;
       ok = tensor_map(&mw, gate_up, (long long)n_mats * 2 * expert_dim * dim / kGemmBlockK,
                       kGemmBlockK, 128) &&
-           tensor_map(&mx, x, rows, dim, kGemmBlockN);
+           tensor_map(&mx, x, rows, dim, kGemmSubRows);
     } else {
       g.m_tiles_routed = dim / 128;
       g.k_blocks_routed = expert_dim / kGemmBlockK;
@@ -426,14 +428,15 @@ int run_ffn(int rows, int dim, int expert_dim, int n_mats, int n_seg, const int*
       g.mode = parrot::kGemmPlain;
       ok = tensor_map(&mw, down, (long long)n_mats * dim * expert_dim / kGemmBlockK, kGemmBlockK,
                       128) &&
-           tensor_map(&mx, hidden, rows, expert_dim, kGemmBlockN);
+           tensor_map(&mx, hidden, rows, expert_dim, kGemmSubRows);
     }
     if (!ok) return fail(PARROT_ECUDA, "cuTensorMapEncodeTiled failed%s");
     // the shared maps are never read (shared_rows == 0)
-    long long grid = (long long)((rows + kGemmBlockN - 1) / kGemmBlockN + n_seg) * g.m_tiles_routed;
+    const int bn = parrot::gemm_token_tile(rows);
+    long long grid = (long long)((rows + bn - 1) / bn + n_seg) * g.m_tiles_routed;
     if (grid > sms) grid = sms;
     if (grid < 1) grid = 1;
-    if (parrot::launch_grouped_gemm(g, &mw, &mx, &mw, &mx, (int)grid, s))
+    if (parrot::launch_grouped_gemm(g, &mw, &mx, &mw, &mx, (int)grid, bn, s))
       return fail(PARROT_ECUDA, "grouped GEMM: could not set shared-memory size%s");
     const int rc = check_launch(swiglu ? "grouped_gemm(ffn gate_up)" : "grouped_gemm(ffn down)");
     if (rc) return rc;

@@ -6,10 +6,14 @@
 // Weights are the MMA M side ("swap-AB"): a routed expert sees a few dozen
 // to a few thousand token rows, and putting tokens on N keeps every MMA
 // at M = 128 while N shrinks to the rows actually present (multiple of 16).
+// Token tiles are up to 256 rows, loaded as 64-row boxes so a tile with few
+// rows moves few bytes; a weight tile is streamed once per 256 tokens of its
+// expert, which matters because routing is often skewed (an expert can take
+// most of a batch while others are empty).
 //
 // Roles (192 threads, one CTA per SM):
 //   warp 0      TMA producer: 128-byte-swizzled K slabs of W and X into a
-//               5-stage shared-memory ring (no multicast anywhere).
+//               4-stage shared-memory ring (no multicast anywhere).
 //   warp 1      TMEM allocator + single-thread MMA issuer; tcgen05.commit
 //               frees ring stages and publishes finished accumulators.
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, then
@@ -18,12 +22,18 @@
 //                             h = bf16(silu_lut[bf16 g] * bf16 u)
 //               plain mode:   y = bf16(acc)
 //               staged through shared memory into row-major bf16 output.
-// Two TMEM accumulators (2 x 128 columns) let the epilogue of one unit run
-// under the MMAs of the next.  Launched with programmatic dependent launch:
-// a CTA whose first unit is static streams that unit's weight slabs before
-// waiting for the kernel that produced its activations.  Every mbarrier wait is bounded; a timeout
-// records a status code, drains in-flight copies and MMAs, frees TMEM and
-// returns.
+// Two TMEM accumulators (2 x 256 columns) let the epilogue of one unit run
+// under the MMAs of the next.
+//
+// Scheduling.  With primary units enabled, CTA b < E * MT owns the first
+// token tile of expert b / MT, M tile b % MT (its "primary" unit) and, before
+// its grid-dependency wait, pulls that unit's weights into L2 — they depend
+// on nothing the upstream kernel writes.  Every other unit (further token
+// tiles, the shared expert, everything when primaries are off) is dealt
+// round-robin over the CTAs, CTAs without a primary unit (empty experts,
+// b >= E * MT) first.  Launched with programmatic dependent launch.  Every
+// mbarrier wait is bounded; a timeout records a status code, drains in-flight
+// copies and MMAs, frees TMEM and returns.
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
@@ -34,26 +44,35 @@ namespace {
 using namespace tc;
 
 constexpr int BM = 128;
-constexpr int BN = kGemmBlockN;
 constexpr int BK = kGemmBlockK;
-constexpr int kStages = 5;
-constexpr int kTileA = BM * BK * 2;
-constexpr int kTileB = BN * BK * 2;
-constexpr int kChunk = 32;                   // TMEM columns per epilogue step
-constexpr int kStaging = kChunk * BM * 2;    // 32 tokens x 128 features bf16
+constexpr int kSubRows = kGemmSubRows;        // 64-row activation boxes
+constexpr int kTileA = BM * BK * 2;           // 16 KB
+constexpr int kSubBytes = kSubRows * BK * 2;  // 8 KB
+constexpr int kChunk = 32;                    // TMEM columns per epilogue step
+constexpr int kStaging = kChunk * BM * 2;     // 32 tokens x 128 features bf16
 constexpr int kThreads = 192;
-constexpr int kTmemCols = 2 * BN;
 constexpr int kSegMax = 2 * kMaxExperts;
 
+// Token tile BN (128 or 256 rows): the ring holds 5 stages of 16 + 16 KB or
+// 4 stages of 16 + 32 KB; the two TMEM accumulators take 2 * BN columns.
+template <int BN>
+constexpr int stages_for() {
+  return BN == 256 ? 4 : 5;
+}
+
+template <int BN>
 struct __align__(8) SmemTail {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[stages_for<BN>()];
+  uint64_t empty[stages_for<BN>()];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
   int scan_carry;
+  int has_primary;      // this CTA's schedule: primary unit present,
+  int rank;             // its position in the round-robin over other units
+  int n_secondary;      // and how many such units exist
   int unit_dst[BN];     // plain-mode scatter: destination row of each token row
   float unit_w[BN];     // and its route weight
   int prefix[kSegMax + 2];
@@ -62,8 +81,11 @@ struct __align__(8) SmemTail {
   int seg_expert[kSegMax];
 };
 
-constexpr size_t kSmemBytes =
-    1024 + (size_t)kStages * (kTileA + kTileB) + 2 * kStaging + sizeof(SmemTail);
+template <int BN>
+constexpr size_t smem_bytes() {
+  return 1024 + (size_t)stages_for<BN>() * (kTileA + BN * BK * 2) + 2 * kStaging +
+         sizeof(SmemTail<BN>);
+}
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -78,70 +100,75 @@ struct Unit {
   int ld;
 };
 
-// Work units, in this order:
-//   static routed  u < E*MT:        capacity segment e = u / MT, M tile u % MT, token tile 0
-//   static shared  next SU units:   shared expert, M tile x token tile
-//   dynamic        the rest:        further token tiles of capacity segments,
-//                                   then every token tile of the overflow segments
-// The static units' weight tiles are known before the routing results exist,
-// so a CTA starts streaming them before its grid-dependency wait.
-__device__ __forceinline__ int extra_tiles(int s, int rows, const GemmArgs& g) {
+__device__ __forceinline__ bool primaries_on(const GemmArgs& g) {
+  return g.static_routed && g.n_experts * g.m_tiles_routed <= (int)gridDim.x;
+}
+
+// token tiles of segment s handed out round-robin (the primary tile excluded)
+template <int BN>
+__device__ __forceinline__ int secondary_tiles(int s, int rows, bool primary, int n_experts) {
   const int tiles = (rows + BN - 1) / BN;
-  return (g.static_routed && s < g.n_experts) ? max(tiles - 1, 0) : tiles;
+  return (primary && s < n_experts) ? max(tiles - 1, 0) : tiles;
 }
 
-__device__ __forceinline__ int static_routed_units(const GemmArgs& g) {
-  return g.static_routed ? g.n_experts * g.m_tiles_routed : 0;
-}
-
-__device__ __forceinline__ int static_units(const GemmArgs& g) {
-  const int shared_tiles = (g.shared_rows + BN - 1) / BN;
-  return static_routed_units(g) + shared_tiles * g.m_tiles_shared;
-}
-
-__device__ __forceinline__ Unit decode_unit(int u, const GemmArgs& g, const SmemTail& t) {
+template <int BN>
+__device__ __forceinline__ Unit routed_unit(const GemmArgs& g, const SmemTail<BN>& t, int s,
+                                            int mt, int nt) {
   Unit r;
-  const int E = g.n_experts, MT = g.m_tiles_routed;
-  const int feat_per_tile = g.mode == kGemmSwiGLU ? BM / 2 : BM;
-  const int s0 = static_routed_units(g);
-  const int shared_tiles = (g.shared_rows + BN - 1) / BN;
-  const int su = shared_tiles * g.m_tiles_shared;
-  int s = -1, mt = 0, nt = 0;
-  if (u < s0) {
-    s = u / MT;
-    mt = u - s * MT;
-  } else if (u >= s0 + su) {
-    const int v = u - s0 - su;
-    s = 0;
-    while (t.prefix[s + 1] <= v) ++s;
-    const int local = v - t.prefix[s];
-    const int n_extra = extra_tiles(s, t.seg_rows[s], g);
-    mt = local / n_extra;
-    nt = local - mt * n_extra + ((g.static_routed && s < E) ? 1 : 0);
-  }
-  if (s >= 0) {
-    const int e = t.seg_expert[s];
-    r.routed = true;
-    r.w_row = (e * MT + mt) * g.k_blocks_routed * BM;
-    r.x_row = t.seg_base[s] + nt * BN;
-    r.valid = max(0, min(BN, t.seg_rows[s] - nt * BN));
-    r.k_blocks = g.k_blocks_routed;
-    r.out = g.out_routed;
-    r.ld = g.ld_out_routed;
-  } else {
-    const int local = u - s0;
-    mt = local / shared_tiles;
-    nt = local - mt * shared_tiles;
-    r.routed = false;
-    r.w_row = mt * g.k_blocks_shared * BM;
-    r.x_row = nt * BN;
-    r.valid = min(BN, g.shared_rows - nt * BN);
-    r.k_blocks = g.k_blocks_shared;
-    r.out = g.out_shared;
-    r.ld = g.ld_out_shared;
-  }
-  r.out_col = mt * feat_per_tile;
+  const int e = t.seg_expert[s];
+  r.routed = true;
+  r.w_row = (e * g.m_tiles_routed + mt) * g.k_blocks_routed * BM;
+  r.x_row = t.seg_base[s] + nt * BN;
+  r.valid = max(0, min(BN, t.seg_rows[s] - nt * BN));
+  r.k_blocks = g.k_blocks_routed;
+  r.out = g.out_routed;
+  r.ld = g.ld_out_routed;
+  r.out_col = mt * (g.mode == kGemmSwiGLU ? BM / 2 : BM);
   return r;
+}
+
+// The k-th unit of this CTA; false when it has no more.
+//   primary (k == 0, when present): segment e = b / MT, M tile b % MT, token tile 0
+//   secondary j = rank + i * grid:  routed tiles segment by segment (M tile
+//                                   major), then the shared expert's tiles
+template <int BN>
+__device__ __forceinline__ bool cta_unit(int k, const GemmArgs& g, const SmemTail<BN>& t,
+                                         Unit& r) {
+  const int MT = g.m_tiles_routed;
+  if (t.has_primary) {
+    if (k == 0) {
+      const int e = blockIdx.x / MT;
+      r = routed_unit<BN>(g, t, e, blockIdx.x - e * MT, 0);
+      return true;
+    }
+    --k;
+  }
+  const int j = t.rank + k * (int)gridDim.x;
+  if (j >= t.n_secondary) return false;
+  const int n_routed = t.prefix[g.n_seg];
+  if (j < n_routed) {
+    const bool prim = primaries_on(g);
+    int s = 0;
+    while (t.prefix[s + 1] <= j) ++s;
+    const int local = j - t.prefix[s];
+    const int n_tiles = secondary_tiles<BN>(s, t.seg_rows[s], prim, g.n_experts);
+    const int mt = local / n_tiles;
+    const int nt = local - mt * n_tiles + ((prim && s < g.n_experts) ? 1 : 0);
+    r = routed_unit<BN>(g, t, s, mt, nt);
+    return true;
+  }
+  const int shared_tiles = (g.shared_rows + BN - 1) / BN;
+  const int local = j - n_routed;
+  const int mt = local / shared_tiles, nt = local - mt * shared_tiles;
+  r.routed = false;
+  r.w_row = mt * g.k_blocks_shared * BM;
+  r.x_row = nt * BN;
+  r.valid = min(BN, g.shared_rows - nt * BN);
+  r.k_blocks = g.k_blocks_shared;
+  r.out = g.out_shared;
+  r.ld = g.ld_out_shared;
+  r.out_col = mt * (g.mode == kGemmSwiGLU ? BM / 2 : BM);
+  return true;
 }
 
 // SiLU of every bf16 value, rounded to bf16: silu_lut[bits(x)] =
@@ -160,18 +187,22 @@ __global__ void build_silu_lut_kernel() {
 
 
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w_routed,
                         const __grid_constant__ CUtensorMap tm_x_routed,
                         const __grid_constant__ CUtensorMap tm_w_shared,
                         const __grid_constant__ CUtensorMap tm_x_shared, const GemmArgs g) {
+  constexpr int kStages = stages_for<BN>();
+  constexpr int kTileB = BN * BK * 2;
+  constexpr int kTmemCols = 2 * BN;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* tiles_a = base;
   unsigned char* tiles_b = base + kStages * kTileA;
   unsigned char* staging = tiles_b + kStages * kTileB;
-  SmemTail& t = *reinterpret_cast<SmemTail*>(staging + 2 * kStaging);
+  SmemTail<BN>& t = *reinterpret_cast<SmemTail<BN>*>(staging + 2 * kStaging);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_seg = g.n_seg;
@@ -200,36 +231,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
 
-  // Weight slabs of a static first unit stream in before the upstream kernel
-  // has finished: they depend on nothing it writes.
-  const int n_static = static_units(g);
-  int prefetched = 0;
-  if (warp == 0 && lane == 0 && (int)blockIdx.x < n_static) {
-    const int u = blockIdx.x;
-    const int s0 = static_routed_units(g);
-    const bool routed = u < s0;
-    const CUtensorMap* mw = routed ? &tm_w_routed : &tm_w_shared;
-    int w_row, kbs;
-    if (routed) {
-      w_row = u * g.k_blocks_routed * BM;  // (e * MT + mt) == u
-      kbs = g.k_blocks_routed;
-    } else {
-      const int shared_tiles = (g.shared_rows + BN - 1) / BN;
-      w_row = ((u - s0) / shared_tiles) * g.k_blocks_shared * BM;
-      kbs = g.k_blocks_shared;
-    }
-    prefetched = min(kStages, kbs);
-    for (int kb = 0; kb < prefetched; ++kb) {
-      mbar_arrive_expect_tx(&t.full[kb], kTileA + kTileB);  // B follows after the wait
-      tma_load_2d(tiles_a + kb * kTileA, mw, 0, w_row + kb * BM, &t.full[kb]);
+  // The weights of this CTA's likely primary unit go to L2 before the
+  // upstream kernel has finished (they depend on nothing it writes).
+  if (warp == 0 && lane == 0 && primaries_on(g) &&
+      (int)blockIdx.x < g.n_experts * g.m_tiles_routed && g.w_routed != nullptr) {
+    const char* w = static_cast<const char*>(g.w_routed) +
+                    (size_t)blockIdx.x * g.k_blocks_routed * kTileA;
+    for (int kb = 0; kb < g.k_blocks_routed; kb += 2) {
+      const unsigned bytes = (unsigned)min(2, g.k_blocks_routed - kb) * kTileA;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w + (size_t)kb * kTileA),
+                   "r"(bytes)
+                   : "memory");
     }
   }
   griddep_wait();
 
   if (warp == 2 || warp == 3) {
-    // prefix of the dynamic units over the 2E segments: one thread per
-    // segment loads its row count, then a two-warp inclusive scan
+    // segment tables and the prefix of the round-robin (secondary) units:
+    // one thread per segment, then a two-warp inclusive scan
     const int s = threadIdx.x - 64;
+    const bool prim = primaries_on(g);
     int rows = 0;
     if (s < n_seg) {
       rows = g.seg_rows[s];
@@ -237,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       t.seg_base[s] = g.seg_base[s];
       t.seg_expert[s] = g.seg_expert != nullptr ? g.seg_expert[s] : s % g.n_experts;
     }
-    int incl = s < n_seg ? extra_tiles(s, rows, g) * g.m_tiles_routed : 0;
+    int incl = s < n_seg ? secondary_tiles<BN>(s, rows, prim, g.n_experts) * g.m_tiles_routed : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int n = __shfl_up_sync(0xffffffffu, incl, o);
@@ -248,42 +269,67 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 3) incl += t.scan_carry;
     if (s < n_seg) t.prefix[s + 1] = incl;
     if (s == 0) t.prefix[0] = 0;
+    if (warp == 2) {
+      // this CTA's place in the schedule (lane e looks at expert e)
+      const int E = g.n_experts, MT = g.m_tiles_routed, b = blockIdx.x;
+      const unsigned empty = __ballot_sync(0xffffffffu, lane < E && rows == 0);
+      if (lane == 0) {
+        int has = 0, rank = b;
+        if (prim) {
+          const int n_empty = __popc(empty);
+          const int n_free = n_empty * MT + ((int)gridDim.x - E * MT);
+          if (b < E * MT) {
+            const int e = b / MT;
+            const unsigned below = (1u << e) - 1u;
+            if (empty & (1u << e)) {
+              rank = __popc(empty & below) * MT + b % MT;
+            } else {
+              has = 1;
+              rank = n_free + __popc(~empty & below) * MT + b % MT;
+            }
+          } else {
+            rank = n_empty * MT + (b - E * MT);
+          }
+        }
+        t.has_primary = has;
+        t.rank = rank;
+      }
+    }
   }
   __syncthreads();
-  if (threadIdx.x == 0) griddep_launch();
+  if (threadIdx.x == 0) {
+    t.n_secondary = t.prefix[n_seg] +
+                    ((g.shared_rows + BN - 1) / BN) * g.m_tiles_shared;
+    griddep_launch();
+  }
+  __syncthreads();
 
   const uint32_t tmem = t.tmem_base;
-  const int total = n_static + t.prefix[n_seg];
   volatile int* abort_flag = &t.abort;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int stage = prefetched % kStages;
-      uint32_t phase = prefetched == kStages ? 1u : 0u;
+      int stage = 0;
+      uint32_t phase = 0;
       bool issued[kStages] = {};
       uint32_t issued_phase[kStages] = {};
-      for (int kb = 0; kb < prefetched; ++kb) issued[kb] = true;  // phase 0
       bool ok = true;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-        const Unit un = decode_unit(u, g, t);
+      Unit un;
+      for (int k = 0; ok && cta_unit<BN>(k, g, t, un); ++k) {
         const CUtensorMap* mw = un.routed ? &tm_w_routed : &tm_w_shared;
         const CUtensorMap* mx = un.routed ? &tm_x_routed : &tm_x_shared;
-        int kb = 0;
-        if (u == (int)blockIdx.x) {
-          // activation slabs of the prefetched stages (their barriers already
-          // expect A and B bytes)
-          for (; kb < prefetched; ++kb)
-            tma_load_2d(tiles_b + kb * kTileB, mx, kb * BK, un.x_row, &t.full[kb]);
-        }
-        for (; kb < un.k_blocks; ++kb) {
+        const int subs = max(1, (un.valid + kSubRows - 1) / kSubRows);
+        for (int kb = 0; kb < un.k_blocks; ++kb) {
           if (!mbar_wait(&t.empty[stage], phase ^ 1, abort_flag, g.status, 10)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&t.full[stage], kTileA + kTileB);
+          mbar_arrive_expect_tx(&t.full[stage], kTileA + subs * kSubBytes);
           tma_load_2d(tiles_a + stage * kTileA, mw, 0, un.w_row + kb * BM, &t.full[stage]);
-          tma_load_2d(tiles_b + stage * kTileB, mx, kb * BK, un.x_row, &t.full[stage]);
+          for (int sb = 0; sb < subs; ++sb)
+            tma_load_2d(tiles_b + stage * kTileB + sb * kSubBytes, mx, kb * BK,
+                        un.x_row + sb * kSubRows, &t.full[stage]);
           issued[stage] = true;
           issued_phase[stage] = phase;
           if (++stage == kStages) {
@@ -305,8 +351,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-        const Unit un = decode_unit(u, g, t);
+      Unit un;
+      for (int k = 0; ok && cta_unit<BN>(k, g, t, un); ++k) {
         if (!mbar_wait(&t.tempty[acc], acc_phase ^ 1, abort_flag, g.status, 20)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * BN;
@@ -346,15 +392,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int chunk_iter = 0;
-    for (int u = blockIdx.x; u < total; u += gridDim.x) {
-      const Unit un = decode_unit(u, g, t);
+    Unit un;
+    for (int k = 0; cta_unit<BN>(k, g, t, un); ++k) {
       const bool scatter = g.mode == kGemmPlain && un.routed && g.row_dst != nullptr;
       if (scatter) {
         // per-row destination and weight, fetched while the MMAs run
         epi_bar();  // the previous unit's stores are done with these arrays
-        if (et < un.valid) {
-          t.unit_dst[et] = __ldg(g.row_dst + un.x_row + et);
-          t.unit_w[et] = round_bf16(__ldg(g.row_w + un.x_row + et));
+        for (int i = et; i < un.valid; i += 128) {
+          t.unit_dst[i] = __ldg(g.row_dst + un.x_row + i);
+          t.unit_w[i] = round_bf16(__ldg(g.row_w + un.x_row + i));
         }
         epi_bar();
       }
@@ -496,30 +542,49 @@ __global__ void pack_tiles_kernel(__nv_bfloat16* __restrict__ dst,
 
 }  // namespace
 
-size_t grouped_gemm_smem_bytes() { return kSmemBytes; }
-
-int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
-                        const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
-                        const CUtensorMap* tm_x_shared, int grid, cudaStream_t stream) {
+template <int BN>
+static int launch_gemm_bn(const GemmArgs& args, const CUtensorMap* tm_w_routed,
+                          const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
+                          const CUtensorMap* tm_x_shared, int grid, cudaStream_t stream) {
+  constexpr size_t smem = smem_bytes<BN>();
+  static_assert(smem <= 227 * 1024, "grouped GEMM shared memory");
   // the attribute belongs to each device's context: set it once per device
   static unsigned long long configured = 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
   if (!(configured & (1ull << dev))) {
-    cudaError_t err = cudaFuncSetAttribute(grouped_gemm_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)kSmemBytes);
-    if (err != cudaSuccess) return -2;
+    if (cudaFuncSetAttribute(grouped_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return -2;
+    configured |= 1ull << dev;
+  }
+  return launch_pdl(grouped_gemm_kernel<BN>, dim3(grid), dim3(kThreads), smem, stream,
+                    *tm_w_routed, *tm_x_routed, *tm_w_shared, *tm_x_shared, args) == cudaSuccess
+             ? 0
+             : -2;
+}
+
+int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
+                        const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
+                        const CUtensorMap* tm_x_shared, int grid, int token_tile,
+                        cudaStream_t stream) {
+  static unsigned long long lut_built = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
+  if (!(lut_built & (1ull << dev))) {
     // the SiLU table of this device, built once on the caller's stream ahead
     // of the first GEMM (which is why the first call should not be captured)
     build_silu_lut_kernel<<<(1 << 16) / 256, 256, 0, stream>>>();
     if (cudaGetLastError() != cudaSuccess) return -2;
-    configured |= 1ull << dev;
+    lut_built |= 1ull << dev;
   }
-  return launch_pdl(grouped_gemm_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream,
-                    *tm_w_routed, *tm_x_routed, *tm_w_shared, *tm_x_shared, args) == cudaSuccess
-             ? 0
-             : -2;
+  if (token_tile == 256)
+    return launch_gemm_bn<256>(args, tm_w_routed, tm_x_routed, tm_w_shared, tm_x_shared, grid,
+                               stream);
+  if (token_tile == 128)
+    return launch_gemm_bn<128>(args, tm_w_routed, tm_x_routed, tm_w_shared, tm_x_shared, grid,
+                               stream);
+  return -1;
 }
 
 static int pack_blocks(size_t vecs) {

@@ -14,8 +14,11 @@ constexpr int kMaxExperts = 32;
 constexpr int kRouteTile = 128;            // tokens per router CTA (the MMA M side)
 constexpr int kGroupTokensPerBlock = 32;   // grouping block / histogram chunk: 64 assignments
 constexpr int kChunksPerTile = kRouteTile / kGroupTokensPerBlock;  // 4
-constexpr int kGemmBlockN = 128;           // token rows per grouped-GEMM tile
+constexpr int kGemmSubRows = 64;           // token rows per activation TMA box
 constexpr int kGemmBlockK = 64;            // 128-byte swizzled K slab
+// Token rows per grouped-GEMM tile: 256 once the rows are many (each weight
+// tile is streamed once per tile of its expert), else 128 (a deeper ring).
+inline int gemm_token_tile(long long rows) { return rows >= 4096 ? 256 : 128; }
 
 struct DepthMixArgs {
   const __nv_bfloat16* sources[kMaxDepthSources];
@@ -112,8 +115,10 @@ struct GemmArgs {
   const int* seg_base;
   const int* seg_expert;  // [n_seg] expert of each segment, or null: segment s is expert s % E
   int n_seg;
-  int static_routed;      // 1: segments e < E are capacity segments whose first token tile is
-                          // a static unit (weights streamed before the grid dependency)
+  int static_routed;      // 1: segment e < E is expert e's first segment; its first token
+                          // tile is a "primary" unit pinned to CTA e * MT + mt, whose
+                          // weights are pulled into L2 before the grid dependency
+  const void* w_routed;   // the routed weights (tiled), for that L2 prefetch, or null
   int n_experts;
   int m_tiles_routed;     // output features / 128
   int k_blocks_routed;    // K / 64
@@ -148,12 +153,13 @@ int launch_combine(const CombineArgs& args, cudaStream_t stream);
 int launch_ep_combine(const EpCombineArgs& args, cudaStream_t stream);
 int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
                         const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
-                        const CUtensorMap* tm_x_shared, int grid, cudaStream_t stream);
+                        const CUtensorMap* tm_x_shared, int grid, int token_tile,
+                        cudaStream_t stream);
 int launch_pack_gate_up(__nv_bfloat16* dst, const __nv_bfloat16* gate, const __nv_bfloat16* up,
                         int n_mats, int hidden, int dim, cudaStream_t stream);
 int launch_pack_tiles(__nv_bfloat16* dst, const __nv_bfloat16* src, int n_mats, int rows,
                       int cols, cudaStream_t stream);
-size_t grouped_gemm_smem_bytes();
+
 
 __host__ __device__ inline int route_blocks(int tokens) {
   return (tokens + kRouteTile - 1) / kRouteTile;

@@ -356,10 +356,18 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
     const int c = count_s[tid];
     a.tab.counts[tid] = c;
     if (a.counts_out != nullptr) a.counts_out[tid] = c;
-    a.tab.seg_rows[tid] = min(c, C);
-    a.tab.seg_base[tid] = tid * C;
-    a.tab.seg_rows[E + tid] = max(c - C, 0);
-    a.tab.seg_base[E + tid] = obase_s[tid];
+    if (C > 0) {
+      a.tab.seg_rows[tid] = min(c, C);
+      a.tab.seg_base[tid] = tid * C;
+      a.tab.seg_rows[E + tid] = max(c - C, 0);
+      a.tab.seg_base[E + tid] = obase_s[tid];
+    } else {
+      // packed rows: the expert's one segment comes first, like a capacity segment
+      a.tab.seg_rows[tid] = c;
+      a.tab.seg_base[tid] = obase_s[tid];
+      a.tab.seg_rows[E + tid] = 0;
+      a.tab.seg_base[E + tid] = obase_s[tid] + c;
+    }
     const float util = (float)c / (float)(2 * T);
     a.tab.stats[tid] = util;
     if (a.stats_out != nullptr) a.stats_out[tid] = util;
