@@ -1,7 +1,8 @@
 // RMSNorm (N3) and Block AttnRes depth mixing fused with its consumer RMSNorm (N5).
 //
-// Both are HBM-bound row kernels: one warp per token row, 16-byte vector
-// loads, fp32 statistics, warp-shuffle reductions and no shared memory.
+// Both are row kernels with 16-byte vector loads and fp32 statistics: RMSNorm
+// takes one warp per token row; the depth mix one CTA per row (a warp per 256
+// columns), so each thread's chain of dependent work stays short.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -85,192 +86,172 @@ int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat
 // them, moe_bf16.metal:331-435): with a peaked softmax over sources, rounding
 // the keys to bf16 first would move the weights by percents.
 //
-// One warp per row.  The warp first issues 16-byte async copies of every
-// source row into its shared-memory slab (all loads in flight at once: one
-// memory round trip), then makes one pass for the S sums of squares and the S
-// raw key.query dots (s_i = rsqrt(...) * sum_d v kw q), reduced together with
-// warp_reduce_many, a lane-parallel softmax, and a second pass for the mix.
+// One CTA of W warps per row (W = ceil(d / 256): 3 at d = 768); thread t owns
+// the row's 16-byte vector t.  A row at a time keeps the per-thread chain
+// short: every source vector is one register load (all S in flight at once),
+// each thread reduces its 8 columns, warp_reduce_many folds the S sums of
+// squares and S raw key.query dots (s_i = rsqrt(mean(v_i^2) + eps) *
+// sum_d v kw q) across the warp, and one shared-memory exchange joins the
+// warps.  Every thread then computes the S scores and the softmax itself (the
+// same order everywhere, so all threads agree bit for bit) and mixes its own
+// vector; a second exchange gives the consumer norm's sum of squares.
 // ---------------------------------------------------------------------------
-constexpr int kDepthWarps = 4;
-
-template <int V>
-__global__ void __launch_bounds__(32 * kDepthWarps) depthmix_kernel(DepthMixArgs a) {
-  extern __shared__ __align__(16) unsigned char depth_smem[];
+template <int W>
+__global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
+  __shared__ float red_ss[W][kMaxDepthSources], red_raw[W][kMaxDepthSources], red_sq[W];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int row = blockIdx.x * kDepthWarps + warp;
+  const int c = threadIdx.x;
+  const int dim = a.dim, nvec = dim >> 3, S = a.n_sources;
+  const bool active = c < nvec;
+  const size_t off = (size_t)blockIdx.x * dim;
+  const bool pending = a.pending_delta != nullptr;
+
+  // the query and norm weights are parameters: read before the grid dependency
+  float q[8], kw[8];
+  uint4 owv = make_uint4(0, 0, 0, 0);
+  if (active) {
+    bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.query) + c), q);
+    bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.key_w) + c), kw);
+    if (a.out_w != nullptr) owv = __ldg(reinterpret_cast<const uint4*>(a.out_w) + c);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = kw[j] = 0.f;
+  }
   griddep_wait();
   griddep_launch();
-  if (row >= a.rows) return;
-  const int dim = a.dim, nvec = dim >> 3, S = a.n_sources;
-  const size_t off = (size_t)row * dim;
-  const bool pending = a.pending_delta != nullptr;
-  uint4* slab = reinterpret_cast<uint4*>(depth_smem) + (size_t)warp * S * nvec;
 
-  // 1. every source slice of this row in flight at once
-  for (int s = 0; s < S; ++s) {
-    if (pending && s == S - 1) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(a.sources[s] + off);
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) cp_async16(slab + s * nvec + c, src + c);
-    }
+  // 1. every source vector of this thread in flight at once
+  uint4 v[kMaxDepthSources];
+  uint4 pb = make_uint4(0, 0, 0, 0), pd = make_uint4(0, 0, 0, 0);
+  if (pending && active) {
+    pb = __ldg(reinterpret_cast<const uint4*>(a.pending_base + off) + c);
+    pd = __ldg(reinterpret_cast<const uint4*>(a.pending_delta + off) + c);
   }
-  // every small vector this warp needs, requested together
-  uint4 qv[V], kwv[V], owv[V];
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int c = lane + 32 * i;
-    if (c < nvec) {
-      qv[i] = __ldg(reinterpret_cast<const uint4*>(a.query) + c);
-      kwv[i] = __ldg(reinterpret_cast<const uint4*>(a.key_w) + c);
-      if (a.out_w != nullptr) owv[i] = __ldg(reinterpret_cast<const uint4*>(a.out_w) + c);
-    }
+  for (int s = 0; s < kMaxDepthSources; ++s) {
+    v[s] = make_uint4(0, 0, 0, 0);
+    if (s < S && active && !(pending && s == S - 1))
+      v[s] = __ldg(reinterpret_cast<const uint4*>(a.sources[s] + off) + c);
   }
-  float q[V][8], kw[V][8];
+  uint4 r = make_uint4(0, 0, 0, 0);
+  if (pending && active) {
+    // the deferred residual add: last source = bf16(base + delta)
+    float b[8], dl[8];
+    bf16x8_to_float(pb, b);
+    bf16x8_to_float(pd, dl);
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int c = lane + 32 * i;
-    if (c < nvec) {
-      bf16x8_to_float(qv[i], q[i]);
-      bf16x8_to_float(kwv[i], kw[i]);
-    }
+    for (int j = 0; j < 8; ++j) b[j] = b[j] + dl[j];
+    r = float_to_bf16x8(b);
+    reinterpret_cast<uint4*>(a.pending_out + off)[c] = r;
   }
-  if (pending) {  // the deferred residual add, resolved in registers
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) {
-        float b[8], dl[8];
-        bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.pending_base + off) + c), b);
-        bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.pending_delta + off) + c), dl);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) b[j] = b[j] + dl[j];
-        const uint4 r = float_to_bf16x8(b);
-        reinterpret_cast<uint4*>(a.pending_out + off)[c] = r;
-        slab[(S - 1) * nvec + c] = r;
-      }
-    }
-  }
-  cp_async_wait_all();  // each lane reads back only the slices it copied
+  // source s as this thread sees it (reads only: a store into v[S - 1] would
+  // make the compiler index the array at run time, in local memory)
+  auto source = [&](int s) { return (pending && s == S - 1) ? r : v[s]; };
 
-  // 2. sums of squares and raw key.query dots of all sources, reduced together
+  // key.query weight per column (the score needs sum_d v kw q, not the key itself)
+  float kq[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) kq[j] = kw[j] * q[j];
+  // 2. per-source sums of squares and raw key.query dots
   float ss[kMaxDepthSources], raw[kMaxDepthSources];
 #pragma unroll
   for (int s = 0; s < kMaxDepthSources; ++s) {
     ss[s] = 0.f;
     raw[s] = 0.f;
     if (s < S) {
+      float f[8];
+      bf16x8_to_float(source(s), f);
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
-        const int c = lane + 32 * i;
-        if (c < nvec) {
-          float f[8];
-          bf16x8_to_float(slab[s * nvec + c], f);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            ss[s] = fmaf(f[j], f[j], ss[s]);
-            raw[s] = fmaf(f[j] * kw[i][j], q[i][j], raw[s]);
-          }
-        }
+      for (int j = 0; j < 8; ++j) {
+        ss[s] = fmaf(f[j], f[j], ss[s]);
+        raw[s] = fmaf(f[j], kq[j], raw[s]);
       }
     }
   }
   const float ss_l = warp_reduce_many<kMaxDepthSources>(ss, lane);
   const float raw_l = warp_reduce_many<kMaxDepthSources>(raw, lane);
-  // lane l now owns source l % 16
-  const int src_l = lane & (kMaxDepthSources - 1);
-  const bool valid = src_l < S;
-  const float score = valid ? rsqrtf(ss_l / (float)dim + a.key_eps) * raw_l : -INFINITY;
-  const float m = warp_max(score);
-  const float e = valid ? expf(score - m) : 0.f;
-  const float den = warp_sum(lane < kMaxDepthSources ? e : 0.f);
-  const float alpha_l = e / den;
+  if (lane < kMaxDepthSources) {  // lane l holds the warp's totals of source l
+    red_ss[warp][lane] = ss_l;
+    red_raw[warp][lane] = raw_l;
+  }
+  __syncthreads();
 
-  // 3. mix, then the consumer RMSNorm
-  float h[V][8];
+  // 3. scores and softmax (every thread, same order), then the mix
+  float alpha[kMaxDepthSources];
+  float m = -INFINITY;
+  // short dependent chains matter here (a few warps per SM): one reciprocal
+  // for the mean, one for the softmax denominator, the fast exp
+  const float inv_dim = 1.0f / (float)dim;
 #pragma unroll
-  for (int i = 0; i < V; ++i)
+  for (int s = 0; s < kMaxDepthSources; ++s) {
+    alpha[s] = -INFINITY;
+    if (s < S) {
+      float tss = 0.f, traw = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) h[i][j] = 0.f;
-  for (int s = 0; s < S; ++s) {
-    const float alpha = __shfl_sync(0xffffffffu, alpha_l, s);
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) {
-        float f[8];
-        bf16x8_to_float(slab[s * nvec + c], f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) h[i][j] = fmaf(alpha, f[j], h[i][j]);
+      for (int w = 0; w < W; ++w) {
+        tss += red_ss[w][s];
+        traw += red_raw[w][s];
       }
+      alpha[s] = rsqrtf(tss * inv_dim + a.key_eps) * traw;
+      m = fmaxf(m, alpha[s]);
+    }
+  }
+  float den = 0.f;
+#pragma unroll
+  for (int s = 0; s < kMaxDepthSources; ++s) {
+    alpha[s] = s < S ? __expf(alpha[s] - m) : 0.f;
+    den += alpha[s];
+  }
+  const float rden = 1.0f / den;
+  float h[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) h[j] = 0.f;
+#pragma unroll
+  for (int s = 0; s < kMaxDepthSources; ++s) {
+    if (s < S) {
+      const float al = alpha[s] * rden;
+      float f[8];
+      bf16x8_to_float(source(s), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = fmaf(al, f[j], h[j]);
     }
   }
   float sq = 0.f;
 #pragma unroll
-  for (int i = 0; i < V; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      h[i][j] = round_bf16(h[i][j]);
-      sq = fmaf(h[i][j], h[i][j], sq);
-    }
-  uint4* orow = reinterpret_cast<uint4*>(a.out + off);
-  if (a.mix_out != nullptr) {
-    uint4* mrow = reinterpret_cast<uint4*>(a.mix_out + off);
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) mrow[c] = float_to_bf16x8(h[i]);
-    }
+  for (int j = 0; j < 8; ++j) {
+    h[j] = round_bf16(h[j]);
+    sq = fmaf(h[j], h[j], sq);
   }
+  if (active && a.mix_out != nullptr) reinterpret_cast<uint4*>(a.mix_out + off)[c] = float_to_bf16x8(h);
   if (a.out_w == nullptr) {
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) orow[c] = float_to_bf16x8(h[i]);
-    }
+    if (active) reinterpret_cast<uint4*>(a.out + off)[c] = float_to_bf16x8(h);
     return;
   }
+  // 4. the consumer RMSNorm
   sq = warp_sum(sq);
-  const float inv = rsqrtf(sq / (float)dim + a.out_eps);
+  if (lane == 0) red_sq[warp] = sq;
+  __syncthreads();
+  float total = 0.f;
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int c = lane + 32 * i;
-    if (c < nvec) {
-      float g[8];
-      bf16x8_to_float(owv[i], g);
+  for (int w = 0; w < W; ++w) total += red_sq[w];
+  const float inv = rsqrtf(total / (float)dim + a.out_eps);
+  if (active) {
+    float g[8];
+    bf16x8_to_float(owv, g);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) g[j] = (h[i][j] * inv) * g[j];
-      orow[c] = float_to_bf16x8(g);
-    }
+    for (int j = 0; j < 8; ++j) g[j] = (h[j] * inv) * g[j];
+    reinterpret_cast<uint4*>(a.out + off)[c] = float_to_bf16x8(g);
   }
-}
-
-template <int V>
-static int launch_depthmix_v(const DepthMixArgs& args, cudaStream_t stream) {
-  const size_t smem = (size_t)kDepthWarps * args.n_sources * (args.dim / 8) * sizeof(uint4);
-  static unsigned long long configured = 0;  // per device: the attribute lives in its context
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
-  if (!(configured & (1ull << dev))) {
-    const int max_smem = kDepthWarps * kMaxDepthSources * (1024 / 8) * (int)sizeof(uint4);
-    if (cudaFuncSetAttribute(depthmix_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             max_smem) != cudaSuccess)
-      return -2;
-    configured |= 1ull << dev;
-  }
-  dim3 grid((args.rows + kDepthWarps - 1) / kDepthWarps), block(32 * kDepthWarps);
-  return launch_pdl(depthmix_kernel<V>, grid, block, smem, stream, args) == cudaSuccess ? 0 : -2;
 }
 
 int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream) {
   if (args.rows == 0) return 0;
-  const int v = (args.dim / 8 + 31) / 32;
-  switch (v) {
-    case 1: return launch_depthmix_v<1>(args, stream);
-    case 2: return launch_depthmix_v<2>(args, stream);
-    case 3: return launch_depthmix_v<3>(args, stream);
-    case 4: return launch_depthmix_v<4>(args, stream);
+  const dim3 grid(args.rows);
+  switch ((args.dim / 8 + 31) / 32) {
+    case 1: return launch_pdl(depthmix_kernel<1>, grid, dim3(32), 0, stream, args) ? -2 : 0;
+    case 2: return launch_pdl(depthmix_kernel<2>, grid, dim3(64), 0, stream, args) ? -2 : 0;
+    case 3: return launch_pdl(depthmix_kernel<3>, grid, dim3(96), 0, stream, args) ? -2 : 0;
+    case 4: return launch_pdl(depthmix_kernel<4>, grid, dim3(128), 0, stream, args) ? -2 : 0;
     default: return -1;
   }
 }
