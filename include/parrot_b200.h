@@ -128,8 +128,9 @@ typedef struct parrot_moe_outputs {
 typedef struct parrot_moe_layout {
   size_t indices, weights, positions;
   size_t chunk_hist;      /* [ceil(T/32), E] int32 expert histogram per 32-token chunk */
-  size_t tile_hist;       /* [ceil(T/128), E] int32 per 128-token router tile */
-  size_t tile_probsum;    /* [ceil(T/128), E] f32 router probability sums per tile */
+  size_t tile_hist;       /* [route_blocks, E] int32 per router tile (32 tokens up to
+                             T = 4096, else 128) */
+  size_t tile_probsum;    /* [route_blocks, E] f32 router probability sums per tile */
   size_t counts, seg_rows, seg_base, stats, status;
   size_t row_dst, row_w;  /* per grouped row: token-major slot, route weight */
   size_t grouped;         /* [E*C + 2T, d] token rows grouped by expert */
@@ -137,7 +138,7 @@ typedef struct parrot_moe_layout {
   size_t contrib;         /* [2T, d] bf16(bf16(y) * bf16(w)), slot 2t + (lower expert id first) */
   size_t shared_hidden, shared_y, total;
   int capacity, grouped_rows;
-  int route_blocks;       /* router CTAs: ceil(T / 128) */
+  int route_blocks;       /* router CTAs: ceil(T / 32) up to T = 4096, else ceil(T / 128) */
   int reserved;
 } parrot_moe_layout;
 

@@ -243,7 +243,7 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ra.n_experts = E;
   ra.status = at<int>(ws, L.status);
   CUtensorMap mx, mw;
-  if (!tensor_map(&mx, x, T, dims->dim, parrot::kRouteTile) ||
+  if (!tensor_map(&mx, x, T, dims->dim, parrot::route_tile(T)) ||
       !tensor_map(&mw, w->router, E, dims->dim, parrot::route_experts_padded(E)))
     return fail(PARROT_ECUDA, "route: cuTensorMapEncodeTiled failed%s");
   if (parrot::launch_route(ra, &mx, &mw, s))

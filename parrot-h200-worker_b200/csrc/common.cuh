@@ -75,15 +75,15 @@ __device__ __forceinline__ float warp_max(float v) {
 // N <= 32).  Halving exchanges move half of the remaining values per step, so
 // N values cost N - 1 + log2(32 / N) shuffles instead of 5 N.  On return,
 // lane l holds the warp-wide total of value index (l % N) in v[0].
-template <int N>
-__device__ __forceinline__ float warp_reduce_many(float (&v)[N], int lane) {
+template <int N, typename V>
+__device__ __forceinline__ V warp_reduce_many(V (&v)[N], int lane) {
 #pragma unroll
   for (int o = N / 2; o >= 1; o >>= 1) {
     const bool upper = (lane & o) != 0;
 #pragma unroll
     for (int j = 0; j < o; ++j) {
-      const float send = upper ? v[j] : v[j + o];
-      const float keep = upper ? v[j + o] : v[j];
+      const V send = upper ? v[j] : v[j + o];
+      const V keep = upper ? v[j + o] : v[j];
       v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
     }
   }

@@ -11,9 +11,7 @@ namespace parrot {
 
 constexpr int kMaxDepthSources = 16;
 constexpr int kMaxExperts = 32;
-constexpr int kRouteTile = 128;            // tokens per router CTA (the MMA M side)
 constexpr int kGroupTokensPerBlock = 32;   // grouping block / histogram chunk: 64 assignments
-constexpr int kChunksPerTile = kRouteTile / kGroupTokensPerBlock;  // 4
 constexpr int kGemmSubRows = 64;           // token rows per activation TMA box
 constexpr int kGemmBlockK = 64;            // 128-byte swizzled K slab
 // Token rows per grouped-GEMM tile: 256 once the rows are many (each weight
@@ -161,8 +159,14 @@ int launch_pack_tiles(__nv_bfloat16* dst, const __nv_bfloat16* src, int n_mats, 
                       int cols, cudaStream_t stream);
 
 
+// Tokens per router CTA: 32 while the batch is small (more CTAs share the
+// load of x), 128 (the MMA's M) once it is large (fewer histogram rows for
+// the grouping kernel to sum).  The MMA always has M = 128; a 32-token tile
+// leaves the other accumulator lanes unused.
+__host__ __device__ inline int route_tile(int tokens) { return tokens <= 4096 ? 32 : 128; }
 __host__ __device__ inline int route_blocks(int tokens) {
-  return (tokens + kRouteTile - 1) / kRouteTile;
+  const int r = route_tile(tokens);
+  return (tokens + r - 1) / r;
 }
 __host__ __device__ inline int route_experts_padded(int n_experts) {
   return n_experts <= 16 ? 16 : 32;

@@ -1,7 +1,8 @@
 // Router (N1) and deterministic capacity grouping (N2).
 //
-// route_kernel:  one CTA per 128 tokens.  The router logits are a skinny GEMM
-//                [128 x d] x [d x E]: TMA streams 64-column slabs of the token
+// route_kernel:  one CTA per 32 tokens (128 for large batches).  The router
+//                logits are a skinny GEMM [128 x d] x [d x E] (a 32-token
+//                tile fills the first 32 rows): TMA streams 64-column slabs of the token
 //                tile and of the router weight through a shared-memory ring,
 //                one thread issues tcgen05.mma (M = 128 tokens, N = E rounded
 //                up to 16/32, fp32 accumulator in TMEM).  Each of the 128
@@ -26,12 +27,22 @@ namespace parrot {
 
 using namespace tc;
 
-constexpr int kRouteStages = 6;
-constexpr int kRouteXTile = kRouteTile * 64 * 2;  // 16 KB slab of 128 tokens x 64 columns
+constexpr int kRouteM = 128;                   // MMA rows (tokens of a tile, padded)
+constexpr int kRouteXTile = kRouteM * 64 * 2;  // 16 KB slab: 128 token rows x 64 columns
+constexpr int kRouteMaxStages = 12;
+
+// As many slab slots as shared memory holds (12 with E <= 16: a whole
+// d = 768 row block in flight at once, no slot reused); a ring beyond that.
+template <int NP>
+constexpr int route_stages() {
+  return (225 * 1024) / (kRouteXTile + NP * 128) < kRouteMaxStages
+             ? (225 * 1024) / (kRouteXTile + NP * 128)
+             : kRouteMaxStages;
+}
 
 struct __align__(8) RouteSmem {
-  uint64_t full[kRouteStages];
-  uint64_t empty[kRouteStages];
+  uint64_t full[kRouteMaxStages];
+  uint64_t empty[kRouteMaxStages];
   uint64_t done;
   uint32_t tmem;
   int abort;
@@ -41,7 +52,7 @@ struct __align__(8) RouteSmem {
 
 template <int NP>
 constexpr size_t route_smem_bytes() {
-  return 1024 + (size_t)kRouteStages * (kRouteXTile + NP * 128) + sizeof(RouteSmem);
+  return 1024 + (size_t)route_stages<NP>() * (kRouteXTile + NP * 128) + sizeof(RouteSmem);
 }
 
 template <int NP>
@@ -49,6 +60,7 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
                                                     const __grid_constant__ CUtensorMap w_map,
                                                     RouteArgs a) {
   constexpr int kWTile = NP * 128;  // NP experts x 64 columns
+  constexpr int kRouteStages = route_stages<NP>();
   extern __shared__ unsigned char route_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(route_raw) + 1023) & ~uintptr_t(1023));
@@ -60,6 +72,8 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
   const int kb_count = a.dim / 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x;
+  const int rows = route_tile(T);                  // token rows this CTA loads (32 or 128)
+  const uint32_t x_bytes = (uint32_t)rows * 128u;  // of each 64-column slab
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRouteStages; ++s) {
@@ -77,12 +91,17 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
   tc_fence_after();
   volatile int* abort_flag = &sm.abort;
 
+  // the harness logit offset is a parameter too
+  float bias[NP];
+#pragma unroll
+  for (int e = 0; e < NP; ++e) bias[e] = (a.bias != nullptr && e < E) ? __ldg(a.bias + e) : 0.f;
+
   // the router weight is a parameter: its slabs stream in before the
   // upstream kernel (which writes x) has finished
   const int pre = min(kRouteStages, kb_count);
   if (threadIdx.x == 0) {
     for (int kb = 0; kb < pre; ++kb) {
-      mbar_arrive_expect_tx(&sm.full[kb], kRouteXTile + kWTile);
+      mbar_arrive_expect_tx(&sm.full[kb], x_bytes + kWTile);
       tma_load_2d(w_tiles + kb * kWTile, &w_map, kb * 64, 0, &sm.full[kb]);
     }
   }
@@ -95,16 +114,16 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
       bool issued[kRouteStages] = {};
       uint32_t issued_phase[kRouteStages] = {};
       for (int kb = 0; kb < pre; ++kb) {
-        tma_load_2d(x_tiles + kb * kRouteXTile, &x_map, kb * 64, tile * kRouteTile, &sm.full[kb]);
+        tma_load_2d(x_tiles + kb * kRouteXTile, &x_map, kb * 64, tile * rows, &sm.full[kb]);
         issued[kb] = true;
       }
       for (int kb = pre; kb < kb_count; ++kb) {
         const int stage = kb % kRouteStages;
         const uint32_t phase = (uint32_t)(kb / kRouteStages) & 1u;
         if (!mbar_wait(&sm.empty[stage], phase ^ 1u, abort_flag, a.status, 20)) break;
-        mbar_arrive_expect_tx(&sm.full[stage], kRouteXTile + kWTile);
+        mbar_arrive_expect_tx(&sm.full[stage], x_bytes + kWTile);
         tma_load_2d(w_tiles + stage * kWTile, &w_map, kb * 64, 0, &sm.full[stage]);
-        tma_load_2d(x_tiles + stage * kRouteXTile, &x_map, kb * 64, tile * kRouteTile,
+        tma_load_2d(x_tiles + stage * kRouteXTile, &x_map, kb * 64, tile * rows,
                     &sm.full[stage]);
         issued[stage] = true;
         issued_phase[stage] = phase;
@@ -117,7 +136,7 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = make_idesc(kRouteTile, NP);
+      const uint32_t idesc = make_idesc(kRouteM, NP);
       for (int kb = 0; kb < kb_count; ++kb) {
         const int stage = kb % kRouteStages;
         const uint32_t phase = (uint32_t)(kb / kRouteStages) & 1u;
@@ -140,8 +159,8 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
   tc_fence_after();
   const bool ok = *abort_flag == 0;
   float p[NP];
-  const int t = tile * kRouteTile + (int)threadIdx.x;
-  const bool valid_tok = ok && t < T;
+  const int t = tile * rows + (int)threadIdx.x;
+  const bool valid_tok = ok && (int)threadIdx.x < rows && t < T;
   {
     uint32_t r[NP];
     const uint32_t addr = sm.tmem + ((uint32_t)(warp * 32) << 16);
@@ -154,19 +173,20 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
     float m = -INFINITY;
 #pragma unroll
     for (int e = 0; e < NP; ++e) {
-      float l = __uint_as_float(r[e]);
-      if (e < E && a.bias != nullptr) l += __ldg(a.bias + e);
+      const float l = __uint_as_float(r[e]) + bias[e];
       p[e] = e < E ? l : -INFINITY;
       m = fmaxf(m, p[e]);
     }
     float den = 0.f;
 #pragma unroll
     for (int e = 0; e < NP; ++e) {
-      p[e] = e < E ? expf(p[e] - m) : 0.f;
+      p[e] = e < E ? __expf(p[e] - m) : 0.f;
       den += p[e];
     }
+    // one reciprocal and the fast exp: the per-thread chain is the cost here
+    const float rden = 1.0f / den;
 #pragma unroll
-    for (int e = 0; e < NP; ++e) p[e] = valid_tok ? p[e] / den : 0.f;
+    for (int e = 0; e < NP; ++e) p[e] = valid_tok ? p[e] * rden : 0.f;
   }
   if (valid_tok) {
     // top-2; equal probabilities resolve to the lower expert id
@@ -208,9 +228,9 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
   if (lane < E) sm.psum[warp][lane] = ps;
   __syncthreads();
   if (ok) {
-    const int chunk0 = tile * kChunksPerTile;
+    const int chunk0 = tile * (rows / kGroupTokensPerBlock);
     const int n_chunks = (T + kGroupTokensPerBlock - 1) / kGroupTokensPerBlock;
-    if (lane < E && chunk0 + warp < n_chunks)
+    if (lane < E && warp < rows / kGroupTokensPerBlock && chunk0 + warp < n_chunks)
       a.tab.chunk_hist[(size_t)(chunk0 + warp) * E + lane] = sm.hist[warp][lane];
     if (threadIdx.x < E) {
       const int e = threadIdx.x;
@@ -308,7 +328,8 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
   {
     // prefix and totals: thread (phase, expert) sums every P-th tile row
     const int P = blockDim.x / E;
-    const int n_tiles = route_blocks(T), my_tile = blk / kChunksPerTile;
+    const int per_tile = route_tile(T) / kGroupTokensPerBlock;  // chunks per router tile
+    const int n_tiles = route_blocks(T), my_tile = blk / per_tile;
     int before = 0, total = 0;
     float ps = 0.f;
     if (tid < P * E) {
@@ -333,7 +354,7 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
         c += red_total[ph * E + tid];
         s += red_psum[ph * E + tid];
       }
-      for (int ch = my_tile * kChunksPerTile; ch < blk; ++ch)
+      for (int ch = my_tile * per_tile; ch < blk; ++ch)
         b += __ldcg(a.tab.chunk_hist + (size_t)ch * E + tid);
       prefix_s[tid] = b;
       count_s[tid] = c;
