@@ -12,8 +12,8 @@ One MoE call on a rank:
    token (``parrot_moe_ep_dispatch_bf16``);
 2. all-to-all of the ``[G, E/G]`` per-(destination, local expert) row counts;
 3. one host read of the counts: the split sizes of the variable all-to-all;
-4. all-to-all of the token rows (the shared expert runs on the local tokens
-   while they travel);
+4. all-to-all of the token rows (the shared expert on the local tokens was
+   queued before the host read, so the GPU computes it while the host waits);
 5. the local experts on the received rows, one segment per (source rank,
    local expert) (``parrot_moe_expert_ffn_bf16``);
 6. the reverse all-to-all of the expert outputs, back into the dispatch's
@@ -143,17 +143,15 @@ class ExpertParallelMoE:
         send = send_counts(counts.to(torch.int32), G).view(-1)
         recv = torch.empty_like(send)
         self.comm.all_to_all(recv, send, None, None)
-        both = torch.cat([send, recv]).cpu().view(2, G, El)  # the one host sync
+        both = torch.cat([send, recv])
+        self.ops.shared(x)  # the GPU computes the shared expert while the host waits below
+        both = both.cpu().view(2, G, El)  # the one host sync: split sizes of the row exchange
         send_split = both[0].sum(1).tolist()
         recv_tab = both[1].tolist()
         recv_split = [sum(r) for r in recv_tab]
         seg = receive_segments(recv_tab)
         received = rows.new_empty((seg.total, rows.shape[1]))
-        work = self.comm.all_to_all(received, rows[:sum(send_split)], recv_split, send_split,
-                                    async_op=True)
-        self.ops.shared(x)  # overlaps the row exchange
-        if work is not None:
-            work.wait()
+        self.comm.all_to_all(received, rows[:sum(send_split)], recv_split, send_split)
         y_local = self.ops.experts(received, seg)
         y_back = rows.new_empty((sum(send_split), rows.shape[1]))
         self.comm.all_to_all(y_back, y_local, send_split, recv_split)
