@@ -232,9 +232,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
 
   // The weights of this CTA's likely primary unit go to L2 before the
-  // upstream kernel has finished (they depend on nothing it writes).
+  // upstream kernel has finished (they depend on nothing it writes) — only
+  // when most experts are likely to have rows (at least eight assignments per
+  // expert on average): at decode sizes it would stream every expert's weights
+  // for the two that are used.
   if (warp == 0 && lane == 0 && primaries_on(g) &&
-      (int)blockIdx.x < g.n_experts * g.m_tiles_routed && g.w_routed != nullptr) {
+      (int)blockIdx.x < g.n_experts * g.m_tiles_routed && g.w_routed != nullptr &&
+      2 * g.shared_rows >= 8 * g.n_experts) {
     const char* w = static_cast<const char*>(g.w_routed) +
                     (size_t)blockIdx.x * g.k_blocks_routed * kTileA;
     for (int kb = 0; kb < g.k_blocks_routed; kb += 2) {
