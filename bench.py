@@ -254,26 +254,32 @@ def time_zipf_layer(tokens: int = 16384, replays: int = 10) -> dict:
 
 
 def time_decode(model, batches=(1, 8, 64), prompt: int = 128, new_tokens: int = 16) -> dict:
-    """prefill 128 ids, then 16 greedy decode_step calls (eager)."""
+    """prefill 128 ids, then 16 greedy decode steps; tokens/s of
+    the decode steps, eager (``decode_step``) and replayed from one captured step
+    (``Parrot.capture_decode``), CUDA events around the 16 steps."""
     from parrot_b200.workloads import random_token_ids
-    out = {}
+    out = {"eager": {}, "graph": {}}
     with torch.inference_mode():
         for b in batches:
             ids = random_token_ids(b, prompt, model.config.vocab_size, seed=b).cuda()
             logits, state = model.prefill(ids)
             nxt = logits.argmax(-1)
             model.decode_step(nxt, state)  # warm the decode path once
-            logits, state = model.prefill(ids)
-            nxt = logits.argmax(-1)
-            torch.cuda.synchronize()
-            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            for _ in range(new_tokens):
-                logits, state = model.decode_step(nxt, state)
+            for mode in ("eager", "graph"):
+                logits, state = model.prefill(ids)
                 nxt = logits.argmax(-1)
-            e.record()
-            torch.cuda.synchronize()
-            out[f"B{b}"] = b * new_tokens / (a.elapsed_time(e) * 1e-3)
+                step = model.capture_decode(state, next_token_only=True) if mode == "graph" else None
+                torch.cuda.synchronize()
+                a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(new_tokens):
+                    if step is None:
+                        nxt, state = model.decode_next(nxt, state)
+                    else:
+                        nxt = step(nxt)
+                e.record()
+                torch.cuda.synchronize()
+                out[mode][f"B{b}"] = b * new_tokens / (a.elapsed_time(e) * 1e-3)
     return out
 
 

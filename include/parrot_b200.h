@@ -85,6 +85,46 @@ int parrot_rope_inplace_bf16(void* x, const void* cos_table, const void* sin_tab
                              int row_stride, int rot_cols, int head_dim, int seq_len, int start,
                              int max_positions, void* stream);
 
+/* As parrot_rope_inplace_bf16 with the first position read from device
+ * memory (*start_dev), so a decode step captured in a CUDA graph can be
+ * replayed at successive positions.  A position at or past max_positions is
+ * recorded in status (device int[4], may be NULL) and that row left as is.
+ * Replaces the position-dependent RoPE of parrot/model.py:218-230 in decode. */
+int parrot_rope_inplace_at_bf16(void* x, const void* cos_table, const void* sin_table, int rows,
+                                int row_stride, int rot_cols, int head_dim, int seq_len,
+                                const int* start_dev, int max_positions, int* status,
+                                void* stream);
+
+/* ------------------------------------------------------------------------
+ * Single-token decode attention with the position in device memory.
+ * Appends this step's key/value at *pos_dev to the cache, then attends each
+ * query head over the keys [max(0, pos - window + 1), pos] of its KV head
+ * (window 0 = no window): softmax(scale * q.k) weighted sum of the values,
+ * fp32 math.
+ *   local GQA (parrot/model.py:303-328, window 2048): q [B, H, D] bf16
+ *     (q_f32 = 0), k_new/v_new [B, KVH, D] bf16, k_cache/v_cache
+ *     [B, KVH, max_positions, D] bf16, out [B, H, D] bf16;
+ *   MLA absorbed (parrot/model.py:399-432): q [B, H, L] fp32 (q_f32 = 1),
+ *     k_new = the new latent [B, 1, L], v_new = v_cache = NULL (values are
+ *     the keys), k_cache = the latent cache [B, 1, max_positions, L],
+ *     out [B, H, L] fp32 (out_f32 = 1), scale = head_dim^-0.5.
+ * Supported (D, H / KVH): (96, 4), (96, 1), (128, 8), (32, 2), (32, 4).
+ * q_row_stride / kv_row_stride: elements between batch rows of q and of
+ * k_new / v_new (0 = packed), so q, k and v can be views of one projection.
+ * partials: parrot_decode_attention_scratch_bytes() of scratch.  A position
+ * outside [0, max_positions) is recorded in status and nothing is written. */
+int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f32,
+                                 long long q_row_stride, const void* k_new, const void* v_new,
+                                 long long kv_row_stride, void* k_cache, void* v_cache,
+                                 const int* pos_dev, int batch, int n_heads, int n_kv_heads,
+                                 int max_positions, int head_dim, int window, float scale,
+                                 void* partials, size_t partial_bytes, int* status,
+                                 void* stream);
+
+/* Scratch bytes parrot_decode_attention_bf16 needs for these sizes. */
+size_t parrot_decode_attention_scratch_bytes(int batch, int n_heads, int max_positions,
+                                             int head_dim);
+
 /* ------------------------------------------------------------------------
  * MoE block: router + top-2 + capacity grouping + grouped SwiGLU experts +
  * shared expert + weighted combine (+ residual add).

@@ -561,9 +561,85 @@ int parrot_rope_inplace_bf16(void* x, const void* cos_table, const void* sin_tab
   if (parrot::launch_rope(static_cast<__nv_bfloat16*>(x),
                           static_cast<const __nv_bfloat16*>(cos_table),
                           static_cast<const __nv_bfloat16*>(sin_table), rows, row_stride,
-                          rot_cols, head_dim, seq_len, start, static_cast<cudaStream_t>(stream)))
+                          rot_cols, head_dim, seq_len, start, nullptr, max_positions, nullptr,
+                          static_cast<cudaStream_t>(stream)))
     return fail(PARROT_ECUDA, "rope: launch failed%s");
   return check_launch("rope_kernel");
+}
+
+int parrot_rope_inplace_at_bf16(void* x, const void* cos_table, const void* sin_table, int rows,
+                                int row_stride, int rot_cols, int head_dim, int seq_len,
+                                const int* start_dev, int max_positions, int* status,
+                                void* stream) {
+  if (rows < 0 || head_dim <= 0 || head_dim % 8 || rot_cols < 0 || rot_cols % head_dim ||
+      row_stride < rot_cols || row_stride % 8 || seq_len <= 0 || max_positions <= 0)
+    return fail(PARROT_EINVAL, "rope_at: need head_dim %% 8 == 0, rot_cols a multiple of "
+                               "head_dim, row_stride %% 8 == 0 and >= rot_cols%s");
+  if (rows == 0 || rot_cols == 0) return PARROT_OK;
+  if (!x || !cos_table || !sin_table || !start_dev || !aligned16(x))
+    return fail(PARROT_EINVAL, "rope_at: null or misaligned pointer%s");
+  if (parrot::launch_rope(static_cast<__nv_bfloat16*>(x),
+                          static_cast<const __nv_bfloat16*>(cos_table),
+                          static_cast<const __nv_bfloat16*>(sin_table), rows, row_stride,
+                          rot_cols, head_dim, seq_len, 0, start_dev, max_positions, status,
+                          static_cast<cudaStream_t>(stream)))
+    return fail(PARROT_ECUDA, "rope_at: launch failed%s");
+  return check_launch("rope_kernel(device position)");
+}
+
+int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f32,
+                                 long long q_row_stride, const void* k_new, const void* v_new,
+                                 long long kv_row_stride, void* k_cache, void* v_cache,
+                                 const int* pos_dev, int batch, int n_heads, int n_kv_heads,
+                                 int max_positions, int head_dim, int window, float scale,
+                                 void* partials, size_t partial_bytes, int* status,
+                                 void* stream) {
+  if (batch < 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads ||
+      max_positions <= 0 || window < 0)
+    return fail(PARROT_EINVAL, "decode_attention: bad sizes%s");
+  const int n_chunks = parrot::decode_attn_chunks(max_positions);
+  if (partial_bytes < parrot_decode_attention_scratch_bytes(batch, n_heads, max_positions, head_dim))
+    return fail(PARROT_EINVAL, "decode_attention: partials smaller than the scratch size%s");
+  if (batch == 0) return PARROT_OK;
+  if (!out || !q || !k_new || !k_cache || !pos_dev || !partials || (v_new == nullptr) != (v_cache == nullptr))
+    return fail(PARROT_EINVAL, "decode_attention: null pointer (v_new and v_cache go together)%s");
+  if (!aligned16(k_new) || !aligned16(k_cache) || (v_new && (!aligned16(v_new) || !aligned16(v_cache))))
+    return fail(PARROT_EINVAL, "decode_attention: K/V must be 16-byte aligned%s");
+  parrot::DecodeAttnArgs a{};
+  a.q = q;
+  a.q_f32 = q_f32;
+  a.k_new = static_cast<const __nv_bfloat16*>(k_new);
+  a.v_new = static_cast<const __nv_bfloat16*>(v_new);
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.pos = pos_dev;
+  a.part = static_cast<float*>(partials);
+  a.out = out;
+  a.out_f32 = out_f32;
+  a.B = batch;
+  a.H = n_heads;
+  a.KVH = n_kv_heads;
+  a.S = max_positions;
+  a.D = head_dim;
+  a.window = window;
+  a.n_chunks = n_chunks;
+  a.q_row = q_row_stride > 0 ? q_row_stride : (long long)n_heads * head_dim;
+  a.kv_row = kv_row_stride > 0 ? kv_row_stride : (long long)n_kv_heads * head_dim;
+  if (a.kv_row % 8 || (long long)n_kv_heads * head_dim > a.kv_row || (long long)n_heads * head_dim > a.q_row)
+    return fail(PARROT_EINVAL, "decode_attention: row strides too small or not 16-byte multiples%s");
+  a.scale = scale;
+  a.status = status;
+  const int rc = parrot::launch_decode_attention(a, static_cast<cudaStream_t>(stream));
+  if (rc == -1)
+    return fail(PARROT_EUNSUPPORTED, "decode_attention: unsupported head width / group size%s");
+  if (rc) return fail(PARROT_ECUDA, "decode_attention: launch failed%s");
+  return check_launch("decode_attn_kernels");
+}
+
+size_t parrot_decode_attention_scratch_bytes(int batch, int n_heads, int max_positions,
+                                             int head_dim) {
+  return (size_t)batch * n_heads * parrot::decode_attn_chunks(max_positions) * (head_dim + 2) *
+         sizeof(float);
 }
 
 int parrot_moe_capacity(int tokens, int n_experts) {

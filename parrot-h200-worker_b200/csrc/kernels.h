@@ -136,12 +136,32 @@ struct GemmArgs {
   int* status;
 };
 
+// Single-token decode attention (decode.cu).
+struct DecodeAttnArgs {
+  const void* q;                 // [B, H, D] bf16, or fp32 when q_f32
+  int q_f32;
+  const __nv_bfloat16* k_new;    // [B, KVH, D] this step's key (RoPE applied)
+  const __nv_bfloat16* v_new;    // [B, KVH, D], or null when the values are the keys
+  __nv_bfloat16* k_cache;        // [B, KVH, S, D]
+  __nv_bfloat16* v_cache;        // [B, KVH, S, D], or null (values = keys)
+  const int* pos;                // device: position of this step's token
+  float* part;                   // [B, H, n_chunks, D + 2] partials (scratch)
+  void* out;                     // [B, H, D] bf16, or fp32 when out_f32
+  int out_f32;
+  int B, H, KVH, S, D, window, n_chunks;
+  long long q_row, kv_row;       // elements between batch rows of q / of k_new and v_new
+  float scale;
+  int* status;
+};
+int launch_decode_attention(const DecodeAttnArgs& args, cudaStream_t stream);
+int decode_attn_chunks(int max_positions);
+
 int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat16* w,
                    int rows, int dim, float eps, cudaStream_t stream);
 int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream);
 int launch_rope(__nv_bfloat16* x, const __nv_bfloat16* cos_t, const __nv_bfloat16* sin_t,
                 int rows, int row_stride, int rot_cols, int head_dim, int seq_len, int start,
-                cudaStream_t stream);
+                const int* start_dev, int max_positions, int* status, cudaStream_t stream);
 // x_map: [T, d] bf16, box 128 rows x 64; w_map: [E, d] bf16, box
 // route_experts_padded(E) rows x 64 (rows past E read as zero).
 int launch_route(const RouteArgs& args, const CUtensorMap* x_map, const CUtensorMap* w_map,

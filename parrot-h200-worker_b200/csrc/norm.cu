@@ -264,11 +264,16 @@ int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream) {
 // c = cos[p][j], s = sin[p][j] (bf16 tables): every product and sum rounded
 // like the reference's bf16 tensor expression.  One thread per 8 columns.
 // ---------------------------------------------------------------------------
+// start_dev (optional) holds the first position in device memory (decode
+// steps replayed from a graph); a position past the tables is reported and
+// the row left unrotated.
 __global__ void __launch_bounds__(256) rope_kernel(__nv_bfloat16* __restrict__ x,
                                                    const __nv_bfloat16* __restrict__ cos_t,
                                                    const __nv_bfloat16* __restrict__ sin_t,
                                                    int rows, int row_stride, int rot_cols,
-                                                   int head_dim, int seq_len, int start) {
+                                                   int head_dim, int seq_len, int start,
+                                                   const int* start_dev, int max_positions,
+                                                   int* status) {
   griddep_wait();
   griddep_launch();
   const int vec_per_row = rot_cols >> 3;
@@ -276,7 +281,11 @@ __global__ void __launch_bounds__(256) rope_kernel(__nv_bfloat16* __restrict__ x
   if (i >= (long long)rows * vec_per_row) return;
   const int r = (int)(i / vec_per_row), v = (int)(i % vec_per_row);
   const int col = v * 8;
-  const int pos = start + r % seq_len;
+  const int pos = (start_dev != nullptr ? __ldg(start_dev) : start) + r % seq_len;
+  if (pos < 0 || pos >= max_positions) {
+    report_status(status, kStatusBadIndex, 41, pos);
+    return;
+  }
   const int j0 = (col % head_dim) >> 1;
   uint4* px = reinterpret_cast<uint4*>(x + (size_t)r * row_stride + col);
   float f[8];
@@ -297,13 +306,15 @@ __global__ void __launch_bounds__(256) rope_kernel(__nv_bfloat16* __restrict__ x
 
 int launch_rope(__nv_bfloat16* x, const __nv_bfloat16* cos_t, const __nv_bfloat16* sin_t,
                 int rows, int row_stride, int rot_cols, int head_dim, int seq_len, int start,
-                cudaStream_t stream) {
+                const int* start_dev, int max_positions, int* status, cudaStream_t stream) {
   const long long total = (long long)rows * (rot_cols / 8);
   if (total == 0) return 0;
   const int threads = 256;
   return launch_pdl(rope_kernel, dim3((unsigned)((total + threads - 1) / threads)),
                     dim3(threads), 0, stream, x, cos_t, sin_t, rows, row_stride, rot_cols,
-                    head_dim, seq_len, start) == cudaSuccess ? 0 : -2;
+                    head_dim, seq_len, start, start_dev, max_positions, status) == cudaSuccess
+             ? 0
+             : -2;
 }
 
 }  // namespace parrot

@@ -54,6 +54,14 @@ _SIGNATURES = {
                                      c_void_p, c_int, c_int, c_void_p]),
     "parrot_rope_inplace_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_int, c_int, c_int, c_int, c_void_p]),
+    "parrot_rope_inplace_at_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                            c_int, c_int, c_void_p, c_int, c_void_p, c_void_p]),
+    "parrot_decode_attention_bf16": (c_int, [c_void_p, c_int, c_void_p, c_int,
+                                             ctypes.c_longlong, c_void_p, c_void_p,
+                                             ctypes.c_longlong, c_void_p, c_void_p, c_void_p,
+                                             c_int, c_int, c_int, c_int, c_int, c_int, c_float,
+                                             c_void_p, c_size_t, c_void_p, c_void_p]),
+    "parrot_decode_attention_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "parrot_moe_capacity": (c_int, [c_int, c_int]),
     "parrot_moe_workspace_layout": (c_int, [POINTER(MoeDims), POINTER(MoeLayout)]),
     "parrot_moe_workspace_init": (c_int, [c_void_p, POINTER(MoeDims), c_void_p]),

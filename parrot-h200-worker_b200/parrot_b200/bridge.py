@@ -106,6 +106,52 @@ def b200_rope_(qkv: Tensor, cos: Tensor, sin: Tensor, rot_heads: int, head_dim: 
     return qkv
 
 
+def b200_rope_at_(qkv: Tensor, cos: Tensor, sin: Tensor, rot_heads: int, head_dim: int,
+                  position: Tensor, status: Tensor | None = None) -> Tensor:
+    """``b200_rope_`` for one decode position held in device memory (``position`` int32 [1])."""
+    _require_device(qkv, "RoPE")
+    b, t, width = qkv.shape
+    if not qkv.is_contiguous():
+        raise RuntimeError("b200_rope_at_ needs a contiguous projection output")
+    _lib.check(_lib.load().parrot_rope_inplace_at_bf16(
+        _p(qkv), _p(cos), _p(sin), b * t, width, rot_heads * head_dim, head_dim, t,
+        _p(position), cos.shape[0], _p(status), _stream()), "parrot_rope_inplace_at_bf16")
+    return qkv
+
+
+_DECODE_SCRATCH: dict = {}
+
+
+def b200_decode_attention(q: Tensor, k_new: Tensor, v_new: Tensor | None, k_cache: Tensor,
+                          v_cache: Tensor | None, position: Tensor, n_heads: int,
+                          n_kv_heads: int, head_dim: int, window: int, scale: float,
+                          out_dtype: torch.dtype) -> Tensor:
+    """One decode step of attention at the device ``position`` (``model.py:303-328, 399-432``).
+
+    ``q`` [B, n_heads * head_dim] (bf16, or fp32 for the absorbed MLA query) and
+    ``k_new`` / ``v_new`` [B, n_kv_heads * head_dim] may be row-strided views of
+    one projection.  The new key/value are appended to the caches at
+    ``position``; returns [B, n_heads * head_dim] in ``out_dtype``.
+    """
+    _require_device(k_cache, "decode attention")
+    b = q.shape[0]
+    s_max = k_cache.shape[-2]
+    lib = _lib.load()
+    key = (k_cache.device.index, b, n_heads, s_max, head_dim)
+    scratch = _DECODE_SCRATCH.get(key)
+    if scratch is None:
+        n = lib.parrot_decode_attention_scratch_bytes(b, n_heads, s_max, head_dim)
+        scratch = torch.empty(int(n), device=k_cache.device, dtype=torch.uint8)
+        _DECODE_SCRATCH[key] = scratch
+    out = torch.empty((b, n_heads * head_dim), device=q.device, dtype=out_dtype)
+    _lib.check(lib.parrot_decode_attention_bf16(
+        _p(out), int(out_dtype == torch.float32), _p(q), int(q.dtype == torch.float32), q.stride(0),
+        _p(k_new), _p(v_new), k_new.stride(0), _p(k_cache), _p(v_cache), _p(position), b,
+        n_heads, n_kv_heads, s_max, head_dim, window, float(scale), _p(scratch),
+        scratch.numel(), None, _stream()), "parrot_decode_attention_bf16")
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Block AttnRes depth mixing  (metal_moe.py:419-500)
 # ---------------------------------------------------------------------------

@@ -59,6 +59,57 @@ class GraphedForward:
         return self.output
 
 
+class GraphedDecode:
+    """``model.decode_step`` on a fixed ``GenerationState``, captured once and replayed.
+
+    The decode kernels read the position from ``state.position_device``, and
+    the step ends by incrementing it, so one graph serves every position:
+    ``__call__(ids)`` copies the [batch, 1] ids in, replays and advances
+    ``state.position``; it returns the captured logits (or next tokens with
+    ``next_token_only``), overwritten by the next call.  Decoding the same
+    state eagerly in between is fine; replacing its tensors is not.
+    """
+
+    def __init__(self, model, state, next_token_only: bool = False):
+        if model.training:
+            raise RuntimeError("capture requires model.eval()")
+        if state.position_device is None:
+            raise ValueError("the state has no device position (it did not come from prefill)")
+        self.model = model
+        self.state = state
+        self.next_token_only = next_token_only
+        device = state.position_device.device
+        self.input_ids = torch.zeros((state.batch_size, 1), dtype=torch.long, device=device)
+        position = state.position
+        side = torch.cuda.Stream(device=device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.inference_mode():
+            with torch.cuda.stream(side):
+                # warm-up step (allocates workspaces); its token is rewritten
+                # by the first real step at the same position
+                model.decode_step(self.input_ids, state, _next_token_only=next_token_only)
+                state.position_device.sub_(1)
+            torch.cuda.current_stream(device).wait_stream(side)
+            state.position = position
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self.output, _ = model.decode_step(self.input_ids, state,
+                                                   _next_token_only=next_token_only)
+            state.position = position  # capture ran the host code, not the kernels
+
+    def __call__(self, input_ids: Tensor):
+        state = self.state
+        if tuple(input_ids.shape) != tuple(self.input_ids.shape):
+            raise ValueError(f"captured for ids of shape {tuple(self.input_ids.shape)}, "
+                             f"got {tuple(input_ids.shape)}")
+        if state.position >= self.model.config.max_seq_len:
+            raise ValueError("Generation state has reached max_seq_len")
+        self.input_ids.copy_(input_ids, non_blocking=True)
+        self.graph.replay()
+        state.position += 1
+        return self.output
+
+
 def capture_calls(fn, repeats: int = 1) -> torch.cuda.CUDAGraph:
     """Capture ``repeats`` calls of ``fn()`` (after one eager warm-up call) in one graph."""
     fn()

@@ -118,6 +118,9 @@ class GenerationState:
     layers: list[LocalKVCache | MLALatentCache]
     position: int
     batch_size: int
+    # the same position as an int32 [1] device tensor: the decode kernels read
+    # it there, so one captured decode step replays at every position
+    position_device: Tensor | None = None
 
 
 @dataclass
@@ -242,11 +245,30 @@ class LocalGQA(nn.Module):
         return self.prefill(x)[0]
 
     def decode(self, x: Tensor, cache: LocalKVCache, position: int,
-               addend: Tensor | None = None, defer_sum: bool = False) -> Tensor:
+               addend: Tensor | None = None, defer_sum: bool = False,
+               position_device: Tensor | None = None) -> Tensor:
         if x.shape[1] != 1:
             raise ValueError("decode expects one model position")
         if defer_sum:
             raise RuntimeError("deferred attention reduction is not part of the b200 backend")
+        c = self.cfg
+        if position_device is not None:
+            # device-position path: RoPE, cache append and attention read the
+            # position from device memory (capturable)
+            b = x.shape[0]
+            w = _packed(self, "_qkv_weight", (self.q.weight, self.k.weight, self.v.weight))
+            qkv = F.linear(x, w)
+            cos, sin = _rope_tables(c, x.device, x.dtype)
+            bridge.b200_rope_at_(qkv, cos, sin, c.n_heads + c.n_kv_heads, c.head_dim,
+                                 position_device)
+            flat = qkv.view(b, -1)
+            qw, kw = c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim
+            y = bridge.b200_decode_attention(
+                flat[:, :qw], flat[:, qw:qw + kw], flat[:, qw + kw:], cache.key, cache.value,
+                position_device, c.n_heads, c.n_kv_heads, c.head_dim, c.window_size,
+                c.head_dim ** -0.5, x.dtype)
+            out = self.out(y.view(b, 1, -1))
+            return out if addend is None else addend + out
         q, k, v = self._qkv(x, position)
         cache.key[:, :, position:position + 1].copy_(k)
         cache.value[:, :, position:position + 1].copy_(v)
@@ -308,7 +330,8 @@ class GlobalMLA(nn.Module):
         return hit[1]
 
     def decode(self, x: Tensor, cache: MLALatentCache, position: int,
-               addend: Tensor | None = None, defer_sum: bool = False) -> Tensor:
+               addend: Tensor | None = None, defer_sum: bool = False,
+               position_device: Tensor | None = None) -> Tensor:
         if x.shape[1] != 1:
             raise ValueError("decode expects one model position")
         if defer_sum:
@@ -316,6 +339,16 @@ class GlobalMLA(nn.Module):
         c = self.cfg
         b = x.shape[0]
         aq, ao = self._absorbed()
+        if position_device is not None:
+            # absorbed latent attention at the device position (capturable):
+            # fp32 query over the bf16 latent cache, fp32 context (model.py:417-432)
+            latent = self.kv_down(x).view(b, -1)
+            q = F.linear(x.float(), aq.float()).view(b, -1)
+            ctx = bridge.b200_decode_attention(
+                q, latent, None, cache.latent.unsqueeze(1), None, position_device, c.n_heads, 1,
+                c.kv_latent_dim, 0, c.head_dim ** -0.5, torch.float32)
+            out = F.linear(ctx.view(b, 1, -1), ao.float()).to(x.dtype)
+            return out if addend is None else addend + out
         cache.latent[:, position:position + 1].copy_(self.kv_down(x))
         seen = cache.latent[:, :position + 1]
         q = F.linear(x.float(), aq.float()).view(b, 1, c.n_heads, c.kv_latent_dim).transpose(1, 2)
@@ -573,7 +606,8 @@ class Parrot(nn.Module):
             index += 1
         h = res.mix(self.depth_mix[-1], self.final_norm) if attnres else self.final_norm(x)
         logits = F.linear(h[:, -1:], self.embedding.weight)
-        return logits, GenerationState(caches, t, b)
+        position = torch.full((1,), t, device=logits.device, dtype=torch.int32)
+        return logits, GenerationState(caches, t, b, position)
 
     @torch.inference_mode()
     def decode_step(self, input_ids: Tensor, state: GenerationState, *,
@@ -602,7 +636,8 @@ class Parrot(nn.Module):
             elif not isinstance(cache, MLALatentCache):
                 raise ValueError("MLA attention received a local cache")
             addend = res.partial if attnres else None
-            delta = block.attention.decode(h, cache, state.position, addend=addend)
+            delta = block.attention.decode(h, cache, state.position, addend=addend,
+                                           position_device=state.position_device)
             if attnres:
                 res.set_partial(delta)
                 res.end_module(index)
@@ -620,12 +655,23 @@ class Parrot(nn.Module):
         h = res.mix(self.depth_mix[-1], self.final_norm) if attnres else self.final_norm(x)
         logits = F.linear(h, self.embedding.weight)
         state.position += 1
+        if state.position_device is not None:
+            state.position_device.add_(1)
         return (logits.argmax(-1) if _next_token_only else logits), state
 
     @torch.inference_mode()
     def decode_next(self, input_ids: Tensor, state: GenerationState):
         """Append one token and return the next greedy token (``model.py:927-931``)."""
         return self.decode_step(input_ids, state, _next_token_only=True)
+
+    def capture_decode(self, state: GenerationState, next_token_only: bool = False):
+        """CUDA-graph replay of ``decode_step`` (or ``decode_next``) on ``state``.
+
+        Returns a ``graphs.GraphedDecode``; each call appends one token to
+        ``state`` (whose caches and device position the graph captured).
+        """
+        from .graphs import GraphedDecode
+        return GraphedDecode(self, state, next_token_only)
 
     def capture(self, batch: int, source_len: int, **forward_kwargs):
         """CUDA-graph replay of ``forward`` for one input shape.

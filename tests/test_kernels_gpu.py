@@ -122,6 +122,45 @@ def test_depth_mix_pending_residual_resolves_the_add():
     assert torch.equal(got, plain)
 
 
+@pytest.mark.parametrize("mode,pos,batch", [("local", 0, 1), ("local", 127, 3), ("local", 128, 2),
+                                            ("local", 2300, 2), ("mla", 5, 2), ("mla", 700, 1)])
+def test_decode_attention_matches_sdpa(mode, pos, batch):
+    """parrot_decode_attention_bf16 at XL shapes against PyTorch SDPA on the
+    same cache contents: local GQA (8 heads x 96 over 2 KV heads, window
+    2048) and absorbed MLA (fp32 query over the 128-wide latent)."""
+    g = torch.Generator().manual_seed(pos + batch)
+    S = 4096
+    position = torch.full((1,), pos, device="cuda", dtype=torch.int32)
+    if mode == "local":
+        H, KVH, D, window = 8, 2, 96, 2048
+        kc = torch.randn(batch, KVH, S, D, generator=g).to("cuda", torch.bfloat16)
+        vc = torch.randn(batch, KVH, S, D, generator=g).to("cuda", torch.bfloat16)
+        qkv = torch.randn(batch, (H + 2 * KVH) * D, generator=g).to("cuda", torch.bfloat16)
+        qw, kw = H * D, KVH * D
+        q, kn, vn = qkv[:, :qw], qkv[:, qw:qw + kw], qkv[:, qw + kw:]
+        out = bridge.b200_decode_attention(q, kn, vn, kc, vc, position, H, KVH, D, window,
+                                           D ** -0.5, torch.bfloat16)
+        assert torch.equal(kc[:, :, pos], kn.view(batch, KVH, D))
+        assert torch.equal(vc[:, :, pos], vn.view(batch, KVH, D))
+        lo = max(0, pos - window + 1)
+        ref = torch.nn.functional.scaled_dot_product_attention(
+            q.view(batch, H, 1, D).float(), kc[:, :, lo:pos + 1].float(),
+            vc[:, :, lo:pos + 1].float(), enable_gqa=True).view(batch, H * D)
+        torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    else:
+        H, L, hd = 8, 128, 96
+        lat = torch.randn(batch, S, L, generator=g).to("cuda", torch.bfloat16)
+        q = (0.1 * torch.randn(batch, H * L, generator=g)).to("cuda")
+        new = torch.randn(batch, L, generator=g).to("cuda", torch.bfloat16)
+        out = bridge.b200_decode_attention(q, new, None, lat.unsqueeze(1), None, position, H, 1,
+                                           L, 0, hd ** -0.5, torch.float32)
+        assert torch.equal(lat[:, pos], new)
+        seen = lat[:, :pos + 1].float()[:, None].expand(-1, H, -1, -1)
+        ref = torch.nn.functional.scaled_dot_product_attention(
+            q.view(batch, H, 1, L), seen, seen, scale=hd ** -0.5).view(batch, H * L)
+        torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+
+
 # ---------------------------------------------------------------------------
 # Router, grouping and the whole MoE block
 # ---------------------------------------------------------------------------

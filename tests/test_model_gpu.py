@@ -139,6 +139,28 @@ def test_prefill_and_decode(batch):
     assert state.position == 145
 
 
+@pytest.mark.parametrize("next_only", [False, True])
+def test_graphed_decode_equals_eager(next_only):
+    """One captured decode step replayed at successive positions gives the
+    eager decode's outputs exactly (the window is exceeded along the way)."""
+    prod, _ = _pair(TINY, seed=12)
+    ids = torch.randint(0, 32768, (2, 134), generator=torch.Generator().manual_seed(13))
+    with torch.inference_mode():
+        _, eager_state = prod.prefill(ids[:, :126].cuda())
+        _, graph_state = prod.prefill(ids[:, :126].cuda())
+        graphed = prod.capture_decode(graph_state, next_token_only=next_only)
+        for step in range(8):
+            nxt = ids[:, 126 + step:127 + step]
+            if next_only:
+                want, eager_state = prod.decode_next(nxt.cuda(), eager_state)
+            else:
+                want, eager_state = prod.decode_step(nxt.cuda(), eager_state)
+            got = graphed(nxt)
+            assert torch.equal(got, want), step
+            assert graph_state.position == eager_state.position == 127 + step
+        assert int(graph_state.position_device.item()) == graph_state.position
+
+
 def test_xl_forward_1x512():
     """Parrot XL default, seed 0, bf16 forward on 1x512 ids."""
     prod, orc = _pair({}, seed=0)
