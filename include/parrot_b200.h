@@ -243,6 +243,19 @@ int parrot_moe_route_bf16(const parrot_moe_dims* dims, const parrot_moe_weights*
                           const void* x, const parrot_moe_outputs* outputs, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* The whole MoE block at decode batch sizes (tokens <= 16), in two kernels:
+ * every CTA routes all tokens, then computes 32 SwiGLU features of one
+ * expert for the tokens routed to it (the shared expert for all); a second
+ * kernel takes (token, 16 output columns) and produces the two routed down
+ * rows, the shared one and their combine (+ residual) exactly as
+ * parrot_moe_forward_bf16 rounds them.  Same arguments as
+ * parrot_moe_forward_bf16; outputs->positions / counts / stats must be NULL.
+ * Replaces model.py:571-585 (MoE.inference) at decode, and the Metal decode
+ * MoE lanes (metal_moe.py:182-221, moe_bf16.metal:898-1024). */
+int parrot_moe_decode_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                           const void* x, const parrot_moe_outputs* outputs, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* Expert GEMMs + shared expert + combine on a workspace filled by
  * parrot_moe_route_bf16 for the same x (metal_moe.py:372-416 after routing). */
 int parrot_moe_experts_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,

@@ -717,6 +717,45 @@ int parrot_moe_forward_bf16(const parrot_moe_dims* dims, const parrot_moe_weight
   return run_experts(dims, weights, x, outputs, workspace, L, s);
 }
 
+int parrot_moe_decode_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                           const void* x, const parrot_moe_outputs* outputs, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  int rc = prepare(dims, weights, x, outputs, workspace, workspace_bytes, &L);
+  if (rc) return rc;
+  if (dims->tokens > parrot::kDecodeMoeMaxTokens || dims->expert_dim > 1024 ||
+      dims->shared_dim > dims->expert_dim || dims->expert_dim % 32 || dims->shared_dim % 32)
+    return fail(PARROT_EINVAL, "moe_decode: tokens <= 16, shared_dim <= expert_dim <= 1024, "
+                               "both multiples of 32%s");
+  if (outputs->counts != nullptr || outputs->stats != nullptr || outputs->positions != nullptr)
+    return fail(PARROT_EINVAL, "moe_decode: no grouping, counts or statistics on this path%s");
+  if (dims->tokens == 0) return PARROT_OK;
+  parrot::MoeDecodeArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.router = static_cast<const __nv_bfloat16*>(weights->router);
+  a.router_bias = weights->router_bias;
+  a.gate_up = static_cast<const __nv_bfloat16*>(weights->gate_up);
+  a.down = static_cast<const __nv_bfloat16*>(weights->down);
+  a.shared_gate_up = static_cast<const __nv_bfloat16*>(weights->shared_gate_up);
+  a.shared_down = static_cast<const __nv_bfloat16*>(weights->shared_down);
+  a.hidden = at<__nv_bfloat16>(workspace, L.hidden);
+  a.indices = at<int>(workspace, L.indices);
+  a.weights = at<float>(workspace, L.weights);
+  a.probs = outputs->probs;
+  a.indices64 = outputs->indices;
+  a.weights_out = outputs->weights;
+  a.residual = static_cast<const __nv_bfloat16*>(outputs->residual);
+  a.out = static_cast<__nv_bfloat16*>(outputs->out);
+  a.tokens = dims->tokens;
+  a.dim = dims->dim;
+  a.n_experts = dims->n_experts;
+  a.expert_dim = dims->expert_dim;
+  a.shared_dim = dims->shared_dim;
+  if (parrot::launch_moe_decode(a, static_cast<cudaStream_t>(stream)))
+    return fail(PARROT_ECUDA, "moe_decode: launch failed%s");
+  return check_launch("moe_decode kernels");
+}
+
 int parrot_moe_gemm_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
                          const void* x, void* workspace, size_t workspace_bytes, int stage,
                          void* stream) {

@@ -136,6 +136,28 @@ struct GemmArgs {
   int* status;
 };
 
+// The MoE block at decode batch sizes (moe_decode.cu).
+constexpr int kDecodeMoeMaxTokens = 16;
+struct MoeDecodeArgs {
+  const __nv_bfloat16* x;            // [T, d]
+  const __nv_bfloat16* router;       // [E, d]
+  const float* router_bias;          // [E] or null
+  const __nv_bfloat16* gate_up;      // tiled packs (the grouped GEMM's)
+  const __nv_bfloat16* down;
+  const __nv_bfloat16* shared_gate_up;
+  const __nv_bfloat16* shared_down;
+  __nv_bfloat16* hidden;             // [T, 3, H] scratch: routed k = 0, 1, shared
+  int* indices;                      // [T, 2]
+  float* weights;                    // [T, 2]
+  float* probs;                      // [T, E] or null
+  long long* indices64;              // [T, 2] or null
+  float* weights_out;                // [T, 2] or null
+  const __nv_bfloat16* residual;     // [T, d] or null
+  __nv_bfloat16* out;                // [T, d]
+  int tokens, dim, n_experts, expert_dim, shared_dim;
+};
+int launch_moe_decode(const MoeDecodeArgs& args, cudaStream_t stream);
+
 // Single-token decode attention (decode.cu).
 struct DecodeAttnArgs {
   const void* q;                 // [B, H, D] bf16, or fp32 when q_f32

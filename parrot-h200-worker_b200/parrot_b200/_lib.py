@@ -72,6 +72,8 @@ _SIGNATURES = {
                                         POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
     "parrot_moe_forward_static_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                                POINTER(MoeOutputs), c_void_p]),
+    "parrot_moe_decode_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
+                                       POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
     "parrot_moe_route_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                       POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
     "parrot_moe_experts_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,

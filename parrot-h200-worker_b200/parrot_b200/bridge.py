@@ -300,6 +300,11 @@ def _router_bias(module) -> Tensor | None:
     return bias.to(device=module.router.weight.device, dtype=torch.float32).contiguous()
 
 
+# Up to this many flattened tokens (and without router statistics) b200_moe
+# takes the small-batch decode kernels instead of route/group/GEMM/combine.
+DECODE_MOE_MAX_TOKENS = 16
+
+
 def b200_moe(module, flat: Tensor, collect_stats: bool, addend: Tensor | None = None):
     """Whole MoE block on ``flat`` [T, d]: returns ``(out, aux, utilization)``.
 
@@ -326,9 +331,15 @@ def b200_moe(module, flat: Tensor, collect_stats: bool, addend: Tensor | None = 
                               None, None, None, None, None,
                               None if stats is None else stats.data_ptr())
     weights = _weights_struct(packed, bias)
-    _lib.check(_lib.load().parrot_moe_forward_bf16(
-        ctypes.byref(dims), ctypes.byref(weights), _p(flat), ctypes.byref(outputs),
-        _p(ws), ws.numel(), _stream()), "parrot_moe_forward_bf16")
+    if stats is None and 0 < T <= DECODE_MOE_MAX_TOKENS and cfg.expert_dim <= 1024:
+        # decode batch sizes: the two-kernel small-batch path
+        _lib.check(_lib.load().parrot_moe_decode_bf16(
+            ctypes.byref(dims), ctypes.byref(weights), _p(flat), ctypes.byref(outputs),
+            _p(ws), ws.numel(), _stream()), "parrot_moe_decode_bf16")
+    else:
+        _lib.check(_lib.load().parrot_moe_forward_bf16(
+            ctypes.byref(dims), ctypes.byref(weights), _p(flat), ctypes.byref(outputs),
+            _p(ws), ws.numel(), _stream()), "parrot_moe_forward_bf16")
     if stats is None:
         return out, None, None
     return out, stats[cfg.n_experts], stats[:cfg.n_experts]

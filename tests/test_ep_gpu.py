@@ -112,7 +112,8 @@ def test_expert_parallel_threads_equal_single_device_block(ranks, zipf):
             if sizes[r] == 0:
                 assert results[r][0].shape[0] == 0
                 continue
-            want, _, _ = bridge.b200_moe(module, xs, False,
+            # router statistics on: the tensor-core path at every shard size
+            want, _, _ = bridge.b200_moe(module, xs, True,
                                          residual[starts[r]:starts[r] + sizes[r]])
             torch.cuda.synchronize()
             assert torch.equal(results[r][0], want), f"rank {r}"
@@ -132,7 +133,7 @@ def _nccl_rank(rank, ranks, port, seed, tokens):
             layer = ep.ExpertParallelMoE(ep.B200EpOps(module, rank, ranks), ep.TorchComm(),
                                          module.cfg.n_experts)
             got = layer(xs)
-            want, _, _ = bridge.b200_moe(module, xs, False) if sizes[rank] else (got, 0, 0)
+            want, _, _ = bridge.b200_moe(module, xs, True) if sizes[rank] else (got, 0, 0)
             torch.cuda.synchronize()
             assert torch.equal(got, want), f"rank {rank}"
         dist.barrier()

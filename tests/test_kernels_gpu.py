@@ -161,6 +161,43 @@ def test_decode_attention_matches_sdpa(mode, pos, batch):
         torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("tokens,residual,zipf", [(1, False, False), (3, True, False),
+                                                   (8, True, True), (16, False, True)])
+def test_decode_moe_matches_oracle_and_gemm_path(tokens, residual, zipf):
+    """parrot_moe_decode_bf16 (small-batch path): routing equal to the oracle's
+    wherever its margin is resolvable, output within the bf16 contract of the
+    fp32 oracle and equal (bar accumulation-order rounding) to the
+    tensor-core path."""
+    cfg = moe_config()
+    prod, orc = build_moe_pair(cfg, seed=60 + tokens)
+    x = hidden_states(tokens, cfg.dim, seed=61 + tokens)
+    if zipf:
+        bias = torch.tensor([3.0, 2.0] + [0.0] * (cfg.n_experts - 2))
+        prod.router_bias = bias.cuda()
+        orc.router_bias = bias
+    res = hidden_states(tokens, cfg.dim, seed=62) if residual else None
+    xd = x.cuda()
+    got, _, _ = bridge.b200_moe(prod, xd, False, None if res is None else res.cuda())
+    dims = bridge.moe_dims(cfg, tokens)
+    layout = bridge.workspace_layout(dims)
+    ws = bridge.workspace(xd.device, dims)
+    idx = workspace_view(ws, layout, "indices", torch.int32, (tokens, 2)).cpu().long()
+    w = workspace_view(ws, layout, "weights", torch.float32, (tokens, 2)).cpu()
+    exp, _, _ = orc(x.float())
+    if res is not None:
+        exp = res.float() + exp
+    trace = orc.last_trace
+    top3 = trace.probabilities.topk(3, dim=-1).values
+    clear = torch.minimum(top3[:, 0] - top3[:, 1], top3[:, 1] - top3[:, 2]) > 1e-5
+    assert torch.equal(idx[clear], trace.indices[clear])
+    torch.testing.assert_close(w[clear], trace.weights[clear], rtol=1e-5, atol=1e-6)
+    assert_bf16_close(got, exp, "decode moe vs fp32 oracle")
+    # the tensor-core path on the same rows (stats on: it does not take the decode path)
+    gemm, _, _ = bridge.b200_moe(prod, xd, True, None if res is None else res.cuda())
+    st = err_stats(got, gemm)
+    assert st["rms_rel"] < 1e-2 and st["mixed"] < 2e-2, st
+
+
 # ---------------------------------------------------------------------------
 # Router, grouping and the whole MoE block
 # ---------------------------------------------------------------------------
