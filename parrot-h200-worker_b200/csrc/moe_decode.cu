@@ -1,23 +1,24 @@
-// The MoE block at decode batch sizes (a few tokens): two kernels instead of
-// router + grouping + two grouped GEMMs + combine.
+// The MoE block at decode batch sizes (a few tokens): three kernels instead
+// of router + grouping + two grouped GEMMs + combine.
 //
-// moe_decode_up_kernel:   every CTA routes all the tokens (fp32 logits of the
-//                         bf16 rows, softmax, top-2 with the lower id on ties,
-//                         renormalised weights; model.py:521-527) — the same
-//                         arithmetic in every CTA, so they agree — then takes 32
-//                         SwiGLU features of one expert (or of the shared
-//                         expert) for the tokens routed to it: one warp per
-//                         feature pair of rows streams the packed gate/up rows
-//                         once and dots them with every such token,
-//                         h = bf16(silu(bf16 gate) * bf16 up).  CTAs of experts
-//                         no token chose return after routing.
-// moe_decode_down_kernel: one CTA per (token, 16 output columns) computes the
-//                         token's two routed rows and the shared row,
-//                         y = bf16(down . h), and combines them exactly as the
-//                         reference's index_add sequence does:
-//                         out = [residual +] bf16(bf16(shared + c_lo) + c_hi),
-//                         c = bf16(y * bf16(w)), lower expert id first
-//                         (model.py:545-551).
+// moe_decode_route_kernel: one warp per token: fp32 logits of the bf16 row,
+//                          softmax, top-2 with the lower id on ties,
+//                          renormalised weights (model.py:521-527).
+// moe_decode_up_kernel:    work item = 16 SwiGLU features of one chosen
+//                          expert (ascending id; at most min(E, 2T) of them)
+//                          or of the shared expert: the CTA stages the
+//                          features' packed gate/up rows and the tokens routed
+//                          to that expert in shared memory with one round of
+//                          async copies, then one warp per feature dots both
+//                          rows with every such token,
+//                          h = bf16(silu(bf16 gate) * bf16 up).
+// moe_decode_down_kernel:  one CTA per (token, 16 output columns) stages the
+//                          token's two routed down rows, the shared one and its
+//                          hidden rows, computes y = bf16(down . h) and combines
+//                          them exactly as the reference's index_add sequence
+//                          does: out = [residual +] bf16(bf16(shared + c_lo) +
+//                          c_hi), c = bf16(y * bf16(w)), lower expert id first
+//                          (model.py:545-551).
 // The weights are the tiled packs the grouped GEMM streams (128 x 64 tiles).
 // All dot products accumulate in fp32; only their order differs from the
 // tensor-core path.  SiLU is computed as x / (1 + expf(-x)) in fp32, the
@@ -29,7 +30,7 @@ namespace parrot {
 
 namespace {
 constexpr int kTileRows = 128, kTileCols = 64;
-constexpr int kFeatPerCta = 32;   // SwiGLU features per up CTA (8 per warp)
+constexpr int kFeatPerCta = 16;   // SwiGLU features per up CTA (4 per warp)
 constexpr int kColsPerCta = 16;   // output columns per down CTA (4 per warp)
 
 // element (row, col) of matrix m in the tiled layout of a [rows, cols] matrix
@@ -40,133 +41,179 @@ __device__ __forceinline__ size_t tiled_index(int m, int row, int col, int rows,
 }
 }  // namespace
 
+// Router: one warp per token (lanes over d, every expert's dot reduced
+// together), softmax, top-2 with the lower id on ties, renormalised weights.
+__global__ void __launch_bounds__(128) moe_decode_route_kernel(MoeDecodeArgs a) {
+  extern __shared__ __align__(16) uint4 rw_s[];  // router weight [E][d / 8], then 4 token rows
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + warp;
+  const int d = a.dim, E = a.n_experts, nvec = d >> 3;
+  uint4* x_s = rw_s + (size_t)E * nvec;
+  // the router weight is a parameter: all of it in flight before the wait
+  for (int i = threadIdx.x; i < E * nvec; i += blockDim.x)
+    cp_async16(rw_s + i, reinterpret_cast<const uint4*>(a.router) + i);
+  griddep_wait();
+  griddep_launch();
+  const int t0 = blockIdx.x * 4, rows = min(4, a.tokens - t0);
+  for (int i = threadIdx.x; i < rows * nvec; i += blockDim.x)
+    cp_async16(x_s + i, reinterpret_cast<const uint4*>(a.x) + (size_t)t0 * nvec + i);
+  cp_async_wait_all();
+  __syncthreads();
+  if (t >= a.tokens) return;
+  float part[kMaxExperts];
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) part[e] = 0.f;
+  for (int c = lane; c < nvec; c += 32) {
+    float xf[8];
+    bf16x8_to_float(x_s[warp * nvec + c], xf);
+#pragma unroll
+    for (int e = 0; e < kMaxExperts; ++e) {
+      if (e < E) {
+        float wf[8];
+        bf16x8_to_float(rw_s[e * nvec + c], wf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) part[e] = fmaf(xf[j], wf[j], part[e]);
+      }
+    }
+  }
+  float logit = warp_reduce_many<kMaxExperts>(part, lane);  // lane e: expert e
+  const bool valid = lane < E;
+  if (valid && a.router_bias != nullptr) logit += __ldg(a.router_bias + lane);
+  const float m = warp_max(valid ? logit : -INFINITY);
+  const float ev = valid ? expf(logit - m) : 0.f;
+  const float p = ev / warp_sum(ev);
+  float v1 = valid ? p : -1.f;
+  int i1 = lane;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v1, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i1, o);
+    if (ov > v1 || (ov == v1 && oi < i1)) { v1 = ov; i1 = oi; }
+  }
+  float v2 = (valid && lane != i1) ? p : -1.f;
+  int i2 = lane;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v2, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i2, o);
+    if (ov > v2 || (ov == v2 && oi < i2)) { v2 = ov; i2 = oi; }
+  }
+  if (valid && a.probs != nullptr) a.probs[(size_t)t * E + lane] = p;
+  if (lane == 0) {
+    const float sel = v1 + v2;
+    const float w1 = v1 / sel, w2 = v2 / sel;
+    a.indices[2 * t] = i1;
+    a.indices[2 * t + 1] = i2;
+    a.weights[2 * t] = w1;
+    a.weights[2 * t + 1] = w2;
+    if (a.indices64 != nullptr) {
+      a.indices64[2 * t] = i1;
+      a.indices64[2 * t + 1] = i2;
+    }
+    if (a.weights_out != nullptr) {
+      a.weights_out[2 * t] = w1;
+      a.weights_out[2 * t + 1] = w2;
+    }
+  }
+}
+
+// Gate/up + SwiGLU.  Work item c: feature block c % blocks of the
+// (c / blocks)-th chosen expert in ascending id, or of the shared expert after
+// the routed items; a CTA past the chosen experts' items returns at once.
 __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
-  __shared__ __align__(16) __nv_bfloat16 x_s[kDecodeMoeMaxTokens][1024];
-  __shared__ int idx_s[kDecodeMoeMaxTokens][2];
-  __shared__ float w_s[kDecodeMoeMaxTokens][2];
+  // [2 * kFeatPerCta rows][d / 8] gate/up rows, then [tokens][d / 8] token rows
+  extern __shared__ __align__(16) uint4 wrows_s[];
   __shared__ int list_s[kDecodeMoeMaxTokens];   // tokens this CTA serves
   __shared__ int slot_s[kDecodeMoeMaxTokens];   // their hidden slot (0, 1: routed k; 2: shared)
-  __shared__ int n_list;
+  __shared__ int n_list, expert_s;
   const int T = a.tokens, d = a.dim, E = a.n_experts, H = a.expert_dim, Hs = a.shared_dim;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nvec = d >> 3;
+  uint4* x_s = wrows_s + (size_t)2 * kFeatPerCta * nvec;
+  const int routed_blocks = H / kFeatPerCta;
+  const int max_chosen = min(E, 2 * T);
+  const bool shared = (int)blockIdx.x >= max_chosen * routed_blocks;
+  const int f0 = (shared ? (int)blockIdx.x - max_chosen * routed_blocks
+                         : (int)blockIdx.x % routed_blocks) * kFeatPerCta;
+  if (shared) {
+    // the shared expert's rows depend on nothing upstream: fetch them now
+    for (int i = threadIdx.x; i < 2 * kFeatPerCta * nvec; i += blockDim.x) {
+      const int r = i / nvec, c = i - r * nvec;
+      const int f = f0 + (r >> 1);
+      const int row = (f / 64) * kTileRows + 2 * (f % 64) + (r & 1);
+      cp_async16(wrows_s + i, a.shared_gate_up + tiled_index(0, row, c * 8, 2 * Hs, d));
+    }
+  }
   griddep_wait();
   griddep_launch();
-  for (int i = threadIdx.x; i < T * nvec; i += blockDim.x) {
-    const int t = i / nvec, c = i - t * nvec;
-    reinterpret_cast<uint4*>(&x_s[t][0])[c] = __ldg(reinterpret_cast<const uint4*>(a.x) + (size_t)t * nvec + c);
-  }
+  __shared__ int ids_s[2 * kDecodeMoeMaxTokens];
+  if (threadIdx.x < 2 * T) ids_s[threadIdx.x] = a.indices[threadIdx.x];  // one parallel load
   __syncthreads();
-
-  // 1. routing, one warp per token (lanes over d, all experts reduced together)
-  for (int t = warp; t < T; t += 4) {
-    float part[kMaxExperts];
-#pragma unroll
-    for (int e = 0; e < kMaxExperts; ++e) part[e] = 0.f;
-    for (int c = lane; c < nvec; c += 32) {
-      float xf[8];
-      bf16x8_to_float(reinterpret_cast<const uint4*>(&x_s[t][0])[c], xf);
-#pragma unroll
-      for (int e = 0; e < kMaxExperts; ++e) {
-        if (e < E) {
-          float wf[8];
-          bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.router + (size_t)e * d) + c), wf);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) part[e] = fmaf(xf[j], wf[j], part[e]);
-        }
-      }
-    }
-    float logit = warp_reduce_many<kMaxExperts>(part, lane);  // lane e: expert e
-    const bool valid = lane < E;
-    if (valid && a.router_bias != nullptr) logit += __ldg(a.router_bias + lane);
-    const float m = warp_max(valid ? logit : -INFINITY);
-    const float ev = valid ? expf(logit - m) : 0.f;
-    const float p = ev / warp_sum(ev);
-    float v1 = valid ? p : -1.f;
-    int i1 = lane;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, v1, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, i1, o);
-      if (ov > v1 || (ov == v1 && oi < i1)) { v1 = ov; i1 = oi; }
-    }
-    float v2 = (valid && lane != i1) ? p : -1.f;
-    int i2 = lane;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, v2, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, i2, o);
-      if (ov > v2 || (ov == v2 && oi < i2)) { v2 = ov; i2 = oi; }
-    }
-    if (lane == 0) {
-      const float sel = v1 + v2;
-      idx_s[t][0] = i1;
-      idx_s[t][1] = i2;
-      w_s[t][0] = v1 / sel;
-      w_s[t][1] = v2 / sel;
-    }
-    if (blockIdx.x == 0) {  // one CTA publishes the decisions
-      if (valid && a.probs != nullptr) a.probs[(size_t)t * E + lane] = p;
-      if (lane == 0) {
-        const float sel = v1 + v2;
-        a.indices[2 * t] = i1;
-        a.indices[2 * t + 1] = i2;
-        a.weights[2 * t] = v1 / sel;
-        a.weights[2 * t + 1] = v2 / sel;
-        if (a.indices64 != nullptr) {
-          a.indices64[2 * t] = i1;
-          a.indices64[2 * t + 1] = i2;
-        }
-        if (a.weights_out != nullptr) {
-          a.weights_out[2 * t] = v1 / sel;
-          a.weights_out[2 * t + 1] = v2 / sel;
-        }
-      }
-    }
-  }
-  __syncthreads();
-
-  // 2. this CTA's expert and features, and the tokens that need them
-  const int routed_ctas = E * (H / kFeatPerCta);
-  const bool shared = (int)blockIdx.x >= routed_ctas;
-  const int e = shared ? -1 : (int)blockIdx.x / (H / kFeatPerCta);
-  const int f0 = (shared ? (int)blockIdx.x - routed_ctas : (int)blockIdx.x % (H / kFeatPerCta)) *
-                 kFeatPerCta;
   if (threadIdx.x == 0) {
-    int n = 0;
-    for (int t = 0; t < T; ++t) {
-      const int k = shared ? 2 : (idx_s[t][0] == e ? 0 : (idx_s[t][1] == e ? 1 : -1));
-      if (k >= 0) {
-        list_s[n] = t;
-        slot_s[n] = k;
-        ++n;
-      }
+    int e = -1;
+    if (!shared) {
+      // the (blockIdx / blocks)-th distinct chosen expert, ascending id
+      unsigned mask = 0;
+      for (int i = 0; i < 2 * T; ++i) mask |= 1u << ids_s[i];
+      const int want = (int)blockIdx.x / routed_blocks;
+      for (int x = 0, seen = 0; x < E; ++x)
+        if (mask & (1u << x)) {
+          if (seen == want) e = x;
+          ++seen;
+        }
     }
+    int n = 0;
+    if (shared || e >= 0)
+      for (int t = 0; t < T; ++t) {
+        const int k = shared ? 2 : (ids_s[2 * t] == e ? 0 : (ids_s[2 * t + 1] == e ? 1 : -1));
+        if (k >= 0) {
+          list_s[n] = t;
+          slot_s[n] = k;
+          ++n;
+        }
+      }
     n_list = n;
+    expert_s = e;
   }
   __syncthreads();
   const int n = n_list;
-  if (n == 0) return;
-  const int hid = shared ? Hs : H;
-  const __nv_bfloat16* gu = shared ? a.shared_gate_up : a.gate_up;
-  const int m = shared ? 0 : e;
+  if (n == 0) {
+    cp_async_wait_all();  // nothing may be in flight when the CTA exits
+    return;
+  }
+  if (!shared) {
+    const int e = expert_s;
+    for (int i = threadIdx.x; i < 2 * kFeatPerCta * nvec; i += blockDim.x) {
+      const int r = i / nvec, c = i - r * nvec;
+      const int f = f0 + (r >> 1);
+      const int row = (f / 64) * kTileRows + 2 * (f % 64) + (r & 1);
+      cp_async16(wrows_s + i, a.gate_up + tiled_index(e, row, c * 8, 2 * H, d));
+    }
+  }
+  for (int i = threadIdx.x; i < n * nvec; i += blockDim.x) {
+    const int li = i / nvec, c = i - li * nvec;
+    cp_async16(x_s + i, reinterpret_cast<const uint4*>(a.x) + (size_t)list_s[li] * nvec + c);
+  }
+  cp_async_wait_all();
+  __syncthreads();
 
-  // 3. gate and up rows of each feature, dotted with every listed token
+  // each feature's gate and up rows, dotted with every listed token
   for (int fi = warp; fi < kFeatPerCta; fi += 4) {
     const int f = f0 + fi;
-    const int row_g = (f / 64) * kTileRows + 2 * (f % 64), row_u = row_g + 1;
+    const uint4* g_row = wrows_s + (size_t)(2 * fi) * nvec;
+    const uint4* u_row = g_row + nvec;
     float acc_g[kDecodeMoeMaxTokens], acc_u[kDecodeMoeMaxTokens];
 #pragma unroll
     for (int i = 0; i < kDecodeMoeMaxTokens; ++i) acc_g[i] = acc_u[i] = 0.f;
     for (int c = lane; c < nvec; c += 32) {
       float gf[8], uf[8];
-      bf16x8_to_float(*reinterpret_cast<const uint4*>(gu + tiled_index(m, row_g, c * 8, 2 * hid, d)), gf);
-      bf16x8_to_float(*reinterpret_cast<const uint4*>(gu + tiled_index(m, row_u, c * 8, 2 * hid, d)), uf);
+      bf16x8_to_float(g_row[c], gf);
+      bf16x8_to_float(u_row[c], uf);
 #pragma unroll
       for (int i = 0; i < kDecodeMoeMaxTokens; ++i) {
         if (i < n) {
           float xf[8];
-          bf16x8_to_float(reinterpret_cast<const uint4*>(&x_s[list_s[i]][0])[c], xf);
+          bf16x8_to_float(x_s[(size_t)i * nvec + c], xf);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             acc_g[i] = fmaf(gf[j], xf[j], acc_g[i]);
@@ -190,32 +237,47 @@ __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
 }
 
 __global__ void __launch_bounds__(128) moe_decode_down_kernel(MoeDecodeArgs a) {
+  // [3][kColsPerCta rows][hid / 8]: routed k = 0, 1 (H wide), shared (Hs wide)
+  extern __shared__ __align__(16) uint4 drows_s[];
   __shared__ __align__(16) __nv_bfloat16 h_s[3][1024];
   const int d = a.dim, H = a.expert_dim, Hs = a.shared_dim;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col_blocks = d / kColsPerCta;
   const int t = blockIdx.x / col_blocks, o0 = (blockIdx.x % col_blocks) * kColsPerCta;
+  const int hv = H / 8, hsv = Hs / 8;
+  uint4* rows[3] = {drows_s, drows_s + kColsPerCta * hv, drows_s + 2 * kColsPerCta * hv};
+  // the shared expert's rows do not depend on the routing: fetch them first
+  for (int i = threadIdx.x; i < kColsPerCta * hsv; i += blockDim.x) {
+    const int r = i / hsv, c = i - r * hsv;
+    cp_async16(rows[2] + i, a.shared_down + tiled_index(0, o0 + r, c * 8, d, Hs));
+  }
   griddep_wait();
   griddep_launch();
   const int e0 = a.indices[2 * t], e1 = a.indices[2 * t + 1];
   const float w0 = round_bf16(a.weights[2 * t]), w1 = round_bf16(a.weights[2 * t + 1]);
+  for (int i = threadIdx.x; i < 2 * kColsPerCta * hv; i += blockDim.x) {
+    const int k = i / (kColsPerCta * hv), rem = i - k * (kColsPerCta * hv);
+    const int r = rem / hv, c = rem - r * hv;
+    cp_async16(rows[k] + rem, a.down + tiled_index(k == 0 ? e0 : e1, o0 + r, c * 8, d, H));
+  }
   for (int i = threadIdx.x; i < (2 * H + Hs) / 8; i += blockDim.x) {
     const int k = i < H / 4 ? i / (H / 8) : 2;
     const int c = k < 2 ? i - k * (H / 8) : i - H / 4;
-    reinterpret_cast<uint4*>(&h_s[k][0])[c] =
-        reinterpret_cast<const uint4*>(a.hidden + ((size_t)t * 3 + k) * H)[c];
+    cp_async16(reinterpret_cast<uint4*>(&h_s[k][0]) + c,
+               reinterpret_cast<const uint4*>(a.hidden + ((size_t)t * 3 + k) * H) + c);
   }
+  cp_async_wait_all();
   __syncthreads();
   for (int oi = warp; oi < kColsPerCta; oi += 4) {
     const int o = o0 + oi;
     float y[3] = {0.f, 0.f, 0.f};
+#pragma unroll
     for (int k = 0; k < 3; ++k) {
-      const int hid = k < 2 ? H : Hs;
-      const __nv_bfloat16* dn = k < 2 ? a.down : a.shared_down;
-      const int mat = k == 0 ? e0 : (k == 1 ? e1 : 0);
-      for (int c = lane; c < hid / 8; c += 32) {
+      const int nv = k < 2 ? hv : hsv;
+      const uint4* wr = rows[k] + (size_t)oi * nv;
+      for (int c = lane; c < nv; c += 32) {
         float wf[8], hf[8];
-        bf16x8_to_float(*reinterpret_cast<const uint4*>(dn + tiled_index(mat, o, c * 8, d, hid)), wf);
+        bf16x8_to_float(wr[c], wf);
         bf16x8_to_float(reinterpret_cast<const uint4*>(&h_s[k][0])[c], hf);
 #pragma unroll
         for (int j = 0; j < 8; ++j) y[k] = fmaf(wf[j], hf[j], y[k]);
@@ -234,11 +296,36 @@ __global__ void __launch_bounds__(128) moe_decode_down_kernel(MoeDecodeArgs a) {
 
 int launch_moe_decode(const MoeDecodeArgs& a, cudaStream_t stream) {
   if (a.tokens == 0) return 0;
-  const int up_ctas = a.n_experts * (a.expert_dim / kFeatPerCta) + a.shared_dim / kFeatPerCta;
-  if (launch_pdl(moe_decode_up_kernel, dim3(up_ctas), dim3(128), 0, stream, a) != cudaSuccess)
+  const size_t up_smem = (size_t)(2 * kFeatPerCta + a.tokens) * a.dim * 2;
+  const size_t down_smem = (size_t)kColsPerCta * (2 * a.expert_dim + a.shared_dim) * 2;
+  static unsigned long long configured = 0;  // per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
+  if (!(configured & (1ull << dev))) {
+    if (cudaFuncSetAttribute(moe_decode_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (kMaxExperts + 4) * 1024 * 2) != cudaSuccess ||
+        cudaFuncSetAttribute(moe_decode_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (2 * kFeatPerCta + kDecodeMoeMaxTokens) * 1024 * 2) != cudaSuccess ||
+        cudaFuncSetAttribute(moe_decode_up_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
+        cudaFuncSetAttribute(moe_decode_down_kernel,
+                             cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
+        cudaFuncSetAttribute(moe_decode_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kColsPerCta * 3 * 1024 * 2) != cudaSuccess)
+      return -2;
+    configured |= 1ull << dev;
+  }
+  const int max_chosen = a.n_experts < 2 * a.tokens ? a.n_experts : 2 * a.tokens;
+  const int up_ctas = max_chosen * (a.expert_dim / kFeatPerCta) + a.shared_dim / kFeatPerCta;
+  const size_t route_smem = (size_t)(a.n_experts + 4) * a.dim * 2;
+  if (launch_pdl(moe_decode_route_kernel, dim3((a.tokens + 3) / 4), dim3(128), route_smem, stream,
+                 a) != cudaSuccess ||
+      launch_pdl(moe_decode_up_kernel, dim3(up_ctas), dim3(128), up_smem, stream, a) !=
+          cudaSuccess)
     return -2;
-  return launch_pdl(moe_decode_down_kernel, dim3(a.tokens * (a.dim / kColsPerCta)), dim3(128), 0,
-                    stream, a) == cudaSuccess
+  return launch_pdl(moe_decode_down_kernel, dim3(a.tokens * (a.dim / kColsPerCta)), dim3(128),
+                    down_smem, stream, a) == cudaSuccess
              ? 0
              : -2;
 }
