@@ -193,13 +193,22 @@ int parrot_moe_workspace_layout(const parrot_moe_dims* dims, parrot_moe_layout* 
 int parrot_moe_workspace_init(void* workspace, const parrot_moe_dims* dims, void* stream);
 
 /* Pack gate/up for the fused SwiGLU GEMM.  Logical packed row p of matrix m
- * is gate (p even) or up (p odd) of feature (p / 128) * 64 + (p % 128) / 2;
+ * is gate (p % 16 < 8) or up of feature (p / 128) * 64 + (p % 128) / 16 * 8 +
+ * p % 8 (within each 16-row group: 8 gate rows, then the same features' up);
  * rows are stored as 128-row x 64-column tiles, each a contiguous 16 KB block,
  * ordered (m, row tile, column slab).  gate, up: [n_mats, hidden, dim];
  * dst: n_mats * 2 * hidden * dim elements; hidden % 64 == 0, dim % 64 == 0.
  * Replaces the weight packing of metal_moe.py:105-131 (pack_combined_weights). */
 int parrot_pack_gate_up_bf16(void* dst, const void* gate, const void* up, int n_mats, int hidden,
                              int dim, void* stream);
+
+/* Elementwise bf16 SiLU exactly as the SwiGLU epilogue of the expert GEMMs
+ * evaluates it: y = bf16(x / (1 + expf(-x))) in fp32, the value PyTorch's
+ * F.silu gives for a bf16 tensor (parrot/model.py:448 and :460,
+ * Expert.forward / SharedExpert.forward).  x, y: n bf16 values.  The epilogue
+ * takes a fast path for almost every input and reads a 65,536-entry table for
+ * the rest; this entry runs the same code so it can be checked exhaustively. */
+int parrot_silu_bf16(const void* x, void* y, int64_t n, void* stream);
 
 /* Pack [n_mats, rows, cols] (down projections, [d, H]) into the same tiled
  * layout: 128 x 64 tiles ordered (m, row tile, column slab).

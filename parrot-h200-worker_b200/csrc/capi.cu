@@ -676,6 +676,15 @@ int parrot_pack_gate_up_bf16(void* dst, const void* gate, const void* up, int n_
   return check_launch("pack_gate_up_kernel");
 }
 
+int parrot_silu_bf16(const void* x, void* y, int64_t n, void* stream) {
+  if (n < 0 || n > INT32_MAX || (n > 0 && (!x || !y)))
+    return fail(PARROT_EINVAL, "silu: bad arguments (n out of range or NULL buffer)%s");
+  if (parrot::launch_silu_bf16(static_cast<const uint16_t*>(x), static_cast<uint16_t*>(y), (int)n,
+                               static_cast<cudaStream_t>(stream)) != 0)
+    return fail(PARROT_ECUDA, "silu: building the SiLU table failed%s");
+  return check_launch("silu_bf16_kernel");
+}
+
 int parrot_pack_down_bf16(void* dst, const void* src, int n_mats, int rows, int cols,
                           void* stream) {
   if (!dst || !src || n_mats <= 0 || rows <= 0 || rows % 128 || cols <= 0 || cols % 64)

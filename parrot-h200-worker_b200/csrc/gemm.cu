@@ -11,17 +11,24 @@
 // expert, which matters because routing is often skewed (an expert can take
 // most of a batch while others are empty).
 //
-// Roles (192 threads, one CTA per SM):
+// Roles (320 threads, one CTA per SM):
 //   warp 0      TMA producer: 128-byte-swizzled K slabs of W and X into a
-//               4-stage shared-memory ring (no multicast anywhere).
+//               4- or 5-stage shared-memory ring (no multicast anywhere).
 //   warp 1      TMEM allocator + single-thread MMA issuer; tcgen05.commit
 //               frees ring stages and publishes finished accumulators.
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, then
-//               SwiGLU mode:  weight rows are packed (gate_j, up_j) pairs, so
-//                             lanes 2i / 2i+1 hold gate / up of one feature;
-//                             h = bf16(silu_lut[bf16 g] * bf16 u)
-//               plain mode:   y = bf16(acc)
-//               staged through shared memory into row-major bf16 output.
+//   warps 2..9  epilogue: warps w and w + 4 read TMEM lane quarter w % 4 and
+//               take alternate 32-column (token) chunks; the loads of the next
+//               chunk are in flight while the current one is converted.  A
+//               chunk is read as two 16-lane fragments (tcgen05.ld .16x256b),
+//               so each thread holds two adjacent tokens of a feature:
+//               SwiGLU mode:  each 16-row group of the weight tile is 8 gate
+//                             rows then the same 8 features' up rows, so a
+//                             thread holds gate and up of one feature:
+//                             h = bf16(silu(bf16 g) * bf16 u)
+//               plain mode:   y = bf16(acc) (routed: bf16(bf16(y) * bf16(w)))
+//               packed two per register, written transposed (token-major) into
+//               the warp's own shared-memory tile by stmatrix, and copied out
+//               as 16-byte vectors (scattered rows: one destination per token).
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of one unit run
 // under the MMAs of the next.
 //
@@ -49,8 +56,9 @@ constexpr int kSubRows = kGemmSubRows;        // 64-row activation boxes
 constexpr int kTileA = BM * BK * 2;           // 16 KB
 constexpr int kSubBytes = kSubRows * BK * 2;  // 8 KB
 constexpr int kChunk = 32;                    // TMEM columns per epilogue step
-constexpr int kStaging = kChunk * BM * 2;     // 32 tokens x 128 features bf16
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                  // two per TMEM lane quarter
+constexpr int kEpiTile = 32 * 64;             // per-warp staging: 32 tokens x 32 features bf16
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSegMax = 2 * kMaxExperts;
 
 // Token tile BN (128 or 256 rows): the ring holds 5 stages of 16 + 16 KB or
@@ -61,7 +69,7 @@ constexpr int stages_for() {
 }
 
 template <int BN>
-struct __align__(8) SmemTail {
+struct __align__(16) SmemTail {
   uint64_t full[stages_for<BN>()];
   uint64_t empty[stages_for<BN>()];
   uint64_t tfull[2];
@@ -73,8 +81,8 @@ struct __align__(8) SmemTail {
   int has_primary;      // this CTA's schedule: primary unit present,
   int rank;             // its position in the round-robin over other units
   int n_secondary;      // and how many such units exist
-  int unit_dst[BN];     // plain-mode scatter: destination row of each token row
-  float unit_w[BN];     // and its route weight
+  alignas(16) int unit_dst[BN];  // plain-mode scatter: destination row of each token row
+  alignas(16) float unit_w[BN];  // and its route weight (read as 16-byte vectors)
   int prefix[kSegMax + 2];
   int seg_rows[kSegMax];
   int seg_base[kSegMax];
@@ -83,11 +91,13 @@ struct __align__(8) SmemTail {
 
 template <int BN>
 constexpr size_t smem_bytes() {
-  return 1024 + (size_t)stages_for<BN>() * (kTileA + BN * BK * 2) + 2 * kStaging +
+  return 1024 + (size_t)stages_for<BN>() * (kTileA + BN * BK * 2) + kEpiWarps * kEpiTile +
          sizeof(SmemTail<BN>);
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
+}
 
 struct Unit {
   bool routed;
@@ -185,6 +195,44 @@ __global__ void build_silu_lut_kernel() {
   silu_lut[i] = __float2bfloat16_rn(x / (1.0f + expf(-x)));
 }
 
+// The same bf16 SiLU without a table read for almost every input.  A table
+// lookup per element is a 32-lane gather over 128 KB: nearly one L1
+// wavefront per lane, which made the SwiGLU epilogue L1-bound.  Instead
+//   y = x * rcp.approx(1 + ex2.approx(-x * log2 e))
+// is within 2^-17 (relative) of the exactly evaluated x / (1 + expf(-x)) for
+// 2^-20 <= |x| <= 64 (the ex2 argument carries |x| * 2^-24 of rounding error,
+// ex2 and rcp a few ulps each), i.e. within about 100 float ulps; when y is
+// more than 256 ulps away from the bf16 rounding midpoint both round to the
+// same bf16.  Inputs outside the range, and the ~1% of results near a
+// midpoint, read the table.  silu_bf16_fast() is checked against PyTorch's
+// bf16 SiLU for all 65,536 inputs.
+struct SiluFast {
+  uint16_t bits;
+  bool exact;  // false: read silu_lut instead
+};
+
+__device__ __forceinline__ SiluFast silu_bf16_fast(uint16_t xb) {
+  const float x = __uint_as_float((uint32_t)xb << 16);
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * -1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  const uint32_t yb = __float_as_uint(x * r);
+  const float ax = fabsf(x);
+  const bool near_mid = ((yb & 0xFFFFu) - (0x8000u - 256u)) < 512u;
+  SiluFast out;
+  out.bits = (uint16_t)((yb + 0x8000u) >> 16);
+  out.exact = ax >= 0x1p-20f && ax <= 64.0f && !near_mid;
+  return out;
+}
+
+__global__ void silu_bf16_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint16_t xb = x[i];
+  const SiluFast f = silu_bf16_fast(xb);
+  y[i] = f.exact ? f.bits : __bfloat16_as_ushort(silu_lut[xb]);
+}
+
 
 
 template <int BN>
@@ -201,8 +249,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* tiles_a = base;
   unsigned char* tiles_b = base + kStages * kTileA;
-  unsigned char* staging = tiles_b + kStages * kTileB;
-  SmemTail<BN>& t = *reinterpret_cast<SmemTail<BN>*>(staging + 2 * kStaging);
+  unsigned char* epi_tiles = tiles_b + kStages * kTileB;
+  SmemTail<BN>& t = *reinterpret_cast<SmemTail<BN>*>(epi_tiles + kEpiWarps * kEpiTile);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_seg = g.n_seg;
@@ -214,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&t.tfull[a], 1);
-      mbar_init(&t.tempty[a], 4);
+      mbar_init(&t.tempty[a], kEpiWarps);
     }
     mbar_init(&t.drain, 1);
     t.abort = 0;
@@ -316,8 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      bool issued[kStages] = {};
-      uint32_t issued_phase[kStages] = {};
+      uint32_t issued = 0, issued_phase = 0;  // per-stage bits
       bool ok = true;
       Unit un;
       for (int k = 0; ok && cta_unit<BN>(k, g, t, un); ++k) {
@@ -325,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* mx = un.routed ? &tm_x_routed : &tm_x_shared;
         const int subs = max(1, (un.valid + kSubRows - 1) / kSubRows);
         for (int kb = 0; kb < un.k_blocks; ++kb) {
-          if (!mbar_wait(&t.empty[stage], phase ^ 1, abort_flag, g.status, 10)) {
+          if (!mbar_wait_fast(&t.empty[stage], phase ^ 1, abort_flag, g.status, 10)) {
             ok = false;
             break;
           }
@@ -334,8 +381,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int sb = 0; sb < subs; ++sb)
             tma_load_2d(tiles_b + stage * kTileB + sb * kSubBytes, mx, kb * BK,
                         un.x_row + sb * kSubRows, &t.full[stage]);
-          issued[stage] = true;
-          issued_phase[stage] = phase;
+          issued |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1;
@@ -344,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // every issued copy has landed before the CTA can exit
       for (int s = 0; s < kStages; ++s)
-        if (issued[s]) mbar_drain(&t.full[s], issued_phase[s]);
+        if (issued & (1u << s)) mbar_drain(&t.full[s], (issued_phase >> s) & 1u);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -362,22 +409,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem + acc * BN;
         const int n = max(16, (un.valid + 15) & ~15);  // an empty expert still drains its slabs
         const uint32_t idesc = make_idesc(BM, n);
+        static_assert(BK == 64, "one slab = four K = 16 MMAs");
         for (int kb = 0; kb < un.k_blocks; ++kb) {
-          if (!mbar_wait(&t.full[stage], phase, abort_flag, g.status, 21)) {
+          if (!mbar_wait_fast(&t.full[stage], phase, abort_flag, g.status, 21)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t da = sw128_desc(tiles_a + stage * kTileA);
-          const uint64_t db = sw128_desc(tiles_b + stage * kTileB);
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          mma_slab(d_tmem, sw128_desc(tiles_a + stage * kTileA),
+                   sw128_desc(tiles_b + stage * kTileB), idesc, kb != 0);
           mma_commit(&t.empty[stage]);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1;
-          }
+          stage = stage + 1 == kStages ? 0 : stage + 1;
+          phase ^= stage == 0 ? 1u : 0u;
         }
         if (!ok) break;
         mma_commit(&t.tfull[acc]);
@@ -390,19 +433,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..9) ----------------
     const int q = warp & 3;                 // TMEM lane quarter of this warp
-    const int et = threadIdx.x - 64;        // 0..127
+    const int half = (warp - 2) >> 2;       // which alternate chunks it takes
+    const int et = threadIdx.x - 64;        // 0..255
+    const uint32_t tile_s = smem_u32(epi_tiles + (warp - 2) * kEpiTile);
+    const unsigned char* tile_p = epi_tiles + (warp - 2) * kEpiTile;
+    const int tq = lane & 3;                // this thread's token pair within 8 columns
     int acc = 0;
     uint32_t acc_phase = 0;
-    int chunk_iter = 0;
     Unit un;
     for (int k = 0; cta_unit<BN>(k, g, t, un); ++k) {
       const bool scatter = g.mode == kGemmPlain && un.routed && g.row_dst != nullptr;
       if (scatter) {
         // per-row destination and weight, fetched while the MMAs run
         epi_bar();  // the previous unit's stores are done with these arrays
-        for (int i = et; i < un.valid; i += 128) {
+        for (int i = et; i < un.valid; i += 32 * kEpiWarps) {
           t.unit_dst[i] = __ldg(g.row_dst + un.x_row + i);
           t.unit_w[i] = round_bf16(__ldg(g.row_w + un.x_row + i));
         }
@@ -411,75 +457,112 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&t.tfull[acc], acc_phase, abort_flag, g.status, 30)) break;
       tc_fence_after();
       const int chunks = (un.valid + kChunk - 1) / kChunk;
-      for (int c = 0; c < chunks; ++c, ++chunk_iter) {
-        uint32_t r[32];
-        tmem_ld32(tmem + acc * BN + c * kChunk + ((uint32_t)(q * 32) << 16), r);
-        __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging + (chunk_iter & 1) * kStaging);
+      const uint32_t taddr = tmem + acc * BN + ((uint32_t)(q * 32) << 16);
+      // one chunk: 32 token columns of this warp's 32 weight rows, as two
+      // 16-lane fragments (registers 0-15: rows +0..15, 16-31: rows +16..31)
+      auto load_chunk = [&](int c, uint32_t (&r)[32]) {
+        tmem_ld_frag16_async<0>(taddr + c * kChunk, r);
+        tmem_ld_frag16_async<16>(taddr + (16u << 16) + c * kChunk, r);
+      };
+      auto store_chunk = [&](const uint32_t (&r)[32], int c) {
         const int rows_here = min(kChunk, un.valid - c * kChunk);
-        __nv_bfloat16* out_base = un.out + (size_t)(un.x_row + c * kChunk) * un.ld + un.out_col;
         if (g.mode == kGemmSwiGLU) {
-          const bool is_up = lane & 1;
-          const int f = q * 16 + (lane >> 1);
-          const int tok0 = is_up ? 16 : 0;
-          // 1. pair exchange: even lanes keep tokens 0-15, odd lanes 16-31
-          uint16_t gbits[16];
-          float up[16];
+          // fragment (h, i): gate / up of feature 16q + 8h + lane / 4 for
+          // tokens 8i + 2 tq, + 1  ->  hp[4h + i] = h of those two tokens
+          uint32_t hp[8];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float mine_other = __uint_as_float(is_up ? r[j] : r[16 + j]);
-            const float recv = __shfl_xor_sync(0xffffffffu, mine_other, 1);
-            const float gate = is_up ? recv : __uint_as_float(r[j]);
-            gbits[j] = __bfloat16_as_ushort(__float2bfloat16_rn(gate));
-            up[j] = round_bf16(is_up ? __uint_as_float(r[16 + j]) : recv);
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t gb = pack_bf16x2(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]));
+            const uint32_t ub = pack_bf16x2(__uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            SiluFast s0 = silu_bf16_fast((uint16_t)(gb & 0xFFFFu));
+            SiluFast s1 = silu_bf16_fast((uint16_t)(gb >> 16));
+            if (!s0.exact) s0.bits = __bfloat16_as_ushort(silu_lut[gb & 0xFFFFu]);
+            if (!s1.exact) s1.bits = __bfloat16_as_ushort(silu_lut[gb >> 16]);
+            hp[j] = pack_bf16x2(__uint_as_float((uint32_t)s0.bits << 16) * __uint_as_float(ub << 16),
+                                __uint_as_float((uint32_t)s1.bits << 16) *
+                                    __uint_as_float(ub & 0xFFFF0000u));
           }
-          // 2. all SiLU lookups in flight together, 3. h = bf16(silu * up)
-          __nv_bfloat16 sv[16];
+          // tile: 32 tokens x 16 features (32-byte rows, the 16-byte half
+          // swizzled by bit 2 of the token so the 8 rows of a matrix hit
+          // distinct banks); thread = token of the row it addresses
 #pragma unroll
-          for (int j = 0; j < 16; ++j) sv[j] = silu_lut[gbits[j]];
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            st[(tok0 + j) * (BM / 2) + f] = __float2bfloat16_rn(__bfloat162float(sv[j]) * up[j]);
-          epi_bar();
-          // 32 tokens x 64 features: 256 16-byte pieces
+          for (int h = 0; h < 2; ++h)
+            stmatrix_x4_trans(tile_s + lane * 32 + ((h ^ ((lane >> 2) & 1)) << 4), hp[4 * h],
+                              hp[4 * h + 1], hp[4 * h + 2], hp[4 * h + 3]);
+          __syncwarp();
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
-            const int idx = et + 128 * i;
-            const int tok = idx >> 3, part = idx & 7;
+            const int v = lane + 32 * i, tok = v >> 1, cc = v & 1;
             if (tok < rows_here)
-              *reinterpret_cast<uint4*>(out_base + (size_t)tok * un.ld + part * 8) =
-                  reinterpret_cast<const uint4*>(st)[idx];
-          }
-        } else if (scatter) {
-          // routed contribution bf16(bf16(y) * bf16(w)) to its token-major slot
-          const int m = q * 32 + lane;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            st[j * BM + m] = __float2bfloat16_rn(
-                round_bf16(__uint_as_float(r[j])) * t.unit_w[c * kChunk + j]);
-          epi_bar();
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int idx = et + 128 * i;
-            const int tok = idx >> 4, part = idx & 15;
-            if (tok < rows_here)
-              *reinterpret_cast<uint4*>(un.out + (size_t)t.unit_dst[c * kChunk + tok] * un.ld +
-                                        un.out_col + part * 8) =
-                  reinterpret_cast<const uint4*>(st)[idx];
+              *reinterpret_cast<uint4*>(un.out + (size_t)(un.x_row + c * kChunk + tok) * un.ld +
+                                        un.out_col + q * 16 + cc * 8) =
+                  *reinterpret_cast<const uint4*>(tile_p + tok * 32 +
+                                                  ((cc ^ ((tok >> 2) & 1)) << 4));
           }
         } else {
-          const int m = q * 32 + lane;
+          // fragment (h, i), rows +0..7 (ab = 0) / +8..15 (ab = 1):
+          // yp[(4h + i) * 2 + ab] = bf16 of feature 32q + 16h + 8ab + lane / 4,
+          // tokens 8i + 2 tq, + 1
+          uint32_t yp[16];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) st[j * BM + m] = __float2bfloat16_rn(__uint_as_float(r[j]));
-          epi_bar();
+          for (int j = 0; j < 8; ++j) {
+            float y0 = __uint_as_float(r[4 * j]), y1 = __uint_as_float(r[4 * j + 1]);
+            float y2 = __uint_as_float(r[4 * j + 2]), y3 = __uint_as_float(r[4 * j + 3]);
+            if (scatter) {
+              // routed contribution bf16(bf16(y) * bf16(w)) of each token
+              const int tok = c * kChunk + 8 * (j & 3) + 2 * tq;
+              const float2 w = *reinterpret_cast<const float2*>(t.unit_w + tok);
+              y0 = round_bf16(y0) * w.x;
+              y1 = round_bf16(y1) * w.y;
+              y2 = round_bf16(y2) * w.x;
+              y3 = round_bf16(y3) * w.y;
+            }
+            yp[2 * j] = pack_bf16x2(y0, y1);
+            yp[2 * j + 1] = pack_bf16x2(y2, y3);
+          }
+          // tile: 32 tokens x 32 features (64-byte rows, 16-byte quarters
+          // swizzled by bits 1-2 of the token); quarter 2h + ab
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int ab = 0; ab < 2; ++ab)
+              stmatrix_x4_trans(tile_s + lane * 64 + (((2 * h + ab) ^ ((lane >> 1) & 3)) << 4),
+                                yp[8 * h + ab], yp[8 * h + 2 + ab], yp[8 * h + 4 + ab],
+                                yp[8 * h + 6 + ab]);
+          __syncwarp();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int idx = et + 128 * i;
-            const int tok = idx >> 4, part = idx & 15;
-            if (tok < rows_here)
-              *reinterpret_cast<uint4*>(out_base + (size_t)tok * un.ld + part * 8) =
-                  reinterpret_cast<const uint4*>(st)[idx];
+            const int v = lane + 32 * i, tok = v >> 2, cc = v & 3;
+            if (tok < rows_here) {
+              const size_t row = scatter ? (size_t)t.unit_dst[c * kChunk + tok]
+                                         : (size_t)(un.x_row + c * kChunk + tok);
+              *reinterpret_cast<uint4*>(un.out + row * un.ld + un.out_col + q * 32 + cc * 8) =
+                  *reinterpret_cast<const uint4*>(tile_p + tok * 64 +
+                                                  ((cc ^ ((tok >> 1) & 3)) << 4));
+            }
           }
         }
+        __syncwarp();  // the tile is read out before the next chunk overwrites it
+      };
+      // chunks half, half + 2, ...: the loads of the next one are in flight
+      // while the current one is converted and stored
+      uint32_t ra[32], rb[32];
+      int c = half;
+      if (c < chunks) {
+        load_chunk(c, ra);
+        tmem_wait_ld(ra);
+      }
+      while (c < chunks) {
+        if (c + 2 < chunks) load_chunk(c + 2, rb);
+        store_chunk(ra, c);
+        c += 2;
+        if (c >= chunks) break;
+        tmem_wait_ld(rb);
+        if (c + 2 < chunks) load_chunk(c + 2, ra);
+        store_chunk(rb, c);
+        c += 2;
+        if (c >= chunks) break;
+        tmem_wait_ld(ra);
       }
       tc_fence_before();
       __syncwarp();
@@ -504,8 +587,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // contiguous 16 KB block of HBM.
 constexpr int kTileVecs = BM * BK / 8;   // 16-byte vectors per tile
 
-// gate/up: packed row p of a tile holds gate (p even) or up (p odd) of
-// feature rt*64 + p/2, so an M tile carries 64 features' gate and up rows.
+// gate/up: packed row p of tile rt holds gate (p % 16 < 8) or up of feature
+// rt*64 + (p / 16) * 8 + p % 8 (packed_gate_up_row), so an M tile carries 64
+// features' gate and up rows and a 16-lane TMEM fragment pairs them.
 __global__ void pack_gate_up_kernel(__nv_bfloat16* __restrict__ dst,
                                     const __nv_bfloat16* __restrict__ gate,
                                     const __nv_bfloat16* __restrict__ up, int n_mats, int hidden,
@@ -519,8 +603,8 @@ __global__ void pack_gate_up_kernel(__nv_bfloat16* __restrict__ dst,
     const int kb = (int)(tile % kb_count);
     const int rt = (int)((tile / kb_count) % rt_count);
     const int m = (int)(tile / ((size_t)kb_count * rt_count));
-    const int feat = rt * (BM / 2) + (r >> 1);
-    const __nv_bfloat16* src = (r & 1) ? up : gate;
+    const int feat = rt * (BM / 2) + (r >> 4) * 8 + (r & 7);
+    const __nv_bfloat16* src = (r & 8) ? up : gate;
     reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(
         src + ((size_t)m * hidden + feat) * dim + kb * BK)[cv];
   }
@@ -545,6 +629,20 @@ __global__ void pack_tiles_kernel(__nv_bfloat16* __restrict__ dst,
 }
 
 }  // namespace
+
+// The SiLU table of the current device, built once on the caller's stream
+// ahead of its first use (which is why that first call should not be captured).
+static int ensure_silu_lut(cudaStream_t stream) {
+  static unsigned long long lut_built = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
+  if (!(lut_built & (1ull << dev))) {
+    build_silu_lut_kernel<<<(1 << 16) / 256, 256, 0, stream>>>();
+    if (cudaGetLastError() != cudaSuccess) return -2;
+    lut_built |= 1ull << dev;
+  }
+  return 0;
+}
 
 template <int BN>
 static int launch_gemm_bn(const GemmArgs& args, const CUtensorMap* tm_w_routed,
@@ -572,16 +670,7 @@ int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
                         const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
                         const CUtensorMap* tm_x_shared, int grid, int token_tile,
                         cudaStream_t stream) {
-  static unsigned long long lut_built = 0;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
-  if (!(lut_built & (1ull << dev))) {
-    // the SiLU table of this device, built once on the caller's stream ahead
-    // of the first GEMM (which is why the first call should not be captured)
-    build_silu_lut_kernel<<<(1 << 16) / 256, 256, 0, stream>>>();
-    if (cudaGetLastError() != cudaSuccess) return -2;
-    lut_built |= 1ull << dev;
-  }
+  if (ensure_silu_lut(stream) != 0) return -2;
   if (token_tile == 256)
     return launch_gemm_bn<256>(args, tm_w_routed, tm_x_routed, tm_w_shared, tm_x_shared, grid,
                                stream);
@@ -589,6 +678,12 @@ int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
     return launch_gemm_bn<128>(args, tm_w_routed, tm_x_routed, tm_w_shared, tm_x_shared, grid,
                                stream);
   return -1;
+}
+
+int launch_silu_bf16(const uint16_t* x, uint16_t* y, int n, cudaStream_t stream) {
+  if (ensure_silu_lut(stream) != 0) return -2;
+  if (n > 0) silu_bf16_kernel<<<(n + 255) / 256, 256, 0, stream>>>(x, y, n);
+  return 0;  // the caller reads the launch status
 }
 
 static int pack_blocks(size_t vecs) {

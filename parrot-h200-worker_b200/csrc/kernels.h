@@ -195,10 +195,19 @@ int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
                         const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
                         const CUtensorMap* tm_x_shared, int grid, int token_tile,
                         cudaStream_t stream);
+// Row of the packed gate/up matrix holding gate (is_up = 0) or up (is_up = 1)
+// of feature f: each 128-row tile carries 64 features as 8 groups of 16 rows,
+// the group's 8 gate rows followed by the same 8 features' up rows, so one
+// 16-lane TMEM fragment holds gate and up of a feature in the same thread.
+__host__ __device__ constexpr int packed_gate_up_row(int f, int is_up) {
+  return (f >> 6) * 128 + ((f & 63) >> 3) * 16 + (f & 7) + 8 * is_up;
+}
+
 int launch_pack_gate_up(__nv_bfloat16* dst, const __nv_bfloat16* gate, const __nv_bfloat16* up,
                         int n_mats, int hidden, int dim, cudaStream_t stream);
 int launch_pack_tiles(__nv_bfloat16* dst, const __nv_bfloat16* src, int n_mats, int rows,
                       int cols, cudaStream_t stream);
+int launch_silu_bf16(const uint16_t* x, uint16_t* y, int n, cudaStream_t stream);
 
 
 // Tokens per router CTA: 32 while the batch is small (more CTAs share the

@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
     for (int i = threadIdx.x; i < 2 * kFeatPerCta * nvec; i += blockDim.x) {
       const int r = i / nvec, c = i - r * nvec;
       const int f = f0 + (r >> 1);
-      const int row = (f / 64) * kTileRows + 2 * (f % 64) + (r & 1);
+      const int row = packed_gate_up_row(f, r & 1);
       cp_async16(wrows_s + i, a.shared_gate_up + tiled_index(0, row, c * 8, 2 * Hs, d));
     }
   }
@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
     for (int i = threadIdx.x; i < 2 * kFeatPerCta * nvec; i += blockDim.x) {
       const int r = i / nvec, c = i - r * nvec;
       const int f = f0 + (r >> 1);
-      const int row = (f / 64) * kTileRows + 2 * (f % 64) + (r & 1);
+      const int row = packed_gate_up_row(f, r & 1);
       cp_async16(wrows_s + i, a.gate_up + tiled_index(e, row, c * 8, 2 * H, d));
     }
   }

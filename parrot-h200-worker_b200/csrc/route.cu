@@ -111,42 +111,44 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      bool issued[kRouteStages] = {};
-      uint32_t issued_phase[kRouteStages] = {};
+      static_assert(kRouteStages <= 32, "per-stage bit masks");
+      uint32_t issued = 0, issued_phase = 0;  // per-stage bits
       for (int kb = 0; kb < pre; ++kb) {
         tma_load_2d(x_tiles + kb * kRouteXTile, &x_map, kb * 64, tile * rows, &sm.full[kb]);
-        issued[kb] = true;
+        issued |= 1u << kb;
       }
+      int stage = pre % kRouteStages;
+      uint32_t phase = (uint32_t)(pre / kRouteStages) & 1u;
       for (int kb = pre; kb < kb_count; ++kb) {
-        const int stage = kb % kRouteStages;
-        const uint32_t phase = (uint32_t)(kb / kRouteStages) & 1u;
-        if (!mbar_wait(&sm.empty[stage], phase ^ 1u, abort_flag, a.status, 20)) break;
+        if (!mbar_wait_fast(&sm.empty[stage], phase ^ 1u, abort_flag, a.status, 20)) break;
         mbar_arrive_expect_tx(&sm.full[stage], x_bytes + kWTile);
         tma_load_2d(w_tiles + stage * kWTile, &w_map, kb * 64, 0, &sm.full[stage]);
         tma_load_2d(x_tiles + stage * kRouteXTile, &x_map, kb * 64, tile * rows,
                     &sm.full[stage]);
-        issued[stage] = true;
-        issued_phase[stage] = phase;
+        issued |= 1u << stage;
+        issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+        stage = stage + 1 == kRouteStages ? 0 : stage + 1;
+        phase ^= stage == 0 ? 1u : 0u;
       }
       // every issued copy has landed before the CTA can exit
-      for (int s = 0; s < kRouteStages; ++s)
-        if (issued[s]) mbar_drain(&sm.full[s], issued_phase[s]);
+      for (int st = 0; st < kRouteStages; ++st)
+        if (issued & (1u << st)) mbar_drain(&sm.full[st], (issued_phase >> st) & 1u);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = make_idesc(kRouteM, NP);
+      int stage = 0;
+      uint32_t phase = 0;
       for (int kb = 0; kb < kb_count; ++kb) {
-        const int stage = kb % kRouteStages;
-        const uint32_t phase = (uint32_t)(kb / kRouteStages) & 1u;
-        if (!mbar_wait(&sm.full[stage], phase, abort_flag, a.status, 21)) break;
+        if (!mbar_wait_fast(&sm.full[stage], phase, abort_flag, a.status, 21)) break;
         tc_fence_after();
-        const uint64_t da = sw128_desc(x_tiles + stage * kRouteXTile);
-        const uint64_t db = sw128_desc(w_tiles + stage * kWTile);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) mma_bf16(sm.tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+        mma_slab(sm.tmem, sw128_desc(x_tiles + stage * kRouteXTile),
+                 sw128_desc(w_tiles + stage * kWTile), idesc, kb != 0);
         mma_commit(&sm.empty[stage]);
+        stage = stage + 1 == kRouteStages ? 0 : stage + 1;
+        phase ^= stage == 0 ? 1u : 0u;
       }
       mma_commit(&sm.done);  // also fires when the loop stopped early: in-flight MMAs drain
     }

@@ -56,6 +56,14 @@ static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, vo
   }
 }
 
+// The common case inline (one try_wait), the bounded loop (a call) only when
+// the phase has not completed yet.  The call alone costs about 200 cycles,
+// more than the four MMAs of a slab.
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort_flag, int* status, int site) {
+  return mbar_try_wait(bar, parity) || mbar_wait(bar, parity, abort_flag, status, site);
+}
+
 // Drain wait used on the way out: ignores the abort flag, still bounded.
 static __device__ __noinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = global_timer_ns();
@@ -101,6 +109,18 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
+// The four K = 16 MMAs of one 64-column, 128-byte-swizzled slab as
+// straight-line code: measured on B200, a tcgen05.mma of M = 128, N <= 64
+// takes about 50 cycles back to back, and any branch between two of them
+// about as much again.  Only the first MMA's accumulate flag varies.
+__device__ __forceinline__ void mma_slab(uint32_t d_tmem, uint64_t da, uint64_t db, uint32_t idesc,
+                                         uint32_t accumulate_first) {
+  mma_bf16(d_tmem, da, db, idesc, accumulate_first);
+  mma_bf16(d_tmem, da + 2, db + 2, idesc, 1u);
+  mma_bf16(d_tmem, da + 4, db + 4, idesc, 1u);
+  mma_bf16(d_tmem, da + 6, db + 6, idesc, 1u);
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -130,7 +150,66 @@ __device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// 32 consecutive TMEM columns of this warp's 32 lanes (one register each).
+// tmem_ld32 without the wait: the registers are valid only after
+// tmem_wait_ld on the same array, which names them as operands so no use of
+// them can be scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t addr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(addr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
+        "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]),
+        "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),
+        "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]),
+        "+r"(r[31])
+      :
+      : "memory");
+}
+
+// 16 lanes x 32 columns in the mma-fragment layout (tcgen05.ld .16x256b.x4),
+// no wait: for t = this thread's lane and i = 0..3,
+//   r[O + 4i + 0, 1] = TMEM lane (base + t / 4),     columns 8i + 2 (t % 4) + {0, 1}
+//   r[O + 4i + 2, 3] = TMEM lane (base + 8 + t / 4), the same columns.
+template <int O>
+__device__ __forceinline__ void tmem_ld_frag16_async(uint32_t addr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[O + 0]), "=r"(r[O + 1]), "=r"(r[O + 2]), "=r"(r[O + 3]), "=r"(r[O + 4]), "=r"(r[O + 5]), "=r"(r[O + 6]), "=r"(r[O + 7]), "=r"(r[O + 8]), "=r"(r[O + 9]), "=r"(r[O + 10]), "=r"(r[O + 11]), "=r"(r[O + 12]), "=r"(r[O + 13]), "=r"(r[O + 14]), "=r"(r[O + 15])
+      : "r"(addr));
+}
+
+// Four 8x8 bf16 matrices from mma-fragment registers (thread t holds row
+// t / 4, columns 2 (t % 4) and + 1 of each) to shared memory transposed:
+// thread 8m + j gives the address of row j of matrix m's transpose.
+__device__ __forceinline__ void stmatrix_x4_trans(uint32_t addr, uint32_t a, uint32_t b,
+                                                  uint32_t c, uint32_t d) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(
+                   addr),
+               "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// Two floats rounded to bf16 and packed (lo in the low half).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// 16 consecutive TMEM columns of this warp's 32 lanes (one register each).
 __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "

@@ -68,6 +68,7 @@ _SIGNATURES = {
     "parrot_pack_gate_up_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_void_p]),
     "parrot_pack_down_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "parrot_silu_bf16": (c_int, [c_void_p, c_void_p, ctypes.c_int64, c_void_p]),
     "parrot_moe_forward_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                         POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
     "parrot_moe_forward_static_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,

@@ -52,6 +52,26 @@ def test_rmsnorm_matches_oracle(rows, dim):
 
 
 # ---------------------------------------------------------------------------
+# SiLU of the SwiGLU epilogue, every bf16 input
+# ---------------------------------------------------------------------------
+def test_silu_matches_pytorch_bf16_for_every_input():
+    """parrot_silu_bf16 runs the epilogue's SiLU (fast path + table fallback);
+    it must equal F.silu on a bf16 tensor (parrot/model.py:448) bit for bit
+    for all 65,536 bf16 bit patterns (NaNs: NaN in both)."""
+    bits = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16)
+    x = bits.view(torch.bfloat16).cuda()
+    y = torch.empty_like(x)
+    _lib.check(_lib.load().parrot_silu_bf16(x.data_ptr(), y.data_ptr(), x.numel(),
+                                            bridge._stream()), "parrot_silu_bf16")
+    want = torch.nn.functional.silu(x)
+    torch.cuda.synchronize()
+    nan = torch.isnan(want)
+    assert torch.equal(torch.isnan(y), nan)
+    same = y.view(torch.int16) == want.view(torch.int16)
+    assert bool(same[~nan].all()), x[~nan & ~same][:8].float().tolist()
+
+
+# ---------------------------------------------------------------------------
 # Block AttnRes depth mix (+ consumer RMSNorm, + deferred residual)
 # ---------------------------------------------------------------------------
 def _depth_modules(dim, seed, q_std=0.5):
