@@ -69,6 +69,20 @@ int parrot_depthmix_bf16(void* out, const void* const* sources, int n_sources,
                          const void* pending_base, const void* pending_delta,
                          void* pending_out, int rows, int dim, void* stream);
 
+/* parrot_depthmix_bf16 whose last source is a deferred MoE block output:
+ *   bf16(pending_base + bf16(bf16(shared + contrib[2t]) + contrib[2t + 1]))
+ * (pending_base optional: without it, no residual add), the combine and
+ * residual add of model.py:546-551 / :702 with the same roundings as
+ * parrot_moe_forward_bf16, also written to pending_out.  pending_shared:
+ * [rows, dim]; pending_contrib: [2 rows, dim] (parrot_moe_forward_deferred_bf16's
+ * workspace regions); sources[n_sources - 1] is not read. */
+int parrot_depthmix_moe_bf16(void* out, const void* const* sources, int n_sources,
+                             const void* query, const void* key_norm_weight, float key_eps,
+                             const void* out_norm_weight, float out_eps, void* mix_out,
+                             const void* pending_base, const void* pending_shared,
+                             const void* pending_contrib, void* pending_out, int rows, int dim,
+                             void* stream);
+
 /* ------------------------------------------------------------------------
  * Rotary position embedding, in place, for the packed q/k/v projection of
  * local attention.  Replaces parrot/model.py:206-216 (LocalGQA._rope) applied
@@ -225,6 +239,19 @@ int parrot_pack_down_bf16(void* dst, const void* src, int n_mats, int rows, int 
 int parrot_moe_forward_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
                             const void* x, const parrot_moe_outputs* outputs, void* workspace,
                             size_t workspace_bytes, void* stream);
+
+/* The MoE block without its final combine: route, grouping and both expert
+ * GEMMs, leaving the weighted routed contributions at layout.contrib
+ * ([2T, d], token-major, row 2t + j the token's j-th lowest expert id) and the
+ * shared expert output at layout.shared_y ([T, d]) in `workspace`;
+ * outputs->out is not used (may be NULL).  The caller finishes the block with
+ * parrot_depthmix_moe_bf16 — the combine of model.py:546-551 (+ the residual
+ * add of :702) folded into the next Block AttnRes depth mix — before the
+ * workspace is used again. */
+int parrot_moe_forward_deferred_bf16(const parrot_moe_dims* dims,
+                                     const parrot_moe_weights* weights, const void* x,
+                                     const parrot_moe_outputs* outputs, void* workspace,
+                                     size_t workspace_bytes, void* stream);
 
 /* Whole MoE block without a caller-provided workspace, for callers that
  * cannot allocate device memory at the point of the call (a runtime that owns

@@ -212,15 +212,16 @@ parrot::MoeTables tables(void* ws, const parrot_moe_layout& L) {
 }
 
 int prepare(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
-            const parrot_moe_outputs* o, void* ws, size_t ws_bytes, parrot_moe_layout* L) {
+            const parrot_moe_outputs* o, void* ws, size_t ws_bytes, parrot_moe_layout* L,
+            bool need_out = true) {
   int rc = layout_of(dims, L);
   if (rc) return rc;
   if ((rc = check_weights(w))) return rc;
-  if (o == nullptr || (dims->tokens > 0 && o->out == nullptr))
+  if (o == nullptr || (need_out && dims->tokens > 0 && o->out == nullptr))
     return fail(PARROT_EINVAL, "outputs->out is required%s");
   if (ws == nullptr || ws_bytes < L->total || !aligned16(ws))
     return fail(PARROT_EINVAL, "workspace missing, misaligned or smaller than the layout total%s");
-  if (dims->tokens > 0 && (x == nullptr || !aligned16(x) || !aligned16(o->out) ||
+  if (dims->tokens > 0 && (x == nullptr || !aligned16(x) || (need_out && !aligned16(o->out)) ||
                            (o->residual && !aligned16(o->residual))))
     return fail(PARROT_EINVAL, "x/out/residual must be non-null and 16-byte aligned%s");
   return PARROT_OK;
@@ -357,10 +358,11 @@ int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights*
 
 int run_experts(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
                 const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L,
-                cudaStream_t s) {
+                cudaStream_t s, bool combine = true) {
   int rc = run_gemm(true, dims, w, x, ws, L, s);
   if (rc) return rc;
   if ((rc = run_gemm(false, dims, w, x, ws, L, s))) return rc;
+  if (!combine) return PARROT_OK;
   parrot::CombineArgs c{};
   c.contrib = at<__nv_bfloat16>(ws, L.contrib);
   c.shared_y = at<__nv_bfloat16>(ws, L.shared_y);
@@ -505,25 +507,23 @@ int parrot_rmsnorm_bf16(void* out, const void* x, const void* weight, int rows, 
   return check_launch("rmsnorm_kernel");
 }
 
-int parrot_depthmix_bf16(void* out, const void* const* sources, int n_sources,
-                         const void* query, const void* key_norm_weight, float key_eps,
-                         const void* out_norm_weight, float out_eps, void* mix_out,
-                         const void* pending_base, const void* pending_delta,
-                         void* pending_out, int rows, int dim, void* stream) {
+namespace {
+// Shared by the two depth-mix entries: the last source is replaced by the
+// deferred value (pending_out) when one is given.
+int depthmix_launch(void* out, const void* const* sources, int n_sources, const void* query,
+                    const void* key_norm_weight, float key_eps, const void* out_norm_weight,
+                    float out_eps, void* mix_out, parrot::DepthMixArgs a, int rows, int dim,
+                    void* stream) {
   if (n_sources < 1 || n_sources > parrot::kMaxDepthSources)
     return fail(PARROT_EINVAL, "depthmix: n_sources must be in [1, 16]%s");
   if (rows < 0 || dim <= 0 || dim % 8 || dim > 1024)
     return fail(PARROT_EINVAL, "depthmix: dim % 8 == 0 and dim <= 1024 required%s");
-  if ((pending_delta == nullptr) != (pending_base == nullptr) ||
-      (pending_delta != nullptr && pending_out == nullptr))
-    return fail(PARROT_EINVAL, "depthmix: pending_base, pending_delta and pending_out go together%s");
   if (rows == 0) return PARROT_OK;
   if (!out || !query || !key_norm_weight || !sources)
     return fail(PARROT_EINVAL, "depthmix: null pointer%s");
-  parrot::DepthMixArgs a{};
+  const bool deferred = a.pending_out != nullptr;
   for (int i = 0; i < n_sources; ++i) {
-    const bool is_pending = pending_delta != nullptr && i == n_sources - 1;
-    const void* p = is_pending ? pending_out : sources[i];
+    const void* p = deferred && i == n_sources - 1 ? a.pending_out : sources[i];
     if (p == nullptr || !aligned16(p))
       return fail(PARROT_EINVAL, "depthmix: sources must be non-null and 16-byte aligned%s");
     a.sources[i] = static_cast<const __nv_bfloat16*>(p);
@@ -536,14 +536,51 @@ int parrot_depthmix_bf16(void* out, const void* const* sources, int n_sources,
   a.out_eps = out_eps;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.mix_out = static_cast<__nv_bfloat16*>(mix_out);
-  a.pending_base = static_cast<const __nv_bfloat16*>(pending_base);
-  a.pending_delta = static_cast<const __nv_bfloat16*>(pending_delta);
-  a.pending_out = static_cast<__nv_bfloat16*>(pending_out);
   a.rows = rows;
   a.dim = dim;
   if (parrot::launch_depthmix(a, static_cast<cudaStream_t>(stream)))
     return fail(PARROT_ECUDA, "depthmix: could not configure shared memory%s");
   return check_launch("depthmix_kernel");
+}
+}  // namespace
+
+int parrot_depthmix_bf16(void* out, const void* const* sources, int n_sources,
+                         const void* query, const void* key_norm_weight, float key_eps,
+                         const void* out_norm_weight, float out_eps, void* mix_out,
+                         const void* pending_base, const void* pending_delta,
+                         void* pending_out, int rows, int dim, void* stream) {
+  if ((pending_delta == nullptr) != (pending_base == nullptr) ||
+      (pending_delta != nullptr) != (pending_out != nullptr))
+    return fail(PARROT_EINVAL, "depthmix: pending_base, pending_delta and pending_out go together%s");
+  if ((pending_base && !aligned16(pending_base)) || (pending_delta && !aligned16(pending_delta)) ||
+      (pending_out && !aligned16(pending_out)))
+    return fail(PARROT_EINVAL, "depthmix: pending buffers must be 16-byte aligned%s");
+  parrot::DepthMixArgs a{};
+  a.pending_base = static_cast<const __nv_bfloat16*>(pending_base);
+  a.pending_delta = static_cast<const __nv_bfloat16*>(pending_delta);
+  a.pending_out = static_cast<__nv_bfloat16*>(pending_out);
+  return depthmix_launch(out, sources, n_sources, query, key_norm_weight, key_eps,
+                         out_norm_weight, out_eps, mix_out, a, rows, dim, stream);
+}
+
+int parrot_depthmix_moe_bf16(void* out, const void* const* sources, int n_sources,
+                             const void* query, const void* key_norm_weight, float key_eps,
+                             const void* out_norm_weight, float out_eps, void* mix_out,
+                             const void* pending_base, const void* pending_shared,
+                             const void* pending_contrib, void* pending_out, int rows, int dim,
+                             void* stream) {
+  if (!pending_shared || !pending_contrib || !pending_out)
+    return fail(PARROT_EINVAL, "depthmix_moe: pending_shared, pending_contrib and pending_out are required%s");
+  if (!aligned16(pending_shared) || !aligned16(pending_contrib) || !aligned16(pending_out) ||
+      (pending_base && !aligned16(pending_base)))
+    return fail(PARROT_EINVAL, "depthmix_moe: pending buffers must be 16-byte aligned%s");
+  parrot::DepthMixArgs a{};
+  a.pending_base = static_cast<const __nv_bfloat16*>(pending_base);
+  a.pending_shared = static_cast<const __nv_bfloat16*>(pending_shared);
+  a.pending_contrib = static_cast<const __nv_bfloat16*>(pending_contrib);
+  a.pending_out = static_cast<__nv_bfloat16*>(pending_out);
+  return depthmix_launch(out, sources, n_sources, query, key_norm_weight, key_eps,
+                         out_norm_weight, out_eps, mix_out, a, rows, dim, stream);
 }
 
 int parrot_rope_inplace_bf16(void* x, const void* cos_table, const void* sin_table, int rows,
@@ -724,6 +761,19 @@ int parrot_moe_forward_bf16(const parrot_moe_dims* dims, const parrot_moe_weight
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = run_route(dims, weights, x, outputs, workspace, L, s))) return rc;
   return run_experts(dims, weights, x, outputs, workspace, L, s);
+}
+
+int parrot_moe_forward_deferred_bf16(const parrot_moe_dims* dims,
+                                     const parrot_moe_weights* weights, const void* x,
+                                     const parrot_moe_outputs* outputs, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  int rc = prepare(dims, weights, x, outputs, workspace, workspace_bytes, &L, false);
+  if (rc) return rc;
+  if (dims->tokens == 0) return PARROT_OK;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = run_route(dims, weights, x, outputs, workspace, L, s))) return rc;
+  return run_experts(dims, weights, x, outputs, workspace, L, s, false);
 }
 
 int parrot_moe_decode_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,

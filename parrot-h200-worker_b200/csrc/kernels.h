@@ -30,6 +30,8 @@ struct DepthMixArgs {
   __nv_bfloat16* mix_out;         // optional un-normalised mix
   const __nv_bfloat16* pending_base;   // optional deferred residual
   const __nv_bfloat16* pending_delta;
+  const __nv_bfloat16* pending_shared;   // optional deferred MoE combine: shared output
+  const __nv_bfloat16* pending_contrib;  // and [2 rows, dim] routed contributions
   __nv_bfloat16* pending_out;
   int rows;
   int dim;

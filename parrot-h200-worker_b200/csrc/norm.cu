@@ -74,7 +74,13 @@ int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat
 
 // ---------------------------------------------------------------------------
 // Depth mix (model.py:149-155) with optional consumer RMSNorm (model.py:157-164)
-// and optional deferred residual (model.py:702: partial = partial + delta).
+// and an optional deferred last source, computed while the sources are read
+// and also written out:
+//   residual add (model.py:702):  bf16(base + delta)
+//   MoE combine (model.py:546-551, then :702):
+//                 bf16(base + bf16(bf16(shared + c_lo) + c_hi)), c_lo / c_hi the
+//                 token's routed contributions of the lower / higher expert id
+//                 (the combine kernel's arithmetic; without base, no add).
 //
 // Per token row t and source i, all in fp32:
 //   key_i  = v_i * rsqrt(mean(v_i^2) + key_eps) * key_w            (F.rms_norm)
@@ -104,7 +110,8 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
   const int dim = a.dim, nvec = dim >> 3, S = a.n_sources;
   const bool active = c < nvec;
   const size_t off = (size_t)blockIdx.x * dim;
-  const bool pending = a.pending_delta != nullptr;
+  const bool pend_moe = a.pending_contrib != nullptr;
+  const bool pending = a.pending_delta != nullptr || pend_moe;
 
   // the query and norm weights are parameters: read before the grid dependency
   float q[8], kw[8];
@@ -123,9 +130,16 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
   // 1. every source vector of this thread in flight at once
   uint4 v[kMaxDepthSources];
   uint4 pb = make_uint4(0, 0, 0, 0), pd = make_uint4(0, 0, 0, 0);
+  uint4 pc0 = make_uint4(0, 0, 0, 0), pc1 = make_uint4(0, 0, 0, 0);
   if (pending && active) {
-    pb = __ldg(reinterpret_cast<const uint4*>(a.pending_base + off) + c);
-    pd = __ldg(reinterpret_cast<const uint4*>(a.pending_delta + off) + c);
+    if (a.pending_base != nullptr) pb = __ldg(reinterpret_cast<const uint4*>(a.pending_base + off) + c);
+    if (pend_moe) {
+      pd = __ldg(reinterpret_cast<const uint4*>(a.pending_shared + off) + c);
+      pc0 = __ldg(reinterpret_cast<const uint4*>(a.pending_contrib + 2 * off) + c);
+      pc1 = __ldg(reinterpret_cast<const uint4*>(a.pending_contrib + 2 * off + dim) + c);
+    } else {
+      pd = __ldg(reinterpret_cast<const uint4*>(a.pending_delta + off) + c);
+    }
   }
 #pragma unroll
   for (int s = 0; s < kMaxDepthSources; ++s) {
@@ -135,13 +149,24 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
   }
   uint4 r = make_uint4(0, 0, 0, 0);
   if (pending && active) {
-    // the deferred residual add: last source = bf16(base + delta)
+    // the deferred last source
     float b[8], dl[8];
     bf16x8_to_float(pb, b);
     bf16x8_to_float(pd, dl);
+    if (pend_moe) {
+      float p0[8], p1[8];
+      bf16x8_to_float(pc0, p0);
+      bf16x8_to_float(pc1, p1);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) b[j] = b[j] + dl[j];
-    r = float_to_bf16x8(b);
+      for (int j = 0; j < 8; ++j) dl[j] = round_bf16(round_bf16(dl[j] + p0[j]) + p1[j]);
+    }
+    if (a.pending_base != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b[j] = b[j] + dl[j];
+      r = float_to_bf16x8(b);
+    } else {
+      r = float_to_bf16x8(dl);
+    }
     reinterpret_cast<uint4*>(a.pending_out + off)[c] = r;
   }
   // source s as this thread sees it (reads only: a store into v[S - 1] would

@@ -52,6 +52,9 @@ _SIGNATURES = {
     "parrot_depthmix_bf16": (c_int, [c_void_p, POINTER(c_void_p), c_int, c_void_p, c_void_p,
                                      c_float, c_void_p, c_float, c_void_p, c_void_p, c_void_p,
                                      c_void_p, c_int, c_int, c_void_p]),
+    "parrot_depthmix_moe_bf16": (c_int, [c_void_p, POINTER(c_void_p), c_int, c_void_p, c_void_p,
+                                         c_float, c_void_p, c_float, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "parrot_rope_inplace_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_int, c_int, c_int, c_int, c_void_p]),
     "parrot_rope_inplace_at_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
@@ -71,6 +74,9 @@ _SIGNATURES = {
     "parrot_silu_bf16": (c_int, [c_void_p, c_void_p, ctypes.c_int64, c_void_p]),
     "parrot_moe_forward_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                         POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
+    "parrot_moe_forward_deferred_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
+                                                 POINTER(MoeOutputs), c_void_p, c_size_t,
+                                                 c_void_p]),
     "parrot_moe_forward_static_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                                POINTER(MoeOutputs), c_void_p]),
     "parrot_moe_decode_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,

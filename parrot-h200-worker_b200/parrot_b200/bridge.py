@@ -11,6 +11,7 @@ raise.
 from __future__ import annotations
 
 import ctypes
+from dataclasses import dataclass
 from typing import Sequence
 
 import torch
@@ -156,6 +157,15 @@ def b200_decode_attention(q: Tensor, k_new: Tensor, v_new: Tensor | None, k_cach
 # Block AttnRes depth mixing  (metal_moe.py:419-500)
 # ---------------------------------------------------------------------------
 def _depth_call(module, sources: Sequence[Tensor], output_norm, pending_delta: Tensor | None):
+    last = sources[-1]
+    if isinstance(last, PendingMoE):
+        if last.value is not None:  # already materialised: an ordinary source
+            out, _ = _depth_call(module, list(sources[:-1]) + [last.value], output_norm, None)
+            return out, last.value
+        _require_inference("depth")
+        out = _resolve_into(last, module.query, module.norm.weight, module.norm.eps,
+                            sources[:-1], output_norm)
+        return out.view(last.shape), last.value
     first = sources[0]
     _require_device(first, "depth")
     _require_inference("depth")
@@ -196,10 +206,14 @@ def b200_depth_mix_norm(module, sources: Sequence[Tensor], output_norm,
 
     With ``pending_delta``, the last source is ``sources[-1] + pending_delta``
     (a residual add the caller deferred) and the call returns
-    ``(normalized, resolved_last_source)``; otherwise it returns ``normalized``.
+    ``(normalized, resolved_last_source)``.  When the last source is a
+    ``PendingMoE`` the kernel also performs that MoE block's combine and the
+    call returns ``(normalized, resolved_last_source)`` too.  Otherwise it
+    returns ``normalized``.
     """
+    deferred = isinstance(sources[-1], PendingMoE)
     out, resolved = _depth_call(module, sources, output_norm, pending_delta)
-    return out if pending_delta is None else (out, resolved)
+    return out if pending_delta is None and not deferred else (out, resolved)
 
 
 # ---------------------------------------------------------------------------
@@ -284,7 +298,67 @@ def workspace(device: torch.device, dims: _lib.MoeDims) -> Tensor:
         layout = workspace_layout(dims)
         ws = torch.zeros(int(layout.total), device=device, dtype=torch.uint8)
         _WORKSPACES[key] = ws
+    live = _LIVE_PENDING.pop(ws.data_ptr(), None)
+    if live is not None:
+        live.resolve()  # its combine still reads this workspace: finish it first
     return ws
+
+
+@dataclass(eq=False)
+class PendingMoE:
+    """An MoE block output whose combine is left to the next depth mix.
+
+    Its value is ``base + bf16(bf16(shared + contrib[2t]) + contrib[2t + 1])``
+    (``base`` optional), the combine of ``model.py:546-551`` plus the residual
+    add of ``:702``.  ``shared`` [T, d] and ``contrib`` [2T, d] are views of
+    the MoE workspace, so the value is computed (by ``b200_depth_mix_norm`` or
+    ``resolve``) before that workspace is used again; ``value`` holds it then.
+    """
+    base: Tensor | None
+    shared: Tensor
+    contrib: Tensor
+    shape: torch.Size
+    workspace_ptr: int
+    value: Tensor | None = None
+
+    def resolve(self) -> Tensor:
+        """The value, materialised on its own (a one-source depth mix is exact)."""
+        if self.value is None:
+            dev, dt = self.shared.device, self.shared.dtype
+            key = (dev.index, dt, self.shared.shape[1])
+            ones = _UNIT_MIX.get(key)
+            if ones is None:
+                ones = _UNIT_MIX[key] = torch.ones(self.shared.shape[1], device=dev, dtype=dt)
+            _resolve_into(self, ones, ones, 1e-6, None)
+        return self.value
+
+
+_LIVE_PENDING: dict[int, PendingMoE] = {}
+_UNIT_MIX: dict[tuple, Tensor] = {}
+
+
+def _resolve_into(p: PendingMoE, query: Tensor, key_w: Tensor, key_eps: float, rest,
+                  output_norm=None):
+    """One depth-mix launch whose last source is ``p``; returns the normalized
+    (or plain) mix and sets ``p.value``.  ``rest``: the other sources (or None)."""
+    rows, dim = p.shared.shape
+    flat = [] if rest is None else [s.reshape(rows, dim).contiguous() for s in rest]
+    n = len(flat) + 1
+    if n > 16:
+        raise RuntimeError("B200 depth mixing supports one to sixteen sources")
+    out = torch.empty((rows, dim), device=p.shared.device, dtype=p.shared.dtype)
+    value = torch.empty_like(out)
+    base = None if p.base is None else p.base.reshape(rows, dim).contiguous()
+    ptrs = (ctypes.c_void_p * n)(*([s.data_ptr() for s in flat] + [value.data_ptr()]))
+    ow = None if output_norm is None else output_norm.weight
+    oe = 0.0 if output_norm is None else float(output_norm.eps)
+    _lib.check(_lib.load().parrot_depthmix_moe_bf16(
+        _p(out), ptrs, n, _p(query), _p(key_w), float(key_eps), _p(ow), oe, None, _p(base),
+        _p(p.shared), _p(p.contrib), _p(value), rows, dim, _stream()), "parrot_depthmix_moe_bf16")
+    p.value = value.view(p.shape)
+    if _LIVE_PENDING.get(p.workspace_ptr) is p:
+        del _LIVE_PENDING[p.workspace_ptr]
+    return out
 
 
 def _weights_struct(packed, bias: Tensor | None) -> _lib.MoeWeights:
@@ -345,6 +419,51 @@ def b200_moe(module, flat: Tensor, collect_stats: bool, addend: Tensor | None = 
     if stats is None:
         return out, None, None
     return out, stats[cfg.n_experts], stats[:cfg.n_experts]
+
+
+# Fold each MoE block's combine into the next depth mix (measured on B200:
+# one kernel fewer per layer of the Parrot XL forward).  False runs the
+# combine kernel instead; the results are identical.
+DEFER_MOE_COMBINE = True
+
+
+def b200_moe_deferred(module, flat: Tensor, collect_stats: bool, addend: Tensor | None, shape):
+    """The MoE block with its combine left to the next depth mix.
+
+    Returns ``(out, aux, utilization)`` like ``b200_moe``, ``out`` a
+    ``PendingMoE`` (value ``addend + moe(flat)``, shaped ``shape``); at decode
+    batch sizes, where the small-batch kernels combine in place, the finished
+    tensor instead.
+    """
+    _require_device(flat, "MoE")
+    _require_inference("MoE")
+    flat = flat.contiguous()
+    T, d = flat.shape
+    cfg = module.cfg
+    if (T <= DECODE_MOE_MAX_TOKENS and not collect_stats) or not DEFER_MOE_COMBINE:
+        out, aux, util = b200_moe(module, flat, collect_stats, addend)
+        return out.view(shape), aux, util
+    packed = pack_weights(module)
+    dims = moe_dims(cfg, T)
+    ws = workspace(flat.device, dims)
+    if addend is not None:
+        addend = addend.reshape(T, d).contiguous()
+        _require_device(addend, "MoE")
+    stats = torch.empty(cfg.n_experts + 1, device=flat.device, dtype=torch.float32) \
+        if collect_stats else None
+    outputs = _lib.MoeOutputs(None, None, None, None, None, None, None,
+                              None if stats is None else stats.data_ptr())
+    _lib.check(_lib.load().parrot_moe_forward_deferred_bf16(
+        ctypes.byref(dims), ctypes.byref(_weights_struct(packed, _router_bias(module))), _p(flat),
+        ctypes.byref(outputs), _p(ws), ws.numel(), _stream()), "parrot_moe_forward_deferred_bf16")
+    lay = workspace_layout(dims)
+    contrib = ws[lay.contrib:lay.contrib + 2 * T * d * 2].view(flat.dtype).view(2 * T, d)
+    shared = ws[lay.shared_y:lay.shared_y + T * d * 2].view(flat.dtype).view(T, d)
+    p = PendingMoE(addend, shared, contrib, torch.Size(shape), ws.data_ptr())
+    _LIVE_PENDING[ws.data_ptr()] = p
+    if stats is None:
+        return p, None, None
+    return p, stats[cfg.n_experts], stats[:cfg.n_experts]
 
 
 def b200_route(module, flat: Tensor, collect_stats: bool):

@@ -392,17 +392,26 @@ class MoE(nn.Module):
         self.shared = SwiGLU(cfg.dim, cfg.shared_expert_dim)
         self.router_bias: Tensor | None = None
 
-    def forward(self, x: Tensor, addend: Tensor | None = None):
-        """``(out, aux, utilization)``; ``out`` includes ``addend`` when given."""
+    def forward(self, x: Tensor, addend: Tensor | None = None, *, defer_combine: bool = False):
+        """``(out, aux, utilization)``; ``out`` includes ``addend`` when given.
+
+        ``defer_combine``: ``out`` may be a ``bridge.PendingMoE`` whose
+        combine the next depth mix performs.
+        """
         flat = x.reshape(-1, x.shape[-1])
+        if defer_combine:
+            return bridge.b200_moe_deferred(self, flat, self.cfg.collect_router_stats, addend,
+                                            x.shape)
         out, aux, util = bridge.b200_moe(self, flat, self.cfg.collect_router_stats, addend)
         return out.view_as(x), aux, util
 
     def inference(self, x: Tensor, *, direct: bool, addend: Tensor | None = None,
-                  defer_sum: bool = False) -> Tensor:
+                  defer_sum: bool = False, defer_combine: bool = False):
         if defer_sum:
             raise ValueError("deferred MoE reduction is not part of the b200 backend")
         flat = x.reshape(-1, x.shape[-1])
+        if defer_combine:
+            return bridge.b200_moe_deferred(self, flat, False, addend, x.shape)[0]
         out, _, _ = bridge.b200_moe(self, flat, False, addend)
         return out.view_as(x)
 
@@ -430,7 +439,10 @@ class _Residuals:
     """Block AttnRes bookkeeping (``model.py:680-705``) with one deferred add.
 
     ``pending`` holds an attention output not yet added to ``partial``; the
-    next depth-mix kernel performs that add while it reads the sources.
+    next depth-mix kernel performs that add while it reads the sources.  The
+    last source itself (``partial``, or the last completed block) may be a
+    ``bridge.PendingMoE``: an MoE output whose combine the next depth mix
+    performs.
     """
 
     def __init__(self, first: Tensor, block: int):
@@ -443,8 +455,16 @@ class _Residuals:
         return self.completed + ([] if self.partial is None else [self.partial])
 
     def mix(self, depth: DepthMix, norm: RMSNorm) -> Tensor:
+        sources = self.sources()
+        if isinstance(sources[-1], bridge.PendingMoE):
+            out, resolved = depth.normalized(sources, norm)
+            if self.partial is not None:
+                self.partial = resolved
+            else:
+                self.completed[-1] = resolved
+            return out
         if self.pending is None:
-            return depth.normalized(self.sources(), norm)
+            return depth.normalized(sources, norm)
         out, resolved = depth.normalized(self.sources(), norm, self.pending)
         self.partial, self.pending = resolved, None
         return out
@@ -515,7 +535,7 @@ class Parrot(nn.Module):
                 h = res.mix(self.depth_mix[index], norm) if attnres else norm(x)
                 if is_moe:
                     base = res.partial if attnres else x
-                    out, aux, usage = block.moe(h, addend=base)
+                    out, aux, usage = block.moe(h, addend=base, defer_combine=attnres)
                     if cfg.collect_router_stats:
                         aux_losses.append(aux)
                         utilization.append(usage)
@@ -597,7 +617,8 @@ class Parrot(nn.Module):
                 x = x + delta
             index += 1
             h = res.mix(self.depth_mix[index], block.moe_norm) if attnres else block.moe_norm(x)
-            out = block.moe.inference(h, direct=False, addend=res.partial if attnres else x)
+            out = block.moe.inference(h, direct=False, addend=res.partial if attnres else x,
+                                      defer_combine=attnres)
             if attnres:
                 res.set_partial(out)
                 res.end_module(index)
@@ -645,7 +666,8 @@ class Parrot(nn.Module):
                 x = x + delta
             index += 1
             h = res.mix(self.depth_mix[index], block.moe_norm) if attnres else block.moe_norm(x)
-            out = block.moe.inference(h, direct=True, addend=res.partial if attnres else x)
+            out = block.moe.inference(h, direct=True, addend=res.partial if attnres else x,
+                                      defer_combine=attnres)
             if attnres:
                 res.set_partial(out)
                 res.end_module(index)

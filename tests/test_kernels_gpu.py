@@ -51,6 +51,40 @@ def test_rmsnorm_matches_oracle(rows, dim):
     assert float(diff.max()) <= float(exp.abs().max()) * 2 ** -7
 
 
+@pytest.mark.parametrize("n_sources,rows,base", [(3, 512, True), (1, 37, False), (6, 64, True)])
+def test_depth_mix_with_deferred_moe_combine(n_sources, rows, base):
+    """parrot_depthmix_moe_bf16 == the combine kernel's arithmetic
+    bf16(base + bf16(bf16(shared + c_lo) + c_hi)) as the last source, then the
+    plain depth mix (which the other tests pin to the oracle)."""
+    dim = 768
+    g = torch.Generator().manual_seed(rows + n_sources)
+    rnd = lambda *s: torch.randn(*s, generator=g).to(torch.bfloat16).cuda()
+    srcs = [rnd(rows, dim) for _ in range(n_sources - 1)]
+    shared, contrib = rnd(rows, dim), rnd(2 * rows, dim) * 0.5
+    b = rnd(rows, dim) if base else None
+    q, kw, ow = rnd(dim) * 0.5, 1 + 0.2 * rnd(dim), 1 + 0.2 * rnd(dim)
+    lib = _lib.load()
+    out = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16)
+    value = torch.empty_like(out)
+    ptrs = (ctypes.c_void_p * n_sources)(*([s.data_ptr() for s in srcs] + [value.data_ptr()]))
+    _lib.check(lib.parrot_depthmix_moe_bf16(
+        out.data_ptr(), ptrs, n_sources, q.data_ptr(), kw.data_ptr(), 1e-6, ow.data_ptr(), 1e-6,
+        None, None if b is None else b.data_ptr(), shared.data_ptr(), contrib.data_ptr(),
+        value.data_ptr(), rows, dim, bridge._stream()), "parrot_depthmix_moe_bf16")
+    moe = ((shared.float() + contrib[0::2].float()).to(torch.bfloat16).float()
+           + contrib[1::2].float()).to(torch.bfloat16)
+    want_value = moe if b is None else (b.float() + moe.float()).to(torch.bfloat16)
+    want = torch.empty_like(out)
+    all_srcs = srcs + [want_value]
+    ptrs2 = (ctypes.c_void_p * n_sources)(*[s.data_ptr() for s in all_srcs])
+    _lib.check(lib.parrot_depthmix_bf16(
+        want.data_ptr(), ptrs2, n_sources, q.data_ptr(), kw.data_ptr(), 1e-6, ow.data_ptr(), 1e-6,
+        None, None, None, None, rows, dim, bridge._stream()), "parrot_depthmix_bf16")
+    torch.cuda.synchronize()
+    assert torch.equal(value, want_value)
+    assert torch.equal(out, want)
+
+
 # ---------------------------------------------------------------------------
 # SiLU of the SwiGLU epilogue, every bf16 input
 # ---------------------------------------------------------------------------

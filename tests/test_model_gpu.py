@@ -192,3 +192,31 @@ def test_graphed_forward_equals_eager():
         ids2 = torch.randint(0, 32768, (2, 64), generator=torch.Generator().manual_seed(11))
         again = graphed(ids2.cuda()).logits.clone()
         assert torch.equal(again, prod(ids2.cuda()).logits)
+
+
+@pytest.mark.parametrize("kw,batch,seq", [(TINY, 2, 64), ({}, 1, 512)])
+def test_deferred_moe_combine_is_bit_identical(kw, batch, seq):
+    """Each MoE block's combine folded into the next depth mix (the default)
+    gives exactly the logits, prefill logits and decode outputs of running
+    the combine kernel."""
+    from parrot_b200 import bridge
+    prod, _ = _pair(kw, seed=3)
+    ids = torch.randint(0, 32768, (batch, seq), generator=torch.Generator().manual_seed(4))
+    outs = {}
+    try:
+        for defer in (True, False):
+            bridge.DEFER_MOE_COMBINE = defer
+            with torch.inference_mode():
+                fwd = prod(ids.cuda())
+                logits = torch.cat([fwd.logits.flatten().float(), fwd.aux_loss.flatten().float(),
+                                    fwd.expert_utilization.flatten().float()])
+                lp, state = prod.prefill(ids[:, :seq - 8].cuda())
+                steps = [prod.decode_step(ids[:, seq - 8 + i:seq - 7 + i].cuda(), state)[0].clone()
+                         for i in range(3)]
+            outs[defer] = (logits, lp.clone(), steps)
+    finally:
+        bridge.DEFER_MOE_COMBINE = True
+    assert torch.equal(outs[True][0], outs[False][0])
+    assert torch.equal(outs[True][1], outs[False][1])
+    for a, b in zip(outs[True][2], outs[False][2]):
+        assert torch.equal(a, b)
