@@ -102,9 +102,11 @@ int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat
 // same order everywhere, so all threads agree bit for bit) and mixes its own
 // vector; a second exchange gives the consumer norm's sum of squares.
 // ---------------------------------------------------------------------------
-template <int W>
+// NS: the source capacity of this instantiation (2, 4, 8 or 16 >= n_sources),
+// so the per-source arrays and loops are sized to the call.
+template <int W, int NS>
 __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
-  __shared__ float red_ss[W][kMaxDepthSources], red_raw[W][kMaxDepthSources], red_sq[W];
+  __shared__ float red_ss[W][NS], red_raw[W][NS], red_sq[W];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = threadIdx.x;
   const int dim = a.dim, nvec = dim >> 3, S = a.n_sources;
@@ -128,7 +130,7 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
   griddep_launch();
 
   // 1. every source vector of this thread in flight at once
-  uint4 v[kMaxDepthSources];
+  uint4 v[NS];
   uint4 pb = make_uint4(0, 0, 0, 0), pd = make_uint4(0, 0, 0, 0);
   uint4 pc0 = make_uint4(0, 0, 0, 0), pc1 = make_uint4(0, 0, 0, 0);
   if (pending && active) {
@@ -142,7 +144,7 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
     }
   }
 #pragma unroll
-  for (int s = 0; s < kMaxDepthSources; ++s) {
+  for (int s = 0; s < NS; ++s) {
     v[s] = make_uint4(0, 0, 0, 0);
     if (s < S && active && !(pending && s == S - 1))
       v[s] = __ldg(reinterpret_cast<const uint4*>(a.sources[s] + off) + c);
@@ -178,9 +180,9 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) kq[j] = kw[j] * q[j];
   // 2. per-source sums of squares and raw key.query dots
-  float ss[kMaxDepthSources], raw[kMaxDepthSources];
+  float ss[NS], raw[NS];
 #pragma unroll
-  for (int s = 0; s < kMaxDepthSources; ++s) {
+  for (int s = 0; s < NS; ++s) {
     ss[s] = 0.f;
     raw[s] = 0.f;
     if (s < S) {
@@ -193,22 +195,22 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
       }
     }
   }
-  const float ss_l = warp_reduce_many<kMaxDepthSources>(ss, lane);
-  const float raw_l = warp_reduce_many<kMaxDepthSources>(raw, lane);
-  if (lane < kMaxDepthSources) {  // lane l holds the warp's totals of source l
+  const float ss_l = warp_reduce_many<NS>(ss, lane);
+  const float raw_l = warp_reduce_many<NS>(raw, lane);
+  if (lane < NS) {  // lane l holds the warp's totals of source l
     red_ss[warp][lane] = ss_l;
     red_raw[warp][lane] = raw_l;
   }
   __syncthreads();
 
   // 3. scores and softmax (every thread, same order), then the mix
-  float alpha[kMaxDepthSources];
+  float alpha[NS];
   float m = -INFINITY;
   // short dependent chains matter here (a few warps per SM): one reciprocal
   // for the mean, one for the softmax denominator, the fast exp
   const float inv_dim = 1.0f / (float)dim;
 #pragma unroll
-  for (int s = 0; s < kMaxDepthSources; ++s) {
+  for (int s = 0; s < NS; ++s) {
     alpha[s] = -INFINITY;
     if (s < S) {
       float tss = 0.f, traw = 0.f;
@@ -223,7 +225,7 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
   }
   float den = 0.f;
 #pragma unroll
-  for (int s = 0; s < kMaxDepthSources; ++s) {
+  for (int s = 0; s < NS; ++s) {
     alpha[s] = s < S ? __expf(alpha[s] - m) : 0.f;
     den += alpha[s];
   }
@@ -232,7 +234,7 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) h[j] = 0.f;
 #pragma unroll
-  for (int s = 0; s < kMaxDepthSources; ++s) {
+  for (int s = 0; s < NS; ++s) {
     if (s < S) {
       const float al = alpha[s] * rden;
       float f[8];
@@ -269,14 +271,26 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
   }
 }
 
+template <int W>
+static int launch_depthmix_w(const DepthMixArgs& args, cudaStream_t stream) {
+  const dim3 grid(args.rows), block(32 * W);
+  const int S = args.n_sources;
+  cudaError_t e;
+  if (S <= 2) e = launch_pdl(depthmix_kernel<W, 2>, grid, block, 0, stream, args);
+  else if (S <= 4) e = launch_pdl(depthmix_kernel<W, 4>, grid, block, 0, stream, args);
+  else if (S <= 8) e = launch_pdl(depthmix_kernel<W, 8>, grid, block, 0, stream, args);
+  else e = launch_pdl(depthmix_kernel<W, kMaxDepthSources>, grid, block, 0, stream, args);
+  return e == cudaSuccess ? 0 : -2;
+}
+
 int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream) {
   if (args.rows == 0) return 0;
-  const dim3 grid(args.rows);
+  if (args.n_sources < 1 || args.n_sources > kMaxDepthSources) return -1;
   switch ((args.dim / 8 + 31) / 32) {
-    case 1: return launch_pdl(depthmix_kernel<1>, grid, dim3(32), 0, stream, args) ? -2 : 0;
-    case 2: return launch_pdl(depthmix_kernel<2>, grid, dim3(64), 0, stream, args) ? -2 : 0;
-    case 3: return launch_pdl(depthmix_kernel<3>, grid, dim3(96), 0, stream, args) ? -2 : 0;
-    case 4: return launch_pdl(depthmix_kernel<4>, grid, dim3(128), 0, stream, args) ? -2 : 0;
+    case 1: return launch_depthmix_w<1>(args, stream);
+    case 2: return launch_depthmix_w<2>(args, stream);
+    case 3: return launch_depthmix_w<3>(args, stream);
+    case 4: return launch_depthmix_w<4>(args, stream);
     default: return -1;
   }
 }
