@@ -364,8 +364,20 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
     }
     __syncthreads();
   }
-  if (tid == 0) {
-    // overflow bases, destination-major for expert parallelism (id order when ep_ranks == 1)
+  if (a.ep_ranks == 1) {
+    // overflow bases in expert id order: an exclusive warp scan of the overflow counts
+    if (warp == 0) {
+      const int over = lane < E ? max(count_s[lane] - C, 0) : 0;
+      int incl = over;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      if (lane < E) obase_s[lane] = E * C + incl - over;
+    }
+  } else if (tid == 0) {
+    // destination-major for expert parallelism: expert e on rank e % G
     const int G = a.ep_ranks, El = E / G;
     int base = E * C;
     for (int q = 0; q < E; ++q) {
@@ -394,13 +406,15 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
     const float util = (float)c / (float)(2 * T);
     a.tab.stats[tid] = util;
     if (a.stats_out != nullptr) a.stats_out[tid] = util;
+    // aux = E * sum_e util_e * mean_t p_te: the terms in parallel (two
+    // divisions each), summed in expert order by one lane below
+    red_total[tid] = __float_as_int(util * (red_psum[tid] / (float)T));
   }
-  if (writer && warp == 1) {
-    // aux = E * sum_e util_e * mean_t p_te, summed in expert order by one lane
-    if (lane == 0) {
+  if (writer) {
+    __syncwarp();
+    if (tid == 0) {
       float aux = 0.f;
-      for (int x = 0; x < E; ++x)
-        aux += ((float)count_s[x] / (float)(2 * T)) * (red_psum[x] / (float)T);
+      for (int x = 0; x < E; ++x) aux += __int_as_float(red_total[x]);
       a.tab.stats[E] = (float)E * aux;
       if (a.stats_out != nullptr) a.stats_out[E] = (float)E * aux;
     }
