@@ -99,16 +99,38 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
   // the router weight is a parameter: its slabs stream in before the
   // upstream kernel (which writes x) has finished
   const int pre = min(kRouteStages, kb_count);
+  // When every slab has its own slot (d <= 64 * stages), all of them land on
+  // one barrier and the MMAs run as one straight chain: a wait and a commit
+  // per 4-MMA slab cost more than the MMAs themselves.
+  const bool whole = kb_count <= kRouteStages;
   if (threadIdx.x == 0) {
+    if (whole) mbar_arrive_expect_tx(&sm.full[0], (uint32_t)kb_count * (x_bytes + kWTile));
     for (int kb = 0; kb < pre; ++kb) {
-      mbar_arrive_expect_tx(&sm.full[kb], x_bytes + kWTile);
-      tma_load_2d(w_tiles + kb * kWTile, &w_map, kb * 64, 0, &sm.full[kb]);
+      uint64_t* bar = whole ? &sm.full[0] : &sm.full[kb];
+      if (!whole) mbar_arrive_expect_tx(bar, x_bytes + kWTile);
+      tma_load_2d(w_tiles + kb * kWTile, &w_map, kb * 64, 0, bar);
     }
   }
   griddep_wait();
   griddep_launch();
 
-  if (warp == 0) {
+  if (whole) {
+    if (warp == 0 && lane == 0) {
+      for (int kb = 0; kb < kb_count; ++kb)
+        tma_load_2d(x_tiles + kb * kRouteXTile, &x_map, kb * 64, tile * rows, &sm.full[0]);
+    } else if (warp == 1 && lane == 0) {
+      const uint32_t idesc = make_idesc(kRouteM, NP);
+      if (mbar_wait(&sm.full[0], 0, abort_flag, a.status, 21)) {
+        tc_fence_after();
+        for (int kb = 0; kb < kb_count; ++kb)
+          mma_slab(sm.tmem, sw128_desc(x_tiles + kb * kRouteXTile),
+                   sw128_desc(w_tiles + kb * kWTile), idesc, kb != 0);
+      }
+      mma_commit(&sm.done);
+    }
+    if (warp == 0 && lane == 0) mbar_drain(&sm.full[0], 0);  // every copy has landed
+    __syncwarp();
+  } else if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       static_assert(kRouteStages <= 32, "per-stage bit masks");
