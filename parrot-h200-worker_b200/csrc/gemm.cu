@@ -13,7 +13,7 @@
 //
 // Roles (320 threads, one CTA per SM):
 //   warp 0      TMA producer: 128-byte-swizzled K slabs of W and X into a
-//               4- or 5-stage shared-memory ring (no multicast anywhere).
+//               4- or 6-stage shared-memory ring (no multicast anywhere).
 //   warp 1      TMEM allocator + single-thread MMA issuer; tcgen05.commit
 //               frees ring stages and publishes finished accumulators.
 //   warps 2..9  epilogue: warps w and w + 4 read TMEM lane quarter w % 4 and
@@ -61,11 +61,13 @@ constexpr int kEpiTile = 32 * 64;             // per-warp staging: 32 tokens x 3
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSegMax = 2 * kMaxExperts;
 
-// Token tile BN (128 or 256 rows): the ring holds 5 stages of 16 + 16 KB or
-// 4 stages of 16 + 32 KB; the two TMEM accumulators take 2 * BN columns.
+// Token tile BN (128 or 256 rows): the ring holds 6 stages of 16 + 16 KB or
+// 4 stages of 16 + 32 KB (as many as shared memory holds: at small batches a
+// unit's loads are bound by the bytes in flight per SM over the L2 latency);
+// the two TMEM accumulators take 2 * BN columns.
 template <int BN>
 constexpr int stages_for() {
-  return BN == 256 ? 4 : 5;
+  return BN == 256 ? 4 : 6;
 }
 
 template <int BN>
