@@ -51,10 +51,21 @@ class GraphedForward:
                 self.output = model(self.input_ids, self.labels, **forward_kwargs)
 
     def __call__(self, input_ids: Tensor):
+        self.stage(input_ids)
+        self.graph.replay()
+        return self.output
+
+    def stage(self, input_ids: Tensor) -> None:
+        """Copy the next ids into the captured input buffer on the current
+        stream, without replaying: a pipelined caller can stage step i + 1's
+        ids (on another stream, ordered with events) while step i computes."""
         if tuple(input_ids.shape) != tuple(self.input_ids.shape):
             raise ValueError(f"captured for ids of shape {tuple(self.input_ids.shape)}, "
                              f"got {tuple(input_ids.shape)}")
         self.input_ids.copy_(input_ids, non_blocking=True)
+
+    def replay(self):
+        """Replay on the current stream with the ids already staged."""
         self.graph.replay()
         return self.output
 
