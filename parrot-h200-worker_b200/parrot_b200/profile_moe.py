@@ -6,7 +6,9 @@
 ``--tokens T`` runs ``iters`` eager calls of one Parrot XL MoE block (seeded
 weights ~N(0, 0.02), x ~ N(0, 1)); each call launches route, group,
 gate_up GEMM, down GEMM and combine, in that order.  ``--forward`` runs
-``iters`` eager Parrot XL forwards on 1 x 512 ids.  Device memory stays under
+``iters`` eager Parrot XL forwards on 1 x 512 ids.  ``--norms ROWS`` runs
+``iters`` rounds of RMSNorm, then the depth mix over 4 and over 8 sources
+(each with the consumer RMSNorm), on [ROWS, 768] bf16 rows.  Device memory stays under
 2 GB, so ``ncu`` captures of these commands end in seconds.
 """
 from __future__ import annotations
@@ -42,6 +44,23 @@ def moe_block(tokens: int, iters: int, zipf: bool) -> None:
     torch.cuda.synchronize()
 
 
+def norms(rows: int, iters: int) -> None:
+    from parrot_b200.model import DepthMix, RMSNorm
+    cfg = ModelConfig()
+    g = torch.Generator().manual_seed(0)
+    src = [torch.randn(rows, cfg.dim, generator=g).to("cuda", torch.bfloat16) for _ in range(8)]
+    norm = RMSNorm(cfg.dim, cfg.norm_eps).to("cuda", torch.bfloat16)
+    depth = DepthMix(cfg).to("cuda", torch.bfloat16)
+    with torch.no_grad():
+        depth.query.copy_(0.5 * torch.randn(cfg.dim, generator=g))
+    with torch.inference_mode():
+        for _ in range(iters):
+            norm(src[0])
+            depth.normalized(src[:4], norm)
+            depth.normalized(src, norm)
+    torch.cuda.synchronize()
+
+
 def forward(iters: int) -> None:
     torch.manual_seed(0)
     model = Parrot(ModelConfig()).to("cuda", torch.bfloat16).eval()
@@ -58,8 +77,11 @@ def main() -> None:
     p.add_argument("--iters", type=int, default=3)
     p.add_argument("--forward", action="store_true")
     p.add_argument("--zipf", action="store_true", help="Zipf(1.2) router bias (overflow path)")
+    p.add_argument("--norms", type=int, default=0, help="rows for the RMSNorm / depth-mix workload")
     a = p.parse_args()
-    if a.forward:
+    if a.norms:
+        norms(a.norms, a.iters)
+    elif a.forward:
         forward(a.iters)
     else:
         moe_block(a.tokens, a.iters, a.zipf)
