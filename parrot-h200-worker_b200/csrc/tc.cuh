@@ -232,5 +232,82 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t cols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
 }
 
+// ---- CTA pairs (cta_group::2): a 2-CTA cluster issues M = 256 MMAs ------
+// Each CTA of the pair holds half of A (its 128 weight rows) and half of B
+// (N / 2 token rows) in shared memory at the same offsets, and its TMEM holds
+// its 128 accumulator rows for all N columns; the even CTA (rank 0) issues
+// the MMAs.  No multicast load anywhere: each CTA's TMA writes only its own
+// shared memory and only signals the leader's barrier.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// every thread of both CTAs: orders shared-memory writes and barrier
+// initialisation with the peer's later remote accesses
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// address of this shared-memory location in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// TMA into this CTA's shared memory, completion counted on the leader's
+// barrier (mbar_cluster: a shared::cluster address from mapa_shared)
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t a, uint64_t b,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_slab_pair(uint32_t d_tmem, uint64_t da, uint64_t db,
+                                              uint32_t idesc, uint32_t accumulate_first) {
+  mma_bf16_pair(d_tmem, da, db, idesc, accumulate_first);
+  mma_bf16_pair(d_tmem, da + 2, db + 2, idesc, 1u);
+  mma_bf16_pair(d_tmem, da + 4, db + 4, idesc, 1u);
+  mma_bf16_pair(d_tmem, da + 6, db + 6, idesc, 1u);
+}
+
+// completion of the pair's MMAs arrives once on the barrier at this offset
+// in every CTA of cta_mask
+__device__ __forceinline__ void mma_commit_pair_mc(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t mbar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(mbar_cluster)
+               : "memory");
+}
+
 }  // namespace tc
 }  // namespace parrot
