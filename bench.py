@@ -145,8 +145,9 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 10))
-    warmup = max(1, min(args.warmup, 2))
+    # a CPU forward takes ~0.2 s: the requested counts (bounded) keep the run short
+    steps = max(1, min(args.steps, 100))
+    warmup = max(1, min(args.warmup, 10))
     base = cpu_reference_forward(steps, warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT,
