@@ -8,6 +8,7 @@ cross-compiles, so this runs on a machine without a GPU.
 from __future__ import annotations
 
 import concurrent.futures as cf
+import fcntl
 import os
 import shutil
 import subprocess
@@ -52,10 +53,26 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
-    """Build the library if any source is newer than it; return its path."""
+    """Build the library if any source is newer than it; return its path.
+
+    Processes that call this at once (the ranks of a torchrun job) take turns
+    on a lock file: the first builds, the others then find it up to date.
+    Without it they overwrote each other's objects and one loaded a library
+    linked from a half-written set."""
     if not force and up_to_date():
         return LIB_PATH
     BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    with open(BUILD_DIR / "build.lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if not force and up_to_date():
+                return LIB_PATH
+            return _build_locked(verbose, ptxas_info)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
+
+
+def _build_locked(verbose: bool, ptxas_info: bool) -> Path:
     exe = nvcc()
     extra = ["-Xptxas", "-v"] if ptxas_info else []
 
@@ -70,7 +87,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as pool:
         results = list(pool.map(compile_one, _sources()))
     logs = "".join(log for _, log in results)
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = LIB_PATH.with_suffix(f".so.{os.getpid()}.tmp")
     cmd = [exe, *ARCH_FLAGS, "-shared", "-o", str(tmp), *[str(o) for o, _ in results],
            "-lcudart_static", "-ldl", "-lrt", "-lpthread"]
     res = subprocess.run(cmd, capture_output=True, text=True)
