@@ -656,11 +656,11 @@ class Parrot(nn.Module):
                     raise ValueError("Local attention received an MLA cache")
             elif not isinstance(cache, MLALatentCache):
                 raise ValueError("MLA attention received a local cache")
-            addend = res.partial if attnres else None
-            delta = block.attention.decode(h, cache, state.position, addend=addend,
+            # the residual add is left to the next depth mix (attnres), as in forward
+            delta = block.attention.decode(h, cache, state.position,
                                            position_device=state.position_device)
             if attnres:
-                res.set_partial(delta)
+                res.add_delta(delta)
                 res.end_module(index)
             else:
                 x = x + delta
