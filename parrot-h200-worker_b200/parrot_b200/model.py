@@ -325,9 +325,17 @@ class GlobalMLA(nn.Module):
             aq = torch.einsum("hdl,hdm->hlm", wk, wq).reshape(c.n_heads * c.kv_latent_dim, c.dim)
             ao = torch.einsum("hdl,mhd->mhl", wv, wo).reshape(c.dim, c.n_heads * c.kv_latent_dim)
             dt = self.q.weight.dtype
-            hit = (version, (aq.to(dt).contiguous(), ao.to(dt).contiguous()))
+            aq, ao = aq.to(dt).contiguous(), ao.to(dt).contiguous()
+            # the fp32 forms the absorbed path multiplies with (model.py:420), kept
+            # with the cache instead of converted on every decode step
+            hit = (version, (aq, ao), (aq.float(), ao.float()))
             self.__dict__["_absorbed_cache"] = hit
         return hit[1]
+
+    def _absorbed_f32(self) -> tuple[Tensor, Tensor]:
+        """``_absorbed()`` as fp32 tensors (the bf16-rounded values, exactly)."""
+        self._absorbed()
+        return self.__dict__["_absorbed_cache"][2]
 
     def decode(self, x: Tensor, cache: MLALatentCache, position: int,
                addend: Tensor | None = None, defer_sum: bool = False,
@@ -338,26 +346,26 @@ class GlobalMLA(nn.Module):
             raise RuntimeError("deferred attention reduction is not part of the b200 backend")
         c = self.cfg
         b = x.shape[0]
-        aq, ao = self._absorbed()
+        aq, ao = self._absorbed_f32()
         if position_device is not None:
             # absorbed latent attention at the device position (capturable):
             # fp32 query over the bf16 latent cache, fp32 context (model.py:417-432)
             latent = self.kv_down(x).view(b, -1)
-            q = F.linear(x.float(), aq.float()).view(b, -1)
+            q = F.linear(x.float(), aq).view(b, -1)
             ctx = bridge.b200_decode_attention(
                 q, latent, None, cache.latent.unsqueeze(1), None, position_device, c.n_heads, 1,
                 c.kv_latent_dim, 0, c.head_dim ** -0.5, torch.float32)
-            out = F.linear(ctx.view(b, 1, -1), ao.float()).to(x.dtype)
+            out = F.linear(ctx.view(b, 1, -1), ao).to(x.dtype)
             return out if addend is None else addend + out
         cache.latent[:, position:position + 1].copy_(self.kv_down(x))
         seen = cache.latent[:, :position + 1]
-        q = F.linear(x.float(), aq.float()).view(b, 1, c.n_heads, c.kv_latent_dim).transpose(1, 2)
+        q = F.linear(x.float(), aq).view(b, 1, c.n_heads, c.kv_latent_dim).transpose(1, 2)
         # the absorbed query is fp32 (model.py:420); attend over the latents in fp32 too
         kv = seen[:, None].expand(-1, c.n_heads, -1, -1).float()
         with sdpa_kernel(_DECODE_SDPA):
             ctx = F.scaled_dot_product_attention(q, kv, kv, scale=c.head_dim ** -0.5)
         ctx = ctx.transpose(1, 2).reshape(b, 1, c.n_heads * c.kv_latent_dim)
-        out = F.linear(ctx, ao.float()).to(x.dtype)
+        out = F.linear(ctx, ao).to(x.dtype)
         return out if addend is None else addend + out
 
 
