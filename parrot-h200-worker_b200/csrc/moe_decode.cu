@@ -120,6 +120,8 @@ __global__ void __launch_bounds__(128) moe_decode_route_kernel(MoeDecodeArgs a) 
 // Gate/up + SwiGLU.  Work item c: feature block c % blocks of the
 // (c / blocks)-th chosen expert in ascending id, or of the shared expert after
 // the routed items; a CTA past the chosen experts' items returns at once.
+// NT: the token capacity of this instantiation (4 or kDecodeMoeMaxTokens).
+template <int NT>
 __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
   // [2 * kFeatPerCta rows][d / 8] gate/up rows, then [tokens][d / 8] token rows
   extern __shared__ __align__(16) uint4 wrows_s[];
@@ -197,39 +199,86 @@ __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
   cp_async_wait_all();
   __syncthreads();
 
-  // each feature's gate and up rows, dotted with every listed token
-  for (int fi = warp; fi < kFeatPerCta; fi += 4) {
-    const int f = f0 + fi;
-    const uint4* g_row = wrows_s + (size_t)(2 * fi) * nvec;
-    const uint4* u_row = g_row + nvec;
-    float acc_g[kDecodeMoeMaxTokens], acc_u[kDecodeMoeMaxTokens];
+  if constexpr (NT <= 4) {
+    // up to 4 tokens: warp w takes features 4w .. 4w + 3 together — one pass
+    // over d accumulates all 2 x 4 x NT dots (gate and up of each feature for
+    // each token), one warp_reduce_many folds them, and lane 2 NT q + i
+    // finishes feature q's token i with the gate total and the up total NT
+    // lanes above it
+    constexpr int FW = kFeatPerCta / 4;
+    constexpr int NV = 2 * FW * NT;  // values to reduce (32 at NT = 4)
+    static_assert(NV <= 32 && (NV & (NV - 1)) == 0, "one value per lane");
+    const int fb = warp * FW;
+    float acc[NV];
 #pragma unroll
-    for (int i = 0; i < kDecodeMoeMaxTokens; ++i) acc_g[i] = acc_u[i] = 0.f;
+    for (int v = 0; v < NV; ++v) acc[v] = 0.f;
     for (int c = lane; c < nvec; c += 32) {
-      float gf[8], uf[8];
-      bf16x8_to_float(g_row[c], gf);
-      bf16x8_to_float(u_row[c], uf);
+      float xf[NT][8];
 #pragma unroll
-      for (int i = 0; i < kDecodeMoeMaxTokens; ++i) {
+      for (int i = 0; i < NT; ++i) {
         if (i < n) {
-          float xf[8];
-          bf16x8_to_float(x_s[(size_t)i * nvec + c], xf);
+          bf16x8_to_float(x_s[(size_t)i * nvec + c], xf[i]);
+        } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            acc_g[i] = fmaf(gf[j], xf[j], acc_g[i]);
-            acc_u[i] = fmaf(uf[j], xf[j], acc_u[i]);
+          for (int j = 0; j < 8; ++j) xf[i][j] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 2 * FW; ++q) {  // row 2 (fb + q / 2) + q % 2: gate / up of a feature
+        float wf[8];
+        bf16x8_to_float(wrows_s[(size_t)(2 * fb + q) * nvec + c], wf);
+#pragma unroll
+        for (int i = 0; i < NT; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[q * NT + i] = fmaf(wf[j], xf[i][j], acc[q * NT + i]);
+      }
+    }
+    const float tot = warp_reduce_many<NV>(acc, lane);  // lane v: total of value v % NV
+    const float up_tot = __shfl_down_sync(0xffffffffu, tot, NT);
+    const int q = (lane % NV) / NT, i = lane % NT;
+    if (lane < NV && (q & 1) == 0 && i < n) {
+      const int f = f0 + fb + q / 2;
+      const float g = round_bf16(tot);
+      const float u = round_bf16(up_tot);
+      const float silu = round_bf16(g / (1.0f + expf(-g)));
+      a.hidden[((size_t)list_s[i] * 3 + slot_s[i]) * H + f] = __float2bfloat16_rn(silu * u);
+    }
+  } else {
+    // each feature's gate and up rows, dotted with every listed token
+    // (a warp per feature, the features of a warp one after the other)
+    for (int fi = warp; fi < kFeatPerCta; fi += 4) {
+      const int f = f0 + fi;
+      const uint4* g_row = wrows_s + (size_t)(2 * fi) * nvec;
+      const uint4* u_row = g_row + nvec;
+      float acc_g[kDecodeMoeMaxTokens], acc_u[kDecodeMoeMaxTokens];
+#pragma unroll
+      for (int i = 0; i < kDecodeMoeMaxTokens; ++i) acc_g[i] = acc_u[i] = 0.f;
+      for (int c = lane; c < nvec; c += 32) {
+        float gf[8], uf[8];
+        bf16x8_to_float(g_row[c], gf);
+        bf16x8_to_float(u_row[c], uf);
+#pragma unroll
+        for (int i = 0; i < kDecodeMoeMaxTokens; ++i) {
+          if (i < n) {
+            float xf[8];
+            bf16x8_to_float(x_s[(size_t)i * nvec + c], xf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              acc_g[i] = fmaf(gf[j], xf[j], acc_g[i]);
+              acc_u[i] = fmaf(uf[j], xf[j], acc_u[i]);
+            }
           }
         }
       }
-    }
 #pragma unroll
-    for (int i = 0; i < kDecodeMoeMaxTokens; ++i) {
-      if (i < n) {
-        const float g = round_bf16(warp_sum(acc_g[i]));
-        const float u = round_bf16(warp_sum(acc_u[i]));
-        if (lane == 0) {
-          const float silu = round_bf16(g / (1.0f + expf(-g)));
-          a.hidden[((size_t)list_s[i] * 3 + slot_s[i]) * H + f] = __float2bfloat16_rn(silu * u);
+      for (int i = 0; i < kDecodeMoeMaxTokens; ++i) {
+        if (i < n) {
+          const float g = round_bf16(warp_sum(acc_g[i]));
+          const float u = round_bf16(warp_sum(acc_u[i]));
+          if (lane == 0) {
+            const float silu = round_bf16(g / (1.0f + expf(-g)));
+            a.hidden[((size_t)list_s[i] * 3 + slot_s[i]) * H + f] = __float2bfloat16_rn(silu * u);
+          }
         }
       }
     }
@@ -304,9 +353,15 @@ int launch_moe_decode(const MoeDecodeArgs& a, cudaStream_t stream) {
   if (!(configured & (1ull << dev))) {
     if (cudaFuncSetAttribute(moe_decode_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (kMaxExperts + 4) * 1024 * 2) != cudaSuccess ||
-        cudaFuncSetAttribute(moe_decode_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(moe_decode_up_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (2 * kFeatPerCta + 4) * 1024 * 2) != cudaSuccess ||
+        cudaFuncSetAttribute(moe_decode_up_kernel<4>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
+        cudaFuncSetAttribute(moe_decode_up_kernel<kDecodeMoeMaxTokens>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (2 * kFeatPerCta + kDecodeMoeMaxTokens) * 1024 * 2) != cudaSuccess ||
-        cudaFuncSetAttribute(moe_decode_up_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+        cudaFuncSetAttribute(moe_decode_up_kernel<kDecodeMoeMaxTokens>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
         cudaFuncSetAttribute(moe_decode_down_kernel,
                              cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -321,8 +376,10 @@ int launch_moe_decode(const MoeDecodeArgs& a, cudaStream_t stream) {
   const size_t route_smem = (size_t)(a.n_experts + 4) * a.dim * 2;
   if (launch_pdl(moe_decode_route_kernel, dim3((a.tokens + 3) / 4), dim3(128), route_smem, stream,
                  a) != cudaSuccess ||
-      launch_pdl(moe_decode_up_kernel, dim3(up_ctas), dim3(128), up_smem, stream, a) !=
-          cudaSuccess)
+      (a.tokens <= 4
+           ? launch_pdl(moe_decode_up_kernel<4>, dim3(up_ctas), dim3(128), up_smem, stream, a)
+           : launch_pdl(moe_decode_up_kernel<kDecodeMoeMaxTokens>, dim3(up_ctas), dim3(128),
+                        up_smem, stream, a)) != cudaSuccess)
     return -2;
   return launch_pdl(moe_decode_down_kernel, dim3(a.tokens * (a.dim / kColsPerCta)), dim3(128),
                     down_smem, stream, a) == cudaSuccess
