@@ -317,29 +317,40 @@ __global__ void __launch_bounds__(128) moe_decode_down_kernel(MoeDecodeArgs a) {
   }
   cp_async_wait_all();
   __syncthreads();
-  for (int oi = warp; oi < kColsPerCta; oi += 4) {
-    const int o = o0 + oi;
-    float y[3] = {0.f, 0.f, 0.f};
+  // warp w takes output columns 4w .. 4w + 3 together: its lanes hold their
+  // slices of the three hidden vectors once, accumulate the 4 x 3 dots in one
+  // pass, one warp_reduce_many folds them (lane 4 c + k: column c, source k)
+  // and lane 4 c combines column c exactly as the block's combine does
+  static_assert(kColsPerCta == 16, "four columns per warp");
+  const int cb = warp * 4;
+  float acc[16];
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      const int nv = k < 2 ? hv : hsv;
-      const uint4* wr = rows[k] + (size_t)oi * nv;
-      for (int c = lane; c < nv; c += 32) {
-        float wf[8], hf[8];
-        bf16x8_to_float(wr[c], wf);
-        bf16x8_to_float(reinterpret_cast<const uint4*>(&h_s[k][0])[c], hf);
+  for (int v = 0; v < 16; ++v) acc[v] = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) y[k] = fmaf(wf[j], hf[j], y[k]);
+  for (int k = 0; k < 3; ++k) {
+    const int nv = k < 2 ? hv : hsv;
+    for (int c = lane; c < nv; c += 32) {
+      float hf[8];
+      bf16x8_to_float(reinterpret_cast<const uint4*>(&h_s[k][0])[c], hf);
+#pragma unroll
+      for (int ci = 0; ci < 4; ++ci) {
+        float wf[8];
+        bf16x8_to_float(rows[k][(size_t)(cb + ci) * nv + c], wf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[4 * ci + k] = fmaf(wf[j], hf[j], acc[4 * ci + k]);
       }
-      y[k] = warp_sum(y[k]);
     }
-    if (lane == 0) {
-      const float c0 = round_bf16(round_bf16(y[0]) * w0), c1 = round_bf16(round_bf16(y[1]) * w1);
-      const float lo = e0 < e1 ? c0 : c1, hi = e0 < e1 ? c1 : c0;
-      float r = round_bf16(round_bf16(round_bf16(y[2]) + lo) + hi);
-      if (a.residual != nullptr) r = __bfloat162float(a.residual[(size_t)t * d + o]) + r;
-      a.out[(size_t)t * d + o] = __float2bfloat16_rn(r);
-    }
+  }
+  const float tot = warp_reduce_many<16>(acc, lane);
+  const float y1 = __shfl_down_sync(0xffffffffu, tot, 1);
+  const float y2 = __shfl_down_sync(0xffffffffu, tot, 2);
+  if (lane < 16 && (lane & 3) == 0) {
+    const int o = o0 + cb + (lane >> 2);
+    const float c0 = round_bf16(round_bf16(tot) * w0), c1 = round_bf16(round_bf16(y1) * w1);
+    const float lo = e0 < e1 ? c0 : c1, hi = e0 < e1 ? c1 : c0;
+    float r = round_bf16(round_bf16(round_bf16(y2) + lo) + hi);
+    if (a.residual != nullptr) r = __bfloat162float(a.residual[(size_t)t * d + o]) + r;
+    a.out[(size_t)t * d + o] = __float2bfloat16_rn(r);
   }
 }
 
