@@ -125,8 +125,11 @@ int parrot_rope_inplace_at_bf16(void* x, const void* cos_table, const void* sin_
  * Supported (D, H / KVH): (96, 4), (96, 1), (128, 8), (32, 2), (32, 4).
  * q_row_stride / kv_row_stride: elements between batch rows of q and of
  * k_new / v_new (0 = packed), so q, k and v can be views of one projection.
- * partials: parrot_decode_attention_scratch_bytes() of scratch.  A position
- * outside [0, max_positions) is recorded in status and nothing is written. */
+ * partials: parrot_decode_attention_scratch_bytes() of scratch, zero-filled
+ * before its first use (it ends every call zero-filled where that matters: the
+ * per-group arrival counters after the partials); calls that share it must be
+ * ordered on one stream.  A position outside [0, max_positions) is recorded in
+ * status and nothing is written. */
 int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f32,
                                  long long q_row_stride, const void* k_new, const void* v_new,
                                  long long kv_row_stride, void* k_cache, void* v_cache,

@@ -634,7 +634,6 @@ int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f3
   if (batch < 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads ||
       max_positions <= 0 || window < 0)
     return fail(PARROT_EINVAL, "decode_attention: bad sizes%s");
-  const int n_chunks = parrot::decode_attn_chunks(max_positions);
   if (partial_bytes < parrot_decode_attention_scratch_bytes(batch, n_heads, max_positions, head_dim))
     return fail(PARROT_EINVAL, "decode_attention: partials smaller than the scratch size%s");
   if (batch == 0) return PARROT_OK;
@@ -650,7 +649,10 @@ int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f3
   a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
   a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
   a.pos = pos_dev;
+  a.slots = parrot::decode_attn_slots(batch, max_positions);
   a.part = static_cast<float*>(partials);
+  a.counters = reinterpret_cast<int*>(static_cast<char*>(partials) +
+                                      (size_t)batch * n_heads * a.slots * (head_dim + 2) * sizeof(float));
   a.out = out;
   a.out_f32 = out_f32;
   a.B = batch;
@@ -659,7 +661,6 @@ int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f3
   a.S = max_positions;
   a.D = head_dim;
   a.window = window;
-  a.n_chunks = n_chunks;
   a.q_row = q_row_stride > 0 ? q_row_stride : (long long)n_heads * head_dim;
   a.kv_row = kv_row_stride > 0 ? kv_row_stride : (long long)n_kv_heads * head_dim;
   if (a.kv_row % 8 || (long long)n_kv_heads * head_dim > a.kv_row || (long long)n_heads * head_dim > a.q_row)
@@ -675,8 +676,10 @@ int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f3
 
 size_t parrot_decode_attention_scratch_bytes(int batch, int n_heads, int max_positions,
                                              int head_dim) {
-  return (size_t)batch * n_heads * parrot::decode_attn_chunks(max_positions) * (head_dim + 2) *
-         sizeof(float);
+  // partials [B, H, slots, D + 2] fp32, then one arrival counter per (batch row, head)
+  return (size_t)batch * n_heads * parrot::decode_attn_slots(batch, max_positions) *
+             (head_dim + 2) * sizeof(float) +
+         (size_t)batch * n_heads * sizeof(int);
 }
 
 int parrot_moe_capacity(int tokens, int n_experts) {

@@ -169,16 +169,18 @@ struct DecodeAttnArgs {
   __nv_bfloat16* k_cache;        // [B, KVH, S, D]
   __nv_bfloat16* v_cache;        // [B, KVH, S, D], or null (values = keys)
   const int* pos;                // device: position of this step's token
-  float* part;                   // [B, H, n_chunks, D + 2] partials (scratch)
+  float* part;                   // [B, H, slots, D + 2] partials (scratch)
+  int* counters;                 // [B, KVH] arrivals per group, zero between launches
   void* out;                     // [B, H, D] bf16, or fp32 when out_f32
   int out_f32;
-  int B, H, KVH, S, D, window, n_chunks;
+  int B, H, KVH, S, D, window, slots;
   long long q_row, kv_row;       // elements between batch rows of q / of k_new and v_new
   float scale;
   int* status;
 };
 int launch_decode_attention(const DecodeAttnArgs& args, cudaStream_t stream);
 int decode_attn_chunks(int max_positions);
+int decode_attn_slots(int batch, int max_positions);
 
 int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat16* w,
                    int rows, int dim, float eps, cudaStream_t stream);

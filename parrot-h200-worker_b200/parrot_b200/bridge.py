@@ -142,7 +142,7 @@ def b200_decode_attention(q: Tensor, k_new: Tensor, v_new: Tensor | None, k_cach
     scratch = _DECODE_SCRATCH.get(key)
     if scratch is None:
         n = lib.parrot_decode_attention_scratch_bytes(b, n_heads, s_max, head_dim)
-        scratch = torch.empty(int(n), device=k_cache.device, dtype=torch.uint8)
+        scratch = torch.zeros(int(n), device=k_cache.device, dtype=torch.uint8)
         _DECODE_SCRATCH[key] = scratch
     out = torch.empty((b, n_heads * head_dim), device=q.device, dtype=out_dtype)
     _lib.check(lib.parrot_decode_attention_bf16(

@@ -176,12 +176,16 @@ def test_depth_mix_pending_residual_resolves_the_add():
     assert torch.equal(got, plain)
 
 
-@pytest.mark.parametrize("mode,pos,batch", [("local", 0, 1), ("local", 127, 3), ("local", 128, 2),
-                                            ("local", 2300, 2), ("mla", 5, 2), ("mla", 700, 1)])
+@pytest.mark.parametrize("mode,pos,batch", [("local", 0, 1), ("local", 31, 1), ("local", 32, 1),
+                                            ("local", 127, 3), ("local", 128, 2), ("local", 2300, 2),
+                                            ("local", 1000, 64), ("local", 2300, 64), ("mla", 0, 1),
+                                            ("mla", 5, 2), ("mla", 700, 1), ("mla", 900, 64)])
 def test_decode_attention_matches_sdpa(mode, pos, batch):
     """parrot_decode_attention_bf16 at XL shapes against PyTorch SDPA on the
     same cache contents: local GQA (8 heads x 96 over 2 KV heads, window
-    2048) and absorbed MLA (fp32 query over the 128-wide latent)."""
+    2048) and absorbed MLA (fp32 query over the 128-wide latent); one chunk
+    (finished in one CTA), chunk edges, the window edge, and batch 64 (four
+    CTAs per group, each looping over chunks)."""
     g = torch.Generator().manual_seed(pos + batch)
     S = 4096
     position = torch.full((1,), pos, device="cuda", dtype=torch.int32)
@@ -194,6 +198,9 @@ def test_decode_attention_matches_sdpa(mode, pos, batch):
         q, kn, vn = qkv[:, :qw], qkv[:, qw:qw + kw], qkv[:, qw + kw:]
         out = bridge.b200_decode_attention(q, kn, vn, kc, vc, position, H, KVH, D, window,
                                            D ** -0.5, torch.bfloat16)
+        # a second call (the arrival counters were reset) gives the same bits
+        assert torch.equal(out, bridge.b200_decode_attention(
+            q, kn, vn, kc, vc, position, H, KVH, D, window, D ** -0.5, torch.bfloat16))
         assert torch.equal(kc[:, :, pos], kn.view(batch, KVH, D))
         assert torch.equal(vc[:, :, pos], vn.view(batch, KVH, D))
         lo = max(0, pos - window + 1)
@@ -208,6 +215,8 @@ def test_decode_attention_matches_sdpa(mode, pos, batch):
         new = torch.randn(batch, L, generator=g).to("cuda", torch.bfloat16)
         out = bridge.b200_decode_attention(q, new, None, lat.unsqueeze(1), None, position, H, 1,
                                            L, 0, hd ** -0.5, torch.float32)
+        assert torch.equal(out, bridge.b200_decode_attention(
+            q, new, None, lat.unsqueeze(1), None, position, H, 1, L, 0, hd ** -0.5, torch.float32))
         assert torch.equal(lat[:, pos], new)
         seen = lat[:, :pos + 1].float()[:, None].expand(-1, H, -1, -1)
         ref = torch.nn.functional.scaled_dot_product_attention(
