@@ -3,7 +3,10 @@
 //
 // moe_decode_route_kernel: one warp per token: fp32 logits of the bf16 row,
 //                          softmax, top-2 with the lower id on ties,
-//                          renormalised weights (model.py:521-527).
+//                          renormalised weights (model.py:521-527).  Up to 4
+//                          tokens it is not launched: every routed gate/up CTA
+//                          computes the same routing itself (route_small) and
+//                          CTA 0 publishes it.
 // moe_decode_up_kernel:    work item = 16 SwiGLU features of one chosen
 //                          expert (ascending id; at most min(E, 2T) of them)
 //                          or of the shared expert: the CTA stages the
@@ -41,6 +44,97 @@ __device__ __forceinline__ size_t tiled_index(int m, int row, int col, int rows,
 }
 }  // namespace
 
+// Softmax, top-2 with the lower id on ties and renormalised weights of token
+// t, from its fp32 logit in lane e (expert e; lanes >= E hold anything).  All
+// lanes get the chosen ids; with `publish` the route outputs are written.
+__device__ __forceinline__ void finish_route(const MoeDecodeArgs& a, int t, float logit, int lane,
+                                             bool publish, int* i1_out, int* i2_out) {
+  const int E = a.n_experts;
+  const bool valid = lane < E;
+  if (valid && a.router_bias != nullptr) logit += __ldg(a.router_bias + lane);
+  const float m = warp_max(valid ? logit : -INFINITY);
+  const float ev = valid ? expf(logit - m) : 0.f;
+  const float p = ev / warp_sum(ev);
+  float v1 = valid ? p : -1.f;
+  int i1 = lane;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v1, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i1, o);
+    if (ov > v1 || (ov == v1 && oi < i1)) { v1 = ov; i1 = oi; }
+  }
+  float v2 = (valid && lane != i1) ? p : -1.f;
+  int i2 = lane;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v2, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i2, o);
+    if (ov > v2 || (ov == v2 && oi < i2)) { v2 = ov; i2 = oi; }
+  }
+  *i1_out = i1;
+  *i2_out = i2;
+  if (!publish) return;
+  if (valid && a.probs != nullptr) a.probs[(size_t)t * E + lane] = p;
+  if (lane == 0) {
+    const float sel = v1 + v2;
+    const float w1 = v1 / sel, w2 = v2 / sel;
+    a.indices[2 * t] = i1;
+    a.indices[2 * t + 1] = i2;
+    a.weights[2 * t] = w1;
+    a.weights[2 * t + 1] = w2;
+    if (a.indices64 != nullptr) {
+      a.indices64[2 * t] = i1;
+      a.indices64[2 * t + 1] = i2;
+    }
+    if (a.weights_out != nullptr) {
+      a.weights_out[2 * t] = w1;
+      a.weights_out[2 * t + 1] = w2;
+    }
+  }
+}
+
+// Router for up to 4 tokens inside a gate/up CTA: all 128 threads split d
+// (thread c: 16-byte vector c of every token row against every expert row),
+// one warp_reduce_many per token and warp, the four warps' partials added in
+// shared memory; warp t finishes token t.  x_s: [T][d / 8] token rows, r_s:
+// [E][d / 8] router rows; the chosen ids land in ids_s.
+__device__ __forceinline__ void route_small(const MoeDecodeArgs& a, const uint4* r_s,
+                                            const uint4* x_s, int* ids_s, float* red_s,
+                                            bool publish) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = a.tokens, E = a.n_experts, nvec = a.dim >> 3;
+  for (int t = 0; t < T; ++t) {
+    float part[kMaxExperts];
+#pragma unroll
+    for (int e = 0; e < kMaxExperts; ++e) part[e] = 0.f;
+    for (int c = threadIdx.x; c < nvec; c += blockDim.x) {
+      float xf[8];
+      bf16x8_to_float(x_s[(size_t)t * nvec + c], xf);
+#pragma unroll
+      for (int e = 0; e < kMaxExperts; ++e) {
+        if (e < E) {
+          float wf[8];
+          bf16x8_to_float(r_s[(size_t)e * nvec + c], wf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) part[e] = fmaf(xf[j], wf[j], part[e]);
+        }
+      }
+    }
+    red_s[(t * 4 + warp) * 32 + lane] = warp_reduce_many<kMaxExperts>(part, lane);
+  }
+  __syncthreads();
+  if (warp < T) {
+    const float* r = red_s + warp * 4 * 32 + lane;
+    const float logit = (r[0] + r[32]) + (r[64] + r[96]);
+    int i1, i2;
+    finish_route(a, warp, logit, lane, publish, &i1, &i2);
+    if (lane == 0) {
+      ids_s[2 * warp] = i1;
+      ids_s[2 * warp + 1] = i2;
+    }
+  }
+}
+
 // Router: one warp per token (lanes over d, every expert's dot reduced
 // together), softmax, top-2 with the lower id on ties, renormalised weights.
 __global__ void __launch_bounds__(128) moe_decode_route_kernel(MoeDecodeArgs a) {
@@ -76,45 +170,9 @@ __global__ void __launch_bounds__(128) moe_decode_route_kernel(MoeDecodeArgs a) 
       }
     }
   }
-  float logit = warp_reduce_many<kMaxExperts>(part, lane);  // lane e: expert e
-  const bool valid = lane < E;
-  if (valid && a.router_bias != nullptr) logit += __ldg(a.router_bias + lane);
-  const float m = warp_max(valid ? logit : -INFINITY);
-  const float ev = valid ? expf(logit - m) : 0.f;
-  const float p = ev / warp_sum(ev);
-  float v1 = valid ? p : -1.f;
-  int i1 = lane;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, v1, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, i1, o);
-    if (ov > v1 || (ov == v1 && oi < i1)) { v1 = ov; i1 = oi; }
-  }
-  float v2 = (valid && lane != i1) ? p : -1.f;
-  int i2 = lane;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, v2, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, i2, o);
-    if (ov > v2 || (ov == v2 && oi < i2)) { v2 = ov; i2 = oi; }
-  }
-  if (valid && a.probs != nullptr) a.probs[(size_t)t * E + lane] = p;
-  if (lane == 0) {
-    const float sel = v1 + v2;
-    const float w1 = v1 / sel, w2 = v2 / sel;
-    a.indices[2 * t] = i1;
-    a.indices[2 * t + 1] = i2;
-    a.weights[2 * t] = w1;
-    a.weights[2 * t + 1] = w2;
-    if (a.indices64 != nullptr) {
-      a.indices64[2 * t] = i1;
-      a.indices64[2 * t + 1] = i2;
-    }
-    if (a.weights_out != nullptr) {
-      a.weights_out[2 * t] = w1;
-      a.weights_out[2 * t + 1] = w2;
-    }
-  }
+  const float logit = warp_reduce_many<kMaxExperts>(part, lane);  // lane e: expert e
+  int i1, i2;
+  finish_route(a, t, logit, lane, true, &i1, &i2);
 }
 
 // Gate/up + SwiGLU.  Work item c: feature block c % blocks of the
@@ -131,7 +189,10 @@ __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
   const int T = a.tokens, d = a.dim, E = a.n_experts, H = a.expert_dim, Hs = a.shared_dim;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nvec = d >> 3;
+  // NT <= 4: every token row [T][d / 8], then the router rows [E][d / 8];
+  // otherwise the listed tokens' rows
   uint4* x_s = wrows_s + (size_t)2 * kFeatPerCta * nvec;
+  uint4* r_s = x_s + (size_t)NT * nvec;
   const int routed_blocks = H / kFeatPerCta;
   const int max_chosen = min(E, 2 * T);
   const bool shared = (int)blockIdx.x >= max_chosen * routed_blocks;
@@ -146,10 +207,28 @@ __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
       cp_async16(wrows_s + i, a.shared_gate_up + tiled_index(0, row, c * 8, 2 * Hs, d));
     }
   }
-  griddep_wait();
-  griddep_launch();
   __shared__ int ids_s[2 * kDecodeMoeMaxTokens];
-  if (threadIdx.x < 2 * T) ids_s[threadIdx.x] = a.indices[threadIdx.x];  // one parallel load
+  if constexpr (NT <= 4) {
+    // routed CTAs route the (at most 4) tokens themselves: the router weight
+    // is a parameter, so it is in flight before the wait
+    if (!shared)
+      for (int i = threadIdx.x; i < E * nvec; i += blockDim.x)
+        cp_async16(r_s + i, reinterpret_cast<const uint4*>(a.router) + i);
+    griddep_wait();
+    griddep_launch();
+    for (int i = threadIdx.x; i < T * nvec; i += blockDim.x)
+      cp_async16(x_s + i, reinterpret_cast<const uint4*>(a.x) + i);
+    if (!shared) {
+      __shared__ float red_s[4 * 4 * 32];
+      cp_async_wait_all();
+      __syncthreads();
+      route_small(a, r_s, x_s, ids_s, red_s, blockIdx.x == 0);  // CTA 0 publishes
+    }
+  } else {
+    griddep_wait();
+    griddep_launch();
+    if (threadIdx.x < 2 * T) ids_s[threadIdx.x] = a.indices[threadIdx.x];  // one parallel load
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     int e = -1;
@@ -192,9 +271,11 @@ __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
       cp_async16(wrows_s + i, a.gate_up + tiled_index(e, row, c * 8, 2 * H, d));
     }
   }
-  for (int i = threadIdx.x; i < n * nvec; i += blockDim.x) {
-    const int li = i / nvec, c = i - li * nvec;
-    cp_async16(x_s + i, reinterpret_cast<const uint4*>(a.x) + (size_t)list_s[li] * nvec + c);
+  if constexpr (NT > 4) {
+    for (int i = threadIdx.x; i < n * nvec; i += blockDim.x) {
+      const int li = i / nvec, c = i - li * nvec;
+      cp_async16(x_s + i, reinterpret_cast<const uint4*>(a.x) + (size_t)list_s[li] * nvec + c);
+    }
   }
   cp_async_wait_all();
   __syncthreads();
@@ -217,7 +298,7 @@ __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
 #pragma unroll
       for (int i = 0; i < NT; ++i) {
         if (i < n) {
-          bf16x8_to_float(x_s[(size_t)i * nvec + c], xf[i]);
+          bf16x8_to_float(x_s[(size_t)list_s[i] * nvec + c], xf[i]);
         } else {
 #pragma unroll
           for (int j = 0; j < 8; ++j) xf[i][j] = 0.f;
@@ -356,7 +437,8 @@ __global__ void __launch_bounds__(128) moe_decode_down_kernel(MoeDecodeArgs a) {
 
 int launch_moe_decode(const MoeDecodeArgs& a, cudaStream_t stream) {
   if (a.tokens == 0) return 0;
-  const size_t up_smem = (size_t)(2 * kFeatPerCta + a.tokens) * a.dim * 2;
+  const size_t up_smem = (size_t)(2 * kFeatPerCta + (a.tokens <= 4 ? 4 + a.n_experts : a.tokens)) *
+                         a.dim * 2;
   const size_t down_smem = (size_t)kColsPerCta * (2 * a.expert_dim + a.shared_dim) * 2;
   static unsigned long long configured = 0;  // per device
   int dev = 0;
@@ -365,7 +447,7 @@ int launch_moe_decode(const MoeDecodeArgs& a, cudaStream_t stream) {
     if (cudaFuncSetAttribute(moe_decode_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (kMaxExperts + 4) * 1024 * 2) != cudaSuccess ||
         cudaFuncSetAttribute(moe_decode_up_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (2 * kFeatPerCta + 4) * 1024 * 2) != cudaSuccess ||
+                             (2 * kFeatPerCta + 4 + kMaxExperts) * 1024 * 2) != cudaSuccess ||
         cudaFuncSetAttribute(moe_decode_up_kernel<4>, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
         cudaFuncSetAttribute(moe_decode_up_kernel<kDecodeMoeMaxTokens>,
@@ -385,8 +467,9 @@ int launch_moe_decode(const MoeDecodeArgs& a, cudaStream_t stream) {
   const int max_chosen = a.n_experts < 2 * a.tokens ? a.n_experts : 2 * a.tokens;
   const int up_ctas = max_chosen * (a.expert_dim / kFeatPerCta) + a.shared_dim / kFeatPerCta;
   const size_t route_smem = (size_t)(a.n_experts + 4) * a.dim * 2;
-  if (launch_pdl(moe_decode_route_kernel, dim3((a.tokens + 3) / 4), dim3(128), route_smem, stream,
-                 a) != cudaSuccess ||
+  // up to 4 tokens the gate/up CTAs route the tokens themselves
+  if ((a.tokens > 4 && launch_pdl(moe_decode_route_kernel, dim3((a.tokens + 3) / 4), dim3(128),
+                                  route_smem, stream, a) != cudaSuccess) ||
       (a.tokens <= 4
            ? launch_pdl(moe_decode_up_kernel<4>, dim3(up_ctas), dim3(128), up_smem, stream, a)
            : launch_pdl(moe_decode_up_kernel<kDecodeMoeMaxTokens>, dim3(up_ctas), dim3(128),
