@@ -35,6 +35,10 @@ __device__ __forceinline__ void report_status(int* status, int code, int site, i
 // ---------------------------------------------------------------------------
 // bf16 <-> fp32 vector helpers (16-byte rows)
 // ---------------------------------------------------------------------------
+// bf16 pair (low half first) -> fp32 pair, exact
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
 __device__ __forceinline__ void bf16x8_to_float(const uint4& v, float f[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll

@@ -104,9 +104,11 @@ int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat
 // ---------------------------------------------------------------------------
 // NS: the source capacity of this instantiation (2, 4, 8 or 16 >= n_sources),
 // so the per-source arrays and loops are sized to the call.
+// Up to 8 sources the kernel fits 80 registers without spilling, so 768
+// threads (8 CTAs at d = 768) stay resident per SM; 16 sources need more.
 template <int W, int NS>
-__global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
-  __shared__ float red_ss[W][NS], red_raw[W][NS], red_sq[W];
+__global__ void __launch_bounds__(32 * W, NS <= 8 ? 768 / (32 * W) : 1) depthmix_kernel(DepthMixArgs a) {
+  __shared__ float red_sr[W][2 * NS], red_sq[W];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = threadIdx.x;
   const int dim = a.dim, nvec = dim >> 3, S = a.n_sources;
@@ -171,77 +173,101 @@ __global__ void __launch_bounds__(32 * W, 1) depthmix_kernel(DepthMixArgs a) {
     }
     reinterpret_cast<uint4*>(a.pending_out + off)[c] = r;
   }
-  // source s as this thread sees it (reads only: a store into v[S - 1] would
-  // make the compiler index the array at run time, in local memory)
-  auto source = [&](int s) { return (pending && s == S - 1) ? r : v[s]; };
-
-  // key.query weight per column (the score needs sum_d v kw q, not the key itself)
-  float kq[8];
+  // source s as this thread sees it.  Up to 8 sources the deferred one takes
+  // its register slot once (a select per slot); with 16 the compiler turns
+  // those selects into a run-time indexed store (local memory), so there each
+  // read selects instead.
+  if constexpr (NS <= 8) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) kq[j] = kw[j] * q[j];
-  // 2. per-source sums of squares and raw key.query dots
-  float ss[NS], raw[NS];
-#pragma unroll
-  for (int s = 0; s < NS; ++s) {
-    ss[s] = 0.f;
-    raw[s] = 0.f;
-    if (s < S) {
-      float f[8];
-      bf16x8_to_float(source(s), f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        ss[s] = fmaf(f[j], f[j], ss[s]);
-        raw[s] = fmaf(f[j], kq[j], raw[s]);
-      }
+    for (int s = 0; s < NS; ++s) {
+      const bool take = pending && s == S - 1;
+      v[s].x = take ? r.x : v[s].x;
+      v[s].y = take ? r.y : v[s].y;
+      v[s].z = take ? r.z : v[s].z;
+      v[s].w = take ? r.w : v[s].w;
     }
   }
-  const float ss_l = warp_reduce_many<NS>(ss, lane);
-  const float raw_l = warp_reduce_many<NS>(raw, lane);
-  if (lane < NS) {  // lane l holds the warp's totals of source l
-    red_ss[warp][lane] = ss_l;
-    red_raw[warp][lane] = raw_l;
+  auto source = [&](int s) {
+    if constexpr (NS <= 8) return v[s];
+    else return (pending && s == S - 1) ? r : v[s];
+  };
+
+  // key.query weight per column pair (the score needs sum_d v kw q, not the
+  // key itself); the per-column sums below run on packed fp32 pairs
+  float2 kq[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) kq[p] = make_float2(kw[2 * p] * q[2 * p], kw[2 * p + 1] * q[2 * p + 1]);
+  // 2. per-source sums of squares and raw key.query dots, folded across the
+  // warp together: lane s holds source s's sum of squares, lane NS + s its dot
+  float sr[2 * NS];
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    sr[s] = 0.f;
+    sr[NS + s] = 0.f;
+    if (s < S) {
+      const uint4 sv = source(s);
+      const uint32_t w[4] = {sv.x, sv.y, sv.z, sv.w};
+      float2 ss2 = make_float2(0.f, 0.f), raw2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const float2 f2 = bf16x2_to_float2(w[p]);
+        ss2 = __ffma2_rn(f2, f2, ss2);
+        raw2 = __ffma2_rn(f2, kq[p], raw2);
+      }
+      sr[s] = ss2.x + ss2.y;
+      sr[NS + s] = raw2.x + raw2.y;
+    }
   }
+  const float sr_l = warp_reduce_many<2 * NS>(sr, lane);
+  if (lane < 2 * NS) red_sr[warp][lane] = sr_l;
   __syncthreads();
 
-  // 3. scores and softmax (every thread, same order), then the mix
-  float alpha[NS];
-  float m = -INFINITY;
-  // short dependent chains matter here (a few warps per SM): one reciprocal
-  // for the mean, one for the softmax denominator, the fast exp
+  // 3. scores and softmax: lane s of every warp scores source s (the warps'
+  // partials added in warp order), the max over lanes, its exponential; each
+  // thread gathers the S exponentials and sums them in source order, so all
+  // threads agree bit for bit.  Short dependent chains matter here (a few
+  // warps per SM): one reciprocal for the mean, one for the denominator, the
+  // fast exp.
   const float inv_dim = 1.0f / (float)dim;
+  float score = -INFINITY;
+  if (lane < S) {
+    float tss = 0.f, traw = 0.f;
 #pragma unroll
-  for (int s = 0; s < NS; ++s) {
-    alpha[s] = -INFINITY;
-    if (s < S) {
-      float tss = 0.f, traw = 0.f;
-#pragma unroll
-      for (int w = 0; w < W; ++w) {
-        tss += red_ss[w][s];
-        traw += red_raw[w][s];
-      }
-      alpha[s] = rsqrtf(tss * inv_dim + a.key_eps) * traw;
-      m = fmaxf(m, alpha[s]);
+    for (int w = 0; w < W; ++w) {
+      tss += red_sr[w][lane];
+      traw += red_sr[w][NS + lane];
     }
+    score = rsqrtf(tss * inv_dim + a.key_eps) * traw;
   }
+  const float m = warp_max(score);
+  const float e_l = lane < S ? __expf(score - m) : 0.f;
+  float alpha[NS];
   float den = 0.f;
 #pragma unroll
   for (int s = 0; s < NS; ++s) {
-    alpha[s] = s < S ? __expf(alpha[s] - m) : 0.f;
+    alpha[s] = __shfl_sync(0xffffffffu, e_l, s);
     den += alpha[s];
   }
   const float rden = 1.0f / den;
-  float h[8];
+  float2 h2[4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) h[j] = 0.f;
+  for (int p = 0; p < 4; ++p) h2[p] = make_float2(0.f, 0.f);
 #pragma unroll
   for (int s = 0; s < NS; ++s) {
     if (s < S) {
       const float al = alpha[s] * rden;
-      float f[8];
-      bf16x8_to_float(source(s), f);
+      const float2 al2 = make_float2(al, al);
+      const uint4 sv = source(s);
+      const uint32_t w[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) h[j] = fmaf(al, f[j], h[j]);
+      for (int p = 0; p < 4; ++p) h2[p] = __ffma2_rn(al2, bf16x2_to_float2(w[p]), h2[p]);
     }
+  }
+  float h[8];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    h[2 * p] = h2[p].x;
+    h[2 * p + 1] = h2[p].y;
   }
   float sq = 0.f;
 #pragma unroll
