@@ -138,6 +138,35 @@ int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f3
                                  void* partials, size_t partial_bytes, int* status,
                                  void* stream);
 
+/* parrot_decode_attention_bf16 for the local GQA layers with the rotary
+ * embedding applied inside (replaces parrot_rope_inplace_at_bf16 on the q and
+ * k heads followed by parrot_decode_attention_bf16; model.py:206-216 then
+ * :303-328): q is bf16 and read unrotated, the query is rotated as it is
+ * loaded and the new key as it is appended, with the same bf16 rounding, so
+ * outputs and cache rows are bit-identical to the two calls.  cos_table /
+ * sin_table: bf16 [rope_positions, head_dim / 2], rope_positions >=
+ * max_positions.  k_new / v_new in memory stay unrotated. */
+int parrot_decode_attention_rope_bf16(void* out, int out_f32, const void* q,
+                                      long long q_row_stride, const void* k_new,
+                                      const void* v_new, long long kv_row_stride, void* k_cache,
+                                      void* v_cache, const int* pos_dev, int batch, int n_heads,
+                                      int n_kv_heads, int max_positions, int head_dim,
+                                      int window, float scale, const void* cos_table,
+                                      const void* sin_table, int rope_positions,
+                                      void* partials, size_t partial_bytes, int* status,
+                                      void* stream);
+
+/* y[t, n] = sum_k x[t, k] w[n, k] for a decode step's projections
+ * (model.py:303-328 q/k/v and out, 399-432 the latent down-projection and the
+ * absorbed query / output), replacing F.linear there: fp32 accumulation and one
+ * rounding of the result to y's type.  rows <= 8, n_out % 16 == 0, k_in % 8
+ * == 0 and <= 1024; x [rows, k_in] and w [n_out, k_in] (nn.Linear layout)
+ * contiguous and 16-byte aligned, each bf16 or fp32 (the *_f32 flags); y
+ * [rows, n_out].  The weights are read before the kernel's grid dependency
+ * wait, so they must not be written by the kernel launched just before. */
+int parrot_linear_small(void* y, int y_f32, const void* x, int x_f32, const void* w, int w_f32,
+                        int rows, int n_out, int k_in, void* stream);
+
 /* Scratch bytes parrot_decode_attention_bf16 needs for these sizes. */
 size_t parrot_decode_attention_scratch_bytes(int batch, int n_heads, int max_positions,
                                              int head_dim);

@@ -624,13 +624,13 @@ int parrot_rope_inplace_at_bf16(void* x, const void* cos_table, const void* sin_
   return check_launch("rope_kernel(device position)");
 }
 
-int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f32,
-                                 long long q_row_stride, const void* k_new, const void* v_new,
-                                 long long kv_row_stride, void* k_cache, void* v_cache,
-                                 const int* pos_dev, int batch, int n_heads, int n_kv_heads,
-                                 int max_positions, int head_dim, int window, float scale,
-                                 void* partials, size_t partial_bytes, int* status,
-                                 void* stream) {
+static int decode_attention(void* out, int out_f32, const void* q, int q_f32,
+                            long long q_row_stride, const void* k_new, const void* v_new,
+                            long long kv_row_stride, void* k_cache, void* v_cache,
+                            const int* pos_dev, int batch, int n_heads, int n_kv_heads,
+                            int max_positions, int head_dim, int window, float scale,
+                            const void* cos_table, const void* sin_table, void* partials,
+                            size_t partial_bytes, int* status, void* stream) {
   if (batch < 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads ||
       max_positions <= 0 || window < 0)
     return fail(PARROT_EINVAL, "decode_attention: bad sizes%s");
@@ -667,11 +667,61 @@ int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f3
     return fail(PARROT_EINVAL, "decode_attention: row strides too small or not 16-byte multiples%s");
   a.scale = scale;
   a.status = status;
+  a.cos_t = static_cast<const __nv_bfloat16*>(cos_table);
+  a.sin_t = static_cast<const __nv_bfloat16*>(sin_table);
   const int rc = parrot::launch_decode_attention(a, static_cast<cudaStream_t>(stream));
   if (rc == -1)
     return fail(PARROT_EUNSUPPORTED, "decode_attention: unsupported head width / group size%s");
   if (rc) return fail(PARROT_ECUDA, "decode_attention: launch failed%s");
   return check_launch("decode_attn_kernels");
+}
+
+int parrot_decode_attention_bf16(void* out, int out_f32, const void* q, int q_f32,
+                                 long long q_row_stride, const void* k_new, const void* v_new,
+                                 long long kv_row_stride, void* k_cache, void* v_cache,
+                                 const int* pos_dev, int batch, int n_heads, int n_kv_heads,
+                                 int max_positions, int head_dim, int window, float scale,
+                                 void* partials, size_t partial_bytes, int* status,
+                                 void* stream) {
+  return decode_attention(out, out_f32, q, q_f32, q_row_stride, k_new, v_new, kv_row_stride,
+                          k_cache, v_cache, pos_dev, batch, n_heads, n_kv_heads, max_positions,
+                          head_dim, window, scale, nullptr, nullptr, partials, partial_bytes,
+                          status, stream);
+}
+
+int parrot_decode_attention_rope_bf16(void* out, int out_f32, const void* q,
+                                      long long q_row_stride, const void* k_new,
+                                      const void* v_new, long long kv_row_stride, void* k_cache,
+                                      void* v_cache, const int* pos_dev, int batch, int n_heads,
+                                      int n_kv_heads, int max_positions, int head_dim,
+                                      int window, float scale, const void* cos_table,
+                                      const void* sin_table, int rope_positions,
+                                      void* partials, size_t partial_bytes, int* status,
+                                      void* stream) {
+  if (!cos_table || !sin_table || rope_positions < max_positions || head_dim % 8)
+    return fail(PARROT_EINVAL, "decode_attention_rope: need cos/sin tables of at least "
+                               "max_positions rows and head_dim %% 8 == 0%s");
+  if (((uintptr_t)q & 3) || q_row_stride % 2)
+    return fail(PARROT_EINVAL, "decode_attention_rope: q rows must be 4-byte aligned%s");
+  return decode_attention(out, out_f32, q, 0, q_row_stride, k_new, v_new, kv_row_stride,
+                          k_cache, v_cache, pos_dev, batch, n_heads, n_kv_heads, max_positions,
+                          head_dim, window, scale, cos_table, sin_table, partials,
+                          partial_bytes, status, stream);
+}
+
+int parrot_linear_small(void* y, int y_f32, const void* x, int x_f32, const void* w, int w_f32,
+                        int rows, int n_out, int k_in, void* stream) {
+  if (rows < 0 || rows > 8 || n_out <= 0 || n_out % 16 || k_in <= 0 || k_in % 8 ||
+      k_in > parrot::kLinearSmallMaxK)
+    return fail(PARROT_EINVAL, "linear_small: need 0 <= rows <= 8, n_out %% 16 == 0 and "
+                               "k_in %% 8 == 0, k_in <= 1024%s");
+  if (rows == 0) return PARROT_OK;
+  if (!y || !x || !w || !aligned16(x) || !aligned16(w) || ((uintptr_t)y & 3))
+    return fail(PARROT_EINVAL, "linear_small: x and w must be 16-byte aligned, y 4-byte%s");
+  parrot::LinearSmallArgs a{x, x_f32, w, w_f32, y, y_f32, rows, n_out, k_in};
+  if (parrot::launch_linear_small(a, static_cast<cudaStream_t>(stream)))
+    return fail(PARROT_ECUDA, "linear_small: launch failed%s");
+  return check_launch("linear_small_kernel");
 }
 
 size_t parrot_decode_attention_scratch_bytes(int batch, int n_heads, int max_positions,

@@ -21,13 +21,38 @@
 // so the result does not depend on timing.  The CTA whose chunk holds pos also
 // writes the new key/value into the cache (no other CTA reads that row).  The
 // position is read from device memory and checked against the cache length; a
-// bad position is reported in the status word and nothing is written.
+// bad position is reported in the status word and nothing is written.  With
+// RoPE tables given (local GQA), the kernel rotates the query as it loads it
+// and the new key as it stages and appends it, so no separate RoPE launch runs.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace parrot {
 
 constexpr int kDecodeChunk = 32;  // keys per chunk: one per lane
+
+// Rotary embedding of one bf16 pair at table row `pos`, column pair j, with
+// the rounding of the RoPE kernel (every product and the sum rounded to bf16).
+__device__ __forceinline__ float2 rope_pair(float e, float o, const DecodeAttnArgs& a, int pos,
+                                            int j) {
+  const size_t t = (size_t)pos * (a.D >> 1) + j;
+  const float c = __bfloat162float(a.cos_t[t]), s = __bfloat162float(a.sin_t[t]);
+  return make_float2(round_bf16(round_bf16(e * c) - round_bf16(o * s)),
+                     round_bf16(round_bf16(e * s) + round_bf16(o * c)));
+}
+
+// The key vector cv (columns 8 cv .. 8 cv + 7) of the new token, rotated.
+__device__ __forceinline__ uint4 rope_vec8(uint4 v, const DecodeAttnArgs& a, int pos, int cv) {
+  float f[8];
+  bf16x8_to_float(v, f);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 r = rope_pair(f[2 * k], f[2 * k + 1], a, pos, cv * 4 + k);
+    f[2 * k] = r.x;
+    f[2 * k + 1] = r.y;
+  }
+  return float_to_bf16x8(f);
+}
 
 template <int D, int G>
 __global__ void __launch_bounds__(32 * G) decode_attn_kernel(DecodeAttnArgs a) {
@@ -64,11 +89,22 @@ __global__ void __launch_bounds__(32 * G) decode_attn_kernel(DecodeAttnArgs a) {
   const uint4* vn =
       sep_v ? reinterpret_cast<const uint4*>(a.v_new + (size_t)b * a.kv_row + (size_t)kvh * D)
             : nullptr;
-  // this warp's query, as fp32
-  for (int d = lane; d < D; d += 32) {
-    const size_t qi = (size_t)b * a.q_row + (size_t)h * D + d;
-    q_s[warp * D + d] = a.q_f32 ? __ldg(static_cast<const float*>(a.q) + qi)
-                                : __bfloat162float(static_cast<const __nv_bfloat16*>(a.q)[qi]);
+  // this warp's query, as fp32 (rotated here when the tables are given)
+  if (a.cos_t != nullptr) {
+    const __nv_bfloat162* qp = reinterpret_cast<const __nv_bfloat162*>(
+        static_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.q_row + (size_t)h * D);
+    for (int j = lane; j < D / 2; j += 32) {
+      const float2 e = __bfloat1622float2(qp[j]);
+      const float2 r = rope_pair(e.x, e.y, a, pos, j);
+      q_s[warp * D + 2 * j] = r.x;
+      q_s[warp * D + 2 * j + 1] = r.y;
+    }
+  } else {
+    for (int d = lane; d < D; d += 32) {
+      const size_t qi = (size_t)b * a.q_row + (size_t)h * D + d;
+      q_s[warp * D + d] = a.q_f32 ? __ldg(static_cast<const float*>(a.q) + qi)
+                                  : __bfloat162float(static_cast<const __nv_bfloat16*>(a.q)[qi]);
+    }
   }
 
   float m = -INFINITY, l = 0.f;
@@ -86,7 +122,7 @@ __global__ void __launch_bounds__(32 * G) decode_attn_kernel(DecodeAttnArgs a) {
       const int j = i / NV, cv = i - j * NV;
       const int key = k0 + j;
       if (key == pos) {
-        const uint4 kv = __ldg(kn + cv);
+        const uint4 kv = a.cos_t != nullptr ? rope_vec8(__ldg(kn + cv), a, pos, cv) : __ldg(kn + cv);
         k_s[j * NVP + cv] = kv;
         reinterpret_cast<uint4*>(a.k_cache + (row0 + pos) * D)[cv] = kv;
         if (sep_v) {

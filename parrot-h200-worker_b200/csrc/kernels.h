@@ -171,6 +171,8 @@ struct DecodeAttnArgs {
   const int* pos;                // device: position of this step's token
   float* part;                   // [B, H, slots, D + 2] partials (scratch)
   int* counters;                 // [B, KVH] arrivals per group, zero between launches
+  const __nv_bfloat16* cos_t;    // [>= S, D / 2] RoPE tables, or null: q and k_new are
+  const __nv_bfloat16* sin_t;    // then rotated in the kernel (bf16 q only)
   void* out;                     // [B, H, D] bf16, or fp32 when out_f32
   int out_f32;
   int B, H, KVH, S, D, window, slots;
@@ -181,6 +183,19 @@ struct DecodeAttnArgs {
 int launch_decode_attention(const DecodeAttnArgs& args, cudaStream_t stream);
 int decode_attn_chunks(int max_positions);
 int decode_attn_slots(int batch, int max_positions);
+
+// Decode-step projections, at most 8 token rows (linear_small.cu).
+constexpr int kLinearSmallMaxK = 1024;
+struct LinearSmallArgs {
+  const void* x;   // [rows, k_in] bf16, or fp32 when x_f32
+  int x_f32;
+  const void* w;   // [n_out, k_in] bf16, or fp32 when w_f32
+  int w_f32;
+  void* y;         // [rows, n_out] bf16, or fp32 when y_f32
+  int y_f32;
+  int rows, n_out, k_in;
+};
+int launch_linear_small(const LinearSmallArgs& args, cudaStream_t stream);
 
 int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat16* w,
                    int rows, int dim, float eps, cudaStream_t stream);

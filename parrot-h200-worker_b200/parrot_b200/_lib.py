@@ -64,6 +64,13 @@ _SIGNATURES = {
                                              ctypes.c_longlong, c_void_p, c_void_p, c_void_p,
                                              c_int, c_int, c_int, c_int, c_int, c_int, c_float,
                                              c_void_p, c_size_t, c_void_p, c_void_p]),
+    "parrot_decode_attention_rope_bf16": (c_int, [c_void_p, c_int, c_void_p, ctypes.c_longlong,
+                                                  c_void_p, c_void_p, ctypes.c_longlong, c_void_p,
+                                                  c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                                  c_int, c_int, c_float, c_void_p, c_void_p,
+                                                  c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "parrot_linear_small": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int,
+                                    c_int, c_int, c_void_p]),
     "parrot_decode_attention_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "parrot_moe_capacity": (c_int, [c_int, c_int]),
     "parrot_moe_workspace_layout": (c_int, [POINTER(MoeDims), POINTER(MoeLayout)]),

@@ -120,19 +120,44 @@ def b200_rope_at_(qkv: Tensor, cos: Tensor, sin: Tensor, rot_heads: int, head_di
     return qkv
 
 
+def b200_linear_small(x: Tensor, w: Tensor, out_dtype: torch.dtype) -> Tensor:
+    """``F.linear(x, w)`` for a decode step (at most 8 rows; ``model.py:303-328,
+    399-432``): x [rows, k] bf16 or fp32, w [n, k] bf16 or fp32, fp32
+    accumulation, the result rounded once to ``out_dtype`` (bf16 or fp32)."""
+    if x.device.type != "cuda" or w.device != x.device:
+        raise RuntimeError(f"The B200 linear_small backend requires CUDA tensors on one device, "
+                           f"got {x.device} and {w.device}")
+    for t in (x, w):
+        if t.dtype not in (torch.bfloat16, torch.float32):
+            raise RuntimeError(f"The B200 linear_small backend takes bf16 or fp32, got {t.dtype}")
+    _require_inference("linear_small")
+    x = x.contiguous()
+    w = w.contiguous()
+    rows, k = x.shape
+    out = torch.empty((rows, w.shape[0]), device=x.device, dtype=out_dtype)
+    _lib.check(_lib.load().parrot_linear_small(
+        _p(out), int(out_dtype == torch.float32), _p(x), int(x.dtype == torch.float32), _p(w),
+        int(w.dtype == torch.float32), rows, w.shape[0], k, _stream()), "parrot_linear_small")
+    return out
+
+
 _DECODE_SCRATCH: dict = {}
 
 
 def b200_decode_attention(q: Tensor, k_new: Tensor, v_new: Tensor | None, k_cache: Tensor,
                           v_cache: Tensor | None, position: Tensor, n_heads: int,
                           n_kv_heads: int, head_dim: int, window: int, scale: float,
-                          out_dtype: torch.dtype) -> Tensor:
+                          out_dtype: torch.dtype,
+                          rope: tuple[Tensor, Tensor] | None = None) -> Tensor:
     """One decode step of attention at the device ``position`` (``model.py:303-328, 399-432``).
 
     ``q`` [B, n_heads * head_dim] (bf16, or fp32 for the absorbed MLA query) and
     ``k_new`` / ``v_new`` [B, n_kv_heads * head_dim] may be row-strided views of
     one projection.  The new key/value are appended to the caches at
-    ``position``; returns [B, n_heads * head_dim] in ``out_dtype``.
+    ``position``; returns [B, n_heads * head_dim] in ``out_dtype``.  With
+    ``rope = (cos, sin)`` (bf16 tables) ``q`` and ``k_new`` are unrotated and the
+    kernel applies the rotary embedding itself (``model.py:206-216``), bit for bit
+    like ``b200_rope_at_`` before the call.
     """
     _require_device(k_cache, "decode attention")
     b = q.shape[0]
@@ -145,6 +170,14 @@ def b200_decode_attention(q: Tensor, k_new: Tensor, v_new: Tensor | None, k_cach
         scratch = torch.zeros(int(n), device=k_cache.device, dtype=torch.uint8)
         _DECODE_SCRATCH[key] = scratch
     out = torch.empty((b, n_heads * head_dim), device=q.device, dtype=out_dtype)
+    if rope is not None:
+        cos, sin = rope
+        _lib.check(lib.parrot_decode_attention_rope_bf16(
+            _p(out), int(out_dtype == torch.float32), _p(q), q.stride(0), _p(k_new), _p(v_new),
+            k_new.stride(0), _p(k_cache), _p(v_cache), _p(position), b, n_heads, n_kv_heads,
+            s_max, head_dim, window, float(scale), _p(cos), _p(sin), cos.shape[0], _p(scratch),
+            scratch.numel(), None, _stream()), "parrot_decode_attention_rope_bf16")
+        return out
     _lib.check(lib.parrot_decode_attention_bf16(
         _p(out), int(out_dtype == torch.float32), _p(q), int(q.dtype == torch.float32), q.stride(0),
         _p(k_new), _p(v_new), k_new.stride(0), _p(k_cache), _p(v_cache), _p(position), b,

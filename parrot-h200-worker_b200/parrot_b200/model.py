@@ -162,6 +162,11 @@ class DepthMix(nn.Module):
         return bridge.b200_depth_mix_norm(self, sources, output_norm, pending_delta)
 
 
+# decode steps of at most this many rows run their attention projections on
+# parrot_linear_small (weights read ahead of the dependency wait); larger ones on cuBLAS
+_SMALL_LINEAR_ROWS = 8
+
+
 def _rope_tables(cfg: ModelConfig, device, dtype) -> tuple[Tensor, Tensor]:
     key = (device.type, device.index, dtype, cfg.max_seq_len, cfg.head_dim, cfg.rope_theta)
     hit = _ROPE.get(key)
@@ -257,17 +262,18 @@ class LocalGQA(nn.Module):
             # position from device memory (capturable)
             b = x.shape[0]
             w = _packed(self, "_qkv_weight", (self.q.weight, self.k.weight, self.v.weight))
-            qkv = F.linear(x, w)
+            small = b <= _SMALL_LINEAR_ROWS
+            qkv = bridge.b200_linear_small(x.view(b, -1), w, x.dtype) if small else F.linear(x, w)
             cos, sin = _rope_tables(c, x.device, x.dtype)
-            bridge.b200_rope_at_(qkv, cos, sin, c.n_heads + c.n_kv_heads, c.head_dim,
-                                 position_device)
             flat = qkv.view(b, -1)
             qw, kw = c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim
+            # RoPE of q and the new key happens inside the attention kernel
             y = bridge.b200_decode_attention(
                 flat[:, :qw], flat[:, qw:qw + kw], flat[:, qw + kw:], cache.key, cache.value,
                 position_device, c.n_heads, c.n_kv_heads, c.head_dim, c.window_size,
-                c.head_dim ** -0.5, x.dtype)
-            out = self.out(y.view(b, 1, -1))
+                c.head_dim ** -0.5, x.dtype, rope=(cos, sin))
+            out = (bridge.b200_linear_small(y, self.out.weight, x.dtype).view(b, 1, -1) if small
+                   else self.out(y.view(b, 1, -1)))
             return out if addend is None else addend + out
         q, k, v = self._qkv(x, position)
         cache.key[:, :, position:position + 1].copy_(k)
@@ -350,12 +356,19 @@ class GlobalMLA(nn.Module):
         if position_device is not None:
             # absorbed latent attention at the device position (capturable):
             # fp32 query over the bf16 latent cache, fp32 context (model.py:417-432)
-            latent = self.kv_down(x).view(b, -1)
-            q = F.linear(x.float(), aq).view(b, -1)
+            small = b <= _SMALL_LINEAR_ROWS
+            if small:
+                xf = x.view(b, -1)
+                latent = bridge.b200_linear_small(xf, self.kv_down.weight, x.dtype)
+                q = bridge.b200_linear_small(xf, aq, torch.float32)  # x.float() is exact
+            else:
+                latent = self.kv_down(x).view(b, -1)
+                q = F.linear(x.float(), aq).view(b, -1)
             ctx = bridge.b200_decode_attention(
                 q, latent, None, cache.latent.unsqueeze(1), None, position_device, c.n_heads, 1,
                 c.kv_latent_dim, 0, c.head_dim ** -0.5, torch.float32)
-            out = F.linear(ctx.view(b, 1, -1), ao).to(x.dtype)
+            out = (bridge.b200_linear_small(ctx, ao, x.dtype).view(b, 1, -1) if small
+                   else F.linear(ctx.view(b, 1, -1), ao).to(x.dtype))
             return out if addend is None else addend + out
         cache.latent[:, position:position + 1].copy_(self.kv_down(x))
         seen = cache.latent[:, :position + 1]

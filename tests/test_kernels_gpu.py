@@ -224,6 +224,63 @@ def test_decode_attention_matches_sdpa(mode, pos, batch):
         torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("rows", [1, 3, 8])
+@pytest.mark.parametrize("n,k,xt,wt,yt", [
+    (1152, 768, torch.bfloat16, torch.bfloat16, torch.bfloat16),  # local qkv
+    (768, 768, torch.bfloat16, torch.bfloat16, torch.bfloat16),   # local out
+    (128, 768, torch.bfloat16, torch.bfloat16, torch.bfloat16),   # MLA latent down
+    (1024, 768, torch.bfloat16, torch.float32, torch.float32),    # absorbed query
+    (768, 1024, torch.float32, torch.float32, torch.bfloat16),    # absorbed output
+])
+def test_linear_small_matches_fp64(rows, n, k, xt, wt, yt):
+    """parrot_linear_small (decode projections) against the fp64 product of
+    the same operands: fp32 accumulation, one rounding to the output type."""
+    g = torch.Generator().manual_seed(rows * 7 + n + k)
+    x = torch.randn(rows, k, generator=g).to("cuda", xt)
+    w = (0.05 * torch.randn(n, k, generator=g)).to("cuda", wt)
+    with torch.inference_mode():
+        y = bridge.b200_linear_small(x, w, yt)
+    assert y.dtype == yt and y.shape == (rows, n)
+    ref = x.double() @ w.double().T
+    if yt == torch.bfloat16:
+        # within one bf16 rounding of the exact value (fp32 accumulation error is far smaller)
+        err = (y.double() - ref).abs()
+        assert bool((err <= ref.abs() * 2.0 ** -8 + 1e-6).all())
+    else:
+        torch.testing.assert_close(y.double(), ref, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("pos,batch", [(0, 1), (135, 1), (31, 3), (2300, 2), (700, 64)])
+def test_decode_attention_rope_fused_is_bit_identical(pos, batch):
+    """parrot_decode_attention_rope_bf16 (RoPE of q and the new key inside the
+    kernel) against parrot_rope_inplace_at_bf16 followed by
+    parrot_decode_attention_bf16: same output bits, same appended cache rows,
+    and the projection left unrotated."""
+    g = torch.Generator().manual_seed(1000 + pos + batch)
+    S, H, KVH, D, window = 4096, 8, 2, 96, 2048
+    position = torch.full((1,), pos, device="cuda", dtype=torch.int32)
+    angle = torch.arange(S).float()[:, None] * (10000.0 ** -(torch.arange(0, D, 2).float() / D))
+    cos, sin = angle.cos().to("cuda", torch.bfloat16), angle.sin().to("cuda", torch.bfloat16)
+    kc = torch.randn(batch, KVH, S, D, generator=g).to("cuda", torch.bfloat16)
+    vc = torch.randn(batch, KVH, S, D, generator=g).to("cuda", torch.bfloat16)
+    qkv = torch.randn(batch, 1, (H + 2 * KVH) * D, generator=g).to("cuda", torch.bfloat16)
+    qw, kw = H * D, KVH * D
+    raw = qkv.clone()
+    kc2, vc2 = kc.clone(), vc.clone()
+    flat = qkv.view(batch, -1)
+    fused = bridge.b200_decode_attention(flat[:, :qw], flat[:, qw:qw + kw], flat[:, qw + kw:],
+                                         kc, vc, position, H, KVH, D, window, D ** -0.5,
+                                         torch.bfloat16, rope=(cos, sin))
+    assert torch.equal(qkv, raw)
+    bridge.b200_rope_at_(qkv, cos, sin, H + KVH, D, position)
+    flat = qkv.view(batch, -1)
+    plain = bridge.b200_decode_attention(flat[:, :qw], flat[:, qw:qw + kw], flat[:, qw + kw:],
+                                         kc2, vc2, position, H, KVH, D, window, D ** -0.5,
+                                         torch.bfloat16)
+    assert torch.equal(fused, plain)
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+
+
 @pytest.mark.parametrize("tokens,residual,zipf", [(1, False, False), (3, True, False),
                                                    (8, True, True), (16, False, True)])
 def test_decode_moe_matches_oracle_and_gemm_path(tokens, residual, zipf):
