@@ -82,6 +82,34 @@ def test_entry_points_reject_bad_arguments_before_launch(lib):
                                        None, 0, None) == _lib.PARROT_EINVAL
 
 
+def test_decode_entry_points_reject_bad_arguments_before_launch(lib):
+    E = _lib.PARROT_EINVAL
+    # small-batch projections: at most 8 rows, n_out % 16, k_in % 8 and <= 1024, pointers
+    assert lib.parrot_linear_small(None, 0, None, 0, None, 0, 9, 768, 768, None) == E
+    assert lib.parrot_linear_small(None, 0, None, 0, None, 0, 1, 100, 768, None) == E
+    assert lib.parrot_linear_small(None, 0, None, 0, None, 0, 1, 768, 2048, None) == E
+    assert lib.parrot_linear_small(None, 0, None, 0, None, 0, 1, 768, 768, None) == E
+    assert lib.parrot_linear_small(None, 0, None, 0, None, 0, 0, 768, 768, None) == _lib.PARROT_OK
+    # RoPE inside decode attention: tables must cover every cache position
+    assert lib.parrot_decode_attention_rope_bf16(
+        None, 0, None, 0, None, None, 0, None, None, None, 1, 8, 2, 4096, 96, 2048, 0.1,
+        None, None, 4096, None, 0, None, None) == E
+    assert lib.parrot_decode_attention_rope_bf16(
+        None, 0, None, 0, None, None, 0, None, None, None, 1, 8, 2, 4096, 96, 2048, 0.1,
+        ctypes.c_void_p(16), ctypes.c_void_p(16), 2048, None, 0, None, None) == E
+
+
+@pytest.mark.parametrize("batch,heads,positions,dim", [(1, 8, 4096, 96), (8, 8, 4096, 128),
+                                                       (64, 8, 4096, 96), (3, 4, 100, 32)])
+def test_decode_attention_scratch_size(lib, batch, heads, positions, dim):
+    """Partials [B, H, slots, D + 2] fp32 plus one arrival counter per (row,
+    head); slots = min(32-key chunks, max(1, 256 // B))."""
+    chunks = (positions + 31) // 32
+    slots = min(chunks, max(1, 256 // batch))
+    want = batch * heads * slots * (dim + 2) * 4 + batch * heads * 4
+    assert lib.parrot_decode_attention_scratch_bytes(batch, heads, positions, dim) == want
+
+
 def tiny_b200(**kw):
     base = dict(vocab_size=32768, dim=128, n_layers=4, n_heads=4, n_kv_heads=2, head_dim=32,
                 kv_latent_dim=32, n_experts=8, expert_dim=128, shared_expert_dim=64,
