@@ -50,17 +50,25 @@ struct __align__(8) RouteSmem {
   float psum[4][kMaxExperts];
 };
 
-template <int NP>
+// 128-token tiles (large batches) stream through a 4-slot ring instead: about
+// 75 KB per CTA, so three CTAs share an SM and one's loads overlap another's
+// MMAs and epilogue (a whole row block per CTA left one CTA per SM, idle
+// between its load and its epilogue).
+constexpr int kRouteLargeStages = 4;
+
+template <int NP, int ST>
 constexpr size_t route_smem_bytes() {
-  return 1024 + (size_t)route_stages<NP>() * (kRouteXTile + NP * 128) + sizeof(RouteSmem);
+  return 1024 + (size_t)ST * (kRouteXTile + NP * 128) + sizeof(RouteSmem);
 }
 
-template <int NP>
+// ST: slab slots in the shared-memory ring.
+template <int NP, int ST>
 __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUtensorMap x_map,
                                                     const __grid_constant__ CUtensorMap w_map,
                                                     RouteArgs a) {
   constexpr int kWTile = NP * 128;  // NP experts x 64 columns
-  constexpr int kRouteStages = route_stages<NP>();
+  constexpr int kRouteStages = ST;
+  static_assert(ST >= 2 && ST <= kRouteMaxStages, "ring slots");
   extern __shared__ unsigned char route_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(route_raw) + 1023) & ~uintptr_t(1023));
@@ -272,23 +280,31 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
   }
 }
 
-template <int NP>
-static int launch_route_np(const RouteArgs& args, const CUtensorMap* x_map,
+template <int NP, int ST>
+static int launch_route_st(const RouteArgs& args, const CUtensorMap* x_map,
                            const CUtensorMap* w_map, cudaStream_t stream) {
-  constexpr size_t smem = route_smem_bytes<NP>();
+  constexpr size_t smem = route_smem_bytes<NP, ST>();
   static unsigned long long configured = 0;  // per device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
   if (!(configured & (1ull << dev))) {
-    if (cudaFuncSetAttribute(route_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(route_kernel<NP, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
       return -2;
     configured |= 1ull << dev;
   }
-  return launch_pdl(route_kernel<NP>, dim3(route_blocks(args.tokens)), dim3(128), smem, stream,
-                    *x_map, *w_map, args) == cudaSuccess
+  return launch_pdl(route_kernel<NP, ST>, dim3(route_blocks(args.tokens)), dim3(128), smem,
+                    stream, *x_map, *w_map, args) == cudaSuccess
              ? 0
              : -2;
+}
+
+template <int NP>
+static int launch_route_np(const RouteArgs& args, const CUtensorMap* x_map,
+                           const CUtensorMap* w_map, cudaStream_t stream) {
+  return route_tile(args.tokens) == 128
+             ? launch_route_st<NP, kRouteLargeStages>(args, x_map, w_map, stream)
+             : launch_route_st<NP, route_stages<NP>()>(args, x_map, w_map, stream);
 }
 
 int launch_route(const RouteArgs& args, const CUtensorMap* x_map, const CUtensorMap* w_map,

@@ -350,6 +350,35 @@ def _check_routing(ex, module_cfg, oracle_trace, T):
     return grouping
 
 
+@pytest.mark.parametrize("tokens,zipf", [(8192, False), (16384, True)])
+def test_xl_moe_layer_large_batch_matches_oracle(tokens, zipf):
+    """Large batches (128-token router tiles streamed through the router's
+    4-slot ring; with the skewed bias, the capacity-overflow path): routing,
+    grouping, statistics and output against the fp32 oracle."""
+    cfg = moe_config()
+    prod, orc = build_moe_pair(cfg, seed=2)
+    x = hidden_states(tokens, cfg.dim, seed=3)
+    if zipf:
+        bias = torch.tensor([3.0, 2.0, 1.0] + [0.0] * (cfg.n_experts - 3))
+        prod.router_bias = bias.cuda()
+        orc.router_bias = bias
+    out, ex, ws, layout = call_moe_forward(prod, x.cuda())
+    assert ex["status"][0] == 0, ex["status"]
+    exp, aux, util = orc(x.float())
+    _check_routing(ex, cfg, orc.last_trace, tokens)
+    if zipf:
+        assert int(ex["counts"].max()) > layout.capacity  # the overflow path ran
+    assert_bf16_close(out, exp, "large-batch moe vs fp32 oracle")
+    stats = ex["stats"].cpu()
+    torch.testing.assert_close(stats[:-1], util, rtol=0, atol=2.0 / (2 * tokens))
+    torch.testing.assert_close(stats[-1], aux, rtol=2e-3, atol=1e-6)
+    grouped = workspace_view(ws, layout, "grouped", torch.bfloat16,
+                             (layout.grouped_rows, cfg.dim)).cpu()
+    pos = ex["positions"].cpu().long()
+    tok = torch.arange(2 * tokens) // 2
+    assert torch.equal(grouped[pos], x[tok])
+
+
 @pytest.mark.parametrize("tokens", [256, 512])
 def test_xl_moe_layer_matches_oracle(tokens):
     cfg = moe_config()
