@@ -373,12 +373,27 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
     int before = 0, total = 0;
     float ps = 0.f;
     if (tid < P * E) {
+      // eight rows' loads in flight before their sums (a load-add loop would
+      // wait on each L2 round trip in turn: 64 of them per thread at 512
+      // router tiles); the sums keep the row order
+      constexpr int U = 8;
       const int ex = tid % E;
-      for (int r = tid / E; r < n_tiles; r += P) {
-        const int v = __ldcg(a.tab.tile_hist + (size_t)r * E + ex);
-        total += v;
-        if (r < my_tile) before += v;
-        if (writer) ps += __ldcg(a.tab.tile_probsum + (size_t)r * E + ex);
+      for (int r0 = tid / E; r0 < n_tiles; r0 += U * P) {
+        int v[U];
+        float pv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int r = r0 + u * P;
+          v[u] = r < n_tiles ? __ldcg(a.tab.tile_hist + (size_t)r * E + ex) : 0;
+          pv[u] = (writer && r < n_tiles) ? __ldcg(a.tab.tile_probsum + (size_t)r * E + ex) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int r = r0 + u * P;
+          total += v[u];
+          if (r < my_tile) before += v[u];
+          if (writer && r < n_tiles) ps += pv[u];
+        }
       }
     }
     red_before[tid] = before;
