@@ -35,6 +35,50 @@ def test_library_exports_every_declared_symbol(lib):
     assert sorted(_lib.exported_names()) == names
 
 
+def _header_prototypes() -> dict[str, tuple[str, list[str]]]:
+    """name -> (return type, parameter declarations) of every prototype in the header."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    protos = {}
+    for m in re.finditer(r"([A-Za-z_][\w\s\*]*?)\b(parrot_\w+)\s*\(([^;{]*?)\)\s*;", text,
+                         flags=re.S):
+        params = m.group(3).strip()
+        protos[m.group(2)] = (" ".join(m.group(1).split()),
+                              [] if params in ("", "void") else [q.strip() for q in params.split(",")])
+    return protos
+
+
+def _expected_ctype(decl: str):
+    """The ctypes type a C declaration (type and name) must be bound as, or
+    "pointer" for any pointer (bound as c_void_p, c_char_p or POINTER(...))."""
+    if "*" in decl:
+        return "pointer"
+    t = " ".join(decl.replace("const", "").split()[:-1])
+    return {"int": ctypes.c_int, "float": ctypes.c_float, "size_t": ctypes.c_size_t,
+            "long long": ctypes.c_longlong, "int64_t": ctypes.c_int64,
+            "unsigned long long": ctypes.c_ulonglong}[t]
+
+
+def _matches(ct, want) -> bool:
+    if want == "pointer":
+        return ct in (ctypes.c_void_p, ctypes.c_char_p) or (
+            isinstance(ct, type) and issubclass(ct, ctypes._Pointer))
+    return ct is want
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every entry point's ctypes binding has the header's parameter count,
+    parameter types and return type, so a prototype changed on one side only
+    fails here rather than on a GPU."""
+    protos = _header_prototypes()
+    assert sorted(protos) == sorted(_lib._SIGNATURES)
+    for name, (res, args) in _lib._SIGNATURES.items():
+        ret, params = protos[name]
+        assert len(args) == len(params), name
+        for i, (decl, ct) in enumerate(zip(params, args)):
+            assert _matches(ct, _expected_ctype(decl)), (name, i, decl, ct)
+        assert _matches(res, _expected_ctype(ret + " r")), (name, ret, res)
+
+
 def test_version_and_error_string(lib):
     assert lib.parrot_b200_version() == 100
     assert isinstance(lib.parrot_b200_last_error(), bytes)
