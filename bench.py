@@ -217,6 +217,138 @@ def time_moe_kernels(model, tokens: int, replays: int = 20) -> dict:
     return out
 
 
+def time_moe_breakdown(model, tokens: int = 256, replays: int = 10) -> dict:
+    """BASELINE config 2 kernel by kernel: one CUDA graph of 16 MoE blocks
+    (cycling the model's 16 layers, so every launch streams its own weights
+    from HBM) replayed under the torch profiler (CUPTI device timestamps, not
+    ncu).  Per kernel kind: mean device duration per block, the exposed part
+    (not overlapped by the previous kernel's tail: launches are programmatic
+    dependent launches), algorithmic bytes, and bytes / duration against the
+    measured HBM bandwidth."""
+    import collections
+
+    from torch.profiler import ProfilerActivity, profile
+
+    from parrot_b200 import bridge
+    from parrot_b200.graphs import capture_calls
+    cfg = model.config
+    layers = [b.moe for b in model.blocks]
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(tokens, cfg.dim, device="cuda", generator=g).to(torch.bfloat16)
+    with torch.inference_mode():
+        for m in layers:
+            bridge.b200_moe(m, x, False)
+        graph = capture_calls(lambda: [bridge.b200_moe(m, x, False) for m in layers])
+        graph.replay()
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for _ in range(replays):
+                graph.replay()
+            torch.cuda.synchronize()
+        del graph
+    evs = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+                 if e.device_type == torch.autograd.DeviceType.CUDA)
+    dur, exp = collections.defaultdict(float), collections.defaultdict(float)
+    prev_end, gemms = evs[0][0], 0
+    for start, end, name in evs:
+        if "route_kernel" in name:
+            kind = "route"
+        elif "group_kernel" in name:
+            kind, gemms = "group", 0
+        elif "grouped_gemm" in name:
+            kind = "gate_up_swiglu" if gemms == 0 else "down"
+            gemms += 1
+        elif "combine_kernel" in name:
+            kind = "combine"
+        else:
+            kind = "other"
+        dur[kind] += end - start
+        exp[kind] += max(0.0, end - max(start, prev_end))
+        prev_end = max(prev_end, end)
+    n = replays * len(layers)
+    T, d, E, H, Hs = tokens, cfg.dim, cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim
+    A = 2 * T
+    algo = {"route": 2 * T * d + 2 * E * d + 16 * T,
+            "group": 2 * T * d + 4 * T * d,
+            "gate_up_swiglu": 2 * (E * 2 * H * d + 2 * Hs * d + A * d + T * d + A * H + T * Hs),
+            "down": 2 * (E * d * H + d * Hs + A * H + T * Hs + A * d + T * d),
+            "combine": 2 * (A * d + T * d) + 2 * T * d}
+    flops = {"gate_up_swiglu": 2 * (A * d * 2 * H + T * d * 2 * Hs),
+             "down": 2 * (A * H * d + T * Hs * d)}
+    peaks, _ = measured_peaks()
+    out = {}
+    for kind in ("route", "group", "gate_up_swiglu", "down", "combine", "other"):
+        if kind not in dur:
+            continue
+        us = dur[kind] / n
+        row = {"us": us, "exposed_us": exp[kind] / n}
+        if kind in algo:
+            gbs = algo[kind] / (us * 1e-6) / 1e9
+            row.update(bytes=algo[kind], gbs=gbs, hbm_frac=gbs / float(peaks["hbm_gbs"]))
+        if kind in flops:
+            row["tflops"] = flops[kind] / (us * 1e-6) / 1e12
+        out[kind] = row
+    return {"tokens": tokens, "kernels": out,
+            "block_exposed_us": sum(exp.values()) / n,
+            "timing": "CUPTI device timestamps (torch profiler) over a graph of 16 blocks, "
+                      f"{replays} replays; per block"}
+
+
+def cpu_baselines() -> dict:
+    """The oracle (the reference's pytorch path restated) on the host cores for
+    BASELINE configs 2, 4 and 5, fp32 and bf16: median of 5 runs after a
+    warm-up, except config 4 (one run each, as the plan allows) and config 5
+    (16 decode steps after an untimed prefill)."""
+    from oracle import parrot_oracle as po
+    from parrot_b200.workloads import (make_hidden_states, make_moe_layer_weights,
+                                       random_token_ids, tune_zipf_router_bias)
+    cores = po.oracle_threads()
+    cfg = po.OracleConfig()
+    w = make_moe_layer_weights(cfg.dim, cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim, 1)
+    out = {"cores": cores, "kind": "port"}
+
+    def med(fn, runs):
+        ts = []
+        for _ in range(runs):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+    with torch.no_grad():
+        for dtype in (torch.float32, torch.bfloat16):
+            name = "fp32" if dtype == torch.float32 else "bf16"
+            moe = po.MoE(cfg)
+            moe.load_state_dict(w)
+            moe = moe.to(dtype).eval()
+            x = make_hidden_states(256, cfg.dim, 0).to(dtype)
+            moe(x)
+            out[f"config2_moe_layer_T256_{name}_ms"] = 1000 * med(lambda: moe(x), 5)
+            x4 = make_hidden_states(16384, cfg.dim, 0)
+            moe.router_bias = tune_zipf_router_bias(x4, w["router.weight"])
+            x4 = x4.to(dtype)
+            out[f"config4_zipf_moe_layer_T16384_{name}_ms"] = 1000 * med(lambda: moe(x4), 1)
+        torch.manual_seed(0)
+        model = po.OracleParrot(cfg).eval()
+        decode = {}
+        for b in (1, 8, 64):
+            ids = random_token_ids(b, 128, cfg.vocab_size, seed=b)
+            logits, state = model.prefill(ids)
+            nxt = logits.argmax(-1)
+            t0 = time.perf_counter()
+            for _ in range(16):
+                logits, state = model.decode_step(nxt, state)
+                nxt = logits.argmax(-1)
+            decode[f"B{b}"] = 16 * b / (time.perf_counter() - t0)
+            del state
+        out["config5_decode_fp32_tokens_per_s"] = decode
+        out["config5_decode_bf16"] = ("not run: the reference's absorbed MLA decode gives SDPA "
+                                      "an fp32 query with a bf16 latent cache, which torch rejects")
+    out["sample"] = (f"oracle on {cores} host threads (torch {torch.__version__}): config 2 "
+                     "median of 5, config 4 one run, config 5 16 decode steps after prefill 128")
+    return out
+
+
 def time_zipf_layer(tokens: int = 16384, replays: int = 10) -> dict:
     """BASELINE config 4 on one GPU: one XL MoE layer, Zipf(1.2)-skewed routing
     (harness router bias), CUDA-graph replays of the whole block."""
@@ -284,12 +416,17 @@ def time_decode(model, batches=(1, 8, 64), prompt: int = 128, new_tokens: int = 
     return out
 
 
-def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 10,
+def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 20,
                   warmup: int = 3) -> dict:
     """BASELINE config 4 expert-parallel: the Zipf-skewed XL MoE layer with its
     16384 tokens split evenly over the ranks and the experts round-robin over
-    them; NCCL all-to-all of counts, rows and outputs.  Every rank runs it;
-    the time is the max over ranks."""
+    them.  The product path exchanges rows and outputs through the other
+    ranks' memory (``ep.PeerExpertParallelMoE``, CUDA IPC over NVLink) with no
+    host synchronisation; it is captured once as a CUDA graph and replayed.
+    Per-phase times come from CUDA events between the phases of one eager
+    call; the NCCL all-to-all path with its host read of the split sizes
+    (``ep.ExpertParallelMoE``) is timed beside it.  Every number is the max
+    over ranks."""
     from parrot_b200 import ModelConfig, ep
     from parrot_b200.model import MoE
     from parrot_b200.workloads import (make_hidden_states, make_moe_layer_weights,
@@ -303,30 +440,75 @@ def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 
     moe.router_bias = tune_zipf_router_bias(x, w["router.weight"]).to("cuda", torch.float32)
     per = total // world
     xs = x[rank * per:(rank + 1) * per].to("cuda", torch.bfloat16)
-    with torch.inference_mode():
-        layer = ep.ExpertParallelMoE(ep.B200EpOps(moe, rank, world), ep.TorchComm(),
-                                     cfg.n_experts)
-        for _ in range(warmup):
-            layer(xs)
+    stream = torch.cuda.current_stream()
+
+    def timed(fn, n) -> float:
         dist.barrier()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(iters):
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        return 1000 * a.elapsed_time(b) / n
+
+    def max_all(values: list[float]) -> list[float]:
+        t = torch.tensor(values, device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    shape = ep.EpShape(world, per, cfg.dim, cfg.n_experts, cfg.expert_dim)
+    peers = ep.PeerSet.connect(shape)
+    with torch.inference_mode():
+        layer = ep.PeerExpertParallelMoE(moe, peers)
+        for _ in range(warmup):
             layer(xs)
-        b.record()
+        eager_us = timed(lambda: layer(xs), iters)
+        # one eager call with an event after every phase
         dist.barrier()
         torch.cuda.synchronize()
-    us = torch.tensor([1000 * a.elapsed_time(b) / iters], device="cuda", dtype=torch.float64)
-    dist.all_reduce(us, op=dist.ReduceOp.MAX)
-    recv = torch.tensor([layer.last_recv_rows], device="cuda", dtype=torch.int64)
+        layer.marks = []
+        layer(xs)
+        torch.cuda.synchronize()
+        marks, layer.marks = layer.marks, None
+        names = [n for n, _ in marks[1:]]
+        phase = [1000 * marks[i][1].elapsed_time(marks[i + 1][1]) for i in range(len(marks) - 1)]
+        received = peers.received_rows()
+        graph = torch.cuda.CUDAGraph()
+        dist.barrier()
+        with torch.cuda.graph(graph):
+            layer(xs)
+        for _ in range(warmup):
+            graph.replay()
+        graph_us = timed(graph.replay, iters)
+        status = peers.status()
+        del graph
+        nccl = ep.ExpertParallelMoE(ep.B200EpOps(moe, rank, world), ep.TorchComm(), cfg.n_experts)
+        for _ in range(warmup):
+            nccl(xs)
+        nccl_us = timed(lambda: nccl(xs), iters)
+    dist.barrier()
+    peers.close()
+    graph_us, eager_us, nccl_us, *phase = max_all([graph_us, eager_us, nccl_us] + phase)
+    recv = torch.tensor([received, status[0]], device="cuda", dtype=torch.int64)
     recv_all = [torch.zeros_like(recv) for _ in range(world)]
     dist.all_gather(recv_all, recv)
-    t_us = float(us.item())
-    return {"us": t_us, "tokens_total": per * world, "tokens_per_s": per * world / (t_us * 1e-6),
+    if any(int(r[1].item()) for r in recv_all):
+        raise RuntimeError(f"expert-parallel status word set on some rank: {status}")
+    flops = 2 * (2 * total * cfg.dim * 3 * cfg.expert_dim + total * cfg.dim * 3 *
+                 cfg.shared_expert_dim + total * cfg.dim * cfg.n_experts)
+    return {"us": graph_us, "tokens_total": per * world,
+            "tokens_per_s": per * world / (graph_us * 1e-6),
+            "tflops_all_ranks": flops / (graph_us * 1e-6) / 1e12,
             "ranks": world, "placement": "round-robin (expert e on rank e % ranks)",
-            "received_rows_per_rank": [int(r.item()) for r in recv_all],
-            "timing": "CUDA events, max over ranks; one host read of the counts per call"}
+            "exchange": "peer memory (CUDA IPC over NVLink): stores + epoch flags, no host read",
+            "received_rows_per_rank": [int(r[0].item()) for r in recv_all],
+            "eager_us": eager_us,
+            "phase_us_eager": dict(zip(names, phase)),
+            "nccl_all_to_all_host_read_us": nccl_us,
+            "timing": "CUDA-graph replay of the whole layer, CUDA events, max over ranks"}
 
 
 def run_b200(args):
@@ -450,6 +632,7 @@ def run_b200(args):
     e2e_ms = max_over_ranks(e2e_ms)
     kern = time_moe_kernels(model, SEQ) if rank == 0 else None
     kern256 = time_moe_kernels(model, 256) if rank == 0 else None
+    breakdown = time_moe_breakdown(model, 256) if rank == 0 else None
     decode = time_decode(model) if rank == 0 else None
     zipf = time_zipf_layer() if rank == 0 else None
     ep_zipf = time_ep_layer(dist, rank, world) if dist is not None else None
@@ -492,14 +675,18 @@ def run_b200(args):
                      "traffic_source": "ncu --set full capture, profiles/traffic.txt"},
         "moe_layer_us": {"T512": 1000 * kern["moe_ms"], "T256": 1000 * kern256["moe_ms"],
                          "gate_up_gemm_T256_us": 1000 * kern256["gemm_ms"]},
+        "config2_moe_layer_T256": dict(breakdown, fused_block_us=1000 * kern256["moe_ms"],
+                                       fused_block_hbm_frac=(38.95e6 + 0.79e6) / (kern256["moe_ms"] * 1e-3)
+                                       / 1e9 / hbm),
         "clocks": clocks,
         "config4_zipf_moe_layer": zipf,
         "config4_ep_zipf_moe_layer": ep_zipf,
         "config5_decode_tokens_per_s": decode,
     }
     if world == 1 and not args.skip_cpu_baseline:
-        base = cpu_reference_forward(steps=2, warmup=1)
+        base = cpu_reference_forward(steps=10, warmup=2)
         line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line["cpu_baselines_other_configs"] = cpu_baselines()
     print(json.dumps(line), flush=True)
 
 

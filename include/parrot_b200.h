@@ -295,7 +295,10 @@ int parrot_moe_forward_deferred_bf16(const parrot_moe_dims* dims,
  * tokens.  Dims whose workspace (parrot_moe_workspace_layout) exceeds 4 MiB are
  * rejected with PARROT_EINVAL.  It calls no allocator.  The first call on a
  * device looks up the array's device address (and, like any first MoE call,
- * builds the SiLU table there); make it before any stream capture.  All calls
+ * builds the SiLU table there); make it before any stream capture.  The
+ * address is cached with the id of the CUDA context it was found in; a call
+ * made in another context (after cudaDeviceReset, or under a caller's own
+ * context) looks it up again, so that call is a first call too.  All calls
  * share the one array: calls whose GPU work overlaps (other streams, other
  * threads) race and must be serialised by the caller.
  * No counterpart in the reference. */
@@ -391,6 +394,134 @@ int parrot_moe_expert_ffn_bf16(int rows, int dim, int expert_dim, int n_mats, in
 int parrot_moe_ep_combine_bf16(const parrot_moe_dims* dims, const void* y, const void* workspace,
                                size_t workspace_bytes, const void* residual, void* out,
                                void* stream);
+
+/* ---- greedy next token -----------------------------------------------------
+ * The tied LM-head projection fused with the argmax over the vocabulary:
+ *   out[t] = argmax_v bf16(sum_k hidden[t, k] * weight[v, k])   (int64)
+ * fp32 accumulation, each logit rounded to bf16 before the comparison (as
+ * F.linear on bf16 tensors), the lowest v among equal values (as
+ * torch.argmax); the [rows, vocab] logits are never written.  Replaces
+ * parrot/model.py:927-931 (decode_next: F.linear(normalized,
+ * embedding.weight).argmax(-1)) and the Metal vocab_argmax_partials_bf16 /
+ * vocab_argmax_reduce_bf16 kernels (moe_bf16.metal:1541-1621, bound in
+ * metal_moe.py:329-353).  hidden [rows, dim], weight [vocab, dim] bf16;
+ * rows <= 8, dim % 8 == 0 and <= 1024.  scratch: 256-byte aligned,
+ * parrot_vocab_argmax_scratch_bytes() bytes, zero-filled before its first
+ * use (the kernel leaves its counter at zero); calls sharing a scratch must
+ * be ordered on one stream. */
+size_t parrot_vocab_argmax_scratch_bytes(void);
+int parrot_vocab_argmax_bf16(long long* out, const void* hidden, const void* weight, int rows,
+                             int dim, int vocab, void* scratch, size_t scratch_bytes,
+                             void* stream);
+
+/* Row-wise argmax of bf16 logits [rows, cols] into int64 out[rows], lowest
+ * column among equal maxima: the argmax(-1) of decode_next (model.py:927-931)
+ * when more than 8 token rows make the projection a GEMM.  cols % 8 == 0. */
+int parrot_argmax_rows_bf16(long long* out, const void* logits, int rows, int cols, void* stream);
+
+/* ---- expert-parallel exchange over peer memory ----------------------------
+ * The same expert-parallel MoE block (model.py:521-551 split over ranks as
+ * above) with the exchange done by these kernels instead of NCCL: every rank
+ * owns one EP buffer (parrot_ep_buffer_layout; zero-filled once when
+ * allocated) that every other rank maps into its address space with
+ * parrot_ipc_export / parrot_ipc_import (CUDA IPC, one node, NVLink /
+ * NVSwitch).  One call of the block on a rank, all on one stream:
+ *   parrot_moe_ep_dispatch_bf16      router + grouping (capacity -1)
+ *   parrot_moe_ep_send_bf16          rows + counts into every rank's buffer
+ *   parrot_moe_shared_ffn_bf16       shared expert (overlaps the arrivals)
+ *   parrot_moe_ep_receive            wait for every source; segment table
+ *   parrot_moe_ep_experts_bf16       local experts on the received rows
+ *   parrot_moe_ep_return_bf16        outputs back into every source's buffer
+ *   parrot_moe_ep_combine_peer_bf16  wait for every return; combine (+ residual)
+ * Nothing is read back to the host and every size is fixed by max_tokens, so
+ * the sequence can be captured in a CUDA graph.  Every rank must make the
+ * same calls in the same order (a rank with no tokens still calls them).
+ * Each flag wait is bounded by wait_ns; a wait that runs out records
+ * {1 (timeout), site, rank} in the EP buffer's status word
+ * (parrot_ep_read_status), counts the missing rank's rows as zero and
+ * returns.  No reference counterpart (the reference has no multi-GPU path). */
+#define PARROT_EP_MAX_RANKS 8
+
+typedef struct parrot_ep_dims {
+  int ranks;        /* G, 1..8, divides n_experts */
+  int rank;         /* this process's rank */
+  int max_tokens;   /* most tokens any rank passes to one call: sizes the regions */
+  int dim;          /* d, as parrot_moe_dims */
+  int n_experts;    /* E */
+  int expert_dim;   /* H */
+  unsigned long long wait_ns;  /* limit of each flag wait; 0 selects 2 s */
+} parrot_ep_dims;
+
+/* Byte offsets inside one EP buffer. */
+typedef struct parrot_ep_layout {
+  /* written by the other ranks */
+  size_t flags_in;    /* [8] u32 arrival flag of each source */
+  size_t flags_back;  /* [8] u32 return flag of each expert rank */
+  size_t meta;        /* [8, 33] int32: each source's counts per local expert, then its row base */
+  size_t recv_rows;   /* [G, 2 * max_tokens, d] rows received, one region per source */
+  size_t back_rows;   /* [2 * max_tokens, d] expert outputs of this rank's rows, dispatch order */
+  /* this rank only */
+  size_t epoch, counters, status;
+  size_t seg_rows, seg_base, seg_expert;  /* [E] segment table of the received rows */
+  size_t back_n, back_base;               /* [8] per source: rows received, their base there */
+  size_t hidden;      /* [G * 2 * max_tokens, H] */
+  size_t y;           /* [G * 2 * max_tokens, d] expert outputs */
+  size_t total;
+  int region_rows;    /* 2 * max_tokens */
+  int reserved;
+} parrot_ep_layout;
+
+/* buffers[r]: rank r's EP buffer as mapped in this process (buffers[rank] is
+ * this rank's own); entries >= ranks are ignored. */
+typedef struct parrot_ep_peers {
+  void* buffers[PARROT_EP_MAX_RANKS];
+} parrot_ep_peers;
+
+int parrot_ep_buffer_layout(const parrot_ep_dims* ep, parrot_ep_layout* layout);
+
+/* CUDA IPC of a device allocation: `handle` (64 bytes) names the allocation
+ * holding `ptr`, `offset` is ptr's offset in it.  parrot_ipc_import maps the
+ * allocation into this process (current device) with peer access enabled and
+ * returns the pointer plus the mapping's base, which parrot_ipc_close unmaps.
+ * Set-up only (outside the per-call path). */
+int parrot_ipc_export(const void* ptr, void* handle, unsigned long long* offset);
+int parrot_ipc_import(const void* handle, unsigned long long offset, void** ptr, void** base);
+int parrot_ipc_close(void* base);
+
+/* Stores this rank's dispatched rows (workspace of parrot_moe_ep_dispatch_bf16,
+ * dims->tokens <= ep->max_tokens) into each destination's receive region for
+ * this source, with the per-local-expert counts and the rows' base in this
+ * rank's dispatch order, then raises this rank's arrival flag there. */
+int parrot_moe_ep_send_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* ep,
+                            const parrot_ep_peers* peers, const void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* Waits for every source's arrival flag, then writes the segment table of the
+ * received rows (one segment per (source, local expert)) into the buffer. */
+int parrot_moe_ep_receive(const parrot_ep_dims* ep, void* buffer, void* stream);
+
+/* The local experts (packed gate_up / down of this rank's n_experts / G
+ * experts, parrot_pack_gate_up_bf16 / parrot_pack_down_bf16 layout) on the
+ * received rows, by the segment table; outputs into the buffer's y. */
+int parrot_moe_ep_experts_bf16(const parrot_ep_dims* ep, void* buffer, const void* gate_up,
+                               const void* down, void* stream);
+
+/* Stores each source's expert outputs back into that source's buffer, in its
+ * dispatch order, then raises this rank's return flag there. */
+int parrot_moe_ep_return_bf16(const parrot_ep_dims* ep, const parrot_ep_peers* peers,
+                              void* stream);
+
+/* Waits for every expert rank's return flag, then parrot_moe_ep_combine_bf16
+ * on the returned rows (buffer's back_rows). */
+int parrot_moe_ep_combine_peer_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* ep,
+                                    const void* buffer, const void* workspace,
+                                    size_t workspace_bytes, const void* residual, void* out,
+                                    void* stream);
+
+/* Copies the EP buffer's status word {code, site, info, 0} to host memory
+ * (synchronises `stream`). */
+int parrot_ep_read_status(const parrot_ep_dims* ep, const void* buffer, int* host_status4,
+                          void* stream);
 
 #ifdef __cplusplus
 }

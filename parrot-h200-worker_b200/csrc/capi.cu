@@ -446,6 +446,73 @@ int run_ffn(int rows, int dim, int expert_dim, int n_mats, int n_seg, const int*
   return PARROT_OK;
 }
 
+// ---- expert-parallel exchange over peer memory -----------------------------
+int ep_layout_of(const parrot_ep_dims* e, parrot_ep_layout* L) {
+  if (e == nullptr || L == nullptr) return fail(PARROT_EINVAL, "ep: null dims or layout%s");
+  if (e->ranks < 1 || e->ranks > parrot::kEpMaxRanks || e->rank < 0 || e->rank >= e->ranks)
+    return fail(PARROT_EINVAL, "ep: 1 <= ranks <= 8 and 0 <= rank < ranks required%s");
+  if (e->n_experts < 2 || e->n_experts > parrot::kMaxExperts || e->n_experts % e->ranks)
+    return fail(PARROT_EINVAL, "ep: 2 <= n_experts <= 32, divisible by ranks, required%s");
+  if (e->dim <= 0 || e->dim % 128 || e->dim > 1024 || e->expert_dim <= 0 || e->expert_dim % 64)
+    return fail(PARROT_EINVAL, "ep: dim % 128 == 0 (<= 1024), expert_dim % 64 == 0 required%s");
+  if (e->max_tokens < 1 || (long long)e->ranks * 2 * e->max_tokens > (1ll << 30))
+    return fail(PARROT_EINVAL, "ep: max_tokens out of range%s");
+  std::memset(L, 0, sizeof(*L));
+  const size_t G = e->ranks, R = 2 * (size_t)e->max_tokens, D = e->dim, E = e->n_experts;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align256(off + bytes);
+    return at;
+  };
+  L->flags_in = take(parrot::kEpMaxRanks * 4);
+  L->flags_back = take(parrot::kEpMaxRanks * 4);
+  L->meta = take(parrot::kEpMaxRanks * parrot::kEpMetaStride * 4);
+  L->recv_rows = take(G * R * D * 2);
+  L->back_rows = take(R * D * 2);
+  L->epoch = take(4);
+  L->counters = take(2 * 4);
+  L->status = take(16);
+  L->seg_rows = take(E * 4);
+  L->seg_base = take(E * 4);
+  L->seg_expert = take(E * 4);
+  L->back_n = take(parrot::kEpMaxRanks * 4);
+  L->back_base = take(parrot::kEpMaxRanks * 4);
+  L->hidden = take(G * R * e->expert_dim * 2);
+  L->y = take(G * R * D * 2);
+  L->total = off;
+  L->region_rows = (int)R;
+  return PARROT_OK;
+}
+
+unsigned long long ep_wait_ns(const parrot_ep_dims* e) {
+  return e->wait_ns ? e->wait_ns : 2000000000ull;  // 2 s, as the kernels' mbarrier waits
+}
+
+int ep_peers_ok(const parrot_ep_dims* e, const parrot_ep_peers* p) {
+  if (p == nullptr) return fail(PARROT_EINVAL, "ep: peers is NULL%s");
+  for (int r = 0; r < e->ranks; ++r)
+    if (p->buffers[r] == nullptr || (reinterpret_cast<uintptr_t>(p->buffers[r]) & 255))
+      return fail(PARROT_EINVAL, "ep: every rank's buffer must be mapped and 256-byte aligned%s");
+  return PARROT_OK;
+}
+
+typedef CUresult (*MemGetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+MemGetAddressRangeFn address_range_fn() {
+  static MemGetAddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<MemGetAddressRangeFn>(p);
+  });
+  return fn;
+}
+
 // ---- allocation-free MoE entry point --------------------------------------
 // Some callers cannot allocate device memory when they call the MoE block: a
 // runtime that hands out all device memory up front and forbids allocation on
@@ -459,24 +526,76 @@ constexpr size_t kStaticWorkspaceBytes = size_t(4) << 20;  // 4 MiB per device
 // cudaGetSymbolAddress with that device current.
 static __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
 
-std::mutex g_static_mutex;
-void* g_static_address[64] = {};
+// The array's device address belongs to the CUDA context that loaded this
+// library's module on the device.  A context that is destroyed and created
+// again (cudaDeviceReset, or a caller's own driver-API context) loads the
+// module afresh and the array can move, so the looked-up address is cached
+// per device together with the process-unique id of the context it was
+// looked up in (cuCtxGetId), and looked up again when the current context's
+// id differs.  Where the id cannot be read, it is looked up on every call.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
 
-// Address of g_static_workspace on the current device, looked up once per device.
+struct CtxFns {
+  CtxGetCurrentFn current = nullptr;
+  CtxGetIdFn id = nullptr;
+};
+
+const CtxFns& ctx_fns() {
+  static CtxFns fns;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fns.current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fns.id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  return fns;
+}
+
+// Id of the calling thread's current context; false when there is none.
+bool current_context_id(unsigned long long* id) {
+  const CtxFns& f = ctx_fns();
+  if (f.current == nullptr || f.id == nullptr) return false;
+  CUcontext c = nullptr;
+  if (f.current(&c) != CUDA_SUCCESS || c == nullptr) return false;
+  return f.id(c, id) == CUDA_SUCCESS;
+}
+
+struct StaticAddress {
+  unsigned long long context_id;
+  void* ptr;  // nullptr: not looked up in any live context yet
+};
+std::mutex g_static_mutex;
+StaticAddress g_static_address[64] = {};
+
+// Address of g_static_workspace on the current device, in the current context.
 int static_workspace_address(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return fail(PARROT_ECUDA, "static workspace: no current CUDA device%s");
+  unsigned long long id = 0;
+  const bool have_id = current_context_id(&id);
   std::lock_guard<std::mutex> lock(g_static_mutex);
-  if (g_static_address[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t err = cudaGetSymbolAddress(&p, g_static_workspace);
-    if (err != cudaSuccess || p == nullptr)
-      return fail(PARROT_ECUDA, "static workspace: cudaGetSymbolAddress failed: %s",
-                  cudaGetErrorString(err));
-    g_static_address[dev] = p;
+  StaticAddress& slot = g_static_address[dev];
+  if (have_id && slot.ptr != nullptr && slot.context_id == id) {
+    *out = slot.ptr;
+    return PARROT_OK;
   }
-  *out = g_static_address[dev];
+  void* p = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(&p, g_static_workspace);
+  if (err != cudaSuccess || p == nullptr)
+    return fail(PARROT_ECUDA, "static workspace: cudaGetSymbolAddress failed: %s",
+                cudaGetErrorString(err));
+  // the lookup makes the device's primary context current if none was
+  unsigned long long now = 0;
+  slot = current_context_id(&now) ? StaticAddress{now, p} : StaticAddress{0, nullptr};
+  *out = p;
   return PARROT_OK;
 }
 
@@ -988,6 +1107,251 @@ int parrot_moe_ep_combine_bf16(const parrot_moe_dims* dims, const void* y, const
   if (parrot::launch_ep_combine(c, static_cast<cudaStream_t>(stream)))
     return fail(PARROT_EINVAL, "ep_combine: unsupported dim%s");
   return check_launch("ep_combine_kernel");
+}
+
+size_t parrot_vocab_argmax_scratch_bytes(void) {
+  return 256 + (size_t)parrot::kVocabMaxGrid * 8 * (sizeof(float) + sizeof(int));
+}
+
+int parrot_vocab_argmax_bf16(long long* out, const void* hidden, const void* weight, int rows,
+                             int dim, int vocab, void* scratch, size_t scratch_bytes,
+                             void* stream) {
+  if (rows < 0 || rows > 8)
+    return fail(PARROT_EINVAL, "vocab_argmax: 0 <= rows <= 8 required%s");
+  if (dim <= 0 || dim % 8 || dim > 1024 || vocab < 1)
+    return fail(PARROT_EINVAL, "vocab_argmax: dim % 8 == 0 (<= 1024) and vocab >= 1 required%s");
+  if (rows == 0) return PARROT_OK;
+  if (!out || !hidden || !weight || !aligned16(hidden) || !aligned16(weight))
+    return fail(PARROT_EINVAL, "vocab_argmax: out and 16-byte aligned hidden/weight required%s");
+  if (!scratch || (reinterpret_cast<uintptr_t>(scratch) & 255) ||
+      scratch_bytes < parrot_vocab_argmax_scratch_bytes())
+    return fail(PARROT_EINVAL, "vocab_argmax: scratch missing, misaligned or too small%s");
+  char* sc = static_cast<char*>(scratch);
+  parrot::VocabArgmaxArgs a{};
+  a.hidden = hidden;
+  a.weight = weight;
+  a.rows = rows;
+  a.dim = dim;
+  a.vocab = vocab;
+  a.counter = reinterpret_cast<unsigned*>(sc);
+  a.partial_value = reinterpret_cast<float*>(sc + 256);
+  a.partial_index = reinterpret_cast<int*>(sc + 256 + (size_t)parrot::kVocabMaxGrid * 8 * 4);
+  a.out = out;
+  int grid = 2 * sm_count();
+  if (grid > parrot::kVocabMaxGrid) grid = parrot::kVocabMaxGrid;
+  if (parrot::launch_vocab_argmax(a, grid, static_cast<cudaStream_t>(stream)))
+    return fail(PARROT_EINVAL, "vocab_argmax: unsupported dim%s");
+  return check_launch("vocab_argmax_kernel");
+}
+
+int parrot_argmax_rows_bf16(long long* out, const void* logits, int rows, int cols, void* stream) {
+  if (rows < 0 || cols < 8 || cols % 8)
+    return fail(PARROT_EINVAL, "argmax_rows: rows >= 0 and cols % 8 == 0 required%s");
+  if (rows == 0) return PARROT_OK;
+  if (!out || !logits || !aligned16(logits))
+    return fail(PARROT_EINVAL, "argmax_rows: out and 16-byte aligned logits required%s");
+  parrot::ArgmaxRowsArgs a{logits, rows, cols, out};
+  parrot::launch_argmax_rows(a, static_cast<cudaStream_t>(stream));
+  return check_launch("argmax_rows_kernel");
+}
+
+int parrot_ep_buffer_layout(const parrot_ep_dims* ep, parrot_ep_layout* layout) {
+  return ep_layout_of(ep, layout);
+}
+
+int parrot_ipc_export(const void* ptr, void* handle, unsigned long long* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr)
+    return fail(PARROT_EINVAL, "ipc_export: null argument%s");
+  MemGetAddressRangeFn range = address_range_fn();
+  if (range == nullptr) return fail(PARROT_ECUDA, "ipc_export: cuMemGetAddressRange unavailable%s");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(PARROT_EINVAL, "ipc_export: not a device allocation%s");
+  cudaIpcMemHandle_t h;
+  const cudaError_t err = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (err != cudaSuccess)
+    return fail(PARROT_ECUDA, "ipc_export: cudaIpcGetMemHandle failed: %s", cudaGetErrorString(err));
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = reinterpret_cast<CUdeviceptr>(ptr) - base;
+  return PARROT_OK;
+}
+
+int parrot_ipc_import(const void* handle, unsigned long long offset, void** ptr, void** base) {
+  if (handle == nullptr || ptr == nullptr || base == nullptr)
+    return fail(PARROT_EINVAL, "ipc_import: null argument%s");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* b = nullptr;
+  const cudaError_t err = cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess)
+    return fail(PARROT_ECUDA, "ipc_import: cudaIpcOpenMemHandle failed: %s", cudaGetErrorString(err));
+  *base = b;
+  *ptr = static_cast<char*>(b) + offset;
+  return PARROT_OK;
+}
+
+int parrot_ipc_close(void* base) {
+  if (base == nullptr) return PARROT_OK;
+  const cudaError_t err = cudaIpcCloseMemHandle(base);
+  if (err != cudaSuccess)
+    return fail(PARROT_ECUDA, "ipc_close: cudaIpcCloseMemHandle failed: %s", cudaGetErrorString(err));
+  return PARROT_OK;
+}
+
+int parrot_moe_ep_send_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* ep,
+                            const parrot_ep_peers* peers, const void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  parrot_ep_layout P;
+  int rc = layout_of(dims, &L);
+  if (rc || (rc = ep_layout_of(ep, &P)) || (rc = ep_peers_ok(ep, peers))) return rc;
+  if (dims->capacity != -1 || dims->dim != ep->dim || dims->n_experts != ep->n_experts)
+    return fail(PARROT_EINVAL, "ep_send: dims must be the packed dispatch dims of this EP set%s");
+  if (dims->tokens > ep->max_tokens)
+    return fail(PARROT_EINVAL, "ep_send: more tokens than ep->max_tokens%s");
+  if (dims->tokens > 0 && (rc = ws_ok(workspace, workspace_bytes, L))) return rc;
+  char* own = static_cast<char*>(peers->buffers[ep->rank]);
+  parrot::EpSendArgs a{};
+  if (dims->tokens > 0) {
+    void* ws = const_cast<void*>(workspace);
+    a.rows = at<__nv_bfloat16>(ws, L.grouped);
+    a.counts = at<int>(ws, L.counts);
+    a.seg_base = at<int>(ws, L.seg_base);
+  }
+  a.tokens = dims->tokens;
+  a.dim = ep->dim;
+  a.n_experts = ep->n_experts;
+  a.ranks = ep->ranks;
+  a.rank = ep->rank;
+  a.max_tokens = ep->max_tokens;
+  for (int r = 0; r < ep->ranks; ++r) a.peers[r] = static_cast<char*>(peers->buffers[r]);
+  a.off_recv = P.recv_rows;
+  a.off_meta = P.meta;
+  a.off_flags_in = P.flags_in;
+  a.epoch = reinterpret_cast<unsigned*>(own + P.epoch);
+  a.counter = reinterpret_cast<unsigned*>(own + P.counters);
+  a.status = reinterpret_cast<int*>(own + P.status);
+  parrot::launch_ep_send(a, sm_count(), static_cast<cudaStream_t>(stream));
+  return check_launch("ep_send_kernel");
+}
+
+int parrot_moe_ep_receive(const parrot_ep_dims* ep, void* buffer, void* stream) {
+  parrot_ep_layout P;
+  int rc = ep_layout_of(ep, &P);
+  if (rc) return rc;
+  if (buffer == nullptr) return fail(PARROT_EINVAL, "ep_receive: buffer is NULL%s");
+  char* b = static_cast<char*>(buffer);
+  parrot::EpReceiveArgs a{};
+  a.flags_in = reinterpret_cast<const unsigned*>(b + P.flags_in);
+  a.meta = reinterpret_cast<const int*>(b + P.meta);
+  a.epoch = reinterpret_cast<const unsigned*>(b + P.epoch);
+  a.ranks = ep->ranks;
+  a.n_experts = ep->n_experts;
+  a.max_tokens = ep->max_tokens;
+  a.seg_rows = reinterpret_cast<int*>(b + P.seg_rows);
+  a.seg_base = reinterpret_cast<int*>(b + P.seg_base);
+  a.seg_expert = reinterpret_cast<int*>(b + P.seg_expert);
+  a.back_n = reinterpret_cast<int*>(b + P.back_n);
+  a.back_base = reinterpret_cast<int*>(b + P.back_base);
+  a.wait_ns = ep_wait_ns(ep);
+  a.status = reinterpret_cast<int*>(b + P.status);
+  parrot::launch_ep_receive(a, static_cast<cudaStream_t>(stream));
+  return check_launch("ep_receive_kernel");
+}
+
+int parrot_moe_ep_experts_bf16(const parrot_ep_dims* ep, void* buffer, const void* gate_up,
+                               const void* down, void* stream) {
+  parrot_ep_layout P;
+  int rc = ep_layout_of(ep, &P);
+  if (rc) return rc;
+  if (buffer == nullptr || gate_up == nullptr || down == nullptr || !aligned16(gate_up) ||
+      !aligned16(down))
+    return fail(PARROT_EINVAL, "ep_experts: buffer and 16-byte aligned weights required%s");
+  char* b = static_cast<char*>(buffer);
+  const int El = ep->n_experts / ep->ranks;
+  return run_ffn(ep->ranks * P.region_rows, ep->dim, ep->expert_dim, El, ep->n_experts,
+                 reinterpret_cast<const int*>(b + P.seg_rows),
+                 reinterpret_cast<const int*>(b + P.seg_base),
+                 reinterpret_cast<const int*>(b + P.seg_expert), gate_up, down, b + P.recv_rows,
+                 b + P.hidden, b + P.y, reinterpret_cast<int*>(b + P.status),
+                 static_cast<cudaStream_t>(stream));
+}
+
+int parrot_moe_ep_return_bf16(const parrot_ep_dims* ep, const parrot_ep_peers* peers,
+                              void* stream) {
+  parrot_ep_layout P;
+  int rc = ep_layout_of(ep, &P);
+  if (rc || (rc = ep_peers_ok(ep, peers))) return rc;
+  char* own = static_cast<char*>(peers->buffers[ep->rank]);
+  parrot::EpReturnArgs a{};
+  a.y = reinterpret_cast<const __nv_bfloat16*>(own + P.y);
+  a.back_n = reinterpret_cast<const int*>(own + P.back_n);
+  a.back_base = reinterpret_cast<const int*>(own + P.back_base);
+  for (int r = 0; r < ep->ranks; ++r) a.peers[r] = static_cast<char*>(peers->buffers[r]);
+  a.off_back = P.back_rows;
+  a.off_flags_back = P.flags_back;
+  a.ranks = ep->ranks;
+  a.rank = ep->rank;
+  a.dim = ep->dim;
+  a.max_tokens = ep->max_tokens;
+  a.epoch = reinterpret_cast<const unsigned*>(own + P.epoch);
+  a.counter = reinterpret_cast<unsigned*>(own + P.counters) + 1;
+  parrot::launch_ep_return(a, sm_count(), static_cast<cudaStream_t>(stream));
+  return check_launch("ep_return_kernel");
+}
+
+int parrot_moe_ep_combine_peer_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* ep,
+                                    const void* buffer, const void* workspace,
+                                    size_t workspace_bytes, const void* residual, void* out,
+                                    void* stream) {
+  parrot_moe_layout L;
+  parrot_ep_layout P;
+  int rc = layout_of(dims, &L);
+  if (rc || (rc = ep_layout_of(ep, &P))) return rc;
+  if (dims->tokens > ep->max_tokens || dims->dim != ep->dim)
+    return fail(PARROT_EINVAL, "ep_combine_peer: dims do not match the EP set%s");
+  if (buffer == nullptr) return fail(PARROT_EINVAL, "ep_combine_peer: buffer is NULL%s");
+  if ((rc = ws_ok(workspace, workspace_bytes, L))) return rc;
+  if (dims->tokens == 0) return PARROT_OK;
+  if (!out || !aligned16(out) || (residual && !aligned16(residual)))
+    return fail(PARROT_EINVAL, "ep_combine_peer: out/residual must be 16-byte aligned%s");
+  void* ws = const_cast<void*>(workspace);
+  char* b = static_cast<char*>(const_cast<void*>(buffer));
+  parrot::EpCombineArgs c{};
+  c.y = reinterpret_cast<const __nv_bfloat16*>(b + P.back_rows);
+  c.indices = at<int>(ws, L.indices);
+  c.weights = at<float>(ws, L.weights);
+  c.positions = at<int>(ws, L.positions);
+  c.shared_y = at<__nv_bfloat16>(ws, L.shared_y);
+  c.residual = static_cast<const __nv_bfloat16*>(residual);
+  c.out = static_cast<__nv_bfloat16*>(out);
+  c.tokens = dims->tokens;
+  c.dim = dims->dim;
+  c.rows = 2 * dims->tokens;
+  c.status = at<int>(ws, L.status);
+  c.wait_flags = reinterpret_cast<const unsigned*>(b + P.flags_back);
+  c.wait_epoch = reinterpret_cast<const unsigned*>(b + P.epoch);
+  c.wait_status = reinterpret_cast<int*>(b + P.status);
+  c.wait_ranks = ep->ranks;
+  c.wait_ns = ep_wait_ns(ep);
+  if (parrot::launch_ep_combine(c, static_cast<cudaStream_t>(stream)))
+    return fail(PARROT_EINVAL, "ep_combine_peer: unsupported dim%s");
+  return check_launch("ep_combine_kernel");
+}
+
+int parrot_ep_read_status(const parrot_ep_dims* ep, const void* buffer, int* host_status4,
+                          void* stream) {
+  parrot_ep_layout P;
+  int rc = ep_layout_of(ep, &P);
+  if (rc) return rc;
+  if (!buffer || !host_status4) return fail(PARROT_EINVAL, "null pointer%s");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(host_status4, static_cast<const char*>(buffer) + P.status, 16,
+                      cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return check_launch("read EP status");
+  return PARROT_OK;
 }
 
 int parrot_moe_read_status(const void* workspace, const parrot_moe_dims* dims, int* host_status4,

@@ -1,0 +1,212 @@
+// Expert-parallel exchange of the MoE block over peer memory (NVLink / NVSwitch).
+//
+// The reference runs every expert of a layer on one device
+// (parrot/model.py:521-551); here G ranks, one process per GPU, each hold
+// their own tokens and n_experts / G experts (expert e on rank e % G).  Every
+// rank owns one "EP buffer" that the other ranks map into their address space
+// (CUDA IPC).  One MoE call moves data only by stores into those buffers:
+//
+//   send     the dispatched rows (packed destination-major by the grouping
+//            kernel) are stored into each destination's receive region for
+//            this source, with this rank's per-local-expert counts and the
+//            offset of those rows in its own dispatch order; then one arrival
+//            flag per destination;
+//   receive  waits for every source's arrival flag and turns the counts into
+//            the expert GEMM's segment table (one segment per (source, local
+//            expert)) on the device;
+//   return   the expert outputs are stored back into each source's return
+//            region at the offsets the source sent, then one flag per source;
+//   combine  (route.cu) waits for every expert rank's return flag, then adds
+//            the weighted outputs to the shared expert's in expert-id order.
+//
+// No host synchronisation and no size known only on the device reaches the
+// host, so the layer can be captured in a CUDA graph.  Flags carry an epoch
+// (the number of sends this rank has made, kept in its own buffer); every
+// rank makes the same calls, so a rank waits for flag >= its own epoch.  A
+// buffer region is only rewritten after its reader has provably finished
+// with it: a source sends call i + 1 only after its combine of call i, which
+// waited for every expert rank's return of call i, which each expert rank
+// issued after its GEMM of call i had read its receive regions.
+//
+// Every wait is bounded (wait_ns): on timeout the kernel records
+// kStatusWaitTimeout in the EP buffer's status word, treats the missing
+// source as sending nothing and returns.  No TMA, no multicast: peer memory
+// is touched only by 16-byte stores and flag loads/stores.
+#include "kernels.h"
+#include "peer.cuh"
+
+namespace parrot {
+
+namespace {
+
+// Copies one row of nvec 16-byte vectors from src to dst (one warp).
+__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src,
+                                         int nvec, int lane) {
+  for (int c = lane; c < nvec; c += 32) dst[c] = __ldcg(src + c);
+}
+
+// Last-CTA election after every CTA's stores: each CTA fences its stores at
+// system scope, then counts itself; the CTA that counts last resets the
+// counter and returns true.
+__device__ bool last_cta(unsigned* counter) {
+  __shared__ bool last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    if (last) *counter = 0;
+  }
+  __syncthreads();
+  return last;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(256) ep_send_kernel(EpSendArgs a) {
+  __shared__ int n_s[kEpMaxRanks], base_s[kEpMaxRanks];
+  griddep_wait();
+  griddep_launch();
+  const int G = a.ranks, El = a.n_experts / G;
+  if (threadIdx.x < G) {
+    const int q = threadIdx.x;
+    int n = 0, base = 0;
+    if (a.tokens > 0) {
+      for (int j = 0; j < El; ++j) n += a.counts[q + j * G];
+      base = a.seg_base[q];  // expert q is rank q's first local expert
+    }
+    n_s[q] = n;
+    base_s[q] = base;
+  }
+  __syncthreads();
+  const int nvec = a.dim >> 3;
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int total = 2 * a.tokens;
+  const size_t region = (size_t)2 * a.max_tokens;
+  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < total; i += gridDim.x * warps) {
+    int q = 0;
+    while (q + 1 < G && i >= base_s[q] + n_s[q]) ++q;
+    const int k = i - base_s[q];
+    if (k < 0 || k >= n_s[q] || k >= (int)region) {
+      if (lane == 0) report_status(a.status, kStatusBadIndex, 20, i);
+      continue;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(a.peers[q] + a.off_recv) +
+                 ((size_t)a.rank * region + k) * nvec;
+    copy_row(dst, reinterpret_cast<const uint4*>(a.rows) + (size_t)i * nvec, nvec, lane);
+  }
+  if (!last_cta(a.counter)) return;
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(a.epoch) + 1;
+  if (threadIdx.x < G) {
+    const int q = threadIdx.x;
+    int* meta = reinterpret_cast<int*>(a.peers[q] + a.off_meta) + a.rank * kEpMetaStride;
+    for (int j = 0; j < El; ++j) meta[j] = a.tokens > 0 ? a.counts[q + j * G] : 0;
+    meta[kEpMetaStride - 1] = base_s[q];
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<unsigned*>(a.peers[q] + a.off_flags_in) + a.rank, e);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *a.epoch = e;
+}
+
+__global__ void __launch_bounds__(32) ep_receive_kernel(EpReceiveArgs a) {
+  __shared__ int n_s[kEpMaxRanks][kMaxExperts];
+  griddep_wait();
+  griddep_launch();
+  const int G = a.ranks, El = a.n_experts / G;
+  const unsigned e = *reinterpret_cast<const volatile unsigned*>(a.epoch);
+  const int region = 2 * a.max_tokens;
+  if (threadIdx.x < G) {
+    const int s = threadIdx.x;
+    bool ok = wait_flag(a.flags_in + s, e, a.wait_ns, a.status);
+    if (!ok) report_status(a.status, kStatusWaitTimeout, 21, s);
+    const int* meta = a.meta + s * kEpMetaStride;
+    int total = 0;
+    for (int j = 0; j < El; ++j) {
+      const int n = ok ? ld_volatile(meta + j) : 0;
+      n_s[s][j] = n;
+      if (n < 0) ok = false;
+      total += n;
+    }
+    int back = ok ? ld_volatile(meta + kEpMetaStride - 1) : 0;
+    if (ok && (total > region || back < 0 || back + total > region)) {
+      report_status(a.status, kStatusBadShape, 22, s);
+      ok = false;
+    }
+    if (!ok) {
+      for (int j = 0; j < El; ++j) n_s[s][j] = 0;
+      total = 0;
+      back = 0;
+    }
+    a.back_n[s] = total;
+    a.back_base[s] = back;
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < G; ++s) {
+      int at = s * region;
+      for (int j = 0; j < El; ++j) {
+        const int g = s * El + j;
+        a.seg_rows[g] = n_s[s][j];
+        a.seg_base[g] = at;
+        a.seg_expert[g] = j;
+        at += n_s[s][j];
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) ep_return_kernel(EpReturnArgs a) {
+  __shared__ int n_s[kEpMaxRanks], start_s[kEpMaxRanks + 1], base_s[kEpMaxRanks];
+  griddep_wait();
+  griddep_launch();
+  const int G = a.ranks;
+  if (threadIdx.x == 0) {
+    int at = 0;
+    for (int s = 0; s < G; ++s) {
+      n_s[s] = a.back_n[s];
+      base_s[s] = a.back_base[s];
+      start_s[s] = at;
+      at += n_s[s];
+    }
+    start_s[G] = at;
+  }
+  __syncthreads();
+  const int nvec = a.dim >> 3;
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const size_t region = (size_t)2 * a.max_tokens;
+  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < start_s[G]; i += gridDim.x * warps) {
+    int s = 0;
+    while (s + 1 < G && i >= start_s[s + 1]) ++s;
+    const int k = i - start_s[s];
+    const uint4* src = reinterpret_cast<const uint4*>(a.y) + ((size_t)s * region + k) * nvec;
+    uint4* dst = reinterpret_cast<uint4*>(a.peers[s] + a.off_back) + (size_t)(base_s[s] + k) * nvec;
+    copy_row(dst, src, nvec, lane);
+  }
+  if (!last_cta(a.counter)) return;
+  const unsigned e = *reinterpret_cast<const volatile unsigned*>(a.epoch);
+  if (threadIdx.x < G) {
+    const int s = threadIdx.x;
+    st_release_sys(reinterpret_cast<unsigned*>(a.peers[s] + a.off_flags_back) + a.rank, e);
+  }
+}
+
+int launch_ep_send(const EpSendArgs& a, int sms, cudaStream_t stream) {
+  const int rows = 2 * a.tokens;
+  int grid = (rows + 7) / 8;
+  if (grid > 2 * sms) grid = 2 * sms;
+  if (grid < 1) grid = 1;
+  return launch_pdl(ep_send_kernel, dim3(grid), dim3(256), 0, stream, a) == cudaSuccess ? 0 : -1;
+}
+
+int launch_ep_receive(const EpReceiveArgs& a, cudaStream_t stream) {
+  return launch_pdl(ep_receive_kernel, dim3(1), dim3(32), 0, stream, a) == cudaSuccess ? 0 : -1;
+}
+
+int launch_ep_return(const EpReturnArgs& a, int sms, cudaStream_t stream) {
+  // the row count is only known on the device: a fixed grid strides over it
+  return launch_pdl(ep_return_kernel, dim3(2 * sms), dim3(256), 0, stream, a) == cudaSuccess
+             ? 0
+             : -1;
+}
+
+}  // namespace parrot

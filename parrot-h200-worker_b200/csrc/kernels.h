@@ -104,6 +104,73 @@ struct EpCombineArgs {
   __nv_bfloat16* out;             // [T, d]
   int tokens, dim, rows;
   int* status;
+  // peer exchange only (else null / 0): wait for return flags [wait_ranks]
+  // to reach *wait_epoch first, at most wait_ns, errors into wait_status
+  const unsigned* wait_flags;
+  const unsigned* wait_epoch;
+  int* wait_status;
+  int wait_ranks;
+  unsigned long long wait_ns;
+};
+
+// ---- greedy next token (vocab.cu) -------------------------------------------
+constexpr int kVocabMaxGrid = 512;
+
+struct VocabArgmaxArgs {
+  const void* hidden;     // [rows, dim] bf16
+  const void* weight;     // [vocab, dim] bf16 (tied embedding)
+  int rows, dim, vocab;
+  float* partial_value;   // [grid, 8] per-CTA best logit per token
+  int* partial_index;     // [grid, 8] and its vocabulary row
+  unsigned* counter;      // last-CTA counter, zero between calls
+  long long* out;         // [rows] token ids
+};
+
+struct ArgmaxRowsArgs {
+  const void* logits;     // [rows, cols] bf16
+  int rows, cols;
+  long long* out;
+};
+
+// ---- expert-parallel exchange over peer memory (ep_peer.cu) ----------------
+constexpr int kEpMaxRanks = 8;
+constexpr int kEpMetaStride = kMaxExperts + 1;  // per source: counts [El], then its row base
+
+struct EpSendArgs {
+  const __nv_bfloat16* rows;  // [2T, d] dispatched rows, packed destination-major
+  const int* counts;          // [E] rows per global expert
+  const int* seg_base;        // [E] first packed row of each expert
+  int tokens, dim, n_experts, ranks, rank, max_tokens;
+  char* peers[kEpMaxRanks];   // every rank's EP buffer, mapped in this process
+  size_t off_recv, off_meta, off_flags_in;
+  unsigned* epoch;            // this rank's send count (own buffer)
+  unsigned* counter;          // last-CTA counter (own buffer)
+  int* status;                // own buffer's status word
+};
+
+struct EpReceiveArgs {
+  const unsigned* flags_in;   // [G] arrival flag of each source (own buffer)
+  const int* meta;            // [G, kEpMetaStride] counts + row base of each source
+  const unsigned* epoch;
+  int ranks, n_experts, max_tokens;
+  int* seg_rows;              // [E] one segment per (source, local expert)
+  int* seg_base;
+  int* seg_expert;
+  int* back_n;                // [G] rows received from each source
+  int* back_base;             // [G] where they go back in the source's order
+  unsigned long long wait_ns;
+  int* status;
+};
+
+struct EpReturnArgs {
+  const __nv_bfloat16* y;     // [G * 2 * max_tokens, d] expert outputs
+  const int* back_n;
+  const int* back_base;
+  char* peers[kEpMaxRanks];
+  size_t off_back, off_flags_back;
+  int ranks, rank, dim, max_tokens;
+  const unsigned* epoch;
+  unsigned* counter;
 };
 
 enum GemmMode : int { kGemmSwiGLU = 0, kGemmPlain = 1 };
@@ -210,6 +277,11 @@ int launch_route(const RouteArgs& args, const CUtensorMap* x_map, const CUtensor
 int launch_group(const GroupArgs& args, cudaStream_t stream);
 int launch_combine(const CombineArgs& args, cudaStream_t stream);
 int launch_ep_combine(const EpCombineArgs& args, cudaStream_t stream);
+int launch_ep_send(const EpSendArgs& args, int sms, cudaStream_t stream);
+int launch_vocab_argmax(const VocabArgmaxArgs& args, int grid, cudaStream_t stream);
+int launch_argmax_rows(const ArgmaxRowsArgs& args, cudaStream_t stream);
+int launch_ep_receive(const EpReceiveArgs& args, cudaStream_t stream);
+int launch_ep_return(const EpReturnArgs& args, int sms, cudaStream_t stream);
 int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
                         const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
                         const CUtensorMap* tm_x_shared, int grid, int token_tile,

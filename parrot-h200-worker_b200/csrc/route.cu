@@ -21,6 +21,7 @@
 //                segment tables, counts and router statistics.
 #include "common.cuh"
 #include "kernels.h"
+#include "peer.cuh"
 #include "tc.cuh"
 
 namespace parrot {
@@ -586,12 +587,30 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
 // weights them exactly as the down GEMM's scatter epilogue does
 // (bf16(bf16(y) * bf16(w))) and adds them to the shared output in ascending
 // expert order, so the result is bit-identical to the single-GPU block.
+//
+// With the peer exchange (wait_flags set), the expert outputs arrive from the
+// other ranks: the CTA first waits (bounded) until every expert rank has
+// raised its return flag for this call.
 template <int V>
 __global__ void __launch_bounds__(128) ep_combine_kernel(EpCombineArgs a) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   griddep_wait();
   griddep_launch();
+  if (a.wait_flags != nullptr) {
+    __shared__ int failed;
+    if (threadIdx.x == 0) failed = 0;
+    __syncthreads();
+    if (threadIdx.x < a.wait_ranks) {
+      const unsigned e = *reinterpret_cast<const volatile unsigned*>(a.wait_epoch);
+      if (!wait_flag(a.wait_flags + threadIdx.x, e, a.wait_ns, a.wait_status)) {
+        report_status(a.wait_status, kStatusWaitTimeout, 23, threadIdx.x);
+        failed = 1;
+      }
+    }
+    __syncthreads();
+    if (failed) return;
+  }
   if (t >= a.tokens) return;
   const int d = a.dim, nvec = d >> 3;
   const int e0 = __ldg(a.indices + 2 * t), e1 = __ldg(a.indices + 2 * t + 1);

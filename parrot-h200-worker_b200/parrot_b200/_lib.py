@@ -44,6 +44,28 @@ class MoeLayout(ctypes.Structure):
         ("reserved", c_int)]
 
 
+EP_MAX_RANKS = 8
+
+
+class EpDims(ctypes.Structure):
+    _fields_ = [("ranks", c_int), ("rank", c_int), ("max_tokens", c_int), ("dim", c_int),
+                ("n_experts", c_int), ("expert_dim", c_int), ("wait_ns", ctypes.c_ulonglong)]
+
+
+EP_LAYOUT_OFFSETS = ("flags_in", "flags_back", "meta", "recv_rows", "back_rows", "epoch",
+                     "counters", "status", "seg_rows", "seg_base", "seg_expert", "back_n",
+                     "back_base", "hidden", "y", "total")
+
+
+class EpLayout(ctypes.Structure):
+    _fields_ = [(name, c_size_t) for name in EP_LAYOUT_OFFSETS] + [
+        ("region_rows", c_int), ("reserved", c_int)]
+
+
+class EpPeers(ctypes.Structure):
+    _fields_ = [("buffers", c_void_p * EP_MAX_RANKS)]
+
+
 _SIGNATURES = {
     "parrot_b200_version": (c_int, []),
     "parrot_b200_last_error": (ctypes.c_char_p, []),
@@ -106,6 +128,25 @@ _SIGNATURES = {
                                            c_void_p, c_void_p, c_void_p]),
     "parrot_moe_ep_combine_bf16": (c_int, [POINTER(MoeDims), c_void_p, c_void_p, c_size_t,
                                            c_void_p, c_void_p, c_void_p]),
+    "parrot_vocab_argmax_scratch_bytes": (c_size_t, []),
+    "parrot_vocab_argmax_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                         c_void_p, c_size_t, c_void_p]),
+    "parrot_argmax_rows_bf16": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "parrot_ep_buffer_layout": (c_int, [POINTER(EpDims), POINTER(EpLayout)]),
+    "parrot_ipc_export": (c_int, [c_void_p, c_void_p, POINTER(ctypes.c_ulonglong)]),
+    "parrot_ipc_import": (c_int, [c_void_p, ctypes.c_ulonglong, POINTER(c_void_p),
+                                  POINTER(c_void_p)]),
+    "parrot_ipc_close": (c_int, [c_void_p]),
+    "parrot_moe_ep_send_bf16": (c_int, [POINTER(MoeDims), POINTER(EpDims), POINTER(EpPeers),
+                                        c_void_p, c_size_t, c_void_p]),
+    "parrot_moe_ep_receive": (c_int, [POINTER(EpDims), c_void_p, c_void_p]),
+    "parrot_moe_ep_experts_bf16": (c_int, [POINTER(EpDims), c_void_p, c_void_p, c_void_p,
+                                           c_void_p]),
+    "parrot_moe_ep_return_bf16": (c_int, [POINTER(EpDims), POINTER(EpPeers), c_void_p]),
+    "parrot_moe_ep_combine_peer_bf16": (c_int, [POINTER(MoeDims), POINTER(EpDims), c_void_p,
+                                                c_void_p, c_size_t, c_void_p, c_void_p,
+                                                c_void_p]),
+    "parrot_ep_read_status": (c_int, [POINTER(EpDims), c_void_p, POINTER(c_int), c_void_p]),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -15,6 +15,7 @@ from dataclasses import dataclass
 from typing import Sequence
 
 import torch
+import torch.nn.functional as F
 from torch import Tensor
 
 from . import _lib
@@ -183,6 +184,44 @@ def b200_decode_attention(q: Tensor, k_new: Tensor, v_new: Tensor | None, k_cach
         _p(k_new), _p(v_new), k_new.stride(0), _p(k_cache), _p(v_cache), _p(position), b,
         n_heads, n_kv_heads, s_max, head_dim, window, float(scale), _p(scratch),
         scratch.numel(), None, _stream()), "parrot_decode_attention_bf16")
+    return out
+
+
+_VOCAB_SCRATCH: dict = {}
+VOCAB_FUSED_MAX_ROWS = 8
+
+
+def b200_vocab_argmax(hidden: Tensor, weight: Tensor) -> Tensor:
+    """Greedy next token from the tied LM head (``metal_moe.py:329-353``
+    ``metal_vocab_argmax``; ``model.py:927-931``): ``hidden`` [batch, (1,) dim]
+    bf16, ``weight`` [vocab, dim] bf16 -> token ids [batch, 1] int64, the
+    ``F.linear(hidden, weight).argmax(-1)`` of ``decode_next``.  Up to 8 rows
+    the projection and the argmax are one kernel and no logits are written;
+    above that the projection is a cuBLAS GEMM and the argmax this library's
+    row kernel."""
+    _require_device(hidden, "vocab argmax")
+    _require_inference("vocab argmax")
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise RuntimeError("The B200 vocab argmax takes bf16 hidden states and weights")
+    batch, dim = hidden.shape[0], hidden.shape[-1]
+    h = hidden.reshape(batch, dim).contiguous()
+    w = weight.contiguous()
+    out = torch.empty((batch, 1), device=hidden.device, dtype=torch.int64)
+    lib = _lib.load()
+    if batch <= VOCAB_FUSED_MAX_ROWS:
+        key = hidden.device.index
+        scratch = _VOCAB_SCRATCH.get(key)
+        if scratch is None:
+            scratch = torch.zeros(int(lib.parrot_vocab_argmax_scratch_bytes()),
+                                  device=hidden.device, dtype=torch.uint8)
+            _VOCAB_SCRATCH[key] = scratch
+        _lib.check(lib.parrot_vocab_argmax_bf16(
+            _p(out), _p(h), _p(w), batch, dim, w.shape[0], _p(scratch), scratch.numel(),
+            _stream()), "parrot_vocab_argmax_bf16")
+        return out
+    logits = F.linear(h, w)
+    _lib.check(lib.parrot_argmax_rows_bf16(_p(out), _p(logits), batch, w.shape[0], _stream()),
+               "parrot_argmax_rows_bf16")
     return out
 
 

@@ -26,6 +26,13 @@ same GEMM arithmetic, and the combine adds the same bf16 values in the same
 order.  The exchanges go through a small communicator interface so the same
 orchestration runs over NCCL (``TorchComm``) or, in tests, gloo on CPU with
 the oracle's arithmetic in place of the kernels.
+
+On GPUs of one node the product path is ``PeerExpertParallelMoE``: the same
+seven steps with the exchange done by this library's kernels through the
+other ranks' memory (CUDA IPC mappings over NVLink / NVSwitch) instead of
+NCCL, with the split sizes kept on the device — no host read, fixed-size
+regions sized by the largest token count, so a layer can be captured in a
+CUDA graph (``parrot_moe_ep_send_bf16`` … ``parrot_moe_ep_combine_peer_bf16``).
 """
 from __future__ import annotations
 
@@ -125,30 +132,57 @@ class EpOps(Protocol):
         """Shared + weighted expert outputs (+ residual) -> [T, d]."""
 
 
-class ExpertParallelMoE:
-    """Runs one MoE layer expert-parallel over ``comm``'s ranks."""
+class ExchangeError(RuntimeError):
+    """A rank received a count table that cannot be right."""
 
-    def __init__(self, ops: EpOps, comm: Comm, n_experts: int):
+
+def check_count_table(table: Tensor, rank: int, max_rows: int | None) -> None:
+    """``table`` [G, El + 1]: row ``s`` holds source ``s``'s row counts for this
+    rank's local experts, then their total.  Raises ``ExchangeError`` for a
+    negative count, a total that is not the sum of the counts, or a total
+    above ``max_rows`` (what one source can send at most)."""
+    counts, totals = table[:, :-1], table[:, -1]
+    for s in range(table.shape[0]):
+        if (counts[s] < 0).any() or int(counts[s].sum()) != int(totals[s]) or (
+                max_rows is not None and int(totals[s]) > max_rows):
+            raise ExchangeError(f"rank {rank}: inconsistent count table from rank {s}: "
+                                f"{table[s].tolist()}")
+
+
+class ExpertParallelMoE:
+    """Runs one MoE layer expert-parallel over ``comm``'s ranks.
+
+    ``max_rows_per_source`` (optional) bounds the rows one source may send to
+    one rank (twice the most tokens a rank holds); a count table above it, or
+    one whose total disagrees with its counts, raises ``ExchangeError`` before
+    any row is exchanged.  A rank that fails or leaves makes the others'
+    next exchange fail with the process group's error (its timeout)."""
+
+    def __init__(self, ops: EpOps, comm: Comm, n_experts: int,
+                 max_rows_per_source: int | None = None):
         if n_experts % comm.size:
             raise ValueError(f"n_experts={n_experts} is not divisible by {comm.size} ranks")
         self.ops = ops
         self.comm = comm
         self.n_experts = n_experts
+        self.max_rows = max_rows_per_source
         self.last_recv_rows = 0
 
     def __call__(self, x: Tensor, residual: Tensor | None = None) -> Tensor:
         G = self.comm.size
         El = self.n_experts // G
         rows, counts = self.ops.dispatch(x)
-        send = send_counts(counts.to(torch.int32), G).view(-1)
+        table = send_counts(counts.to(torch.int32), G)
+        send = torch.cat([table, table.sum(1, keepdim=True)], 1).view(-1)
         recv = torch.empty_like(send)
         self.comm.all_to_all(recv, send, None, None)
         both = torch.cat([send, recv])
         self.ops.shared(x)  # the GPU computes the shared expert while the host waits below
-        both = both.cpu().view(2, G, El)  # the one host sync: split sizes of the row exchange
-        send_split = both[0].sum(1).tolist()
-        recv_tab = both[1].tolist()
-        recv_split = [sum(r) for r in recv_tab]
+        both = both.cpu().view(2, G, El + 1)  # the one host sync: split sizes of the row exchange
+        check_count_table(both[1], self.comm.rank, self.max_rows)
+        send_split = both[0, :, El].tolist()
+        recv_tab = both[1, :, :El].tolist()
+        recv_split = both[1, :, El].tolist()
         seg = receive_segments(recv_tab)
         received = rows.new_empty((seg.total, rows.shape[1]))
         self.comm.all_to_all(received, rows[:sum(send_split)], recv_split, send_split)
@@ -242,3 +276,203 @@ class B200EpOps:
             ctypes.byref(dims), bridge._p(y), bridge._p(ws), ws.numel(), bridge._p(residual),
             bridge._p(out), bridge._stream()), "parrot_moe_ep_combine_bf16")
         return out
+
+
+# ---- the peer-memory exchange (one node, one process per GPU) -------------------
+
+@dataclass(frozen=True)
+class EpShape:
+    """Sizes of one expert-parallel set: ``max_tokens`` bounds every rank's
+    tokens per call and sizes the fixed receive and return regions."""
+    ranks: int
+    max_tokens: int
+    dim: int
+    n_experts: int
+    expert_dim: int
+    wait_ns: int = 0  # limit of each device-side flag wait; 0 = 2 s
+
+    def dims(self, rank: int) -> _lib.EpDims:
+        return _lib.EpDims(self.ranks, rank, self.max_tokens, self.dim, self.n_experts,
+                           self.expert_dim, self.wait_ns)
+
+    def layout(self) -> _lib.EpLayout:
+        lay = _lib.EpLayout()
+        _lib.check(_lib.load().parrot_ep_buffer_layout(ctypes.byref(self.dims(0)),
+                                                       ctypes.byref(lay)), "EP buffer layout")
+        return lay
+
+
+class PeerSet:
+    """Every rank's EP buffer as this rank sees it.
+
+    ``connect`` maps the other processes' buffers with CUDA IPC (set-up only:
+    one all-gather of the handles over the process group); ``local`` builds all
+    ranks' buffers in this process on one device, for running the ranks one
+    after another on a single GPU.
+    """
+
+    def __init__(self, shape: EpShape, rank: int, own: Tensor, pointers: list[int],
+                 mapped: list[int] | None = None):
+        self.shape = shape
+        self.rank = rank
+        self.own = own
+        self.pointers = pointers
+        self._mapped = mapped or []
+        self.dims = shape.dims(rank)
+        self.peers = _lib.EpPeers()
+        for r, p in enumerate(pointers):
+            self.peers.buffers[r] = p
+
+    @staticmethod
+    def _allocate(shape: EpShape, device) -> Tensor:
+        # zero-filled once: flags, epoch and counters start at 0
+        return torch.zeros(int(shape.layout().total), device=device, dtype=torch.uint8)
+
+    @classmethod
+    def connect(cls, shape: EpShape, group=None) -> "PeerSet":
+        import torch.distributed as dist
+        rank, ranks = dist.get_rank(group), dist.get_world_size(group)
+        if ranks != shape.ranks:
+            raise ValueError(f"process group has {ranks} ranks, the EP shape {shape.ranks}")
+        lib = _lib.load()
+        own = cls._allocate(shape, torch.device("cuda", torch.cuda.current_device()))
+        handle = (ctypes.c_ubyte * 64)()
+        offset = ctypes.c_ulonglong()
+        _lib.check(lib.parrot_ipc_export(ctypes.c_void_p(own.data_ptr()), handle,
+                                         ctypes.byref(offset)), "parrot_ipc_export")
+        torch.cuda.synchronize()  # the zero fill is done before any peer writes
+        gathered: list = [None] * ranks
+        dist.all_gather_object(gathered, (bytes(handle), offset.value), group=group)
+        pointers, mapped = [], []
+        for r, (h, off) in enumerate(gathered):
+            if r == rank:
+                pointers.append(own.data_ptr())
+                continue
+            ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+            buf = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+            _lib.check(lib.parrot_ipc_import(buf, off, ctypes.byref(ptr), ctypes.byref(base)),
+                       "parrot_ipc_import")
+            pointers.append(ptr.value)
+            mapped.append(base.value)
+        dist.barrier(group=group)
+        return cls(shape, rank, own, pointers, mapped)
+
+    @classmethod
+    def local(cls, shape: EpShape, device) -> list["PeerSet"]:
+        bufs = [cls._allocate(shape, device) for _ in range(shape.ranks)]
+        ptrs = [b.data_ptr() for b in bufs]
+        return [cls(shape, r, bufs[r], ptrs) for r in range(shape.ranks)]
+
+    def status(self) -> list[int]:
+        """The EP buffer's status word {code, site, info, 0} (synchronises)."""
+        out = (ctypes.c_int * 4)()
+        _lib.check(_lib.load().parrot_ep_read_status(
+            ctypes.byref(self.dims), ctypes.c_void_p(self.own.data_ptr()), out,
+            bridge._stream()), "parrot_ep_read_status")
+        return list(out)
+
+    def received_rows(self) -> int:
+        """Rows this rank received in its last call (reads the device; synchronises)."""
+        lay = self.shape.layout()
+        n = self.own[lay.back_n:lay.back_n + 4 * self.shape.ranks].view(torch.int32)
+        return int(n.sum().item())
+
+    def close(self) -> None:
+        lib = _lib.load()
+        for base in self._mapped:
+            lib.parrot_ipc_close(ctypes.c_void_p(base))
+        self._mapped = []
+
+
+class PeerExpertParallelMoE:
+    """One MoE layer expert-parallel over the ranks of ``peers``, exchanged
+    through peer memory.  ``__call__`` enqueues the whole layer on the current
+    stream with no host synchronisation; every rank must call it the same
+    number of times (with zero tokens if it has none).  The three phases are
+    also callable on their own (``send``, ``experts``, ``finish``) so that
+    ranks sharing one GPU can run one after another in tests."""
+
+    def __init__(self, module, peers: PeerSet):
+        cfg = module.cfg
+        shape = peers.shape
+        if (shape.dim, shape.n_experts, shape.expert_dim) != (cfg.dim, cfg.n_experts,
+                                                             cfg.expert_dim):
+            raise ValueError("EP shape does not match the MoE module's dims")
+        self.peers = peers
+        self.ops = B200EpOps(module, peers.rank, shape.ranks)
+        self.cfg = cfg
+        self._pending: tuple | None = None
+        # (name, event) after each phase when a list is set (instrumentation only)
+        self.marks: list | None = None
+
+    def _mark(self, name: str) -> None:
+        if self.marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.marks.append((name, ev))
+
+    def send(self, x: Tensor) -> None:
+        ops, peers = self.ops, self.peers
+        bridge._require_device(x, "MoE")
+        bridge._require_inference("MoE")
+        x = x.contiguous()
+        T = x.shape[0]
+        if T > peers.shape.max_tokens:
+            raise ValueError(f"{T} tokens, more than the EP set's max_tokens "
+                             f"{peers.shape.max_tokens}")
+        dims = bridge.moe_dims(self.cfg, T, capacity=-1)
+        ws = ops._workspace(dims)
+        w = bridge._weights_struct(ops.packed, ops.bias)
+        lib, stream = _lib.load(), bridge._stream()
+        outputs = _lib.MoeOutputs(None, None, None, None, None, None, None, None)
+        _lib.check(lib.parrot_moe_ep_dispatch_bf16(
+            ctypes.byref(dims), ctypes.byref(w), bridge._p(x), ctypes.byref(outputs), peers.shape.ranks,
+            bridge._p(ws), ws.numel(), stream), "parrot_moe_ep_dispatch_bf16")
+        self._mark("dispatch")
+        _lib.check(lib.parrot_moe_ep_send_bf16(
+            ctypes.byref(dims), ctypes.byref(peers.dims), ctypes.byref(peers.peers), bridge._p(ws),
+            ws.numel(), stream), "parrot_moe_ep_send_bf16")
+        self._mark("send")
+        self._pending = (x, dims, ws, w)
+
+    def experts(self) -> None:
+        x, dims, ws, w = self._pending
+        ops, peers = self.ops, self.peers
+        lib, stream = _lib.load(), bridge._stream()
+        own = ctypes.c_void_p(peers.own.data_ptr())
+        # the shared expert runs while the other ranks' rows arrive
+        _lib.check(lib.parrot_moe_shared_ffn_bf16(
+            ctypes.byref(dims), ctypes.byref(w), bridge._p(x), bridge._p(ws), ws.numel(),
+            stream), "parrot_moe_shared_ffn_bf16")
+        self._mark("shared")
+        _lib.check(lib.parrot_moe_ep_receive(ctypes.byref(peers.dims), own, stream),
+                   "parrot_moe_ep_receive")
+        self._mark("receive")
+        _lib.check(lib.parrot_moe_ep_experts_bf16(
+            ctypes.byref(peers.dims), own, bridge._p(ops.gate_up), bridge._p(ops.down), stream),
+            "parrot_moe_ep_experts_bf16")
+        self._mark("experts")
+        _lib.check(lib.parrot_moe_ep_return_bf16(ctypes.byref(peers.dims),
+                                                 ctypes.byref(peers.peers), stream),
+                   "parrot_moe_ep_return_bf16")
+        self._mark("return")
+
+    def finish(self, residual: Tensor | None = None) -> Tensor:
+        x, dims, ws, _ = self._pending
+        self._pending = None
+        out = torch.empty_like(x)
+        if residual is not None:
+            residual = residual.reshape(out.shape).contiguous()
+        _lib.check(_lib.load().parrot_moe_ep_combine_peer_bf16(
+            ctypes.byref(dims), ctypes.byref(self.peers.dims),
+            ctypes.c_void_p(self.peers.own.data_ptr()), bridge._p(ws), ws.numel(),
+            bridge._p(residual), bridge._p(out), bridge._stream()),
+            "parrot_moe_ep_combine_peer_bf16")
+        self._mark("combine")
+        return out
+
+    def __call__(self, x: Tensor, residual: Tensor | None = None) -> Tensor:
+        self._mark("start")
+        self.send(x)
+        self.experts()
+        return self.finish(residual)

@@ -696,11 +696,15 @@ class Parrot(nn.Module):
                 x = out
             index += 1
         h = res.mix(self.depth_mix[-1], self.final_norm) if attnres else self.final_norm(x)
-        logits = F.linear(h, self.embedding.weight)
+        if _next_token_only:
+            # the projection and the argmax in one pass, no logits (model.py:927-931)
+            output = bridge.b200_vocab_argmax(h, self.embedding.weight)
+        else:
+            output = F.linear(h, self.embedding.weight)
         state.position += 1
         if state.position_device is not None:
             state.position_device.add_(1)
-        return (logits.argmax(-1) if _next_token_only else logits), state
+        return output, state
 
     @torch.inference_mode()
     def decode_next(self, input_ids: Tensor, state: GenerationState):

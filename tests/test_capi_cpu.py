@@ -214,3 +214,54 @@ def test_bridge_refuses_cpu_tensors():
     norm = Parrot(cfg).final_norm
     with torch.inference_mode(), pytest.raises(RuntimeError, match="CUDA"):
         bridge.b200_rms_norm(norm, torch.zeros(2, 128, dtype=torch.bfloat16))
+
+
+def _ep_dims(**kw):
+    d = dict(ranks=4, rank=1, max_tokens=2048, dim=768, n_experts=16, expert_dim=512, wait_ns=0)
+    d.update(kw)
+    return _lib.EpDims(*d.values())
+
+
+def test_ep_buffer_layout_is_aligned_and_sized(lib):
+    lay = _lib.EpLayout()
+    assert lib.parrot_ep_buffer_layout(ctypes.byref(_ep_dims()), ctypes.byref(lay)) == 0
+    offsets = [getattr(lay, n) for n in _lib.EP_LAYOUT_OFFSETS]
+    assert all(o % 256 == 0 for o in offsets)
+    assert offsets == sorted(offsets)
+    assert lay.region_rows == 4096
+    # peer-written regions: one receive region per source, one return region
+    assert lay.back_rows - lay.recv_rows >= 4 * 4096 * 768 * 2
+    assert lay.hidden - lay.back_rows >= 4096 * 768 * 2
+    assert lay.total - lay.y >= 4 * 4096 * 768 * 2
+
+
+@pytest.mark.parametrize("field,value", [("ranks", 0), ("ranks", 9), ("rank", 4), ("rank", -1),
+                                         ("n_experts", 18), ("dim", 96), ("expert_dim", 100),
+                                         ("max_tokens", 0)])
+def test_ep_layout_rejects_unsupported_dims(lib, field, value):
+    lay = _lib.EpLayout()
+    assert lib.parrot_ep_buffer_layout(ctypes.byref(_ep_dims(**{field: value})),
+                                       ctypes.byref(lay)) == _lib.PARROT_EINVAL
+    assert b"ep:" in lib.parrot_b200_last_error()
+
+
+def test_ep_calls_reject_bad_arguments_before_any_launch(lib):
+    """Argument errors come back as PARROT_EINVAL without touching a device."""
+    ep = _ep_dims(ranks=2, rank=0, max_tokens=64)
+    peers = _lib.EpPeers()  # no buffers mapped
+    dims = _lib.MoeDims(64, 768, 16, 2, 512, 256, -1)
+    assert lib.parrot_moe_ep_send_bf16(ctypes.byref(dims), ctypes.byref(ep), ctypes.byref(peers),
+                                       None, 0, None) == _lib.PARROT_EINVAL
+    assert b"mapped" in lib.parrot_b200_last_error()
+    peers.buffers[0] = peers.buffers[1] = 256
+    too_many = _lib.MoeDims(65, 768, 16, 2, 512, 256, -1)
+    assert lib.parrot_moe_ep_send_bf16(ctypes.byref(too_many), ctypes.byref(ep),
+                                       ctypes.byref(peers), None, 0, None) == _lib.PARROT_EINVAL
+    assert b"max_tokens" in lib.parrot_b200_last_error()
+    capacity = _lib.MoeDims(64, 768, 16, 2, 512, 256, 0)
+    assert lib.parrot_moe_ep_send_bf16(ctypes.byref(capacity), ctypes.byref(ep),
+                                       ctypes.byref(peers), None, 0, None) == _lib.PARROT_EINVAL
+    assert lib.parrot_moe_ep_receive(ctypes.byref(ep), None, None) == _lib.PARROT_EINVAL
+    assert lib.parrot_moe_ep_experts_bf16(ctypes.byref(ep), None, None, None,
+                                          None) == _lib.PARROT_EINVAL
+    assert lib.parrot_ipc_export(None, None, None) == _lib.PARROT_EINVAL

@@ -152,3 +152,122 @@ def _free_port() -> int:
 def test_expert_parallel_over_nccl_equals_single_device_block():
     ranks = min(torch.cuda.device_count(), 8)
     mp.spawn(_nccl_rank, args=(ranks, _free_port(), 21, 4096), nprocs=ranks, join=True)
+
+
+# ---- the peer-memory exchange -------------------------------------------------
+
+def _peer_layers(module, sizes, wait_ns=200_000_000):
+    cfg = module.cfg
+    shape = ep.EpShape(len(sizes), max(1, max(sizes)), cfg.dim, cfg.n_experts, cfg.expert_dim,
+                       wait_ns)
+    peers = ep.PeerSet.local(shape, torch.device("cuda"))
+    return peers, [ep.PeerExpertParallelMoE(module, p) for p in peers]
+
+
+@pytest.mark.parametrize("ranks,zipf", [(1, False), (2, False), (4, True), (8, True)])
+def test_peer_exchange_ranks_in_turn_equal_single_device_block(ranks, zipf):
+    """All ranks' buffers on one GPU, the ranks' phases issued in turn on one
+    stream: every send before any receive, every return before any combine, so
+    each flag a kernel waits for was raised by a kernel that already finished.
+    Two calls in a row (the epoch advances, the regions are reused)."""
+    tokens = 3000
+    with torch.inference_mode():
+        if zipf:
+            module, x = zipf_module(seed=12, tokens=tokens)
+        else:
+            cfg = moe_config()
+            module, _ = build_moe_pair(cfg, seed=12)
+            x = hidden_states(tokens, cfg.dim, seed=13).cuda()
+        residual = hidden_states(tokens, module.cfg.dim, seed=14).cuda()
+        sizes = shard_sizes(tokens, ranks)
+        starts = [sum(sizes[:r]) for r in range(ranks)]
+        peers, layers = _peer_layers(module, sizes)
+        for call in range(2):
+            xs = [x[starts[r]:starts[r] + sizes[r]] * (1 + call) for r in range(ranks)]
+            rs = [residual[starts[r]:starts[r] + sizes[r]] for r in range(ranks)]
+            for r in range(ranks):
+                layers[r].send(xs[r])
+            for r in range(ranks):
+                layers[r].experts()
+            outs = [layers[r].finish(rs[r]) for r in range(ranks)]
+            torch.cuda.synchronize()
+            for r in range(ranks):
+                assert peers[r].status() == [0, 0, 0, 0], f"rank {r}"
+                if sizes[r] == 0:
+                    assert outs[r].shape[0] == 0
+                    continue
+                want, _, _ = bridge.b200_moe(module, xs[r], True, rs[r])
+                torch.cuda.synchronize()
+                assert torch.equal(outs[r], want), f"call {call}, rank {r}"
+
+
+def test_peer_exchange_wait_for_a_missing_rank_times_out_with_status():
+    """A two-rank set whose second rank never runs: rank 0's wait for its rows
+    (and later for its returned outputs) runs out after the short limit, the
+    status word says so, and the device stays usable."""
+    cfg = moe_config()
+    with torch.inference_mode():
+        module, _ = build_moe_pair(cfg, seed=3)
+        x = hidden_states(64, cfg.dim, seed=4).cuda()
+        peers, layers = _peer_layers(module, [64, 64], wait_ns=50_000_000)
+        layers[0].send(x)
+        layers[0].experts()
+        layers[0].finish()
+        torch.cuda.synchronize()
+        code, site, info, _ = peers[0].status()
+        assert (code, site, info) == (1, 21, 1)  # timeout, receive wait, source rank 1
+        want, _, _ = bridge.b200_moe(module, x, True)
+        torch.cuda.synchronize()
+        assert torch.isfinite(want).all()
+
+
+def _peer_rank(rank, ranks, port, seed, tokens):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=ranks,
+                            device_id=torch.device("cuda", rank))
+    peers = None
+    try:
+        with torch.inference_mode():
+            module, x = zipf_module(seed=seed, tokens=tokens)
+            residual = hidden_states(tokens, module.cfg.dim, seed=seed + 1).cuda()
+            sizes = shard_sizes(tokens, ranks)
+            start = sum(sizes[:rank])
+            xs = x[start:start + sizes[rank]]
+            rs = residual[start:start + sizes[rank]]
+            cfg = module.cfg
+            shape = ep.EpShape(ranks, max(sizes), cfg.dim, cfg.n_experts, cfg.expert_dim,
+                               1_000_000_000)
+            peers = ep.PeerSet.connect(shape)
+            layer = ep.PeerExpertParallelMoE(module, peers)
+            want = bridge.b200_moe(module, xs, True, rs)[0] if sizes[rank] else None
+            for _ in range(3):
+                got = layer(xs, rs)
+            torch.cuda.synchronize()
+            assert peers.status() == [0, 0, 0, 0], f"rank {rank}"
+            if want is not None:
+                assert torch.equal(got, want), f"rank {rank}"
+            # the same layer captured once and replayed
+            graph = torch.cuda.CUDAGraph()
+            dist.barrier()
+            with torch.cuda.graph(graph):
+                static_out = layer(xs, rs)
+            for _ in range(2):
+                graph.replay()
+            torch.cuda.synchronize()
+            assert peers.status() == [0, 0, 0, 0], f"rank {rank} (graph)"
+            if want is not None:
+                assert torch.equal(static_out, want), f"rank {rank} (graph)"
+            del graph
+        dist.barrier()
+    finally:
+        if peers is not None:
+            peers.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_peer_exchange_over_nvlink_equals_single_device_block():
+    ranks = min(torch.cuda.device_count(), 8)
+    mp.spawn(_peer_rank, args=(ranks, _free_port(), 31, 4096), nprocs=ranks, join=True)

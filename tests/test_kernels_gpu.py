@@ -574,3 +574,64 @@ def test_rope_inplace_is_bit_exact_to_reference_bf16(batch, seq, start):
     assert torch.equal(qkv[..., :qw].view(batch, seq, H, hd).transpose(1, 2), q_ref)
     assert torch.equal(qkv[..., qw:qw + kw].view(batch, seq, KV, hd).transpose(1, 2), k_ref)
     assert torch.equal(qkv[..., qw + kw:], v_ref)
+
+
+# ---------------------------------------------------------------------------
+# Greedy next token: LM-head projection fused with the vocabulary argmax
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("rows,dim", [(1, 768), (2, 768), (3, 768), (5, 768), (8, 768),
+                                      (9, 768), (64, 768), (3, 128), (8, 1024)])
+def test_vocab_argmax_matches_linear_argmax(rows, dim):
+    """decode_next's F.linear(h, W).argmax(-1) (model.py:927-931).  The fused
+    kernel (<= 8 rows) and the GEMM + row-argmax path (> 8) must pick a token
+    whose exact logit is a maximum up to bf16 rounding of the logits, and the
+    very token torch picks wherever the exact top-2 margin exceeds that
+    rounding."""
+    vocab = 32768
+    g = torch.Generator().manual_seed(100 + rows)
+    w = (torch.randn(vocab, dim, generator=g) * 0.02).to(torch.bfloat16)
+    h = torch.randn(rows, 1, dim, generator=g).to(torch.bfloat16)
+    got = bridge.b200_vocab_argmax(h.cuda(), w.cuda())
+    want = torch.nn.functional.linear(h.cuda(), w.cuda()).argmax(-1)
+    torch.cuda.synchronize()
+    assert got.shape == (rows, 1) and got.dtype == torch.int64
+    exact = h.double().reshape(rows, dim) @ w.double().t()
+    top2 = exact.topk(2, dim=-1).values
+    ulp = 2.0 ** (torch.floor(torch.log2(top2[:, 0].abs())) - 7)  # bf16 spacing at the max
+    got_c = got.cpu().reshape(rows)
+    picked = exact.gather(1, got_c[:, None]).squeeze(1)
+    assert (picked >= top2[:, 0] - 2 * ulp).all()
+    clear = (top2[:, 0] - top2[:, 1]) > 2 * ulp
+    assert clear.sum() >= rows // 2
+    assert torch.equal(got_c[clear], exact.argmax(-1)[clear])
+    assert torch.equal(got_c[clear], want.cpu().reshape(rows)[clear])
+
+
+@pytest.mark.parametrize("rows", [1, 4, 16])
+def test_vocab_argmax_ties_go_to_the_lowest_index(rows):
+    vocab, dim = 32768, 768
+    g = torch.Generator().manual_seed(7)
+    w = (torch.randn(vocab, dim, generator=g) * 0.02).to(torch.bfloat16)
+    h = torch.randn(rows, 1, dim, generator=g).to(torch.bfloat16)
+    hot = (h[0, 0].float() * 0.5).to(torch.bfloat16)  # one row far above the rest, copied thrice
+    for v in (30001, 100, 5000):
+        w[v] = hot
+    h[:] = h[0]
+    got = bridge.b200_vocab_argmax(h.cuda(), w.cuda())
+    torch.cuda.synchronize()
+    assert got.cpu().reshape(rows).tolist() == [100] * rows
+
+
+def test_vocab_argmax_is_repeatable_and_graph_capturable():
+    vocab, dim = 32768, 768
+    g = torch.Generator().manual_seed(9)
+    w = (torch.randn(vocab, dim, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    h = torch.randn(4, 1, dim, generator=g).to(torch.bfloat16).cuda()
+    first = bridge.b200_vocab_argmax(h, w)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static = bridge.b200_vocab_argmax(h, w)
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(static, first)
