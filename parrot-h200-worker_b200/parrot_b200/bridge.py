@@ -345,6 +345,24 @@ def invalidate_packed_weights(module) -> None:
     module.__dict__.pop("_b200_pack", None)
 
 
+def check_config(cfg) -> None:
+    """The shapes the sm_100a kernels take, for a config selecting
+    ``moe_backend="b200"`` / ``depth_backend="b200"`` (the b200 counterpart of
+    the reference's per-backend checks, ``parrot/model.py:58-80``).  Raises
+    ``ValueError`` like them."""
+    if cfg.top_k != 2:
+        raise ValueError("b200 requires top_k=2")
+    if cfg.n_experts > 32 or cfg.n_experts < 2:
+        raise ValueError("b200 supports 2 to 32 routed experts")
+    if cfg.dim % 128 or cfg.dim > 1024:
+        raise ValueError("b200 requires dim divisible by 128 and at most 1024")
+    if cfg.expert_dim % 64 or cfg.shared_expert_dim % 64:
+        raise ValueError("b200 requires expert widths divisible by 64")
+    sources = 1 + (2 * cfg.n_layers + cfg.depth_block_size - 1) // cfg.depth_block_size
+    if cfg.residual == "attnres" and sources > 16:
+        raise ValueError("b200 depth mixing supports at most sixteen sources")
+
+
 def moe_dims(cfg, tokens: int, capacity: int = 0) -> _lib.MoeDims:
     return _lib.MoeDims(tokens, cfg.dim, cfg.n_experts, cfg.top_k, cfg.expert_dim,
                         cfg.shared_expert_dim, capacity)

@@ -85,16 +85,7 @@ class ModelConfig:
             raise ValueError("parrot_b200 implements moe_backend='b200' only")
         if self.depth_backend != "b200":
             raise ValueError("parrot_b200 implements depth_backend='b200' only")
-        if self.top_k != 2:
-            raise ValueError("b200 requires top_k=2")
-        if self.n_experts > 32 or self.n_experts < 2:
-            raise ValueError("b200 supports 2 to 32 routed experts")
-        if self.dim % 128 or self.dim > 1024:
-            raise ValueError("b200 requires dim divisible by 128 and at most 1024")
-        if self.expert_dim % 64 or self.shared_expert_dim % 64:
-            raise ValueError("b200 requires expert widths divisible by 64")
-        if self.residual == "attnres" and self.depth_sources > 16:
-            raise ValueError("b200 depth mixing supports at most sixteen sources")
+        bridge.check_config(self)
 
     @property
     def depth_sources(self) -> int:
