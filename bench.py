@@ -419,15 +419,15 @@ def time_decode(model, batches=(1, 8, 64), prompt: int = 128, new_tokens: int = 
 def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 20,
                   warmup: int = 3) -> dict:
     """BASELINE config 4 expert-parallel: the Zipf-skewed XL MoE layer with its
-    16384 tokens split evenly over the ranks and the experts round-robin over
-    them.  The product path exchanges rows and outputs through the other
-    ranks' memory (``ep.PeerExpertParallelMoE``, CUDA IPC over NVLink) with no
-    host synchronisation; it is captured once as a CUDA graph and replayed.
-    Per-phase times come from CUDA events between the phases of one eager
-    call; the NCCL all-to-all path with its host read of the split sizes
-    (``ep.ExpertParallelMoE``) is timed beside it.  Every number is the max
-    over ranks."""
-    from parrot_b200 import ModelConfig, ep
+    16384 tokens split evenly over the ranks.  The product path exchanges rows
+    and outputs through the other ranks' memory (``ep.PeerExpertParallelMoE``,
+    CUDA IPC over NVLink) with no host synchronisation; it is captured once as
+    a CUDA graph and replayed, with a load-balanced placement and with
+    round-robin placement.  Per-phase times come from CUDA events between the
+    phases of one eager call; the NCCL all-to-all path with its host read of
+    the split sizes (``ep.ExpertParallelMoE``, round-robin) is timed beside it.
+    Every number is the max over ranks."""
+    from parrot_b200 import ModelConfig, bridge, ep
     from parrot_b200.model import MoE
     from parrot_b200.workloads import (make_hidden_states, make_moe_layer_weights,
                                        tune_zipf_router_bias)
@@ -459,56 +459,80 @@ def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.tolist()
 
-    shape = ep.EpShape(world, per, cfg.dim, cfg.n_experts, cfg.expert_dim)
-    peers = ep.PeerSet.connect(shape)
     with torch.inference_mode():
-        layer = ep.PeerExpertParallelMoE(moe, peers)
-        for _ in range(warmup):
+        # routing counts of the whole batch (identical on every rank): the
+        # load-balanced placement replicates the experts above 1 / world of them
+        _, _, util = bridge.b200_moe(moe, x.to("cuda", torch.bfloat16), True)
+        counts = (util.float() * 2 * total).round().int().tolist()
+    placements = {"balanced": ep.Placement.balanced(counts, world),
+                  "round_robin": ep.Placement.round_robin(world, cfg.n_experts)}
+    res = {}
+    for name, placement in placements.items():
+        shape = ep.EpShape(world, per, cfg.dim, cfg.n_experts, cfg.expert_dim,
+                           placement=placement)
+        peers = ep.PeerSet.connect(shape)
+        with torch.inference_mode():
+            layer = ep.PeerExpertParallelMoE(moe, peers)
+            for _ in range(warmup):
+                layer(xs)
+            eager_us = timed(lambda: layer(xs), iters)
+            # one eager call with an event after every phase; the GPU first
+            # spins (~1 ms) while the host enqueues the whole layer, so the
+            # events time device work, not launch gaps
+            dist.barrier()
+            torch.cuda.synchronize()
+            layer.marks = []
+            torch.cuda._sleep(2_000_000)
             layer(xs)
-        eager_us = timed(lambda: layer(xs), iters)
-        # one eager call with an event after every phase
+            torch.cuda.synchronize()
+            marks, layer.marks = layer.marks, None
+            names = [n for n, _ in marks[1:]]
+            phase = [1000 * marks[i][1].elapsed_time(marks[i + 1][1])
+                     for i in range(len(marks) - 1)]
+            received = peers.received_rows()
+            graph = torch.cuda.CUDAGraph()
+            dist.barrier()
+            with torch.cuda.graph(graph):
+                layer(xs)
+            for _ in range(warmup):
+                graph.replay()
+            graph_us = timed(graph.replay, iters)
+            status = peers.status()
+            del graph
         dist.barrier()
-        torch.cuda.synchronize()
-        layer.marks = []
-        layer(xs)
-        torch.cuda.synchronize()
-        marks, layer.marks = layer.marks, None
-        names = [n for n, _ in marks[1:]]
-        phase = [1000 * marks[i][1].elapsed_time(marks[i + 1][1]) for i in range(len(marks) - 1)]
-        received = peers.received_rows()
-        graph = torch.cuda.CUDAGraph()
-        dist.barrier()
-        with torch.cuda.graph(graph):
-            layer(xs)
-        for _ in range(warmup):
-            graph.replay()
-        graph_us = timed(graph.replay, iters)
-        status = peers.status()
-        del graph
-        nccl = ep.ExpertParallelMoE(ep.B200EpOps(moe, rank, world), ep.TorchComm(), cfg.n_experts)
+        peers.close()
+        graph_us, eager_us, *phase = max_all([graph_us, eager_us] + phase)
+        recv = torch.tensor([received, status[0]], device="cuda", dtype=torch.int64)
+        recv_all = [torch.zeros_like(recv) for _ in range(world)]
+        dist.all_gather(recv_all, recv)
+        if any(int(r[1].item()) for r in recv_all):
+            raise RuntimeError(f"expert-parallel status word set on some rank: {status}")
+        res[name] = {"us": graph_us, "eager_us": eager_us, "phase_us": dict(zip(names, phase)),
+                     "received_rows_per_rank": [int(r[0].item()) for r in recv_all],
+                     "slots": [list(q) for q in placement.slots],
+                     "replicated": sorted(placement.replicated)}
+    with torch.inference_mode():
+        nccl = ep.ExpertParallelMoE(ep.B200EpOps(moe, rank, world), ep.TorchComm(),
+                                    cfg.n_experts)
         for _ in range(warmup):
             nccl(xs)
-        nccl_us = timed(lambda: nccl(xs), iters)
-    dist.barrier()
-    peers.close()
-    graph_us, eager_us, nccl_us, *phase = max_all([graph_us, eager_us, nccl_us] + phase)
-    recv = torch.tensor([received, status[0]], device="cuda", dtype=torch.int64)
-    recv_all = [torch.zeros_like(recv) for _ in range(world)]
-    dist.all_gather(recv_all, recv)
-    if any(int(r[1].item()) for r in recv_all):
-        raise RuntimeError(f"expert-parallel status word set on some rank: {status}")
+        nccl_us = max_all([timed(lambda: nccl(xs), iters)])[0]
     flops = 2 * (2 * total * cfg.dim * 3 * cfg.expert_dim + total * cfg.dim * 3 *
                  cfg.shared_expert_dim + total * cfg.dim * cfg.n_experts)
-    return {"us": graph_us, "tokens_total": per * world,
-            "tokens_per_s": per * world / (graph_us * 1e-6),
-            "tflops_all_ranks": flops / (graph_us * 1e-6) / 1e12,
-            "ranks": world, "placement": "round-robin (expert e on rank e % ranks)",
+    best = res["balanced"]
+    return {"us": best["us"], "tokens_total": per * world,
+            "tokens_per_s": per * world / (best["us"] * 1e-6),
+            "tflops_all_ranks": flops / (best["us"] * 1e-6) / 1e12,
+            "ranks": world,
+            "placement": "load-balanced from the batch's routing counts: experts above 1/ranks "
+                         "of the rows replicated (each source computes its own rows of them), "
+                         "the rest largest first onto the least-loaded rank",
             "exchange": "peer memory (CUDA IPC over NVLink): stores + epoch flags, no host read",
-            "received_rows_per_rank": [int(r[0].item()) for r in recv_all],
-            "eager_us": eager_us,
-            "phase_us_eager": dict(zip(names, phase)),
+            "balanced": best, "round_robin": res["round_robin"],
             "nccl_all_to_all_host_read_us": nccl_us,
-            "timing": "CUDA-graph replay of the whole layer, CUDA events, max over ranks"}
+            "timing": "CUDA-graph replay of the whole layer, CUDA events, max over ranks; "
+                      "phase_us: one eager call behind a GPU sleep, events between phases, "
+                      "max over ranks per phase"}
 
 
 def run_b200(args):

@@ -443,13 +443,21 @@ int parrot_argmax_rows_bf16(long long* out, const void* logits, int rows, int co
 #define PARROT_EP_MAX_RANKS 8
 
 typedef struct parrot_ep_dims {
-  int ranks;        /* G, 1..8, divides n_experts */
+  int ranks;        /* G, 1..8 */
   int rank;         /* this process's rank */
   int max_tokens;   /* most tokens any rank passes to one call: sizes the regions */
   int dim;          /* d, as parrot_moe_dims */
   int n_experts;    /* E */
   int expert_dim;   /* H */
   unsigned long long wait_ns;  /* limit of each flag wait; 0 selects 2 s */
+  /* Placement.  slots = 0: round-robin, expert e on rank e % G as local slot
+   * e / G (G must divide E).  Otherwise this rank holds `slots` experts
+   * (ranks * slots <= 64) and plan[q][j] is the global expert of rank q's
+   * slot j whose rows THIS rank sends there, or -1: every expert must appear
+   * exactly once in this rank's plan.  An expert that every rank holds may be
+   * planned to this rank itself (each source computes its own rows of it). */
+  int slots;
+  signed char plan[PARROT_EP_MAX_RANKS][32];
 } parrot_ep_dims;
 
 /* Byte offsets inside one EP buffer. */
@@ -488,20 +496,30 @@ int parrot_ipc_export(const void* ptr, void* handle, unsigned long long* offset)
 int parrot_ipc_import(const void* handle, unsigned long long offset, void** ptr, void** base);
 int parrot_ipc_close(void* base);
 
-/* Stores this rank's dispatched rows (workspace of parrot_moe_ep_dispatch_bf16,
- * dims->tokens <= ep->max_tokens) into each destination's receive region for
- * this source, with the per-local-expert counts and the rows' base in this
- * rank's dispatch order, then raises this rank's arrival flag there. */
+/* Router + grouping for the peer exchange: parrot_moe_ep_dispatch_bf16 with
+ * the rows packed in the order of ep's plan (destination rank major, then
+ * the destination's slot order, then ascending token). */
+int parrot_moe_ep_dispatch_planned_bf16(const parrot_moe_dims* dims,
+                                        const parrot_moe_weights* weights, const void* x,
+                                        const parrot_moe_outputs* outputs,
+                                        const parrot_ep_dims* ep, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
+/* Stores this rank's dispatched rows (workspace of
+ * parrot_moe_ep_dispatch_planned_bf16 with the same ep, dims->tokens <=
+ * ep->max_tokens) into each destination's receive region for this source,
+ * with the per-slot counts and the rows' base in this rank's dispatch order,
+ * then raises this rank's arrival flag there. */
 int parrot_moe_ep_send_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* ep,
                             const parrot_ep_peers* peers, const void* workspace,
                             size_t workspace_bytes, void* stream);
 
 /* Waits for every source's arrival flag, then writes the segment table of the
- * received rows (one segment per (source, local expert)) into the buffer. */
+ * received rows (one segment per (source, local slot)) into the buffer. */
 int parrot_moe_ep_receive(const parrot_ep_dims* ep, void* buffer, void* stream);
 
-/* The local experts (packed gate_up / down of this rank's n_experts / G
- * experts, parrot_pack_gate_up_bf16 / parrot_pack_down_bf16 layout) on the
+/* The local experts (packed gate_up / down of this rank's slots, in slot
+ * order, parrot_pack_gate_up_bf16 / parrot_pack_down_bf16 layout) on the
  * received rows, by the segment table; outputs into the buffer's y. */
 int parrot_moe_ep_experts_bf16(const parrot_ep_dims* ep, void* buffer, const void* gate_up,
                                const void* down, void* stream);

@@ -227,9 +227,11 @@ int prepare(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void
   return PARROT_OK;
 }
 
+// ep_order (expert parallelism): the packing order of the experts' rows,
+// destination rank major; nullptr: expert id order.
 int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
               const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L, cudaStream_t s,
-              int ep_ranks = 1) {
+              const signed char* ep_order = nullptr) {
   const int T = dims->tokens, E = dims->n_experts;
   parrot::RouteArgs ra{};
   ra.bias = w->router_bias;
@@ -244,10 +246,11 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ra.n_experts = E;
   ra.status = at<int>(ws, L.status);
   CUtensorMap mx, mw;
-  if (!tensor_map(&mx, x, T, dims->dim, parrot::route_tile(T)) ||
-      !tensor_map(&mw, w->router, E, dims->dim, parrot::route_experts_padded(E)))
+  if (parrot::route_tile(T) != parrot::kRouteSmallTile &&
+      (!tensor_map(&mx, x, T, dims->dim, parrot::route_tile(T)) ||
+       !tensor_map(&mw, w->router, E, dims->dim, parrot::route_experts_padded(E))))
     return fail(PARROT_ECUDA, "route: cuTensorMapEncodeTiled failed%s");
-  if (parrot::launch_route(ra, &mx, &mw, s))
+  if (parrot::launch_route(ra, x, w->router, &mx, &mw, s))
     return fail(PARROT_ECUDA, "route: unsupported dim or shared-memory setup failed%s");
   int rc = check_launch("route_kernel");
   if (rc) return rc;
@@ -268,7 +271,9 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ga.dim = dims->dim;
   ga.n_experts = E;
   ga.capacity = L.capacity;
-  ga.ep_ranks = ep_ranks;
+  ga.ep_packed = ep_order != nullptr;
+  if (ep_order != nullptr)
+    for (int q = 0; q < E; ++q) ga.ep_order[q] = ep_order[q];
   const int ng = parrot::group_blocks(T);
   const int want = (2 * sm_count() + ng - 1) / ng;  // about two blocks per SM
   int split = 1;
@@ -451,8 +456,12 @@ int ep_layout_of(const parrot_ep_dims* e, parrot_ep_layout* L) {
   if (e == nullptr || L == nullptr) return fail(PARROT_EINVAL, "ep: null dims or layout%s");
   if (e->ranks < 1 || e->ranks > parrot::kEpMaxRanks || e->rank < 0 || e->rank >= e->ranks)
     return fail(PARROT_EINVAL, "ep: 1 <= ranks <= 8 and 0 <= rank < ranks required%s");
-  if (e->n_experts < 2 || e->n_experts > parrot::kMaxExperts || e->n_experts % e->ranks)
-    return fail(PARROT_EINVAL, "ep: 2 <= n_experts <= 32, divisible by ranks, required%s");
+  if (e->n_experts < 2 || e->n_experts > parrot::kMaxExperts)
+    return fail(PARROT_EINVAL, "ep: 2 <= n_experts <= 32 required%s");
+  if (e->slots == 0 && e->n_experts % e->ranks)
+    return fail(PARROT_EINVAL, "ep: round-robin placement needs ranks dividing n_experts%s");
+  if (e->slots < 0 || e->slots > parrot::kMaxExperts || e->ranks * e->slots > 2 * parrot::kMaxExperts)
+    return fail(PARROT_EINVAL, "ep: 0 <= slots <= 32 and ranks * slots <= 64 required%s");
   if (e->dim <= 0 || e->dim % 128 || e->dim > 1024 || e->expert_dim <= 0 || e->expert_dim % 64)
     return fail(PARROT_EINVAL, "ep: dim % 128 == 0 (<= 1024), expert_dim % 64 == 0 required%s");
   if (e->max_tokens < 1 || (long long)e->ranks * 2 * e->max_tokens > (1ll << 30))
@@ -473,9 +482,9 @@ int ep_layout_of(const parrot_ep_dims* e, parrot_ep_layout* L) {
   L->epoch = take(4);
   L->counters = take(2 * 4);
   L->status = take(16);
-  L->seg_rows = take(E * 4);
-  L->seg_base = take(E * 4);
-  L->seg_expert = take(E * 4);
+  L->seg_rows = take(2 * parrot::kMaxExperts * 4);
+  L->seg_base = take(2 * parrot::kMaxExperts * 4);
+  L->seg_expert = take(2 * parrot::kMaxExperts * 4);
   L->back_n = take(parrot::kEpMaxRanks * 4);
   L->back_base = take(parrot::kEpMaxRanks * 4);
   L->hidden = take(G * R * e->expert_dim * 2);
@@ -483,6 +492,42 @@ int ep_layout_of(const parrot_ep_dims* e, parrot_ep_layout* L) {
   L->total = off;
   L->region_rows = (int)R;
   return PARROT_OK;
+}
+
+int ep_slots(const parrot_ep_dims* e) { return e->slots ? e->slots : e->n_experts / e->ranks; }
+
+// This rank's send plan (round-robin when e->slots == 0); every expert must
+// appear exactly once.
+int ep_plan(const parrot_ep_dims* e, signed char plan[parrot::kEpMaxRanks][parrot::kMaxExperts]) {
+  const int G = e->ranks, E = e->n_experts;
+  for (int q = 0; q < parrot::kEpMaxRanks; ++q)
+    for (int j = 0; j < parrot::kMaxExperts; ++j) {
+      int x = -1;
+      if (q < G) {
+        if (e->slots == 0) x = j < E / G ? q + j * G : -1;
+        else x = e->plan[q][j];
+      }
+      plan[q][j] = (signed char)x;
+    }
+  int seen[parrot::kMaxExperts] = {};
+  for (int q = 0; q < G; ++q)
+    for (int j = 0; j < parrot::kMaxExperts; ++j) {
+      const int x = plan[q][j];
+      if (x < -1 || x >= E) return fail(PARROT_EINVAL, "ep: plan entry out of range%s");
+      if (x >= 0) ++seen[x];
+    }
+  for (int x = 0; x < E; ++x)
+    if (seen[x] != 1) return fail(PARROT_EINVAL, "ep: every expert must appear once in the plan%s");
+  return PARROT_OK;
+}
+
+// The packing order of the dispatched rows: destination major, slot order.
+void ep_order(const signed char plan[parrot::kEpMaxRanks][parrot::kMaxExperts], int G,
+              signed char* order) {
+  int n = 0;
+  for (int q = 0; q < G; ++q)
+    for (int j = 0; j < parrot::kMaxExperts; ++j)
+      if (plan[q][j] >= 0) order[n++] = plan[q][j];
 }
 
 unsigned long long ep_wait_ns(const parrot_ep_dims* e) {
@@ -1045,8 +1090,34 @@ int parrot_moe_ep_dispatch_bf16(const parrot_moe_dims* dims, const parrot_moe_we
   if (outputs == nullptr) return fail(PARROT_EINVAL, "ep_dispatch: outputs is NULL%s");
   if (dims->tokens == 0) return PARROT_OK;
   if (x == nullptr || !aligned16(x)) return fail(PARROT_EINVAL, "x must be 16-byte aligned%s");
+  signed char order[parrot::kMaxExperts];
+  const int G = ep_ranks, El = dims->n_experts / G;
+  for (int q = 0; q < dims->n_experts; ++q) order[q] = (signed char)((q % El) * G + q / El);
   return run_route(dims, weights, x, outputs, workspace, L, static_cast<cudaStream_t>(stream),
-                   ep_ranks);
+                   order);
+}
+
+int parrot_moe_ep_dispatch_planned_bf16(const parrot_moe_dims* dims,
+                                        const parrot_moe_weights* weights, const void* x,
+                                        const parrot_moe_outputs* outputs,
+                                        const parrot_ep_dims* ep, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  parrot_ep_layout P;
+  int rc = layout_of(dims, &L);
+  if (rc || (rc = ep_layout_of(ep, &P))) return rc;
+  if (dims->capacity != -1 || dims->n_experts != ep->n_experts || dims->dim != ep->dim)
+    return fail(PARROT_EINVAL, "ep_dispatch: dims must be packed (capacity -1) and match ep%s");
+  signed char plan[parrot::kEpMaxRanks][parrot::kMaxExperts];
+  if ((rc = ep_plan(ep, plan))) return rc;
+  if ((rc = check_router(weights)) || (rc = ws_ok(workspace, workspace_bytes, L))) return rc;
+  if (outputs == nullptr) return fail(PARROT_EINVAL, "ep_dispatch: outputs is NULL%s");
+  if (dims->tokens == 0) return PARROT_OK;
+  if (x == nullptr || !aligned16(x)) return fail(PARROT_EINVAL, "x must be 16-byte aligned%s");
+  signed char order[parrot::kMaxExperts];
+  ep_order(plan, ep->ranks, order);
+  return run_route(dims, weights, x, outputs, workspace, L, static_cast<cudaStream_t>(stream),
+                   order);
 }
 
 int parrot_moe_shared_ffn_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
@@ -1213,11 +1284,11 @@ int parrot_moe_ep_send_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* e
   if (dims->tokens > 0 && (rc = ws_ok(workspace, workspace_bytes, L))) return rc;
   char* own = static_cast<char*>(peers->buffers[ep->rank]);
   parrot::EpSendArgs a{};
+  if ((rc = ep_plan(ep, a.plan))) return rc;
   if (dims->tokens > 0) {
     void* ws = const_cast<void*>(workspace);
     a.rows = at<__nv_bfloat16>(ws, L.grouped);
     a.counts = at<int>(ws, L.counts);
-    a.seg_base = at<int>(ws, L.seg_base);
   }
   a.tokens = dims->tokens;
   a.dim = ep->dim;
@@ -1247,7 +1318,7 @@ int parrot_moe_ep_receive(const parrot_ep_dims* ep, void* buffer, void* stream) 
   a.meta = reinterpret_cast<const int*>(b + P.meta);
   a.epoch = reinterpret_cast<const unsigned*>(b + P.epoch);
   a.ranks = ep->ranks;
-  a.n_experts = ep->n_experts;
+  a.slots = ep_slots(ep);
   a.max_tokens = ep->max_tokens;
   a.seg_rows = reinterpret_cast<int*>(b + P.seg_rows);
   a.seg_base = reinterpret_cast<int*>(b + P.seg_base);
@@ -1269,8 +1340,8 @@ int parrot_moe_ep_experts_bf16(const parrot_ep_dims* ep, void* buffer, const voi
       !aligned16(down))
     return fail(PARROT_EINVAL, "ep_experts: buffer and 16-byte aligned weights required%s");
   char* b = static_cast<char*>(buffer);
-  const int El = ep->n_experts / ep->ranks;
-  return run_ffn(ep->ranks * P.region_rows, ep->dim, ep->expert_dim, El, ep->n_experts,
+  const int slots = ep_slots(ep);
+  return run_ffn(ep->ranks * P.region_rows, ep->dim, ep->expert_dim, slots, ep->ranks * slots,
                  reinterpret_cast<const int*>(b + P.seg_rows),
                  reinterpret_cast<const int*>(b + P.seg_base),
                  reinterpret_cast<const int*>(b + P.seg_expert), gate_up, down, b + P.recv_rows,

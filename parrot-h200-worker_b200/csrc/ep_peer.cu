@@ -2,7 +2,10 @@
 //
 // The reference runs every expert of a layer on one device
 // (parrot/model.py:521-551); here G ranks, one process per GPU, each hold
-// their own tokens and n_experts / G experts (expert e on rank e % G).  Every
+// their own tokens and a set of expert slots.  Each source's plan names the
+// rank that computes its rows of each expert: one owner per expert, except
+// that an expert every rank holds (a replicated, heavily routed one) is
+// computed by each source on its own rows.  Every
 // rank owns one "EP buffer" that the other ranks map into their address space
 // (CUDA IPC).  One MoE call moves data only by stores into those buffers:
 //
@@ -13,7 +16,7 @@
 //            flag per destination;
 //   receive  waits for every source's arrival flag and turns the counts into
 //            the expert GEMM's segment table (one segment per (source, local
-//            expert)) on the device;
+//            expert slot)) on the device;
 //   return   the expert outputs are stored back into each source's return
 //            region at the offsets the source sent, then one flag per source;
 //   combine  (route.cu) waits for every expert rank's return flag, then adds
@@ -39,10 +42,34 @@ namespace parrot {
 
 namespace {
 
-// Copies one row of nvec 16-byte vectors from src to dst (one warp).
-__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src,
-                                         int nvec, int lane) {
-  for (int c = lane; c < nvec; c += 32) dst[c] = __ldcg(src + c);
+// Rows a warp moves per batch: every load of the batch is issued before its
+// stores, so a lane keeps up to kRowBatch * 4 16-byte loads in flight.
+constexpr int kRowBatch = 4;
+
+// One warp copies rows [first, first + n), n <= kRowBatch, of nvec 16-byte
+// vectors each (nvec <= 128): row k goes from src(k) to dst(k).
+template <typename Src, typename Dst>
+__device__ __forceinline__ void copy_rows(int first, int n, int nvec, int lane, Src src, Dst dst) {
+  uint4 v[kRowBatch][4];
+#pragma unroll
+  for (int k = 0; k < kRowBatch; ++k) {
+    if (k < n) {
+      const uint4* s = src(first + k);
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (lane + 32 * c < nvec) v[k][c] = __ldcg(s + lane + 32 * c);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kRowBatch; ++k) {
+    if (k < n) {
+      uint4* d = dst(first + k);
+      if (d == nullptr) continue;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (lane + 32 * c < nvec) d[lane + 32 * c] = v[k][c];
+    }
+  }
 }
 
 // Last-CTA election after every CTA's stores: each CTA fences its stores at
@@ -66,40 +93,53 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpSendArgs a) {
   __shared__ int n_s[kEpMaxRanks], base_s[kEpMaxRanks];
   griddep_wait();
   griddep_launch();
-  const int G = a.ranks, El = a.n_experts / G;
+  const int G = a.ranks;
   if (threadIdx.x < G) {
     const int q = threadIdx.x;
-    int n = 0, base = 0;
-    if (a.tokens > 0) {
-      for (int j = 0; j < El; ++j) n += a.counts[q + j * G];
-      base = a.seg_base[q];  // expert q is rank q's first local expert
-    }
+    int n = 0;
+    if (a.tokens > 0)
+      for (int j = 0; j < kMaxExperts; ++j)
+        if (a.plan[q][j] >= 0) n += a.counts[a.plan[q][j]];
     n_s[q] = n;
-    base_s[q] = base;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // the packed rows are destination-major from row 0
+    int at = 0;
+    for (int q = 0; q < G; ++q) {
+      base_s[q] = at;
+      at += n_s[q];
+    }
   }
   __syncthreads();
   const int nvec = a.dim >> 3;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int total = 2 * a.tokens;
   const size_t region = (size_t)2 * a.max_tokens;
-  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < total; i += gridDim.x * warps) {
-    int q = 0;
-    while (q + 1 < G && i >= base_s[q] + n_s[q]) ++q;
-    const int k = i - base_s[q];
-    if (k < 0 || k >= n_s[q] || k >= (int)region) {
-      if (lane == 0) report_status(a.status, kStatusBadIndex, 20, i);
-      continue;
-    }
-    uint4* dst = reinterpret_cast<uint4*>(a.peers[q] + a.off_recv) +
+  const uint4* rows = reinterpret_cast<const uint4*>(a.rows);
+  for (int i = (blockIdx.x * warps + (threadIdx.x >> 5)) * kRowBatch; i < total;
+       i += gridDim.x * warps * kRowBatch) {
+    copy_rows(
+        i, min(kRowBatch, total - i), nvec, lane,
+        [&](int r) { return rows + (size_t)r * nvec; },
+        [&](int r) -> uint4* {
+          int q = 0;
+          while (q + 1 < G && r >= base_s[q] + n_s[q]) ++q;
+          const int k = r - base_s[q];
+          if (k < 0 || k >= n_s[q] || k >= (int)region) {
+            if (lane == 0) report_status(a.status, kStatusBadIndex, 20, r);
+            return nullptr;
+          }
+          return reinterpret_cast<uint4*>(a.peers[q] + a.off_recv) +
                  ((size_t)a.rank * region + k) * nvec;
-    copy_row(dst, reinterpret_cast<const uint4*>(a.rows) + (size_t)i * nvec, nvec, lane);
+        });
   }
   if (!last_cta(a.counter)) return;
   const unsigned e = *reinterpret_cast<volatile unsigned*>(a.epoch) + 1;
   if (threadIdx.x < G) {
     const int q = threadIdx.x;
     int* meta = reinterpret_cast<int*>(a.peers[q] + a.off_meta) + a.rank * kEpMetaStride;
-    for (int j = 0; j < El; ++j) meta[j] = a.tokens > 0 ? a.counts[q + j * G] : 0;
+    for (int j = 0; j < kMaxExperts; ++j)
+      meta[j] = (a.tokens > 0 && a.plan[q][j] >= 0) ? a.counts[a.plan[q][j]] : 0;
     meta[kEpMetaStride - 1] = base_s[q];
     __threadfence_system();
     st_release_sys(reinterpret_cast<unsigned*>(a.peers[q] + a.off_flags_in) + a.rank, e);
@@ -112,7 +152,7 @@ __global__ void __launch_bounds__(32) ep_receive_kernel(EpReceiveArgs a) {
   __shared__ int n_s[kEpMaxRanks][kMaxExperts];
   griddep_wait();
   griddep_launch();
-  const int G = a.ranks, El = a.n_experts / G;
+  const int G = a.ranks, El = a.slots;
   const unsigned e = *reinterpret_cast<const volatile unsigned*>(a.epoch);
   const int region = 2 * a.max_tokens;
   if (threadIdx.x < G) {
@@ -174,13 +214,26 @@ __global__ void __launch_bounds__(256) ep_return_kernel(EpReturnArgs a) {
   const int nvec = a.dim >> 3;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const size_t region = (size_t)2 * a.max_tokens;
-  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < start_s[G]; i += gridDim.x * warps) {
+  const uint4* y = reinterpret_cast<const uint4*>(a.y);
+  const int total = start_s[G];
+  auto source_of = [&](int r) {
     int s = 0;
-    while (s + 1 < G && i >= start_s[s + 1]) ++s;
-    const int k = i - start_s[s];
-    const uint4* src = reinterpret_cast<const uint4*>(a.y) + ((size_t)s * region + k) * nvec;
-    uint4* dst = reinterpret_cast<uint4*>(a.peers[s] + a.off_back) + (size_t)(base_s[s] + k) * nvec;
-    copy_row(dst, src, nvec, lane);
+    while (s + 1 < G && r >= start_s[s + 1]) ++s;
+    return s;
+  };
+  for (int i = (blockIdx.x * warps + (threadIdx.x >> 5)) * kRowBatch; i < total;
+       i += gridDim.x * warps * kRowBatch) {
+    copy_rows(
+        i, min(kRowBatch, total - i), nvec, lane,
+        [&](int r) {
+          const int s = source_of(r);
+          return y + ((size_t)s * region + (r - start_s[s])) * nvec;
+        },
+        [&](int r) -> uint4* {
+          const int s = source_of(r);
+          return reinterpret_cast<uint4*>(a.peers[s] + a.off_back) +
+                 (size_t)(base_s[s] + r - start_s[s]) * nvec;
+        });
   }
   if (!last_cta(a.counter)) return;
   const unsigned e = *reinterpret_cast<const volatile unsigned*>(a.epoch);
@@ -192,7 +245,7 @@ __global__ void __launch_bounds__(256) ep_return_kernel(EpReturnArgs a) {
 
 int launch_ep_send(const EpSendArgs& a, int sms, cudaStream_t stream) {
   const int rows = 2 * a.tokens;
-  int grid = (rows + 7) / 8;
+  int grid = (rows + 8 * kRowBatch - 1) / (8 * kRowBatch);
   if (grid > 2 * sms) grid = 2 * sms;
   if (grid < 1) grid = 1;
   return launch_pdl(ep_send_kernel, dim3(grid), dim3(256), 0, stream, a) == cudaSuccess ? 0 : -1;

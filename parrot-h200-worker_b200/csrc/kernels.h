@@ -43,7 +43,8 @@ struct DepthMixArgs {
 // and statistics that the GEMMs and the caller read.
 struct MoeTables {
   int* chunk_hist;     // [chunks, E]  assignments per expert in each 32-token chunk
-  int* tile_hist;      // [tiles, E]   the same per 128-token router tile
+                       //              (written by the 128-token tensor-core router)
+  int* tile_hist;      // [tiles, E]   the same per router tile (8 or 128 tokens)
   float* tile_probsum;  // [tiles, E]  sum of router probabilities per expert
   int* counts;         // [E]
   int* seg_rows;       // [2E] rows in capacity segment e, overflow segment e
@@ -76,10 +77,12 @@ struct GroupArgs {
   int* counts_out;            // [E] or null
   float* stats_out;           // [E + 1] or null
   int tokens, dim, n_experts, capacity;
-  // overflow segments are laid out destination-major for ep_ranks expert-
-  // parallel ranks: expert e lives on rank e % ep_ranks as local expert
-  // e / ep_ranks, so rank r's rows form one contiguous block (1: id order)
-  int ep_ranks;
+  // ep_packed (expert parallelism): the overflow segments are packed in the
+  // order ep_order lists the experts (destination rank major, then the
+  // destination's slot order), so each destination's rows form one
+  // contiguous block; 0: expert id order
+  int ep_packed;
+  signed char ep_order[kMaxExperts];
   int copy_split;
   int* status;
 };
@@ -139,7 +142,9 @@ constexpr int kEpMetaStride = kMaxExperts + 1;  // per source: counts [El], then
 struct EpSendArgs {
   const __nv_bfloat16* rows;  // [2T, d] dispatched rows, packed destination-major
   const int* counts;          // [E] rows per global expert
-  const int* seg_base;        // [E] first packed row of each expert
+  // plan[q][j]: the global expert of rank q's slot j whose rows this rank
+  // sends there, -1 for none; the packing order of `rows` follows it
+  signed char plan[kEpMaxRanks][kMaxExperts];
   int tokens, dim, n_experts, ranks, rank, max_tokens;
   char* peers[kEpMaxRanks];   // every rank's EP buffer, mapped in this process
   size_t off_recv, off_meta, off_flags_in;
@@ -152,8 +157,8 @@ struct EpReceiveArgs {
   const unsigned* flags_in;   // [G] arrival flag of each source (own buffer)
   const int* meta;            // [G, kEpMetaStride] counts + row base of each source
   const unsigned* epoch;
-  int ranks, n_experts, max_tokens;
-  int* seg_rows;              // [E] one segment per (source, local expert)
+  int ranks, slots, max_tokens;  // slots: this rank's local experts
+  int* seg_rows;              // [ranks * slots] one segment per (source, slot)
   int* seg_base;
   int* seg_expert;
   int* back_n;                // [G] rows received from each source
@@ -272,8 +277,10 @@ int launch_rope(__nv_bfloat16* x, const __nv_bfloat16* cos_t, const __nv_bfloat1
                 const int* start_dev, int max_positions, int* status, cudaStream_t stream);
 // x_map: [T, d] bf16, box 128 rows x 64; w_map: [E, d] bf16, box
 // route_experts_padded(E) rows x 64 (rows past E read as zero).
-int launch_route(const RouteArgs& args, const CUtensorMap* x_map, const CUtensorMap* w_map,
-                 cudaStream_t stream);
+// Up to 4096 tokens the router reads x [T, d] and the router weight [E, d]
+// directly (x_map / w_map unused); above, through the tensor maps.
+int launch_route(const RouteArgs& args, const void* x, const void* router_w,
+                 const CUtensorMap* x_map, const CUtensorMap* w_map, cudaStream_t stream);
 int launch_group(const GroupArgs& args, cudaStream_t stream);
 int launch_combine(const CombineArgs& args, cudaStream_t stream);
 int launch_ep_combine(const EpCombineArgs& args, cudaStream_t stream);
@@ -305,7 +312,12 @@ int launch_silu_bf16(const uint16_t* x, uint16_t* y, int n, cudaStream_t stream)
 // load of x), 128 (the MMA's M) once it is large (fewer histogram rows for
 // the grouping kernel to sum).  The MMA always has M = 128; a 32-token tile
 // leaves the other accumulator lanes unused.
-__host__ __device__ inline int route_tile(int tokens) { return tokens <= 4096 ? 32 : 128; }
+// Tokens per router CTA: 8 up to 4096 tokens (CUDA-core router), else 128
+// (tensor-core router).
+constexpr int kRouteSmallTile = 8;
+__host__ __device__ inline int route_tile(int tokens) {
+  return tokens <= 4096 ? kRouteSmallTile : 128;
+}
 __host__ __device__ inline int route_blocks(int tokens) {
   const int r = route_tile(tokens);
   return (tokens + r - 1) / r;

@@ -1,16 +1,21 @@
 // Router (N1) and deterministic capacity grouping (N2).
 //
-// route_kernel:  one CTA per 32 tokens (128 for large batches).  The router
-//                logits are a skinny GEMM [128 x d] x [d x E] (a 32-token
-//                tile fills the first 32 rows): TMA streams 64-column slabs of the token
-//                tile and of the router weight through a shared-memory ring,
-//                one thread issues tcgen05.mma (M = 128 tokens, N = E rounded
-//                up to 16/32, fp32 accumulator in TMEM).  Each of the 128
-//                threads then reads its token's E logits from TMEM with one
-//                tcgen05.ld and does the softmax, top-2 and renormalisation
-//                in registers (no cross-lane reductions).  Each warp (32
-//                tokens) records its expert histogram; the CTA records its
-//                tile histogram and probability sums.
+// route_small_kernel (up to 4096 tokens): one CTA per 8 tokens on CUDA
+//                cores; the router weight is staged in shared memory before
+//                the grid-dependency wait, each warp folds its tokens' E dots
+//                with one warp_reduce_many, softmax and top-2 are shuffle
+//                reductions (see the kernel).
+// route_kernel (above 4096 tokens): one CTA per 128 tokens.  The router
+//                logits are a skinny GEMM [128 x d] x [d x E]: TMA streams
+//                64-column slabs of the token tile and of the router weight
+//                through a shared-memory ring, one thread issues tcgen05.mma
+//                (M = 128 tokens, N = E rounded up to 16/32, fp32 accumulator
+//                in TMEM).  Each of the 128 threads then reads its token's E
+//                logits from TMEM with one tcgen05.ld and does the softmax,
+//                top-2 and renormalisation in registers (no cross-lane
+//                reductions).  Each warp (32 tokens) records its expert
+//                histogram; the CTA records its tile histogram and
+//                probability sums.
 // group_kernel:  every block derives its exclusive per-expert prefix from the
 //                tile and chunk histograms (no serial pass, no spinning),
 //                ranks each assignment inside its block with warp match -> a
@@ -32,15 +37,6 @@ constexpr int kRouteM = 128;                   // MMA rows (tokens of a tile, pa
 constexpr int kRouteXTile = kRouteM * 64 * 2;  // 16 KB slab: 128 token rows x 64 columns
 constexpr int kRouteMaxStages = 12;
 
-// As many slab slots as shared memory holds (12 with E <= 16: a whole
-// d = 768 row block in flight at once, no slot reused); a ring beyond that.
-template <int NP>
-constexpr int route_stages() {
-  return (225 * 1024) / (kRouteXTile + NP * 128) < kRouteMaxStages
-             ? (225 * 1024) / (kRouteXTile + NP * 128)
-             : kRouteMaxStages;
-}
-
 struct __align__(8) RouteSmem {
   uint64_t full[kRouteMaxStages];
   uint64_t empty[kRouteMaxStages];
@@ -51,7 +47,7 @@ struct __align__(8) RouteSmem {
   float psum[4][kMaxExperts];
 };
 
-// 128-token tiles (large batches) stream through a 4-slot ring instead: about
+// The 128-token tiles stream through a 4-slot ring: about
 // 75 KB per CTA, so three CTAs share an SM and one's loads overlap another's
 // MMAs and epilogue (a whole row block per CTA left one CTA per SM, idle
 // between its load and its epilogue).
@@ -281,6 +277,172 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
   }
 }
 
+// ---------------------------------------------------------------------------
+// Router up to 4096 tokens, on CUDA cores: one CTA per 8-token tile (64 CTAs
+// at 512 tokens, where 32-token tensor-core tiles gave 16 CTAs, each MMA row
+// block three-quarters padding; 4 warps with 16 experts, 8 with 32).  The router weight [E, d] is a parameter:
+// every CTA copies it into shared memory before its grid-dependency wait, so
+// the copy overlaps the kernel that writes x.  Each warp takes 32 / NP tokens
+// (NP = E padded to 16 or 32): its lanes hold 16-byte vectors of the token
+// rows in registers, accumulate the NP x (32 / NP) dots in packed fp32 pairs
+// in one pass over d, and one warp_reduce_many leaves lane l with the logit
+// of token l / NP, expert l % NP.  Softmax, top-2 (lower id on equal
+// probabilities) and renormalisation are shuffle reductions over each
+// token's NP lanes, with the tensor-core router's formulas.  The CTA writes
+// its tile histogram and (in token order) its probability sums.
+// ---------------------------------------------------------------------------
+template <int NP>
+__device__ __forceinline__ void best_of_group(float& v, int& i) {
+#pragma unroll
+  for (int o = NP / 2; o >= 1; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
+template <int NP>
+__global__ void __launch_bounds__(32 * kRouteSmallTile)
+    route_small_kernel(RouteArgs a, const __nv_bfloat16* __restrict__ x,
+                       const __nv_bfloat16* __restrict__ router_w) {
+  constexpr int TW = 32 / NP;               // tokens per warp
+  constexpr int kTile = kRouteSmallTile;    // tokens per CTA: kTile / TW warps
+  extern __shared__ __align__(16) uint4 rw_s[];    // [E][d / 8] router weight rows
+  __shared__ int hist[NP];
+  __shared__ float psum[kTile][NP];
+  const int E = a.n_experts, T = a.tokens, nvec = a.dim >> 3;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x;
+  {
+    const uint4* wg = reinterpret_cast<const uint4*>(router_w);
+    for (int i = threadIdx.x; i < E * nvec; i += blockDim.x) cp_async16(rw_s + i, wg + i);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  if (threadIdx.x < NP) hist[threadIdx.x] = 0;
+  const int ex = lane % NP, tw = lane / NP;
+  const float bias = (a.bias != nullptr && ex < E) ? __ldg(a.bias + ex) : 0.f;
+  griddep_wait();
+  griddep_launch();
+
+  // this warp's token rows, 16-byte vectors c = lane + 32 k (d <= 1024)
+  const int t_first = tile * kTile + warp * TW;
+  float2 xf[TW][4][4];
+#pragma unroll
+  for (int t = 0; t < TW; ++t) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = lane + 32 * k;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (c < nvec && t_first + t < T)
+        v = __ldg(reinterpret_cast<const uint4*>(x) + (size_t)(t_first + t) * nvec + c);
+      xf[t][k][0] = bf16x2_to_float2(v.x);
+      xf[t][k][1] = bf16x2_to_float2(v.y);
+      xf[t][k][2] = bf16x2_to_float2(v.z);
+      xf[t][k][3] = bf16x2_to_float2(v.w);
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  float2 acc[TW * NP];
+#pragma unroll
+  for (int v = 0; v < TW * NP; ++v) acc[v] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int e = 0; e < NP; ++e) {
+    if (e < E) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int c = lane + 32 * k;
+        if (c < nvec) {
+          const uint4 w = rw_s[e * nvec + c];
+          const float2 w0 = bf16x2_to_float2(w.x), w1 = bf16x2_to_float2(w.y);
+          const float2 w2 = bf16x2_to_float2(w.z), w3 = bf16x2_to_float2(w.w);
+#pragma unroll
+          for (int t = 0; t < TW; ++t) {
+            float2 s = acc[t * NP + e];
+            s = __ffma2_rn(w0, xf[t][k][0], s);
+            s = __ffma2_rn(w1, xf[t][k][1], s);
+            s = __ffma2_rn(w2, xf[t][k][2], s);
+            s = __ffma2_rn(w3, xf[t][k][3], s);
+            acc[t * NP + e] = s;
+          }
+        }
+      }
+    }
+  }
+  float dots[TW * NP];
+#pragma unroll
+  for (int v = 0; v < TW * NP; ++v) dots[v] = acc[v].x + acc[v].y;
+  // lane l: logit of token l / NP, expert l % NP
+  const float logit = warp_reduce_many<TW * NP>(dots, lane) + bias;
+  const bool valid_e = ex < E;
+  const int t = t_first + tw;
+  const bool valid_t = t < T;
+  float m = valid_e ? logit : -INFINITY;
+#pragma unroll
+  for (int o = NP / 2; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float p = valid_e ? __expf(logit - m) : 0.f;
+  float den = p;
+#pragma unroll
+  for (int o = NP / 2; o >= 1; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+  p = valid_t ? p * (1.0f / den) : 0.f;
+  // top-2; equal probabilities resolve to the lower expert id (every p >= 0)
+  float v1 = valid_e ? p : -1.f;
+  int i1 = ex;
+  best_of_group<NP>(v1, i1);
+  float v2 = (valid_e && ex != i1) ? p : -1.f;
+  int i2 = ex;
+  best_of_group<NP>(v2, i2);
+  if (valid_t && ex == 0) {
+    const float sel = v1 + v2;
+    const float w1 = v1 / sel, w2 = v2 / sel;
+    reinterpret_cast<int2*>(a.indices)[t] = make_int2(i1, i2);
+    reinterpret_cast<float2*>(a.weights)[t] = make_float2(w1, w2);
+    if (a.weights_out != nullptr) reinterpret_cast<float2*>(a.weights_out)[t] = make_float2(w1, w2);
+    if (a.indices64 != nullptr) {
+      a.indices64[2 * t] = i1;
+      a.indices64[2 * t + 1] = i2;
+    }
+    atomicAdd(&hist[i1], 1);
+    atomicAdd(&hist[i2], 1);
+  }
+  if (valid_t && valid_e && a.probs != nullptr) a.probs[(size_t)t * E + ex] = p;
+  psum[warp * TW + tw][ex] = p;
+  __syncthreads();
+  if (threadIdx.x < E) {
+    const int e = threadIdx.x;
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTile; ++k) s += psum[k][e];
+    a.tab.tile_hist[(size_t)tile * E + e] = hist[e];
+    a.tab.tile_probsum[(size_t)tile * E + e] = s;
+  }
+}
+
+template <int NP>
+static int launch_route_small(const RouteArgs& args, const void* x, const void* router_w,
+                              cudaStream_t stream) {
+  const size_t smem = (size_t)args.n_experts * args.dim * 2;
+  static unsigned long long configured = 0;  // per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -2;
+  if (!(configured & (1ull << dev))) {
+    if (cudaFuncSetAttribute(route_small_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             64 * 1024) != cudaSuccess)
+      return -2;
+    configured |= 1ull << dev;
+  }
+  return launch_pdl(route_small_kernel<NP>, dim3(route_blocks(args.tokens)),
+                    dim3(32 * kRouteSmallTile * NP / 32), smem, stream, args,
+                    static_cast<const __nv_bfloat16*>(x),
+                    static_cast<const __nv_bfloat16*>(router_w)) == cudaSuccess
+             ? 0
+             : -2;
+}
+
 template <int NP, int ST>
 static int launch_route_st(const RouteArgs& args, const CUtensorMap* x_map,
                            const CUtensorMap* w_map, cudaStream_t stream) {
@@ -300,21 +462,16 @@ static int launch_route_st(const RouteArgs& args, const CUtensorMap* x_map,
              : -2;
 }
 
-template <int NP>
-static int launch_route_np(const RouteArgs& args, const CUtensorMap* x_map,
-                           const CUtensorMap* w_map, cudaStream_t stream) {
-  return route_tile(args.tokens) == 128
-             ? launch_route_st<NP, kRouteLargeStages>(args, x_map, w_map, stream)
-             : launch_route_st<NP, route_stages<NP>()>(args, x_map, w_map, stream);
-}
-
-int launch_route(const RouteArgs& args, const CUtensorMap* x_map, const CUtensorMap* w_map,
-                 cudaStream_t stream) {
+int launch_route(const RouteArgs& args, const void* x, const void* router_w,
+                 const CUtensorMap* x_map, const CUtensorMap* w_map, cudaStream_t stream) {
   if (args.tokens == 0) return 0;
   if (args.dim % 64 || args.dim > 1024) return -1;
-  return route_experts_padded(args.n_experts) == 16
-             ? launch_route_np<16>(args, x_map, w_map, stream)
-             : launch_route_np<32>(args, x_map, w_map, stream);
+  const bool e16 = route_experts_padded(args.n_experts) == 16;
+  if (route_tile(args.tokens) == kRouteSmallTile)
+    return e16 ? launch_route_small<16>(args, x, router_w, stream)
+               : launch_route_small<32>(args, x, router_w, stream);
+  return e16 ? launch_route_st<16, kRouteLargeStages>(args, x_map, w_map, stream)
+             : launch_route_st<32, kRouteLargeStages>(args, x_map, w_map, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -369,8 +526,11 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
   {
     // prefix and totals: thread (phase, expert) sums every P-th tile row
     const int P = blockDim.x / E;
-    const int per_tile = route_tile(T) / kGroupTokensPerBlock;  // chunks per router tile
-    const int n_tiles = route_blocks(T), my_tile = blk / per_tile;
+    // whole router tiles before this block's first token; with tiles larger
+    // than a block, the 32-token chunks of its own tile before it come after
+    const int tile_tok = route_tile(T), n_tiles = route_blocks(T);
+    const int tiles_before = blk * kGroupTokensPerBlock / tile_tok;
+    const int chunk_from = tiles_before * tile_tok / kGroupTokensPerBlock;
     int before = 0, total = 0;
     float ps = 0.f;
     if (tid < P * E) {
@@ -392,7 +552,7 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
         for (int u = 0; u < U; ++u) {
           const int r = r0 + u * P;
           total += v[u];
-          if (r < my_tile) before += v[u];
+          if (r < tiles_before) before += v[u];
           if (writer && r < n_tiles) ps += pv[u];
         }
       }
@@ -410,7 +570,7 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
         c += red_total[ph * E + tid];
         s += red_psum[ph * E + tid];
       }
-      for (int ch = my_tile * per_tile; ch < blk; ++ch)
+      for (int ch = chunk_from; ch < blk; ++ch)
         b += __ldcg(a.tab.chunk_hist + (size_t)ch * E + tid);
       prefix_s[tid] = b;
       count_s[tid] = c;
@@ -418,7 +578,7 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
     }
     __syncthreads();
   }
-  if (a.ep_ranks == 1) {
+  if (!a.ep_packed) {
     // overflow bases in expert id order: an exclusive warp scan of the overflow counts
     if (warp == 0) {
       const int over = lane < E ? max(count_s[lane] - C, 0) : 0;
@@ -431,11 +591,10 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
       if (lane < E) obase_s[lane] = E * C + incl - over;
     }
   } else if (tid == 0) {
-    // destination-major for expert parallelism: expert e on rank e % G
-    const int G = a.ep_ranks, El = E / G;
+    // destination-major for expert parallelism: experts in the send order
     int base = E * C;
     for (int q = 0; q < E; ++q) {
-      const int ex = (q % El) * G + q / El;
+      const int ex = a.ep_order[q];
       obase_s[ex] = base;
       base += max(count_s[ex] - C, 0);
     }

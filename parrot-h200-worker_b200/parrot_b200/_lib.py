@@ -49,7 +49,8 @@ EP_MAX_RANKS = 8
 
 class EpDims(ctypes.Structure):
     _fields_ = [("ranks", c_int), ("rank", c_int), ("max_tokens", c_int), ("dim", c_int),
-                ("n_experts", c_int), ("expert_dim", c_int), ("wait_ns", ctypes.c_ulonglong)]
+                ("n_experts", c_int), ("expert_dim", c_int), ("wait_ns", ctypes.c_ulonglong),
+                ("slots", c_int), ("plan", (ctypes.c_byte * 32) * EP_MAX_RANKS)]
 
 
 EP_LAYOUT_OFFSETS = ("flags_in", "flags_back", "meta", "recv_rows", "back_rows", "epoch",
@@ -137,6 +138,10 @@ _SIGNATURES = {
     "parrot_ipc_import": (c_int, [c_void_p, ctypes.c_ulonglong, POINTER(c_void_p),
                                   POINTER(c_void_p)]),
     "parrot_ipc_close": (c_int, [c_void_p]),
+    "parrot_moe_ep_dispatch_planned_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights),
+                                                    c_void_p, POINTER(MoeOutputs),
+                                                    POINTER(EpDims), c_void_p, c_size_t,
+                                                    c_void_p]),
     "parrot_moe_ep_send_bf16": (c_int, [POINTER(MoeDims), POINTER(EpDims), POINTER(EpPeers),
                                         c_void_p, c_size_t, c_void_p]),
     "parrot_moe_ep_receive": (c_int, [POINTER(EpDims), c_void_p, c_void_p]),

@@ -194,14 +194,16 @@ class ExpertParallelMoE:
 
 
 class B200EpOps:
-    """B200 kernels for one rank: packed weights of its local experts only."""
+    """B200 kernels for one rank: packed weights of its local experts only
+    (``slots``: their global ids in slot order; round-robin by default)."""
 
-    def __init__(self, module, rank: int, ranks: int):
+    def __init__(self, module, rank: int, ranks: int, slots: list[int] | None = None):
         cfg = module.cfg
         self.module = module
         self.cfg = cfg
         self.ranks = ranks
-        self.local = local_experts(rank, ranks, cfg.n_experts)
+        self.local = list(slots) if slots is not None else local_experts(rank, ranks,
+                                                                          cfg.n_experts)
         router, gate_up, down, sgu, sd = bridge.pack_weights(module)
         idx = torch.tensor(self.local, device=gate_up.device)
         # packed tiles of one expert are contiguous, so selecting experts keeps the layout
@@ -281,19 +283,98 @@ class B200EpOps:
 # ---- the peer-memory exchange (one node, one process per GPU) -------------------
 
 @dataclass(frozen=True)
+class Placement:
+    """Which experts each rank holds and which rank computes a source's rows.
+
+    ``slots[q]``: the global experts rank ``q`` holds, in slot order.  An
+    expert in every rank's slots is *replicated*: each source computes its own
+    rows of it (data parallel); any other expert has one owner, which computes
+    every source's rows of it.
+    """
+    ranks: int
+    n_experts: int
+    slots: tuple[tuple[int, ...], ...]
+
+    def __post_init__(self):
+        held = [e for q in self.slots for e in q]
+        if len(self.slots) != self.ranks or sorted(set(held)) != list(range(self.n_experts)):
+            raise ValueError("every expert must be held by at least one rank")
+        for e in set(held):
+            n = held.count(e)
+            if n not in (1, self.ranks):
+                raise ValueError(f"expert {e} must be held by one rank or by all of them")
+        if any(len(set(q)) != len(q) for q in self.slots):
+            raise ValueError("a rank holds an expert twice")
+
+    @property
+    def replicated(self) -> frozenset[int]:
+        return frozenset(self.slots[0]).intersection(*map(set, self.slots[1:])) \
+            if self.ranks > 1 else frozenset()
+
+    @staticmethod
+    def round_robin(ranks: int, n_experts: int) -> "Placement":
+        return Placement(ranks, n_experts,
+                         tuple(tuple(local_experts(r, ranks, n_experts)) for r in range(ranks)))
+
+    @staticmethod
+    def balanced(counts: list[int], ranks: int) -> "Placement":
+        """For routing with counts ``counts`` [E]: an expert with more than
+        1 / ranks of the assignments is replicated on every rank; the others
+        go largest first to the rank with the least load so far (its share of
+        the replicated experts' rows included)."""
+        E = len(counts)
+        total = max(1, sum(counts))
+        hot = [e for e in range(E) if ranks > 1 and counts[e] * ranks > total]
+        load = [sum(counts[e] for e in hot) / ranks] * ranks
+        owned: list[list[int]] = [[] for _ in range(ranks)]
+        for e in sorted((e for e in range(E) if e not in hot), key=lambda e: (-counts[e], e)):
+            q = min(range(ranks), key=lambda r: (load[r], len(owned[r]), r))
+            owned[q].append(e)
+            load[q] += counts[e]
+        return Placement(ranks, E, tuple(tuple(sorted(hot + owned[q])) for q in range(ranks)))
+
+    def dest(self, source: int, expert: int) -> int:
+        """The rank that computes ``source``'s rows of ``expert``."""
+        if expert in self.replicated:
+            return source
+        return next(q for q, held in enumerate(self.slots) if expert in held)
+
+    def plan(self, source: int) -> list[list[int]]:
+        """plan[q][j]: the expert of rank q's slot j whose rows ``source``
+        sends there, or -1."""
+        return [[e if self.dest(source, e) == q else -1 for e in held] for q, held in
+                enumerate(self.slots)]
+
+
+@dataclass(frozen=True)
 class EpShape:
     """Sizes of one expert-parallel set: ``max_tokens`` bounds every rank's
-    tokens per call and sizes the fixed receive and return regions."""
+    tokens per call and sizes the fixed receive and return regions;
+    ``placement`` (round-robin when None) says which rank holds which expert."""
     ranks: int
     max_tokens: int
     dim: int
     n_experts: int
     expert_dim: int
     wait_ns: int = 0  # limit of each device-side flag wait; 0 = 2 s
+    placement: Placement | None = None
 
     def dims(self, rank: int) -> _lib.EpDims:
-        return _lib.EpDims(self.ranks, rank, self.max_tokens, self.dim, self.n_experts,
-                           self.expert_dim, self.wait_ns)
+        d = _lib.EpDims(self.ranks, rank, self.max_tokens, self.dim, self.n_experts,
+                        self.expert_dim, self.wait_ns)
+        if self.placement is not None:
+            d.slots = len(self.placement.slots[rank])
+            for q, row in enumerate(self.placement.plan(rank)):
+                for j, e in enumerate(row):
+                    d.plan[q][j] = e
+                for j in range(len(row), 32):
+                    d.plan[q][j] = -1
+        return d
+
+    def slots(self, rank: int) -> list[int]:
+        if self.placement is None:
+            return local_experts(rank, self.ranks, self.n_experts)
+        return list(self.placement.slots[rank])
 
     def layout(self) -> _lib.EpLayout:
         lay = _lib.EpLayout()
@@ -399,7 +480,7 @@ class PeerExpertParallelMoE:
                                                              cfg.expert_dim):
             raise ValueError("EP shape does not match the MoE module's dims")
         self.peers = peers
-        self.ops = B200EpOps(module, peers.rank, shape.ranks)
+        self.ops = B200EpOps(module, peers.rank, shape.ranks, shape.slots(peers.rank))
         self.cfg = cfg
         self._pending: tuple | None = None
         # (name, event) after each phase when a list is set (instrumentation only)
@@ -425,9 +506,10 @@ class PeerExpertParallelMoE:
         w = bridge._weights_struct(ops.packed, ops.bias)
         lib, stream = _lib.load(), bridge._stream()
         outputs = _lib.MoeOutputs(None, None, None, None, None, None, None, None)
-        _lib.check(lib.parrot_moe_ep_dispatch_bf16(
-            ctypes.byref(dims), ctypes.byref(w), bridge._p(x), ctypes.byref(outputs), peers.shape.ranks,
-            bridge._p(ws), ws.numel(), stream), "parrot_moe_ep_dispatch_bf16")
+        _lib.check(lib.parrot_moe_ep_dispatch_planned_bf16(
+            ctypes.byref(dims), ctypes.byref(w), bridge._p(x), ctypes.byref(outputs),
+            ctypes.byref(peers.dims), bridge._p(ws), ws.numel(), stream),
+            "parrot_moe_ep_dispatch_planned_bf16")
         self._mark("dispatch")
         _lib.check(lib.parrot_moe_ep_send_bf16(
             ctypes.byref(dims), ctypes.byref(peers.dims), ctypes.byref(peers.peers), bridge._p(ws),

@@ -91,3 +91,56 @@ def test_placement_and_segment_tables():
     assert (seg.rows, seg.base, seg.expert, seg.total) == ([3, 0, 1, 2], [0, 3, 3, 4], [0, 1, 0, 1], 6)
     with pytest.raises(ValueError):
         ep.local_experts(0, 3, 16)
+
+
+ZIPF_COUNTS = [11965, 5210, 3213, 2265, 1733, 1423, 1143, 979, 847, 749, 694, 617, 553, 488,
+               463, 426]  # the config-4 routing of 16384 tokens
+
+
+def _busiest_share(p: ep.Placement, counts) -> float:
+    """Largest share of the assignments one rank computes, rows of replicated
+    experts split evenly over the sources."""
+    total = sum(counts)
+    load = [0.0] * p.ranks
+    for e, n in enumerate(counts):
+        if e in p.replicated:
+            for q in range(p.ranks):
+                load[q] += n / p.ranks
+        else:
+            load[p.dest(0, e)] += n
+    return max(load) / total
+
+
+@pytest.mark.parametrize("ranks", [1, 2, 4, 8])
+def test_balanced_placement_plans(ranks):
+    p = ep.Placement.balanced(ZIPF_COUNTS, ranks)
+    rr = ep.Placement.round_robin(ranks, 16)
+    assert _busiest_share(p, ZIPF_COUNTS) <= _busiest_share(rr, ZIPF_COUNTS)
+    if ranks >= 4:  # expert 0 (36.5% of the rows) is replicated, so no rank exceeds its share
+        assert 0 in p.replicated
+        assert _busiest_share(p, ZIPF_COUNTS) < 0.5 * _busiest_share(rr, ZIPF_COUNTS) + 0.1
+    for source in range(ranks):
+        plan = p.plan(source)
+        sent = [e for row in plan for e in row if e >= 0]
+        assert sorted(sent) == list(range(16))        # every expert once per source
+        for e in p.replicated:
+            assert plan[source][p.slots[source].index(e)] == e  # its own rows, computed locally
+    assert rr.slots[-1] == tuple(ep.local_experts(ranks - 1, ranks, 16))
+
+
+def test_placement_rejects_partial_replication():
+    with pytest.raises(ValueError):
+        ep.Placement(3, 4, ((0, 1), (0, 2), (3,)))   # expert 0 on two of three ranks
+    with pytest.raises(ValueError):
+        ep.Placement(2, 4, ((0, 1), (2,)))           # expert 3 nowhere
+
+
+def test_ep_dims_carry_the_plan():
+    p = ep.Placement.balanced(ZIPF_COUNTS, 4)
+    shape = ep.EpShape(4, 64, 768, 16, 512, placement=p)
+    d = shape.dims(2)
+    assert d.slots == len(p.slots[2])
+    for q in range(4):
+        row = [d.plan[q][j] for j in range(32)]
+        assert row[:len(p.slots[q])] == p.plan(2)[q]
+        assert all(v == -1 for v in row[len(p.slots[q]):])

@@ -156,20 +156,32 @@ def test_expert_parallel_over_nccl_equals_single_device_block():
 
 # ---- the peer-memory exchange -------------------------------------------------
 
-def _peer_layers(module, sizes, wait_ns=200_000_000):
+def _peer_layers(module, sizes, wait_ns=200_000_000, placement=None):
     cfg = module.cfg
     shape = ep.EpShape(len(sizes), max(1, max(sizes)), cfg.dim, cfg.n_experts, cfg.expert_dim,
-                       wait_ns)
+                       wait_ns, placement)
     peers = ep.PeerSet.local(shape, torch.device("cuda"))
     return peers, [ep.PeerExpertParallelMoE(module, p) for p in peers]
 
 
-@pytest.mark.parametrize("ranks,zipf", [(1, False), (2, False), (4, True), (8, True)])
-def test_peer_exchange_ranks_in_turn_equal_single_device_block(ranks, zipf):
+def _balanced(module, x, ranks):
+    """Load-balanced placement from this batch's routing counts."""
+    _, _, util = bridge.b200_moe(module, x, True)
+    counts = (util.float() * 2 * x.shape[0]).round().int().tolist()
+    return ep.Placement.balanced(counts, ranks)
+
+
+@pytest.mark.parametrize("ranks,zipf,placement", [(1, False, "rr"), (2, False, "rr"),
+                                                  (4, True, "rr"), (8, True, "rr"),
+                                                  (2, True, "balanced"), (4, True, "balanced"),
+                                                  (8, True, "balanced")])
+def test_peer_exchange_ranks_in_turn_equal_single_device_block(ranks, zipf, placement):
     """All ranks' buffers on one GPU, the ranks' phases issued in turn on one
     stream: every send before any receive, every return before any combine, so
     each flag a kernel waits for was raised by a kernel that already finished.
-    Two calls in a row (the epoch advances, the regions are reused)."""
+    Two calls in a row (the epoch advances, the regions are reused).  Round-
+    robin placement, and load-balanced placements whose hot experts are
+    replicated (each source computes its own rows of them)."""
     tokens = 3000
     with torch.inference_mode():
         if zipf:
@@ -181,7 +193,10 @@ def test_peer_exchange_ranks_in_turn_equal_single_device_block(ranks, zipf):
         residual = hidden_states(tokens, module.cfg.dim, seed=14).cuda()
         sizes = shard_sizes(tokens, ranks)
         starts = [sum(sizes[:r]) for r in range(ranks)]
-        peers, layers = _peer_layers(module, sizes)
+        plan = _balanced(module, x, ranks) if placement == "balanced" else None
+        if plan is not None and ranks >= 4:
+            assert plan.replicated  # the Zipf head is computed where its rows are
+        peers, layers = _peer_layers(module, sizes, placement=plan)
         for call in range(2):
             xs = [x[starts[r]:starts[r] + sizes[r]] * (1 + call) for r in range(ranks)]
             rs = [residual[starts[r]:starts[r] + sizes[r]] for r in range(ranks)]
@@ -221,7 +236,7 @@ def test_peer_exchange_wait_for_a_missing_rank_times_out_with_status():
         assert torch.isfinite(want).all()
 
 
-def _peer_rank(rank, ranks, port, seed, tokens):
+def _peer_rank(rank, ranks, port, seed, tokens, balanced):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=ranks,
@@ -236,8 +251,9 @@ def _peer_rank(rank, ranks, port, seed, tokens):
             xs = x[start:start + sizes[rank]]
             rs = residual[start:start + sizes[rank]]
             cfg = module.cfg
+            plan = _balanced(module, x, ranks) if balanced else None
             shape = ep.EpShape(ranks, max(sizes), cfg.dim, cfg.n_experts, cfg.expert_dim,
-                               1_000_000_000)
+                               1_000_000_000, plan)
             peers = ep.PeerSet.connect(shape)
             layer = ep.PeerExpertParallelMoE(module, peers)
             want = bridge.b200_moe(module, xs, True, rs)[0] if sizes[rank] else None
@@ -268,6 +284,7 @@ def _peer_rank(rank, ranks, port, seed, tokens):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
-def test_peer_exchange_over_nvlink_equals_single_device_block():
+@pytest.mark.parametrize("balanced", [False, True])
+def test_peer_exchange_over_nvlink_equals_single_device_block(balanced):
     ranks = min(torch.cuda.device_count(), 8)
-    mp.spawn(_peer_rank, args=(ranks, _free_port(), 31, 4096), nprocs=ranks, join=True)
+    mp.spawn(_peer_rank, args=(ranks, _free_port(), 31, 4096, balanced), nprocs=ranks, join=True)
