@@ -285,6 +285,35 @@ int parrot_moe_forward_deferred_bf16(const parrot_moe_dims* dims,
                                      const parrot_moe_outputs* outputs, void* workspace,
                                      size_t workspace_bytes, void* stream);
 
+/* parrot_depthmix_bf16 (with its optional pending residual) whose normalised
+ * output is the input of an MoE block, with that block's router folded in:
+ * besides the depth mix it computes the router logits, softmax, top-2 and
+ * renormalised weights of every output row (model.py:521-527, the router of
+ * parrot_moe_forward_bf16) into `workspace` (the block's workspace for
+ * `dims`), plus outputs->probs / indices / weights when non-NULL.
+ * rows == dims->tokens <= 4096; out_norm_weight required.  The block then
+ * runs from its grouping on with parrot_moe_forward_routed_bf16.  One launch
+ * instead of a depth mix and a router launch.  The logits' summation order
+ * differs from the router kernel's: expert ids follow this call's own
+ * probabilities. */
+int parrot_depthmix_route_bf16(void* out, const void* const* sources, int n_sources,
+                               const void* query, const void* key_norm_weight, float key_eps,
+                               const void* out_norm_weight, float out_eps, void* mix_out,
+                               const void* pending_base, const void* pending_delta,
+                               void* pending_out, int rows, int dim,
+                               const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                               const parrot_moe_outputs* outputs, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* The MoE block after parrot_depthmix_route_bf16 routed its input x:
+ * grouping, experts and (deferred == 0) the combine, as
+ * parrot_moe_forward_bf16 / (deferred != 0) parrot_moe_forward_deferred_bf16
+ * from their grouping on.  outputs->probs / indices / weights must be NULL
+ * (the routing call writes them). */
+int parrot_moe_forward_routed_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                                   const void* x, const parrot_moe_outputs* outputs, int deferred,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
 /* Whole MoE block without a caller-provided workspace, for callers that
  * cannot allocate device memory at the point of the call (a runtime that owns
  * all device memory and forbids allocation on its hot path, or code that must

@@ -227,12 +227,10 @@ int prepare(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void
   return PARROT_OK;
 }
 
-// ep_order (expert parallelism): the packing order of the experts' rows,
-// destination rank major; nullptr: expert id order.
-int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
-              const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L, cudaStream_t s,
-              const signed char* ep_order = nullptr) {
-  const int T = dims->tokens, E = dims->n_experts;
+// The router's arguments: its outputs in the workspace (and the caller's
+// optional copies).
+parrot::RouteArgs route_args(const parrot_moe_dims* dims, const parrot_moe_weights* w,
+                             const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L) {
   parrot::RouteArgs ra{};
   ra.bias = w->router_bias;
   ra.probs = o->probs;
@@ -241,25 +239,29 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   ra.indices64 = o->indices;
   ra.weights_out = o->weights;
   ra.tab = tables(ws, L);
-  ra.tokens = T;
+  ra.tokens = dims->tokens;
   ra.dim = dims->dim;
-  ra.n_experts = E;
+  ra.n_experts = dims->n_experts;
   ra.status = at<int>(ws, L.status);
-  CUtensorMap mx, mw;
-  if (parrot::route_tile(T) != parrot::kRouteSmallTile &&
-      (!tensor_map(&mx, x, T, dims->dim, parrot::route_tile(T)) ||
-       !tensor_map(&mw, w->router, E, dims->dim, parrot::route_experts_padded(E))))
-    return fail(PARROT_ECUDA, "route: cuTensorMapEncodeTiled failed%s");
-  if (parrot::launch_route(ra, x, w->router, &mx, &mw, s))
-    return fail(PARROT_ECUDA, "route: unsupported dim or shared-memory setup failed%s");
-  int rc = check_launch("route_kernel");
-  if (rc) return rc;
+  return ra;
+}
 
+// Grouping (capacity slots, overflow, the 16-byte row scatter) after the
+// router's outputs are in the workspace.  ep_order (expert parallelism): the
+// packing order of the experts' rows, destination rank major; nullptr:
+// expert id order.
+// x_from_upstream: x was written by the kernel just before this one on the
+// stream (the depth mix with the router folded in), so the grouping may only
+// read it after its dependency wait.
+int run_group(const parrot_moe_dims* dims, const void* x, const parrot_moe_outputs* o, void* ws,
+              const parrot_moe_layout& L, cudaStream_t s, const signed char* ep_order = nullptr,
+              bool x_from_upstream = false) {
+  const int T = dims->tokens, E = dims->n_experts;
   parrot::GroupArgs ga{};
   ga.x = static_cast<const __nv_bfloat16*>(x);
-  ga.indices = ra.indices;
-  ga.tab = ra.tab;
-  ga.weights = ra.weights;
+  ga.indices = at<int>(ws, L.indices);
+  ga.tab = tables(ws, L);
+  ga.weights = at<float>(ws, L.weights);
   ga.positions = at<int>(ws, L.positions);
   ga.positions_out = o->positions;
   ga.row_dst = at<int>(ws, L.row_dst);
@@ -279,9 +281,28 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   int split = 1;
   while (split * 2 <= want && split < 8) split *= 2;
   ga.copy_split = split;
-  ga.status = ra.status;
+  ga.status = at<int>(ws, L.status);
+  ga.x_from_upstream = x_from_upstream ? 1 : 0;
   if (parrot::launch_group(ga, s)) return fail(PARROT_ECUDA, "group: shared-memory setup failed%s");
   return check_launch("group_kernel");
+}
+
+// Router + grouping.
+int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
+              const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L, cudaStream_t s,
+              const signed char* ep_order = nullptr) {
+  const int T = dims->tokens, E = dims->n_experts;
+  const parrot::RouteArgs ra = route_args(dims, w, o, ws, L);
+  CUtensorMap mx, mw;
+  if (parrot::route_tile(T) != parrot::kRouteSmallTile &&
+      (!tensor_map(&mx, x, T, dims->dim, parrot::route_tile(T)) ||
+       !tensor_map(&mw, w->router, E, dims->dim, parrot::route_experts_padded(E))))
+    return fail(PARROT_ECUDA, "route: cuTensorMapEncodeTiled failed%s");
+  if (parrot::launch_route(ra, x, w->router, &mx, &mw, s))
+    return fail(PARROT_ECUDA, "route: unsupported dim or shared-memory setup failed%s");
+  int rc = check_launch("route_kernel");
+  if (rc) return rc;
+  return run_group(dims, x, o, ws, L, s, ep_order);
 }
 
 int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights* w,
@@ -674,10 +695,11 @@ int parrot_rmsnorm_bf16(void* out, const void* x, const void* weight, int rows, 
 namespace {
 // Shared by the two depth-mix entries: the last source is replaced by the
 // deferred value (pending_out) when one is given.
+// route (optional): the router folded in (the output is an MoE block's input)
 int depthmix_launch(void* out, const void* const* sources, int n_sources, const void* query,
                     const void* key_norm_weight, float key_eps, const void* out_norm_weight,
                     float out_eps, void* mix_out, parrot::DepthMixArgs a, int rows, int dim,
-                    void* stream) {
+                    void* stream, const parrot::DepthRouteArgs* route = nullptr) {
   if (n_sources < 1 || n_sources > parrot::kMaxDepthSources)
     return fail(PARROT_EINVAL, "depthmix: n_sources must be in [1, 16]%s");
   if (rows < 0 || dim <= 0 || dim % 8 || dim > 1024)
@@ -702,6 +724,11 @@ int depthmix_launch(void* out, const void* const* sources, int n_sources, const 
   a.mix_out = static_cast<__nv_bfloat16*>(mix_out);
   a.rows = rows;
   a.dim = dim;
+  if (route != nullptr) {
+    if (parrot::launch_depthmix_route(a, *route, static_cast<cudaStream_t>(stream)))
+      return fail(PARROT_ECUDA, "depthmix (router): unsupported shape or shared-memory setup%s");
+    return check_launch("depthmix_kernel (router)");
+  }
   if (parrot::launch_depthmix(a, static_cast<cudaStream_t>(stream)))
     return fail(PARROT_ECUDA, "depthmix: could not configure shared memory%s");
   return check_launch("depthmix_kernel");
@@ -991,6 +1018,54 @@ int parrot_moe_forward_deferred_bf16(const parrot_moe_dims* dims,
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = run_route(dims, weights, x, outputs, workspace, L, s))) return rc;
   return run_experts(dims, weights, x, outputs, workspace, L, s, false);
+}
+
+int parrot_depthmix_route_bf16(void* out, const void* const* sources, int n_sources,
+                               const void* query, const void* key_norm_weight, float key_eps,
+                               const void* out_norm_weight, float out_eps, void* mix_out,
+                               const void* pending_base, const void* pending_delta,
+                               void* pending_out, int rows, int dim,
+                               const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                               const parrot_moe_outputs* outputs, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  int rc = layout_of(dims, &L);
+  if (rc) return rc;
+  if (dims->tokens != rows || dims->dim != dim || rows > 4096 || out_norm_weight == nullptr)
+    return fail(PARROT_EINVAL, "depthmix_route: rows == dims->tokens <= 4096, dims->dim == dim "
+                               "and the consumer norm weight required%s");
+  if ((rc = check_router(weights)) || (rc = ws_ok(workspace, workspace_bytes, L))) return rc;
+  if (outputs == nullptr) return fail(PARROT_EINVAL, "depthmix_route: outputs is NULL%s");
+  if ((pending_delta == nullptr) != (pending_base == nullptr) ||
+      (pending_delta != nullptr) != (pending_out != nullptr))
+    return fail(PARROT_EINVAL, "depthmix_route: pending base, delta and out go together%s");
+  if ((pending_base && !aligned16(pending_base)) || (pending_delta && !aligned16(pending_delta)) ||
+      (pending_out && !aligned16(pending_out)))
+    return fail(PARROT_EINVAL, "depthmix_route: pending buffers must be 16-byte aligned%s");
+  parrot::DepthMixArgs a{};
+  a.pending_base = static_cast<const __nv_bfloat16*>(pending_base);
+  a.pending_delta = static_cast<const __nv_bfloat16*>(pending_delta);
+  a.pending_out = static_cast<__nv_bfloat16*>(pending_out);
+  parrot::DepthRouteArgs r{};
+  r.router_w = static_cast<const __nv_bfloat16*>(weights->router);
+  r.r = route_args(dims, weights, outputs, workspace, L);
+  return depthmix_launch(out, sources, n_sources, query, key_norm_weight, key_eps,
+                         out_norm_weight, out_eps, mix_out, a, rows, dim, stream, &r);
+}
+
+int parrot_moe_forward_routed_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                                   const void* x, const parrot_moe_outputs* outputs, int deferred,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  int rc = prepare(dims, weights, x, outputs, workspace, workspace_bytes, &L, !deferred);
+  if (rc) return rc;
+  if (outputs->probs != nullptr || outputs->indices != nullptr || outputs->weights != nullptr)
+    return fail(PARROT_EINVAL, "moe_forward_routed: probs, indices and weights come from the "
+                               "routing call%s");
+  if (dims->tokens == 0) return PARROT_OK;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = run_group(dims, x, outputs, workspace, L, s, nullptr, true))) return rc;
+  return run_experts(dims, weights, x, outputs, workspace, L, s, !deferred);
 }
 
 int parrot_moe_decode_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,

@@ -96,6 +96,21 @@ __device__ __forceinline__ V warp_reduce_many(V (&v)[N], int lane) {
   return v[0];
 }
 
+// Arg-max over aligned groups of NP lanes (NP a power of two): every lane
+// ends with its group's largest v, the lowest i among equal values.
+template <int NP>
+__device__ __forceinline__ void best_of_group(float& v, int& i) {
+#pragma unroll
+  for (int o = NP / 2; o >= 1; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
 // 16-byte global -> shared asynchronous copy (bypasses L1), and its fences.
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));

@@ -64,6 +64,13 @@ struct RouteArgs {
   int* status;
 };
 
+// The router folded into a depth mix whose normalised output is the MoE
+// block's input (norm.cu): the router weight and the router's outputs.
+struct DepthRouteArgs {
+  const __nv_bfloat16* router_w;  // [E, d]
+  RouteArgs r;                    // tokens == the depth mix's rows
+};
+
 struct GroupArgs {
   const __nv_bfloat16* x;     // [T, d]
   const int* indices;         // [T, 2]
@@ -83,6 +90,7 @@ struct GroupArgs {
   // contiguous block; 0: expert id order
   int ep_packed;
   signed char ep_order[kMaxExperts];
+  int x_from_upstream;  // x is written by the kernel this one waits for (router fused into it)
   int copy_split;
   int* status;
 };
@@ -279,6 +287,8 @@ int launch_rope(__nv_bfloat16* x, const __nv_bfloat16* cos_t, const __nv_bfloat1
 // route_experts_padded(E) rows x 64 (rows past E read as zero).
 // Up to 4096 tokens the router reads x [T, d] and the router weight [E, d]
 // directly (x_map / w_map unused); above, through the tensor maps.
+int launch_depthmix_route(const DepthMixArgs& args, const DepthRouteArgs& route,
+                          cudaStream_t stream);
 int launch_route(const RouteArgs& args, const void* x, const void* router_w,
                  const CUtensorMap* x_map, const CUtensorMap* w_map, cudaStream_t stream);
 int launch_group(const GroupArgs& args, cudaStream_t stream);
@@ -312,9 +322,9 @@ int launch_silu_bf16(const uint16_t* x, uint16_t* y, int n, cudaStream_t stream)
 // load of x), 128 (the MMA's M) once it is large (fewer histogram rows for
 // the grouping kernel to sum).  The MMA always has M = 128; a 32-token tile
 // leaves the other accumulator lanes unused.
-// Tokens per router CTA: 8 up to 4096 tokens (CUDA-core router), else 128
-// (tensor-core router).
-constexpr int kRouteSmallTile = 8;
+// Tokens per router CTA: 4 up to 4096 tokens (CUDA-core router, or the
+// router folded into the depth mix), else 128 (tensor-core router).
+constexpr int kRouteSmallTile = 4;
 __host__ __device__ inline int route_tile(int tokens) {
   return tokens <= 4096 ? kRouteSmallTile : 128;
 }

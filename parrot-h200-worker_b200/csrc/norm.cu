@@ -106,14 +106,36 @@ int launch_rmsnorm(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat
 // so the per-source arrays and loops are sized to the call.
 // Up to 8 sources the kernel fits 80 registers without spilling, so 768
 // threads (8 CTAs at d = 768) stay resident per SM; 16 sources need more.
-template <int W, int NS>
-__global__ void __launch_bounds__(32 * W, NS <= 8 ? 768 / (32 * W) : 1) depthmix_kernel(DepthMixArgs a) {
-  __shared__ float red_sr[W][2 * NS], red_sq[W];
+//
+// With a router (NP = E padded to 16 or 32; NP = 0: none) the mixed,
+// normalised rows are an MoE block's input and the kernel routes them too,
+// the router kernel's job (route.cu) folded in: a CTA takes R =
+// kRouteSmallTile (4) rows (blockDim.y), the router weight is copied into shared
+// memory before the grid-dependency wait, each thread dots its 8 columns of
+// the bf16 output with the E weight rows, and after one warp_reduce_many and
+// a shared-memory join warp 0 of each row does the softmax, top-2 and
+// renormalisation (the router kernel's formulas); the CTA writes its tile's
+// histogram and probability sums.
+template <int W, int NS, int R, int NP>
+__global__ void __launch_bounds__(32 * W * R, (NS <= 8 && R == 1) ? 768 / (32 * W) : 1)
+    depthmix_kernel(DepthMixArgs a, DepthRouteArgs ra) {
+  static_assert(NP == 0 || R == kRouteSmallTile, "a routing CTA covers one router tile");
+  __shared__ float red_sr[R][W][2 * NS], red_sq[R][W];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = threadIdx.x;
+  const int ty = R > 1 ? (int)threadIdx.y : 0;
+  const int row = blockIdx.x * R + ty;
   const int dim = a.dim, nvec = dim >> 3, S = a.n_sources;
-  const bool active = c < nvec;
-  const size_t off = (size_t)blockIdx.x * dim;
+  const bool active = c < nvec && row < a.rows;
+  const size_t off = (size_t)row * dim;
+  if constexpr (NP > 0) {
+    // the router weight is a parameter: staged before the dependency wait
+    extern __shared__ __align__(16) uint4 dm_rw[];  // [E][nvec]
+    const int tid = ty * blockDim.x + c, nthreads = blockDim.x * R;
+    const uint4* wg = reinterpret_cast<const uint4*>(ra.router_w);
+    for (int i = tid; i < ra.r.n_experts * nvec; i += nthreads) cp_async16(dm_rw + i, wg + i);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   const bool pend_moe = a.pending_contrib != nullptr;
   const bool pending = a.pending_delta != nullptr || pend_moe;
 
@@ -219,7 +241,8 @@ __global__ void __launch_bounds__(32 * W, NS <= 8 ? 768 / (32 * W) : 1) depthmix
     }
   }
   const float sr_l = warp_reduce_many<2 * NS>(sr, lane);
-  if (lane < 2 * NS) red_sr[warp][lane] = sr_l;
+  if (lane < 2 * NS) red_sr[ty][warp][lane] = sr_l;
+  if constexpr (NP > 0) cp_async_wait_all();  // the router weight, visible after the barrier
   __syncthreads();
 
   // 3. scores and softmax: lane s of every warp scores source s (the warps'
@@ -234,8 +257,8 @@ __global__ void __launch_bounds__(32 * W, NS <= 8 ? 768 / (32 * W) : 1) depthmix
     float tss = 0.f, traw = 0.f;
 #pragma unroll
     for (int w = 0; w < W; ++w) {
-      tss += red_sr[w][lane];
-      traw += red_sr[w][NS + lane];
+      tss += red_sr[ty][w][lane];
+      traw += red_sr[ty][w][NS + lane];
     }
     score = rsqrtf(tss * inv_dim + a.key_eps) * traw;
   }
@@ -282,18 +305,96 @@ __global__ void __launch_bounds__(32 * W, NS <= 8 ? 768 / (32 * W) : 1) depthmix
   }
   // 4. the consumer RMSNorm
   sq = warp_sum(sq);
-  if (lane == 0) red_sq[warp] = sq;
+  if (lane == 0) red_sq[ty][warp] = sq;
   __syncthreads();
   float total = 0.f;
 #pragma unroll
-  for (int w = 0; w < W; ++w) total += red_sq[w];
+  for (int w = 0; w < W; ++w) total += red_sq[ty][w];
   const float inv = rsqrtf(total / (float)dim + a.out_eps);
+  float gb[8];  // the output as the bf16 tensor it is
+#pragma unroll
+  for (int j = 0; j < 8; ++j) gb[j] = 0.f;
   if (active) {
     float g[8];
     bf16x8_to_float(owv, g);
 #pragma unroll
     for (int j = 0; j < 8; ++j) g[j] = (h[j] * inv) * g[j];
-    reinterpret_cast<uint4*>(a.out + off)[c] = float_to_bf16x8(g);
+    const uint4 ov = float_to_bf16x8(g);
+    reinterpret_cast<uint4*>(a.out + off)[c] = ov;
+    bf16x8_to_float(ov, gb);
+  }
+  if constexpr (NP > 0) {
+    // 5. the router (MoE.forward's logits / softmax / top-2, model.py:521-527)
+    extern __shared__ __align__(16) uint4 dm_rw[];
+    __shared__ float red_r[R][W][NP];
+    __shared__ float psum[R][NP];
+    __shared__ int hist[NP];
+    const int E = ra.r.n_experts;
+    if (ty == 0 && c < NP) hist[c] = 0;
+    float pr[NP];
+#pragma unroll
+    for (int e = 0; e < NP; ++e) {
+      pr[e] = 0.f;
+      if (active && e < E) {
+        const uint4 w = dm_rw[e * nvec + c];
+        float2 t2 = make_float2(0.f, 0.f);
+        t2 = __ffma2_rn(bf16x2_to_float2(w.x), make_float2(gb[0], gb[1]), t2);
+        t2 = __ffma2_rn(bf16x2_to_float2(w.y), make_float2(gb[2], gb[3]), t2);
+        t2 = __ffma2_rn(bf16x2_to_float2(w.z), make_float2(gb[4], gb[5]), t2);
+        t2 = __ffma2_rn(bf16x2_to_float2(w.w), make_float2(gb[6], gb[7]), t2);
+        pr[e] = t2.x + t2.y;
+      }
+    }
+    const float wsum = warp_reduce_many<NP>(pr, lane);
+    if (lane < NP) red_r[ty][warp][lane] = wsum;
+    __syncthreads();
+    if (warp == 0) {
+      const int ex = lane % NP;
+      const bool valid_e = ex < E, valid_t = row < a.rows;
+      float logit = 0.f;
+#pragma unroll
+      for (int w = 0; w < W; ++w) logit += red_r[ty][w][ex];
+      if (ra.r.bias != nullptr && valid_e) logit += __ldg(ra.r.bias + ex);
+      float m = valid_e ? logit : -INFINITY;
+#pragma unroll
+      for (int o = NP / 2; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float p = valid_e ? __expf(logit - m) : 0.f;
+      float den = p;
+#pragma unroll
+      for (int o = NP / 2; o >= 1; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+      p = valid_t ? p * (1.0f / den) : 0.f;
+      float v1 = valid_e ? p : -1.f;
+      int i1 = ex;
+      best_of_group<NP>(v1, i1);
+      float v2 = (valid_e && ex != i1) ? p : -1.f;
+      int i2 = ex;
+      best_of_group<NP>(v2, i2);
+      if (valid_t && lane == 0) {
+        const float sel = v1 + v2;
+        const float w1 = v1 / sel, w2 = v2 / sel;
+        reinterpret_cast<int2*>(ra.r.indices)[row] = make_int2(i1, i2);
+        reinterpret_cast<float2*>(ra.r.weights)[row] = make_float2(w1, w2);
+        if (ra.r.weights_out != nullptr)
+          reinterpret_cast<float2*>(ra.r.weights_out)[row] = make_float2(w1, w2);
+        if (ra.r.indices64 != nullptr) {
+          ra.r.indices64[2 * row] = i1;
+          ra.r.indices64[2 * row + 1] = i2;
+        }
+        atomicAdd(&hist[i1], 1);
+        atomicAdd(&hist[i2], 1);
+      }
+      if (valid_t && valid_e && lane < NP && ra.r.probs != nullptr)
+        ra.r.probs[(size_t)row * E + ex] = p;
+      if (lane < NP) psum[ty][lane] = p;
+    }
+    __syncthreads();
+    if (ty == 0 && c < E) {
+      float sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < R; ++k) sum += psum[k][c];
+      ra.r.tab.tile_hist[(size_t)blockIdx.x * E + c] = hist[c];
+      ra.r.tab.tile_probsum[(size_t)blockIdx.x * E + c] = sum;
+    }
   }
 }
 
@@ -301,12 +402,67 @@ template <int W>
 static int launch_depthmix_w(const DepthMixArgs& args, cudaStream_t stream) {
   const dim3 grid(args.rows), block(32 * W);
   const int S = args.n_sources;
+  const DepthRouteArgs none{};
   cudaError_t e;
-  if (S <= 2) e = launch_pdl(depthmix_kernel<W, 2>, grid, block, 0, stream, args);
-  else if (S <= 4) e = launch_pdl(depthmix_kernel<W, 4>, grid, block, 0, stream, args);
-  else if (S <= 8) e = launch_pdl(depthmix_kernel<W, 8>, grid, block, 0, stream, args);
-  else e = launch_pdl(depthmix_kernel<W, kMaxDepthSources>, grid, block, 0, stream, args);
+  if (S <= 2) e = launch_pdl(depthmix_kernel<W, 2, 1, 0>, grid, block, 0, stream, args, none);
+  else if (S <= 4) e = launch_pdl(depthmix_kernel<W, 4, 1, 0>, grid, block, 0, stream, args, none);
+  else if (S <= 8) e = launch_pdl(depthmix_kernel<W, 8, 1, 0>, grid, block, 0, stream, args, none);
+  else
+    e = launch_pdl(depthmix_kernel<W, kMaxDepthSources, 1, 0>, grid, block, 0, stream, args, none);
   return e == cudaSuccess ? 0 : -2;
+}
+
+template <int W, int NS, int NP>
+static cudaError_t launch_depthmix_route_k(const DepthMixArgs& args, const DepthRouteArgs& route,
+                                           cudaStream_t stream) {
+  constexpr int R = kRouteSmallTile;
+  static unsigned long long configured = 0;  // per device: the router weight may exceed 48 KB
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!(configured & (1ull << dev))) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        depthmix_kernel<W, NS, R, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    if (e != cudaSuccess) return e;
+    configured |= 1ull << dev;
+  }
+  const size_t smem = (size_t)route.r.n_experts * args.dim * 2;
+  return launch_pdl(depthmix_kernel<W, NS, R, NP>, dim3((args.rows + R - 1) / R),
+                    dim3(32 * W, R), smem, stream, args, route);
+}
+
+template <int W, int NP>
+static int launch_depthmix_route_w(const DepthMixArgs& args, const DepthRouteArgs& route,
+                                   cudaStream_t stream) {
+  const int S = args.n_sources;
+  cudaError_t e;
+  if (S <= 2) e = launch_depthmix_route_k<W, 2, NP>(args, route, stream);
+  else if (S <= 4) e = launch_depthmix_route_k<W, 4, NP>(args, route, stream);
+  else if (S <= 8) e = launch_depthmix_route_k<W, 8, NP>(args, route, stream);
+  else e = launch_depthmix_route_k<W, kMaxDepthSources, NP>(args, route, stream);
+  return e == cudaSuccess ? 0 : -2;
+}
+
+template <int NP>
+static int launch_depthmix_route_np(const DepthMixArgs& args, const DepthRouteArgs& route,
+                                    cudaStream_t stream) {
+  switch ((args.dim / 8 + 31) / 32) {
+    case 1: return launch_depthmix_route_w<1, NP>(args, route, stream);
+    case 2: return launch_depthmix_route_w<2, NP>(args, route, stream);
+    case 3: return launch_depthmix_route_w<3, NP>(args, route, stream);
+    case 4: return launch_depthmix_route_w<4, NP>(args, route, stream);
+    default: return -1;
+  }
+}
+
+int launch_depthmix_route(const DepthMixArgs& args, const DepthRouteArgs& route,
+                          cudaStream_t stream) {
+  if (args.rows == 0) return 0;
+  if (args.n_sources < 1 || args.n_sources > kMaxDepthSources || args.out_w == nullptr ||
+      route.r.tokens != args.rows || route_tile(args.rows) != kRouteSmallTile)
+    return -1;
+  return route_experts_padded(route.r.n_experts) == 16
+             ? launch_depthmix_route_np<16>(args, route, stream)
+             : launch_depthmix_route_np<32>(args, route, stream);
 }
 
 int launch_depthmix(const DepthMixArgs& args, cudaStream_t stream) {

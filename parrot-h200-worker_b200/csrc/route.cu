@@ -1,6 +1,6 @@
 // Router (N1) and deterministic capacity grouping (N2).
 //
-// route_small_kernel (up to 4096 tokens): one CTA per 8 tokens on CUDA
+// route_small_kernel (up to 4096 tokens): one CTA per 4 tokens on CUDA
 //                cores; the router weight is staged in shared memory before
 //                the grid-dependency wait, each warp folds its tokens' E dots
 //                with one warp_reduce_many, softmax and top-2 are shuffle
@@ -278,9 +278,9 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
 }
 
 // ---------------------------------------------------------------------------
-// Router up to 4096 tokens, on CUDA cores: one CTA per 8-token tile (64 CTAs
-// at 512 tokens, where 32-token tensor-core tiles gave 16 CTAs, each MMA row
-// block three-quarters padding; 4 warps with 16 experts, 8 with 32).  The router weight [E, d] is a parameter:
+// Router up to 4096 tokens, on CUDA cores: one CTA per 4-token tile (128
+// CTAs at 512 tokens, where 32-token tensor-core tiles gave 16 CTAs, each MMA
+// row block three-quarters padding; 2 warps with 16 experts, 4 with 32).  The router weight [E, d] is a parameter:
 // every CTA copies it into shared memory before its grid-dependency wait, so
 // the copy overlaps the kernel that writes x.  Each warp takes 32 / NP tokens
 // (NP = E padded to 16 or 32): its lanes hold 16-byte vectors of the token
@@ -291,19 +291,6 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
 // token's NP lanes, with the tensor-core router's formulas.  The CTA writes
 // its tile histogram and (in token order) its probability sums.
 // ---------------------------------------------------------------------------
-template <int NP>
-__device__ __forceinline__ void best_of_group(float& v, int& i) {
-#pragma unroll
-  for (int o = NP / 2; o >= 1; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
-    if (ov > v || (ov == v && oi < i)) {
-      v = ov;
-      i = oi;
-    }
-  }
-}
-
 template <int NP>
 __global__ void __launch_bounds__(32 * kRouteSmallTile)
     route_small_kernel(RouteArgs a, const __nv_bfloat16* __restrict__ x,
@@ -511,14 +498,19 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
   const int tok_lo = blk * kGroupTokensPerBlock + lo / 2;
   const int n_tok = max(0, min(T - tok_lo, (hi - lo) / 2));
   uint4* x_s = reinterpret_cast<uint4*>(group_smem);
-  {
-    // the token rows are the router's input, not its output
+  auto stage_rows = [&] {
     const uint4* xg = reinterpret_cast<const uint4*>(a.x + (size_t)tok_lo * d);
     for (int i = tid; i < n_tok * nvec; i += blockDim.x) cp_async16(x_s + i, xg + i);
     asm volatile("cp.async.commit_group;" ::: "memory");
-  }
+  };
+  // The token rows are the router's input: complete before the router kernel
+  // that precedes this one began, so they are read before the dependency
+  // wait.  When the router was folded into the kernel that writes them
+  // (x_from_upstream), that kernel is the one being waited for.
+  if (!a.x_from_upstream) stage_rows();
   griddep_wait();
   griddep_launch();
+  if (a.x_from_upstream) stage_rows();
 
   const int a_idx = blk * kAssign + tid;
   int e = -1;

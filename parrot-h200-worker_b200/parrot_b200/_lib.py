@@ -109,6 +109,14 @@ _SIGNATURES = {
                                                  c_void_p]),
     "parrot_moe_forward_static_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                                POINTER(MoeOutputs), c_void_p]),
+    "parrot_depthmix_route_bf16": (c_int, [c_void_p, POINTER(c_void_p), c_int, c_void_p,
+                                           c_void_p, c_float, c_void_p, c_float, c_void_p,
+                                           c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                           POINTER(MoeDims), POINTER(MoeWeights),
+                                           POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
+    "parrot_moe_forward_routed_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
+                                               POINTER(MoeOutputs), c_int, c_void_p, c_size_t,
+                                               c_void_p]),
     "parrot_moe_decode_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                        POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
     "parrot_moe_route_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,

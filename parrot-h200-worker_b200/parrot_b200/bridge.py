@@ -228,7 +228,23 @@ def b200_vocab_argmax(hidden: Tensor, weight: Tensor) -> Tensor:
 # ---------------------------------------------------------------------------
 # Block AttnRes depth mixing  (metal_moe.py:419-500)
 # ---------------------------------------------------------------------------
-def _depth_call(module, sources: Sequence[Tensor], output_norm, pending_delta: Tensor | None):
+# Fold each MoE block's router into the depth mix that produces its input
+# (parrot_depthmix_route_bf16: one launch fewer per layer).  False runs the
+# router kernel instead.
+FUSE_MOE_ROUTER = True
+
+
+def _routes_in_mix(route, rows: int) -> bool:
+    """Whether the mix producing ``route``'s (an MoE module's, or None) input of
+    ``rows`` tokens also routes it: the grouped-GEMM path up to 4096 tokens
+    (at most DECODE_MOE_MAX_TOKENS rows usually take the small-batch kernels,
+    which route themselves)."""
+    return (route is not None and FUSE_MOE_ROUTER and
+            DECODE_MOE_MAX_TOKENS < rows <= 4096)
+
+
+def _depth_call(module, sources: Sequence[Tensor], output_norm, pending_delta: Tensor | None,
+                route=None):
     last = sources[-1]
     if isinstance(last, PendingMoE):
         if last.value is not None:  # already materialised: an ordinary source
@@ -257,10 +273,23 @@ def _depth_call(module, sources: Sequence[Tensor], output_norm, pending_delta: T
     lib = _lib.load()
     ow = None if output_norm is None else output_norm.weight
     oe = 0.0 if output_norm is None else float(output_norm.eps)
-    _lib.check(lib.parrot_depthmix_bf16(
-        _p(out), ptrs, n, _p(module.query), _p(module.norm.weight), float(module.norm.eps),
-        _p(ow), oe, None, _p(base), _p(pending_delta), _p(pending_out), rows, dim, _stream()),
-        "parrot_depthmix_bf16")
+    if output_norm is not None and _routes_in_mix(route, rows):
+        # the mix is the MoE block's input: route it in the same launch
+        dims = moe_dims(route.cfg, rows)
+        ws = workspace(first.device, dims)
+        wst = _weights_struct(pack_weights(route), _router_bias(route))
+        outputs = _lib.MoeOutputs(None, None, None, None, None, None, None, None)
+        _lib.check(lib.parrot_depthmix_route_bf16(
+            _p(out), ptrs, n, _p(module.query), _p(module.norm.weight), float(module.norm.eps),
+            _p(ow), oe, None, _p(base), _p(pending_delta), _p(pending_out), rows, dim,
+            ctypes.byref(dims), ctypes.byref(wst), ctypes.byref(outputs), _p(ws), ws.numel(),
+            _stream()), "parrot_depthmix_route_bf16")
+        ws.__dict__["_b200_fused_route"] = out.data_ptr()
+    else:
+        _lib.check(lib.parrot_depthmix_bf16(
+            _p(out), ptrs, n, _p(module.query), _p(module.norm.weight), float(module.norm.eps),
+            _p(ow), oe, None, _p(base), _p(pending_delta), _p(pending_out), rows, dim,
+            _stream()), "parrot_depthmix_bf16")
     out = out.view_as(first)
     if pending_delta is None:
         return out, None
@@ -273,7 +302,7 @@ def b200_depth_mix(module, sources: Sequence[Tensor]) -> Tensor:
 
 
 def b200_depth_mix_norm(module, sources: Sequence[Tensor], output_norm,
-                        pending_delta: Tensor | None = None):
+                        pending_delta: Tensor | None = None, route=None):
     """``output_norm(DepthMix(sources))`` in one kernel.
 
     With ``pending_delta``, the last source is ``sources[-1] + pending_delta``
@@ -281,10 +310,13 @@ def b200_depth_mix_norm(module, sources: Sequence[Tensor], output_norm,
     ``(normalized, resolved_last_source)``.  When the last source is a
     ``PendingMoE`` the kernel also performs that MoE block's combine and the
     call returns ``(normalized, resolved_last_source)`` too.  Otherwise it
-    returns ``normalized``.
+    returns ``normalized``.  ``route``: the MoE module whose input this is;
+    up to 4096 rows the kernel routes the output for it as well, and that
+    module's next ``b200_moe`` / ``b200_moe_deferred`` call on the output
+    starts from the grouping.
     """
     deferred = isinstance(sources[-1], PendingMoE)
-    out, resolved = _depth_call(module, sources, output_norm, pending_delta)
+    out, resolved = _depth_call(module, sources, output_norm, pending_delta, route)
     return out if pending_delta is None and not deferred else (out, resolved)
 
 
@@ -497,11 +529,16 @@ def b200_moe(module, flat: Tensor, collect_stats: bool, addend: Tensor | None = 
                               None, None, None, None, None,
                               None if stats is None else stats.data_ptr())
     weights = _weights_struct(packed, bias)
+    routed = ws.__dict__.pop("_b200_fused_route", None) == flat.data_ptr()
     if stats is None and 0 < T <= DECODE_MOE_MAX_TOKENS and cfg.expert_dim <= 1024:
         # decode batch sizes: the two-kernel small-batch path
         _lib.check(_lib.load().parrot_moe_decode_bf16(
             ctypes.byref(dims), ctypes.byref(weights), _p(flat), ctypes.byref(outputs),
             _p(ws), ws.numel(), _stream()), "parrot_moe_decode_bf16")
+    elif routed:
+        _lib.check(_lib.load().parrot_moe_forward_routed_bf16(
+            ctypes.byref(dims), ctypes.byref(weights), _p(flat), ctypes.byref(outputs), 0,
+            _p(ws), ws.numel(), _stream()), "parrot_moe_forward_routed_bf16")
     else:
         _lib.check(_lib.load().parrot_moe_forward_bf16(
             ctypes.byref(dims), ctypes.byref(weights), _p(flat), ctypes.byref(outputs),
@@ -543,9 +580,15 @@ def b200_moe_deferred(module, flat: Tensor, collect_stats: bool, addend: Tensor 
         if collect_stats else None
     outputs = _lib.MoeOutputs(None, None, None, None, None, None, None,
                               None if stats is None else stats.data_ptr())
-    _lib.check(_lib.load().parrot_moe_forward_deferred_bf16(
-        ctypes.byref(dims), ctypes.byref(_weights_struct(packed, _router_bias(module))), _p(flat),
-        ctypes.byref(outputs), _p(ws), ws.numel(), _stream()), "parrot_moe_forward_deferred_bf16")
+    wst = _weights_struct(packed, _router_bias(module))
+    if ws.__dict__.pop("_b200_fused_route", None) == flat.data_ptr():
+        _lib.check(_lib.load().parrot_moe_forward_routed_bf16(
+            ctypes.byref(dims), ctypes.byref(wst), _p(flat), ctypes.byref(outputs), 1, _p(ws),
+            ws.numel(), _stream()), "parrot_moe_forward_routed_bf16")
+    else:
+        _lib.check(_lib.load().parrot_moe_forward_deferred_bf16(
+            ctypes.byref(dims), ctypes.byref(wst), _p(flat), ctypes.byref(outputs), _p(ws),
+            ws.numel(), _stream()), "parrot_moe_forward_deferred_bf16")
     lay = workspace_layout(dims)
     contrib = ws[lay.contrib:lay.contrib + 2 * T * d * 2].view(flat.dtype).view(2 * T, d)
     shared = ws[lay.shared_y:lay.shared_y + T * d * 2].view(flat.dtype).view(T, d)

@@ -148,9 +148,10 @@ class DepthMix(nn.Module):
         return bridge.b200_depth_mix(self, sources)
 
     def normalized(self, sources: list[Tensor], output_norm: RMSNorm,
-                   pending_delta: Tensor | None = None):
-        """``output_norm(self(sources))`` in one kernel; see ``bridge.b200_depth_mix_norm``."""
-        return bridge.b200_depth_mix_norm(self, sources, output_norm, pending_delta)
+                   pending_delta: Tensor | None = None, route=None):
+        """``output_norm(self(sources))`` in one kernel; see ``bridge.b200_depth_mix_norm``
+        (``route``: the MoE module this output feeds, routed in the same kernel)."""
+        return bridge.b200_depth_mix_norm(self, sources, output_norm, pending_delta, route)
 
 
 # decode steps of at most this many rows run their attention projections on
@@ -466,7 +467,9 @@ class _Residuals:
     def sources(self) -> list[Tensor]:
         return self.completed + ([] if self.partial is None else [self.partial])
 
-    def mix(self, depth: DepthMix, norm: RMSNorm) -> Tensor:
+    def mix(self, depth: DepthMix, norm: RMSNorm, route=None) -> Tensor:
+        """The normalised depth mix feeding the next module; ``route``: that
+        module when it is an MoE block (its router runs in the same kernel)."""
         sources = self.sources()
         if isinstance(sources[-1], bridge.PendingMoE):
             out, resolved = depth.normalized(sources, norm)
@@ -476,8 +479,8 @@ class _Residuals:
                 self.completed[-1] = resolved
             return out
         if self.pending is None:
-            return depth.normalized(sources, norm)
-        out, resolved = depth.normalized(self.sources(), norm, self.pending)
+            return depth.normalized(sources, norm, route=route)
+        out, resolved = depth.normalized(self.sources(), norm, self.pending, route=route)
         self.partial, self.pending = resolved, None
         return out
 
@@ -544,7 +547,8 @@ class Parrot(nn.Module):
         for block in self.blocks:
             for is_moe in (False, True):
                 norm = block.moe_norm if is_moe else block.attention_norm
-                h = res.mix(self.depth_mix[index], norm) if attnres else norm(x)
+                h = res.mix(self.depth_mix[index], norm, block.moe if is_moe else None) \
+                    if attnres else norm(x)
                 if is_moe:
                     base = res.partial if attnres else x
                     out, aux, usage = block.moe(h, addend=base, defer_combine=attnres)
@@ -628,7 +632,8 @@ class Parrot(nn.Module):
             else:
                 x = x + delta
             index += 1
-            h = res.mix(self.depth_mix[index], block.moe_norm) if attnres else block.moe_norm(x)
+            h = res.mix(self.depth_mix[index], block.moe_norm, block.moe) if attnres \
+                else block.moe_norm(x)
             out = block.moe.inference(h, direct=False, addend=res.partial if attnres else x,
                                       defer_combine=attnres)
             if attnres:
@@ -677,7 +682,8 @@ class Parrot(nn.Module):
             else:
                 x = x + delta
             index += 1
-            h = res.mix(self.depth_mix[index], block.moe_norm) if attnres else block.moe_norm(x)
+            h = res.mix(self.depth_mix[index], block.moe_norm, block.moe) if attnres \
+                else block.moe_norm(x)
             out = block.moe.inference(h, direct=True, addend=res.partial if attnres else x,
                                       defer_combine=attnres)
             if attnres:

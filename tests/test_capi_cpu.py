@@ -98,7 +98,7 @@ def test_workspace_layout_is_aligned_and_ordered(lib):
     assert all(o % 256 == 0 for o in offsets)
     assert lay.capacity == 128
     assert lay.grouped_rows == 16 * 128 + 1024
-    assert lay.route_blocks == 64  # 8-token router tiles up to T = 4096
+    assert lay.route_blocks == 128  # 4-token router tiles up to T = 4096
     assert lay.shared_y + 512 * 768 * 2 <= lay.total
 
 

@@ -635,3 +635,83 @@ def test_vocab_argmax_is_repeatable_and_graph_capturable():
         graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(static, first)
+
+
+# ---------------------------------------------------------------------------
+# The router folded into the depth mix that produces the MoE input
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("rows,n_sources,pending", [(512, 6, True), (37, 3, False),
+                                                    (4096, 9, True), (9, 1, False)])
+def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending):
+    """parrot_depthmix_route_bf16 + parrot_moe_forward_routed_bf16 against
+    parrot_depthmix_bf16 + parrot_moe_forward_bf16: the mix is bit-identical;
+    expert ids agree wherever the router's top-2 / top-3 probability margin
+    exceeds 1e-5 and equal top-2 of the fused call's own probabilities; the
+    block output is identical on every token routed alike."""
+    cfg = moe_config()
+    module, _ = build_moe_pair(cfg, seed=31)
+    dim = cfg.dim
+    g = torch.Generator().manual_seed(rows + n_sources)
+    srcs = [(torch.randn(rows, dim, generator=g) * (1 + i)).to(torch.bfloat16).cuda()
+            for i in range(n_sources)]
+    query = (0.3 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    key_w = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    out_w = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    delta = torch.randn(rows, dim, generator=g).to(torch.bfloat16).cuda() if pending else None
+    lib = _lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    ptrs = (ctypes.c_void_p * n_sources)(*[s.data_ptr() for s in srcs])
+    dims = bridge.moe_dims(cfg, rows)
+    w = bridge._weights_struct(bridge.pack_weights(module), None)
+    results = {}
+    for fused in (False, True):
+        out = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16)
+        pend_out = torch.empty_like(out) if pending else None
+        ws = torch.zeros(int(bridge.workspace_layout(dims).total), device="cuda",
+                         dtype=torch.uint8)
+        probs = torch.empty(rows, cfg.n_experts, device="cuda")
+        idx = torch.empty(rows, 2, device="cuda", dtype=torch.int64)
+        y = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16)
+        args = (ctypes.c_void_p(out.data_ptr()), ptrs, n_sources, ctypes.c_void_p(query.data_ptr()),
+                ctypes.c_void_p(key_w.data_ptr()), 1e-6, ctypes.c_void_p(out_w.data_ptr()), 1e-6,
+                None, bridge._p(srcs[-1] if pending else None), bridge._p(delta),
+                bridge._p(pend_out), rows, dim)
+        if fused:
+            ro = _lib.MoeOutputs(None, None, probs.data_ptr(), idx.data_ptr(), None, None, None,
+                                 None)
+            _lib.check(lib.parrot_depthmix_route_bf16(
+                *args, ctypes.byref(dims), ctypes.byref(w), ctypes.byref(ro),
+                ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream), "depthmix_route")
+            mo = _lib.MoeOutputs(y.data_ptr(), None, None, None, None, None, None, None)
+            _lib.check(lib.parrot_moe_forward_routed_bf16(
+                ctypes.byref(dims), ctypes.byref(w), ctypes.c_void_p(out.data_ptr()),
+                ctypes.byref(mo), 0, ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream),
+                "moe_forward_routed")
+        else:
+            _lib.check(lib.parrot_depthmix_bf16(*args, stream), "depthmix")
+            mo = _lib.MoeOutputs(y.data_ptr(), None, probs.data_ptr(), idx.data_ptr(), None,
+                                 None, None, None)
+            _lib.check(lib.parrot_moe_forward_bf16(
+                ctypes.byref(dims), ctypes.byref(w), ctypes.c_void_p(out.data_ptr()),
+                ctypes.byref(mo), ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream),
+                "moe_forward")
+        torch.cuda.synchronize()
+        status = (ctypes.c_int * 4)()
+        _lib.check(lib.parrot_moe_read_status(ctypes.c_void_p(ws.data_ptr()), ctypes.byref(dims),
+                                              status, stream), "status")
+        assert list(status) == [0, 0, 0, 0]
+        results[fused] = (out.clone(), None if pend_out is None else pend_out.clone(),
+                          probs.cpu(), idx.cpu(), y.clone())
+    (o0, p0, pr0, i0, y0), (o1, p1, pr1, i1, y1) = results[False], results[True]
+    assert torch.equal(o0, o1)
+    if pending:
+        assert torch.equal(p0, p1)
+    top = pr1.topk(2, dim=-1).indices
+    assert torch.equal(i1, top)                       # own probabilities
+    top3 = pr0.topk(3, dim=-1).values
+    clear = ((top3[:, 1] - top3[:, 2]) > 1e-5) & ((top3[:, 0] - top3[:, 1]) > 1e-5)
+    assert torch.equal(i0[clear], i1[clear])
+    torch.testing.assert_close(pr1, pr0, rtol=0, atol=1e-5)
+    same = (i0 == i1).all(-1).cuda()
+    assert torch.equal(y0[same], y1[same]) or \
+        float((y0[same].float() - y1[same].float()).abs().max()) <= 2 ** -6 * float(y0.float().abs().max())
