@@ -1283,9 +1283,7 @@ int parrot_vocab_argmax_bf16(long long* out, const void* hidden, const void* wei
   a.partial_value = reinterpret_cast<float*>(sc + 256);
   a.partial_index = reinterpret_cast<int*>(sc + 256 + (size_t)parrot::kVocabMaxGrid * 8 * 4);
   a.out = out;
-  int grid = 2 * sm_count();
-  if (grid > parrot::kVocabMaxGrid) grid = parrot::kVocabMaxGrid;
-  if (parrot::launch_vocab_argmax(a, grid, static_cast<cudaStream_t>(stream)))
+  if (parrot::launch_vocab_argmax(a, sm_count(), static_cast<cudaStream_t>(stream)))
     return fail(PARROT_EINVAL, "vocab_argmax: unsupported dim%s");
   return check_launch("vocab_argmax_kernel");
 }

@@ -125,7 +125,7 @@ struct EpCombineArgs {
 };
 
 // ---- greedy next token (vocab.cu) -------------------------------------------
-constexpr int kVocabMaxGrid = 512;
+constexpr int kVocabMaxGrid = 1024;
 
 struct VocabArgmaxArgs {
   const void* hidden;     // [rows, dim] bf16
@@ -295,7 +295,7 @@ int launch_group(const GroupArgs& args, cudaStream_t stream);
 int launch_combine(const CombineArgs& args, cudaStream_t stream);
 int launch_ep_combine(const EpCombineArgs& args, cudaStream_t stream);
 int launch_ep_send(const EpSendArgs& args, int sms, cudaStream_t stream);
-int launch_vocab_argmax(const VocabArgmaxArgs& args, int grid, cudaStream_t stream);
+int launch_vocab_argmax(const VocabArgmaxArgs& args, int sms, cudaStream_t stream);
 int launch_argmax_rows(const ArgmaxRowsArgs& args, cudaStream_t stream);
 int launch_ep_receive(const EpReceiveArgs& args, cudaStream_t stream);
 int launch_ep_return(const EpReturnArgs& args, int sms, cudaStream_t stream);

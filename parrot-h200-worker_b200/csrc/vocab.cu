@@ -17,7 +17,8 @@
 // embedding is a parameter; only h comes from the previous kernel).  A warp's
 // 4 x NT dots are folded by one warp_reduce_many; the per-CTA best (value,
 // row) per token goes to a partial table and the last CTA to finish reduces
-// the table, in CTA order, to the token ids.
+// the table to the token ids (the lowest row among equal values, whatever the
+// order of the reduction).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -152,17 +153,35 @@ __global__ void __launch_bounds__(32 * kVocabWarps) vocab_argmax_kernel(VocabArg
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // warp w reduces tokens w, w + 4, ...: lanes stride over the CTAs
-  for (int t = warp; t < B; t += kVocabWarps) {
-    Best b{-INFINITY, 0x7fffffff};
-    for (int c = lane; c < (int)gridDim.x; c += 32) {
-      const float v = __ldcg(a.partial_value + (size_t)c * NT + t);
-      const int i = __ldcg(a.partial_index + (size_t)c * NT + t);
-      if (better(v, i, b.v, b.i)) b = Best{v, i};
+  // The last CTA reduces the partials token by token: each thread loads its
+  // share of the CTAs' entries at once (a chain of dependent L2 loads per lane
+  // was this kernel's tail), then shuffles and one shared-memory join.
+  constexpr int kPer = kVocabMaxGrid / (32 * kVocabWarps);
+  for (int t = 0; t < B; ++t) {
+    float v[kPer];
+    int ix[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int c = threadIdx.x + k * (32 * kVocabWarps);
+      const bool in = c < (int)gridDim.x;
+      v[k] = in ? __ldcg(a.partial_value + (size_t)c * NT + t) : -INFINITY;
+      ix[k] = in ? __ldcg(a.partial_index + (size_t)c * NT + t) : 0x7fffffff;
     }
+    Best b{v[0], ix[0]};
+#pragma unroll
+    for (int k = 1; k < kPer; ++k)
+      if (better(v[k], ix[k], b.v, b.i)) b = Best{v[k], ix[k]};
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) b = shfl_best(b, m);
-    if (lane == 0) a.out[t] = b.i;
+    if (lane == 0) warp_best[warp][0] = b;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      Best r = warp_best[0][0];
+      for (int w = 1; w < kVocabWarps; ++w)
+        if (better(warp_best[w][0].v, warp_best[w][0].i, r.v, r.i)) r = warp_best[w][0];
+      a.out[t] = r.i;
+    }
+    __syncthreads();
   }
 }
 
@@ -196,15 +215,38 @@ __global__ void __launch_bounds__(512) argmax_rows_kernel(ArgmaxRowsArgs a) {
   }
 }
 
-int launch_vocab_argmax(const VocabArgmaxArgs& a, int grid, cudaStream_t stream) {
+// Grid: as many CTAs as fit on every SM at once (register-bound: 4 per SM at
+// one token row, fewer at eight), up to kVocabMaxGrid; a grid of two CTAs per
+// SM kept a third of the HBM bandwidth busy at one row (ncu: 12% of warp
+// slots active).
+template <int NT, int NV>
+static int launch_vocab_nt(const VocabArgmaxArgs& a, int sms, cudaStream_t stream) {
+  const size_t smem = (size_t)NT * a.dim * sizeof(float);
+  static int cached[64] = {};  // CTAs per SM, per device (smem is at most 8 x 1024 floats)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  int per_sm = cached[dev];
+  if (per_sm == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, vocab_argmax_kernel<NT, NV>, 32 * kVocabWarps,
+            (size_t)NT * 1024 * sizeof(float)) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    cached[dev] = per_sm;
+  }
+  int grid = sms * per_sm;
+  if (grid > kVocabMaxGrid) grid = kVocabMaxGrid;
+  return launch_pdl(vocab_argmax_kernel<NT, NV>, dim3(grid), dim3(32 * kVocabWarps), smem, stream,
+                    a) == cudaSuccess
+             ? 0
+             : -1;
+}
+
+int launch_vocab_argmax(const VocabArgmaxArgs& a, int sms, cudaStream_t stream) {
   const int nt = a.rows <= 1 ? 1 : a.rows <= 2 ? 2 : a.rows <= 4 ? 4 : 8;
-  const size_t smem = (size_t)nt * a.dim * sizeof(float);
-  const dim3 g(grid), blk(32 * kVocabWarps);
   const int nv = (a.dim + 255) / 256;
-#define PARROT_VOCAB_CASE(NT, NV)                                                              \
-  if (nt == NT && nv == NV)                                                                    \
-    return launch_pdl(vocab_argmax_kernel<NT, NV>, g, blk, smem, stream, a) == cudaSuccess ? 0 \
-                                                                                           : -1;
+#define PARROT_VOCAB_CASE(NT, NV) \
+  if (nt == NT && nv == NV) return launch_vocab_nt<NT, NV>(a, sms, stream);
 #define PARROT_VOCAB_NV(NV) \
   PARROT_VOCAB_CASE(1, NV) PARROT_VOCAB_CASE(2, NV) PARROT_VOCAB_CASE(4, NV) PARROT_VOCAB_CASE(8, NV)
   PARROT_VOCAB_NV(1)

@@ -6,7 +6,9 @@
 ``--tokens T`` runs ``iters`` eager calls of one Parrot XL MoE block (seeded
 weights ~N(0, 0.02), x ~ N(0, 1)); each call launches route, group,
 gate_up GEMM, down GEMM and combine, in that order.  ``--forward`` runs
-``iters`` eager Parrot XL forwards on 1 x 512 ids.  ``--norms ROWS`` runs
+``iters`` eager Parrot XL forwards on 1 x 512 ids.  ``--vocab B`` runs ``iters``
+greedy next-token calls (the tied LM head fused with the argmax) for B rows
+over the 32768 x 768 embedding.  ``--norms ROWS`` runs
 ``iters`` rounds of RMSNorm, then the depth mix over 4 and over 8 sources
 (each with the consumer RMSNorm), on [ROWS, 768] bf16 rows.  Device memory stays under
 2 GB, so ``ncu`` captures of these commands end in seconds.
@@ -61,6 +63,17 @@ def norms(rows: int, iters: int) -> None:
     torch.cuda.synchronize()
 
 
+def vocab(rows: int, iters: int) -> None:
+    from parrot_b200 import bridge
+    g = torch.Generator().manual_seed(0)
+    w = (0.02 * torch.randn(32768, 768, generator=g)).to("cuda", torch.bfloat16)
+    h = torch.randn(rows, 1, 768, generator=g).to("cuda", torch.bfloat16)
+    with torch.inference_mode():
+        for _ in range(iters):
+            bridge.b200_vocab_argmax(h, w)
+    torch.cuda.synchronize()
+
+
 def forward(iters: int) -> None:
     torch.manual_seed(0)
     model = Parrot(ModelConfig()).to("cuda", torch.bfloat16).eval()
@@ -78,8 +91,11 @@ def main() -> None:
     p.add_argument("--forward", action="store_true")
     p.add_argument("--zipf", action="store_true", help="Zipf(1.2) router bias (overflow path)")
     p.add_argument("--norms", type=int, default=0, help="rows for the RMSNorm / depth-mix workload")
+    p.add_argument("--vocab", type=int, default=0, help="rows for the fused LM-head argmax")
     a = p.parse_args()
-    if a.norms:
+    if a.vocab:
+        vocab(a.vocab, a.iters)
+    elif a.norms:
         norms(a.norms, a.iters)
     elif a.forward:
         forward(a.iters)
