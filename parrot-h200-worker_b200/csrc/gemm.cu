@@ -98,7 +98,7 @@ struct __align__(16) SmemTail {
   int stride;           // (CTAs, or CTA pairs, sharing that round-robin)
   int n_secondary;      // and how many such units exist
   alignas(16) int unit_dst[BN];  // plain-mode scatter: destination row of each token row
-  alignas(16) float unit_w[BN];  // and its route weight (read as 16-byte vectors)
+  alignas(16) uint16_t unit_wb[BN];  // and its route weight in bf16 (read as pairs)
   int prefix[kSegMax + 2];
   int seg_rows[kSegMax];
   int seg_base[kSegMax];
@@ -521,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         epi_bar();  // the previous unit's stores are done with these arrays
         for (int i = et; i < un.valid; i += 32 * kEpiWarps) {
           t.unit_dst[i] = __ldg(g.row_dst + un.x_row + i);
-          t.unit_w[i] = round_bf16(__ldg(g.row_w + un.x_row + i));
+          t.unit_wb[i] = __bfloat16_as_ushort(__float2bfloat16_rn(__ldg(g.row_w + un.x_row + i)));
         }
         epi_bar();
       }
@@ -549,9 +549,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             SiluFast s1 = silu_bf16_fast((uint16_t)(gb >> 16));
             if (!s0.exact) s0.bits = __bfloat16_as_ushort(silu_lut[gb & 0xFFFFu]);
             if (!s1.exact) s1.bits = __bfloat16_as_ushort(silu_lut[gb >> 16]);
-            hp[j] = pack_bf16x2(__uint_as_float((uint32_t)s0.bits << 16) * __uint_as_float(ub << 16),
-                                   __uint_as_float((uint32_t)s1.bits << 16) *
-                                       __uint_as_float(ub & 0xFFFF0000u));
+            // bf16(silu * up): both factors are bf16, their product is exact
+            // in fp32, so one bf16x2 multiply rounds it the same way
+            hp[j] = mul_bf16x2((uint32_t)s0.bits | ((uint32_t)s1.bits << 16), ub);
           }
           // tile: 32 tokens x 16 features (32-byte rows, the 16-byte half
           // swizzled by bit 2 of the token so the 8 rows of a matrix hit
@@ -577,19 +577,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t yp[16];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            float y0 = __uint_as_float(r[4 * j]), y1 = __uint_as_float(r[4 * j + 1]);
-            float y2 = __uint_as_float(r[4 * j + 2]), y3 = __uint_as_float(r[4 * j + 3]);
+            yp[2 * j] = pack_bf16x2(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]));
+            yp[2 * j + 1] =
+                pack_bf16x2(__uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
             if (scatter) {
-              // routed contribution bf16(bf16(y) * bf16(w)) of each token
+              // routed contribution bf16(bf16(y) * bf16(w)) of each token: the
+              // product of two bf16 values is exact in fp32, so one bf16x2
+              // multiply (rounded once) equals the fp32 multiply then rounding
               const int tok = c * kChunk + 8 * (j & 3) + 2 * tq;
-              const float2 w = *reinterpret_cast<const float2*>(t.unit_w + tok);
-              y0 = round_bf16(y0) * w.x;
-              y1 = round_bf16(y1) * w.y;
-              y2 = round_bf16(y2) * w.x;
-              y3 = round_bf16(y3) * w.y;
+              const uint32_t w = *reinterpret_cast<const uint32_t*>(t.unit_wb + tok);
+              yp[2 * j] = mul_bf16x2(yp[2 * j], w);
+              yp[2 * j + 1] = mul_bf16x2(yp[2 * j + 1], w);
             }
-            yp[2 * j] = pack_bf16x2(y0, y1);
-            yp[2 * j + 1] = pack_bf16x2(y2, y3);
           }
           // tile: 32 tokens x 32 features (64-byte rows, 16-byte quarters
           // swizzled by bits 1-2 of the token); quarter 2h + ab

@@ -209,6 +209,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// Lane-wise bf16 product of two packed pairs, rounded to nearest even once.
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // 16 consecutive TMEM columns of this warp's 32 lanes (one register each).
 __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&r)[16]) {
   asm volatile(

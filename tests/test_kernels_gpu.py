@@ -495,6 +495,52 @@ def test_zipf_skew_overflow_matches_oracle():
     assert_bf16_close(out, exp, "zipf")
 
 
+PARTNER_BIAS = [0.9, 0.6, 0.45, 0.3, 0.15] + [0.0] * 11
+
+
+def _primary_partners(counts, capacity: int, bn: int) -> set:
+    """Which primary-partner cases the grouped GEMM meets (its rule, restated):
+    1 = expert e's capacity segment has exactly two token tiles, 2 = it has one
+    and its overflow fits one."""
+    kinds = set()
+    for c in counts:
+        rows, over = (min(c, capacity), max(c - capacity, 0)) if capacity > 0 else (c, 0)
+        if rows > bn:
+            kinds.add(1 if rows <= 2 * bn else 0)
+        else:
+            kinds.add(2 if 0 < over <= bn else 0)
+    return kinds
+
+
+@pytest.mark.parametrize("tokens,capacity,kinds", [
+    (512, 0, {2}), (512, 96, {2}), (512, 200, {1}), (512, -1, {1}),
+    (4096, 200, {2}), (4096, 384, {1}),
+])
+def test_gemm_primary_partner_tiles(tokens, capacity, kinds):
+    """A primary CTA takes the expert's second token tile, or its overflow
+    segment, into its own K loop (the other TMEM accumulator).  Skewed routing
+    at T = 512 (128-token tiles) and T = 4096 (256-token tiles of the down
+    GEMM) under capacities that produce both kinds: the output matches the
+    oracle and is bit-identical across capacities (the same products, tiled
+    differently)."""
+    cfg = moe_config()
+    prod, orc = build_moe_pair(cfg, seed=4)
+    x = hidden_states(tokens, cfg.dim, seed=6)
+    bias = torch.tensor(PARTNER_BIAS)
+    prod.router_bias = bias.cuda()
+    orc.router_bias = bias
+    out, ex, _, layout = call_moe_forward(prod, x.cuda(), capacity=capacity)
+    assert ex["status"][0] == 0, ex["status"]
+    bn = 256 if 2 * tokens >= 4096 else 128  # the launch's token tile
+    got = _primary_partners(ex["counts"].cpu().tolist(), layout.capacity if capacity != -1 else 0,
+                            bn)
+    assert kinds <= got, (got, ex["counts"].cpu().tolist())
+    exp, _, _ = orc(x.float())
+    assert_bf16_close(out, exp, f"partner tiles T={tokens} C={capacity}")
+    packed, _, _, _ = call_moe_forward(prod, x.cuda(), capacity=-1 if capacity != -1 else 0)
+    assert torch.equal(out, packed)
+
+
 def test_residual_is_fused_into_combine():
     cfg = moe_config()
     prod, orc = build_moe_pair(cfg, seed=2)
