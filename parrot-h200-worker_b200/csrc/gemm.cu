@@ -160,9 +160,14 @@ __device__ __forceinline__ Unit routed_unit(const GemmArgs& g, const SmemTail<BN
 //                                     major), then the shared expert's tiles
 // A unit covers kMPerUnit weight tiles: on a CTA pair, M unit u is tiles
 // 2u (rank 0) and 2u + 1 (rank 1), and this CTA loads and stores its own.
+// seg: the caller's segment cursor (0 before its first call, k increasing):
+// j grows with k, so the segment search resumes where the last one stopped
+// (from segment 0 each time it was up to 32 dependent shared-memory loads
+// per unit, on the critical path of the producer, the MMA issuer and the
+// epilogue alike).
 template <int BN, bool PAIR>
 __device__ __forceinline__ bool cta_unit(int k, const GemmArgs& g, const SmemTail<BN, PAIR>& t,
-                                         Unit& r, int crank) {
+                                         Unit& r, int crank, int& seg) {
   constexpr int MD = GemmCfg<BN, PAIR>::kMPerUnit;
   const int MT = g.m_tiles_routed;
   if (t.has_primary) {
@@ -178,8 +183,9 @@ __device__ __forceinline__ bool cta_unit(int k, const GemmArgs& g, const SmemTai
   const int n_routed = t.prefix[g.n_seg];
   if (j < n_routed) {
     const bool prim = primaries_on<PAIR>(g);
-    int s = 0;
+    int s = seg;
     while (t.prefix[s + 1] <= j) ++s;
+    seg = s;
     const int local = j - t.prefix[s];
     const int n_tiles = secondary_tiles<BN>(s, t.seg_rows[s], prim, g.n_experts);
     const int mu = local / n_tiles;
@@ -405,7 +411,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t issued = 0, issued_phase = 0;  // per-stage bits
       bool ok = true;
       Unit un;
-      for (int k = 0; ok && cta_unit<BN, PAIR>(k, g, t, un, crank); ++k) {
+      int seg = 0;
+      for (int k = 0; ok && cta_unit<BN, PAIR>(k, g, t, un, crank, seg); ++k) {
         const CUtensorMap* mw = un.routed ? &tm_w_routed : &tm_w_shared;
         const CUtensorMap* mx = un.routed ? &tm_x_routed : &tm_x_shared;
         // this CTA's token rows of the tile: all of them, or on a pair its
@@ -462,7 +469,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       Unit un;
-      for (int k = 0; ok && cta_unit<BN, PAIR>(k, g, t, un, crank); ++k) {
+      int seg = 0;
+      for (int k = 0; ok && cta_unit<BN, PAIR>(k, g, t, un, crank, seg); ++k) {
         if (!mbar_wait(&t.tempty[acc], acc_phase ^ 1, abort_flag, g.status, 20)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * BN;
@@ -514,7 +522,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     Unit un;
-    for (int k = 0; cta_unit<BN, PAIR>(k, g, t, un, crank); ++k) {
+    int seg = 0;
+    for (int k = 0; cta_unit<BN, PAIR>(k, g, t, un, crank, seg); ++k) {
       const bool scatter = g.mode == kGemmPlain && un.routed && g.row_dst != nullptr;
       if (scatter) {
         // per-row destination and weight, fetched while the MMAs run
