@@ -295,7 +295,16 @@ int parrot_moe_forward_deferred_bf16(const parrot_moe_dims* dims,
  * runs from its grouping on with parrot_moe_forward_routed_bf16.  One launch
  * instead of a depth mix and a router launch.  The logits' summation order
  * differs from the router kernel's: expert ids follow this call's own
- * probabilities. */
+ * probabilities.
+ * Slot mode, when dims->capacity >= 2 * dims->tokens (no expert can
+ * overflow its region): this call also does the grouping.  Each assignment
+ * takes the next slot of its expert from a per-expert counter kept in the
+ * workspace's zeroed status region, and its row, position, contribution slot
+ * and route weight are written there and then; the group kernel does not
+ * run.  Rows of one expert are in no particular order within its region
+ * (positions say where each went; the block output does not depend on it).
+ * The call must be followed by parrot_moe_forward_routed_bf16 on the same
+ * workspace, which reads the counters and leaves them zero. */
 int parrot_depthmix_route_bf16(void* out, const void* const* sources, int n_sources,
                                const void* query, const void* key_norm_weight, float key_eps,
                                const void* out_norm_weight, float out_eps, void* mix_out,
@@ -309,7 +318,10 @@ int parrot_depthmix_route_bf16(void* out, const void* const* sources, int n_sour
  * grouping, experts and (deferred == 0) the combine, as
  * parrot_moe_forward_bf16 / (deferred != 0) parrot_moe_forward_deferred_bf16
  * from their grouping on.  outputs->probs / indices / weights must be NULL
- * (the routing call writes them). */
+ * (the routing call writes them).  In slot mode (above) the grouping was done
+ * by the routing call: the GEMMs take the expert counters as their segments,
+ * the down projection writes counts, statistics and positions and zeroes the
+ * counters. */
 int parrot_moe_forward_routed_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
                                    const void* x, const parrot_moe_outputs* outputs, int deferred,
                                    void* workspace, size_t workspace_bytes, void* stream);

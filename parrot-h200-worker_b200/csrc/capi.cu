@@ -158,8 +158,9 @@ int layout_of(const parrot_moe_dims* d, parrot_moe_layout* L) {
     off = align256(off + bytes);
     return at;
   };
-  // the status word first: the region parrot_moe_workspace_init zeroes
-  L->status = take(16);
+  // the status word first, then the slot-mode counters [E] and ticket: the
+  // region parrot_moe_workspace_init zeroes
+  L->status = take(16 + 4 * (E + 1));
   L->indices = take(A * 4);
   L->weights = take(A * 4);
   L->positions = take(A * 4);
@@ -287,6 +288,17 @@ int run_group(const parrot_moe_dims* dims, const void* x, const parrot_moe_outpu
   return check_launch("group_kernel");
 }
 
+// Slot mode: the routing depth mix does the grouping too (an atomic slot per
+// assignment, the rows written straight to their grouped rows), and the
+// routed block that follows reads the per-expert counters as its segments and
+// zeroes them.  Chosen by a capacity that no expert can overflow (C >= 2T).
+bool slot_mode(const parrot_moe_dims* d, const parrot_moe_layout& L) {
+  return L.capacity >= 2 * d->tokens && d->tokens <= 4096;
+}
+int* slot_counters(void* ws, const parrot_moe_layout& L) {
+  return reinterpret_cast<int*>(static_cast<char*>(ws) + L.status + 16);  // [E], then the ticket
+}
+
 // Router + grouping.
 int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
               const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L, cudaStream_t s,
@@ -307,7 +319,7 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
 
 int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights* w,
              const void* x, void* ws, const parrot_moe_layout& L, cudaStream_t s,
-             bool shared_only = false) {
+             bool shared_only = false, const parrot_moe_outputs* slots = nullptr) {
   const int T = dims->tokens, D = dims->dim, E = dims->n_experts, H = dims->expert_dim,
             Hs = dims->shared_dim, R = L.grouped_rows;
   parrot::GemmArgs g{};
@@ -315,6 +327,27 @@ int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights*
   g.seg_base = at<int>(ws, L.seg_base);
   g.seg_expert = nullptr;
   g.n_seg = shared_only ? 0 : 2 * E;
+  if (slots != nullptr && !shared_only) {
+    // slot mode: one segment per expert, its rows counted by the depth mix
+    int* counters = slot_counters(ws, L);
+    g.seg_rows = counters;
+    g.seg_stride = L.capacity;
+    g.n_seg = E;
+    if (!swiglu) {  // the last reader zeroes them; CTA grid - 1 writes the statistics
+      g.slot_counts = counters;
+      g.slot_ticket = counters + E;
+      const parrot::MoeTables tab = tables(ws, L);
+      g.st.tile_probsum = tab.tile_probsum;
+      g.st.route_tiles = parrot::route_blocks(T);
+      g.st.tokens = T;
+      g.st.counts = tab.counts;
+      g.st.counts_out = slots->counts;
+      g.st.stats = tab.stats;
+      g.st.stats_out = slots->stats;
+      g.st.positions = at<int>(ws, L.positions);
+      g.st.positions_out = slots->positions;
+    }
+  }
   g.static_routed = shared_only ? 0 : 1;
   g.n_experts = E;
   g.shared_rows = T;
@@ -384,10 +417,10 @@ int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights*
 
 int run_experts(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
                 const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L,
-                cudaStream_t s, bool combine = true) {
-  int rc = run_gemm(true, dims, w, x, ws, L, s);
+                cudaStream_t s, bool combine = true, bool slots = false) {
+  int rc = run_gemm(true, dims, w, x, ws, L, s, false, slots ? o : nullptr);
   if (rc) return rc;
-  if ((rc = run_gemm(false, dims, w, x, ws, L, s))) return rc;
+  if ((rc = run_gemm(false, dims, w, x, ws, L, s, false, slots ? o : nullptr))) return rc;
   if (!combine) return PARROT_OK;
   parrot::CombineArgs c{};
   c.contrib = at<__nv_bfloat16>(ws, L.contrib);
@@ -1049,6 +1082,14 @@ int parrot_depthmix_route_bf16(void* out, const void* const* sources, int n_sour
   parrot::DepthRouteArgs r{};
   r.router_w = static_cast<const __nv_bfloat16*>(weights->router);
   r.r = route_args(dims, weights, outputs, workspace, L);
+  if (slot_mode(dims, L)) {
+    r.slot_counts = slot_counters(workspace, L);
+    r.slot_stride = L.capacity;
+    r.grouped = at<__nv_bfloat16>(workspace, L.grouped);
+    r.positions = at<int>(workspace, L.positions);
+    r.row_dst = at<int>(workspace, L.row_dst);
+    r.row_w = at<float>(workspace, L.row_w);
+  }
   return depthmix_launch(out, sources, n_sources, query, key_norm_weight, key_eps,
                          out_norm_weight, out_eps, mix_out, a, rows, dim, stream, &r);
 }
@@ -1064,8 +1105,9 @@ int parrot_moe_forward_routed_bf16(const parrot_moe_dims* dims, const parrot_moe
                                "routing call%s");
   if (dims->tokens == 0) return PARROT_OK;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if ((rc = run_group(dims, x, outputs, workspace, L, s, nullptr, true))) return rc;
-  return run_experts(dims, weights, x, outputs, workspace, L, s, !deferred);
+  const bool slots = slot_mode(dims, L);  // the routing depth mix grouped the rows
+  if (!slots && (rc = run_group(dims, x, outputs, workspace, L, s, nullptr, true))) return rc;
+  return run_experts(dims, weights, x, outputs, workspace, L, s, !deferred, slots);
 }
 
 int parrot_moe_decode_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,

@@ -262,6 +262,62 @@ __global__ void silu_bf16_kernel(const uint16_t* __restrict__ x, uint16_t* __res
 
 
 
+// Slot mode: the counts, router statistics and positions copy that the
+// grouping kernel writes otherwise, by the epilogue warps of the last CTA
+// before its first unit (the segment table in shared memory holds the
+// counts).  Utilisation = count / 2T; aux = E * sum_e util_e * (probability
+// sum_e / T) with the probability sums added in the grouping kernel's order:
+// per (phase, expert) over every P-th router tile, P = 128 / E, then over the
+// phases.  scratch: 128 floats of the epilogue staging tiles, unused yet.
+template <int BN, bool PAIR>
+__device__ __forceinline__ void slot_stats(const GemmArgs& g, const SmemTail<BN, PAIR>& t,
+                                        float* scratch, int tid) {
+  const GemmArgs::SlotStats& st = g.st;
+  const int E = g.n_experts, P = 128 / E, A2 = 2 * st.tokens;
+  float ps = 0.f;
+  if (tid < P * E) {
+    constexpr int U = 16;  // sixteen tiles' loads in flight before their in-order sum
+    const int ex = tid % E;
+    for (int r0 = tid / E; r0 < st.route_tiles; r0 += U * P) {
+      float pv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int r = r0 + u * P;
+        pv[u] = r < st.route_tiles ? __ldcg(st.tile_probsum + (size_t)r * E + ex) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (r0 + u * P < st.route_tiles) ps += pv[u];
+    }
+  }
+  if (tid < 128) scratch[tid] = ps;
+  epi_bar();
+  float term = 0.f;
+  if (tid < E) {
+    float sum = 0.f;
+    for (int ph = 0; ph < P; ++ph) sum += scratch[ph * E + tid];
+    const int cnt = t.seg_rows[tid];
+    st.counts[tid] = cnt;
+    if (st.counts_out != nullptr) st.counts_out[tid] = cnt;
+    const float util = (float)cnt / (float)A2;
+    st.stats[tid] = util;
+    if (st.stats_out != nullptr) st.stats_out[tid] = util;
+    term = util * (sum / (float)st.tokens);
+  }
+  epi_bar();
+  if (tid < E) scratch[tid] = term;
+  epi_bar();
+  if (tid == 0) {
+    float aux = 0.f;
+    for (int x = 0; x < E; ++x) aux += scratch[x];
+    st.stats[E] = (float)E * aux;
+    if (st.stats_out != nullptr) st.stats_out[E] = (float)E * aux;
+  }
+  if (st.positions_out != nullptr)
+    for (int i = tid; i < A2; i += 32 * kEpiWarps) st.positions_out[i] = st.positions[i];
+  epi_bar();  // the staging tiles are the epilogue's again
+}
+
 template <int BN, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w_routed,
@@ -348,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (s < n_seg) {
       rows = g.seg_rows[s];
       t.seg_rows[s] = rows;
-      t.seg_base[s] = g.seg_base[s];
+      t.seg_base[s] = g.seg_stride > 0 ? s * g.seg_stride : g.seg_base[s];
       t.seg_expert[s] = g.seg_expert != nullptr ? g.seg_expert[s] : s % g.n_experts;
     }
     int incl =
@@ -397,6 +453,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     t.n_secondary = t.prefix[n_seg] +
                     ((g.shared_rows + BN - 1) / BN) * (g.m_tiles_shared / Cfg::kMPerUnit);
     griddep_launch();
+    // slot mode: this CTA has copied the counters; the last CTA to do so
+    // zeroes them for the next block (the kernels after this one start once
+    // it has completed)
+    if (g.slot_ticket != nullptr && atomicAdd(g.slot_ticket, 1) == (int)gridDim.x - 1) {
+      for (int e = 0; e < g.n_experts; ++e) g.slot_counts[e] = 0;
+      *g.slot_ticket = 0;
+    }
   }
   __syncthreads();
 
@@ -513,6 +576,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
+    if (g.st.stats != nullptr && blockIdx.x == gridDim.x - 1)
+      slot_stats(g, t, reinterpret_cast<float*>(epi_tiles), threadIdx.x - 64);
     const int q = warp & 3;                 // TMEM lane quarter of this warp
     const int half = (warp - 2) >> 2;       // which alternate chunks it takes
     const int et = threadIdx.x - 64;        // 0..255

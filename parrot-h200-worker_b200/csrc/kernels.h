@@ -69,6 +69,18 @@ struct RouteArgs {
 struct DepthRouteArgs {
   const __nv_bfloat16* router_w;  // [E, d]
   RouteArgs r;                    // tokens == the depth mix's rows
+  // Slot mode (slot_counts != null): the grouping done here too.  Each
+  // assignment takes the next slot of its expert from a per-expert counter
+  // (zero before the call), its row goes to grouped row e * slot_stride +
+  // slot with the position, contribution slot and route weight; the GEMMs
+  // read the counters as segment sizes.  Rows keep no order within an expert
+  // (the products do not depend on it).
+  int* slot_counts;               // [E]
+  int slot_stride;                // rows per expert region (>= 2T: no overflow)
+  __nv_bfloat16* grouped;
+  int* positions;                 // [2T]
+  int* row_dst;                   // [E * slot_stride]
+  float* row_w;
 };
 
 struct GroupArgs {
@@ -216,6 +228,25 @@ struct GemmArgs {
   int ld_out_shared;
   int mode;
   int* status;
+  // slot mode (the depth mix did the grouping): segment s has g.seg_rows[s]
+  // rows from row s * seg_stride (0: g.seg_base)
+  int seg_stride;
+  // slot mode, down GEMM: every CTA takes a ticket once it has read the
+  // counters; the last zeroes them for the next block (null: off)
+  int* slot_counts;
+  int* slot_ticket;
+  // slot mode, down GEMM, CTA grid - 1: the counts, statistics and
+  // positions copy the grouping kernel would have written (null: off)
+  struct SlotStats {
+    const float* tile_probsum;  // [route_tiles, E]
+    int route_tiles, tokens;
+    int* counts;                // [E] workspace copy
+    int* counts_out;            // or null
+    float* stats;               // [E + 1]
+    float* stats_out;           // or null
+    const int* positions;       // [2T]
+    int* positions_out;         // or null
+  } st;
 };
 
 // The MoE block at decode batch sizes (moe_decode.cu).

@@ -312,6 +312,7 @@ __global__ void __launch_bounds__(32 * W * R, (NS <= 8 && R == 1) ? 768 / (32 * 
   for (int w = 0; w < W; ++w) total += red_sq[ty][w];
   const float inv = rsqrtf(total / (float)dim + a.out_eps);
   float gb[8];  // the output as the bf16 tensor it is
+  uint4 ov = make_uint4(0, 0, 0, 0);
 #pragma unroll
   for (int j = 0; j < 8; ++j) gb[j] = 0.f;
   if (active) {
@@ -319,7 +320,7 @@ __global__ void __launch_bounds__(32 * W * R, (NS <= 8 && R == 1) ? 768 / (32 * 
     bf16x8_to_float(owv, g);
 #pragma unroll
     for (int j = 0; j < 8; ++j) g[j] = (h[j] * inv) * g[j];
-    const uint4 ov = float_to_bf16x8(g);
+    ov = float_to_bf16x8(g);
     reinterpret_cast<uint4*>(a.out + off)[c] = ov;
     bf16x8_to_float(ov, gb);
   }
@@ -329,6 +330,7 @@ __global__ void __launch_bounds__(32 * W * R, (NS <= 8 && R == 1) ? 768 / (32 * 
     __shared__ float red_r[R][W][NP];
     __shared__ float psum[R][NP];
     __shared__ int hist[NP];
+    __shared__ int slot_row[R][2];  // slot mode: the grouped rows of this row's two assignments
     const int E = ra.r.n_experts;
     if (ty == 0 && c < NP) hist[c] = 0;
     float pr[NP];
@@ -382,12 +384,31 @@ __global__ void __launch_bounds__(32 * W * R, (NS <= 8 && R == 1) ? 768 / (32 * 
         }
         atomicAdd(&hist[i1], 1);
         atomicAdd(&hist[i2], 1);
+        if (ra.slot_counts != nullptr) {
+          // the grouping: the next free slot of each expert, then the row's
+          // position, contribution slot (the lower expert id first) and weight
+          const int r1 = i1 * ra.slot_stride + atomicAdd(ra.slot_counts + i1, 1);
+          const int r2 = i2 * ra.slot_stride + atomicAdd(ra.slot_counts + i2, 1);
+          reinterpret_cast<int2*>(ra.positions)[row] = make_int2(r1, r2);
+          ra.row_dst[r1] = 2 * row + (i1 < i2 ? 0 : 1);
+          ra.row_dst[r2] = 2 * row + (i2 < i1 ? 0 : 1);
+          ra.row_w[r1] = w1;
+          ra.row_w[r2] = w2;
+          slot_row[ty][0] = r1;
+          slot_row[ty][1] = r2;
+        }
       }
       if (valid_t && valid_e && lane < NP && ra.r.probs != nullptr)
         ra.r.probs[(size_t)row * E + ex] = p;
       if (lane < NP) psum[ty][lane] = p;
     }
     __syncthreads();
+    if (ra.slot_counts != nullptr && active && row < a.rows) {
+      // this thread's 16 bytes of the row, into both grouped rows
+      const size_t nv = (size_t)nvec;
+      reinterpret_cast<uint4*>(ra.grouped)[(size_t)slot_row[ty][0] * nv + c] = ov;
+      reinterpret_cast<uint4*>(ra.grouped)[(size_t)slot_row[ty][1] * nv + c] = ov;
+    }
     if (ty == 0 && c < E) {
       float sum = 0.f;
 #pragma unroll

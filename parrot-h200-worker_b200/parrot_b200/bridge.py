@@ -234,6 +234,21 @@ def b200_vocab_argmax(hidden: Tensor, weight: Tensor) -> Tensor:
 FUSE_MOE_ROUTER = True
 
 
+# With the router folded in, the depth mix also groups the rows (slot mode of
+# parrot_depthmix_route_bf16: each assignment takes an atomic slot of its
+# expert and its row is written there), so the group kernel does not run.
+# It needs a capacity no expert can overflow (2 T rows per expert region),
+# taken up to SLOT_GROUPING_MAX_TOKENS.
+SLOT_GROUPING = True
+SLOT_GROUPING_MAX_TOKENS = 1024
+
+
+def _route_dims(cfg, rows: int) -> _lib.MoeDims:
+    """The MoE dims of a block whose router runs inside the depth mix."""
+    slots = SLOT_GROUPING and rows <= SLOT_GROUPING_MAX_TOKENS
+    return moe_dims(cfg, rows, 2 * rows if slots else 0)
+
+
 def _routes_in_mix(route, rows: int) -> bool:
     """Whether the mix producing ``route``'s (an MoE module's, or None) input of
     ``rows`` tokens also routes it: the grouped-GEMM path up to 4096 tokens
@@ -275,7 +290,7 @@ def _depth_call(module, sources: Sequence[Tensor], output_norm, pending_delta: T
     oe = 0.0 if output_norm is None else float(output_norm.eps)
     if output_norm is not None and _routes_in_mix(route, rows):
         # the mix is the MoE block's input: route it in the same launch
-        dims = moe_dims(route.cfg, rows)
+        dims = _route_dims(route.cfg, rows)
         ws = workspace(first.device, dims)
         wst = _weights_struct(pack_weights(route), _router_bias(route))
         outputs = _lib.MoeOutputs(None, None, None, None, None, None, None, None)
@@ -407,14 +422,29 @@ def workspace_layout(dims: _lib.MoeDims) -> _lib.MoeLayout:
     return layout
 
 
+def _ws_key(device: torch.device, dims: _lib.MoeDims) -> tuple:
+    return (device.index if device.index is not None else torch.cuda.current_device(),
+            dims.tokens, dims.dim, dims.n_experts, dims.expert_dim, dims.shared_dim,
+            dims.capacity)
+
+
+def _routed_workspace(device: torch.device, cfg, tokens: int, flat: Tensor):
+    """(dims, workspace) of a block whose input ``flat`` a depth mix routed,
+    or None when it was not routed there (the marker is consumed)."""
+    dims = _route_dims(cfg, tokens)
+    ws = _WORKSPACES.get(_ws_key(device, dims))
+    if ws is None or ws.__dict__.get("_b200_fused_route") != flat.data_ptr():
+        return None
+    del ws.__dict__["_b200_fused_route"]
+    return dims, workspace(device, dims)
+
+
 def workspace(device: torch.device, dims: _lib.MoeDims) -> Tensor:
     """Zero-initialised workspace shared by all MoE layers of one shape on ``device``.
 
     Calls that share a workspace must be ordered on one stream.
     """
-    key = (device.index if device.index is not None else torch.cuda.current_device(),
-           dims.tokens, dims.dim, dims.n_experts, dims.expert_dim, dims.shared_dim,
-           dims.capacity)
+    key = _ws_key(device, dims)
     ws = _WORKSPACES.get(key)
     if ws is None:
         layout = workspace_layout(dims)
@@ -516,8 +546,11 @@ def b200_moe(module, flat: Tensor, collect_stats: bool, addend: Tensor | None = 
     T, d = flat.shape
     cfg = module.cfg
     packed = pack_weights(module)
-    dims = moe_dims(cfg, T)
-    ws = workspace(flat.device, dims)
+    fused = _routed_workspace(flat.device, cfg, T, flat)
+    routed = fused is not None
+    dims, ws = fused if routed else (moe_dims(cfg, T), None)
+    if ws is None:
+        ws = workspace(flat.device, dims)
     out = torch.empty_like(flat)
     if addend is not None:
         addend = addend.reshape(T, d).contiguous()
@@ -529,8 +562,7 @@ def b200_moe(module, flat: Tensor, collect_stats: bool, addend: Tensor | None = 
                               None, None, None, None, None,
                               None if stats is None else stats.data_ptr())
     weights = _weights_struct(packed, bias)
-    routed = ws.__dict__.pop("_b200_fused_route", None) == flat.data_ptr()
-    if stats is None and 0 < T <= DECODE_MOE_MAX_TOKENS and cfg.expert_dim <= 1024:
+    if stats is None and 0 < T <= DECODE_MOE_MAX_TOKENS and cfg.expert_dim <= 1024 and not routed:
         # decode batch sizes: the two-kernel small-batch path
         _lib.check(_lib.load().parrot_moe_decode_bf16(
             ctypes.byref(dims), ctypes.byref(weights), _p(flat), ctypes.byref(outputs),
@@ -571,8 +603,10 @@ def b200_moe_deferred(module, flat: Tensor, collect_stats: bool, addend: Tensor 
         out, aux, util = b200_moe(module, flat, collect_stats, addend)
         return out.view(shape), aux, util
     packed = pack_weights(module)
-    dims = moe_dims(cfg, T)
-    ws = workspace(flat.device, dims)
+    fused = _routed_workspace(flat.device, cfg, T, flat)
+    dims, ws = fused if fused is not None else (moe_dims(cfg, T), None)
+    if ws is None:
+        ws = workspace(flat.device, dims)
     if addend is not None:
         addend = addend.reshape(T, d).contiguous()
         _require_device(addend, "MoE")
@@ -581,7 +615,7 @@ def b200_moe_deferred(module, flat: Tensor, collect_stats: bool, addend: Tensor 
     outputs = _lib.MoeOutputs(None, None, None, None, None, None, None,
                               None if stats is None else stats.data_ptr())
     wst = _weights_struct(packed, _router_bias(module))
-    if ws.__dict__.pop("_b200_fused_route", None) == flat.data_ptr():
+    if fused is not None:
         _lib.check(_lib.load().parrot_moe_forward_routed_bf16(
             ctypes.byref(dims), ctypes.byref(wst), _p(flat), ctypes.byref(outputs), 1, _p(ws),
             ws.numel(), _stream()), "parrot_moe_forward_routed_bf16")

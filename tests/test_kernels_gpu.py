@@ -686,14 +686,19 @@ def test_vocab_argmax_is_repeatable_and_graph_capturable():
 # ---------------------------------------------------------------------------
 # The router folded into the depth mix that produces the MoE input
 # ---------------------------------------------------------------------------
-@pytest.mark.parametrize("rows,n_sources,pending", [(512, 6, True), (37, 3, False),
-                                                    (4096, 9, True), (9, 1, False)])
-def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending):
+@pytest.mark.parametrize("rows,n_sources,pending,slots", [
+    (512, 6, True, False), (37, 3, False, False), (4096, 9, True, False), (9, 1, False, False),
+    (512, 6, True, True), (37, 3, False, True), (1024, 9, True, True), (9, 1, False, True)])
+def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending, slots):
     """parrot_depthmix_route_bf16 + parrot_moe_forward_routed_bf16 against
     parrot_depthmix_bf16 + parrot_moe_forward_bf16: the mix is bit-identical;
     expert ids agree wherever the router's top-2 / top-3 probability margin
     exceeds 1e-5 and equal top-2 of the fused call's own probabilities; the
-    block output is identical on every token routed alike."""
+    block output is identical on every token routed alike.  Slot mode
+    (capacity 2T: the depth mix groups the rows itself, no group kernel):
+    each expert's positions fill its region, every grouped row holds its
+    token's row, counts and statistics equal the grouping kernel's, and a
+    second call (the counters were left at zero) gives the same output."""
     cfg = moe_config()
     module, _ = build_moe_pair(cfg, seed=31)
     dim = cfg.dim
@@ -707,17 +712,20 @@ def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending
     lib = _lib.load()
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     ptrs = (ctypes.c_void_p * n_sources)(*[s.data_ptr() for s in srcs])
-    dims = bridge.moe_dims(cfg, rows)
     w = bridge._weights_struct(bridge.pack_weights(module), None)
     results = {}
     for fused in (False, True):
+        dims = bridge.moe_dims(cfg, rows, 2 * rows if (fused and slots) else 0)
         out = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16)
         pend_out = torch.empty_like(out) if pending else None
-        ws = torch.zeros(int(bridge.workspace_layout(dims).total), device="cuda",
-                         dtype=torch.uint8)
+        layout = bridge.workspace_layout(dims)
+        ws = torch.zeros(int(layout.total), device="cuda", dtype=torch.uint8)
         probs = torch.empty(rows, cfg.n_experts, device="cuda")
         idx = torch.empty(rows, 2, device="cuda", dtype=torch.int64)
         y = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16)
+        pos = torch.full((2 * rows,), -1, device="cuda", dtype=torch.int32)
+        counts = torch.full((cfg.n_experts,), -1, device="cuda", dtype=torch.int32)
+        stats = torch.full((cfg.n_experts + 1,), float("nan"), device="cuda")
         args = (ctypes.c_void_p(out.data_ptr()), ptrs, n_sources, ctypes.c_void_p(query.data_ptr()),
                 ctypes.c_void_p(key_w.data_ptr()), 1e-6, ctypes.c_void_p(out_w.data_ptr()), 1e-6,
                 None, bridge._p(srcs[-1] if pending else None), bridge._p(delta),
@@ -728,7 +736,8 @@ def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending
             _lib.check(lib.parrot_depthmix_route_bf16(
                 *args, ctypes.byref(dims), ctypes.byref(w), ctypes.byref(ro),
                 ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream), "depthmix_route")
-            mo = _lib.MoeOutputs(y.data_ptr(), None, None, None, None, None, None, None)
+            mo = _lib.MoeOutputs(y.data_ptr(), None, None, None, None, pos.data_ptr(),
+                                 counts.data_ptr(), stats.data_ptr())
             _lib.check(lib.parrot_moe_forward_routed_bf16(
                 ctypes.byref(dims), ctypes.byref(w), ctypes.c_void_p(out.data_ptr()),
                 ctypes.byref(mo), 0, ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream),
@@ -736,7 +745,7 @@ def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending
         else:
             _lib.check(lib.parrot_depthmix_bf16(*args, stream), "depthmix")
             mo = _lib.MoeOutputs(y.data_ptr(), None, probs.data_ptr(), idx.data_ptr(), None,
-                                 None, None, None)
+                                 pos.data_ptr(), counts.data_ptr(), stats.data_ptr())
             _lib.check(lib.parrot_moe_forward_bf16(
                 ctypes.byref(dims), ctypes.byref(w), ctypes.c_void_p(out.data_ptr()),
                 ctypes.byref(mo), ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream),
@@ -748,6 +757,33 @@ def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending
         assert list(status) == [0, 0, 0, 0]
         results[fused] = (out.clone(), None if pend_out is None else pend_out.clone(),
                           probs.cpu(), idx.cpu(), y.clone())
+        if fused and slots:
+            C = layout.capacity
+            cnt, pos_c, idx_c = counts.cpu(), pos.cpu().long(), idx.cpu().flatten()
+            assert C >= 2 * rows and int(cnt.sum()) == 2 * rows
+            assert torch.equal(cnt, torch.bincount(idx_c, minlength=cfg.n_experts).int())
+            for e in range(cfg.n_experts):
+                got = torch.sort(pos_c[idx_c == e]).values
+                assert torch.equal(got, e * C + torch.arange(int(cnt[e]))), e
+            grouped = workspace_view(ws, layout, "grouped", torch.bfloat16,
+                                     (layout.grouped_rows, dim)).cpu()
+            assert torch.equal(grouped[pos_c], out.cpu()[torch.arange(2 * rows) // 2])
+            util = cnt.float() / (2 * rows)
+            assert torch.equal(stats.cpu()[:-1], util)
+            aux = cfg.n_experts * float((util * probs.cpu().mean(0)).sum())
+            assert abs(float(stats[-1]) - aux) <= 1e-5 * max(1.0, abs(aux))
+            # the counters were left at zero: the same call again gives the same block
+            y_first = y.clone()
+            _lib.check(lib.parrot_depthmix_route_bf16(
+                *args, ctypes.byref(dims), ctypes.byref(w), ctypes.byref(ro),
+                ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream), "depthmix_route")
+            _lib.check(lib.parrot_moe_forward_routed_bf16(
+                ctypes.byref(dims), ctypes.byref(w), ctypes.c_void_p(out.data_ptr()),
+                ctypes.byref(mo), 0, ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream),
+                "moe_forward_routed")
+            torch.cuda.synchronize()
+            assert torch.equal(y, y_first)
+            assert torch.equal(counts.cpu(), cnt)
     (o0, p0, pr0, i0, y0), (o1, p1, pr1, i1, y1) = results[False], results[True]
     assert torch.equal(o0, o1)
     if pending:
