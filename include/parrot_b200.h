@@ -184,7 +184,9 @@ typedef struct parrot_moe_dims {
   int shared_dim;  /* Hs, % 64 == 0 */
   int capacity;    /* slots per expert; 0 selects parrot_moe_capacity();
                       -1 packs all rows per expert, experts in id order (no capacity
-                      region: the expert-parallel send layout) */
+                      region: the expert-parallel send layout); -2 slot mode (up to
+                      4096 tokens): a region of 2T rows per expert that the router
+                      fills itself, see parrot_depthmix_route_bf16 */
 } parrot_moe_dims;
 
 /* Expert weights start in torch.nn.Linear [out, in] layout and are packed
@@ -296,8 +298,8 @@ int parrot_moe_forward_deferred_bf16(const parrot_moe_dims* dims,
  * instead of a depth mix and a router launch.  The logits' summation order
  * differs from the router kernel's: expert ids follow this call's own
  * probabilities.
- * Slot mode, when dims->capacity >= 2 * dims->tokens (no expert can
- * overflow its region): this call also does the grouping.  Each assignment
+ * Slot mode, when dims->capacity == -2 (every expert a region of 2T rows,
+ * which it cannot overflow): this call also does the grouping.  Each assignment
  * takes the next slot of its expert from a per-expert counter kept in the
  * workspace's zeroed status region, and its row, position, contribution slot
  * and route weight are written there and then; the group kernel does not
@@ -321,7 +323,9 @@ int parrot_depthmix_route_bf16(void* out, const void* const* sources, int n_sour
  * (the routing call writes them).  In slot mode (above) the grouping was done
  * by the routing call: the GEMMs take the expert counters as their segments,
  * the down projection writes counts, statistics and positions and zeroes the
- * counters. */
+ * counters.  parrot_moe_forward_bf16 / _deferred_bf16 / _static_bf16 with
+ * dims->capacity == -2 run slot mode with their own router kernel (no group
+ * kernel; positions in no particular order within an expert). */
 int parrot_moe_forward_routed_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
                                    const void* x, const parrot_moe_outputs* outputs, int deferred,
                                    void* workspace, size_t workspace_bytes, void* stream);

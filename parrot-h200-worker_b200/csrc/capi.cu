@@ -134,7 +134,7 @@ int validate_dims(const parrot_moe_dims* d) {
     return fail(PARROT_EINVAL, "expert_dim must be a positive multiple of 64%s");
   if (d->shared_dim <= 0 || d->shared_dim % 64)
     return fail(PARROT_EINVAL, "shared_dim must be a positive multiple of 64%s");
-  if (d->capacity < -1) return fail(PARROT_EINVAL, "capacity must be >= -1%s");
+  if (d->capacity < -2) return fail(PARROT_EINVAL, "capacity must be >= -2%s");
   return PARROT_OK;
 }
 
@@ -144,10 +144,12 @@ int layout_of(const parrot_moe_dims* d, parrot_moe_layout* L) {
   std::memset(L, 0, sizeof(*L));
   const size_t T = d->tokens, D = d->dim, E = d->n_experts, H = d->expert_dim,
                Hs = d->shared_dim;
-  // capacity 0 selects the default; -1 packs every row per expert (no capacity region)
-  const int C = d->capacity > 0    ? d->capacity
-                : d->capacity == 0 ? parrot_moe_capacity(d->tokens, d->n_experts)
-                                   : 0;
+  // capacity 0 selects the default; -1 packs every row per expert (no capacity
+  // region); -2 (slot mode) gives every expert a region of 2T rows
+  const int C = d->capacity > 0     ? d->capacity
+                : d->capacity == 0  ? parrot_moe_capacity(d->tokens, d->n_experts)
+                : d->capacity == -1 ? 0
+                                    : 2 * d->tokens;
   const size_t A = 2 * T;
   const size_t n_tiles = (size_t)parrot::route_blocks(d->tokens);
   const size_t n_chunks = (size_t)parrot::group_blocks(d->tokens);
@@ -288,23 +290,34 @@ int run_group(const parrot_moe_dims* dims, const void* x, const parrot_moe_outpu
   return check_launch("group_kernel");
 }
 
-// Slot mode: the routing depth mix does the grouping too (an atomic slot per
-// assignment, the rows written straight to their grouped rows), and the
-// routed block that follows reads the per-expert counters as its segments and
-// zeroes them.  Chosen by a capacity that no expert can overflow (C >= 2T).
+// Slot mode (dims->capacity == -2): the router (kernel, or folded into the
+// depth mix) does the grouping too (an atomic slot per assignment in a 2T-row
+// region of its expert, the rows written straight to their grouped rows), and
+// the block's GEMMs read the per-expert counters as their segments; the down
+// GEMM leaves them zero.  Up to 4096 tokens (the routers that can do it).
 bool slot_mode(const parrot_moe_dims* d, const parrot_moe_layout& L) {
-  return L.capacity >= 2 * d->tokens && d->tokens <= 4096;
+  return d->capacity == -2 && d->tokens <= 4096 && L.capacity == 2 * d->tokens;
 }
 int* slot_counters(void* ws, const parrot_moe_layout& L) {
   return reinterpret_cast<int*>(static_cast<char*>(ws) + L.status + 16);  // [E], then the ticket
 }
 
-// Router + grouping.
+void set_slots(parrot::RouteArgs* ra, void* ws, const parrot_moe_layout& L) {
+  ra->slot_counts = slot_counters(ws, L);
+  ra->slot_stride = L.capacity;
+  ra->grouped = at<__nv_bfloat16>(ws, L.grouped);
+  ra->positions = at<int>(ws, L.positions);
+  ra->row_dst = at<int>(ws, L.row_dst);
+  ra->row_w = at<float>(ws, L.row_w);
+}
+
+// Router + grouping (slots: the router groups the rows itself, slot mode).
 int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
               const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L, cudaStream_t s,
-              const signed char* ep_order = nullptr) {
+              const signed char* ep_order = nullptr, bool slots = false) {
   const int T = dims->tokens, E = dims->n_experts;
-  const parrot::RouteArgs ra = route_args(dims, w, o, ws, L);
+  parrot::RouteArgs ra = route_args(dims, w, o, ws, L);
+  if (slots) set_slots(&ra, ws, L);
   CUtensorMap mx, mw;
   if (parrot::route_tile(T) != parrot::kRouteSmallTile &&
       (!tensor_map(&mx, x, T, dims->dim, parrot::route_tile(T)) ||
@@ -313,7 +326,7 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
   if (parrot::launch_route(ra, x, w->router, &mx, &mw, s))
     return fail(PARROT_ECUDA, "route: unsupported dim or shared-memory setup failed%s");
   int rc = check_launch("route_kernel");
-  if (rc) return rc;
+  if (rc || slots) return rc;
   return run_group(dims, x, o, ws, L, s, ep_order);
 }
 
@@ -1036,8 +1049,9 @@ int parrot_moe_forward_bf16(const parrot_moe_dims* dims, const parrot_moe_weight
   if (rc) return rc;
   if (dims->tokens == 0) return PARROT_OK;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if ((rc = run_route(dims, weights, x, outputs, workspace, L, s))) return rc;
-  return run_experts(dims, weights, x, outputs, workspace, L, s);
+  const bool slots = slot_mode(dims, L);
+  if ((rc = run_route(dims, weights, x, outputs, workspace, L, s, nullptr, slots))) return rc;
+  return run_experts(dims, weights, x, outputs, workspace, L, s, true, slots);
 }
 
 int parrot_moe_forward_deferred_bf16(const parrot_moe_dims* dims,
@@ -1049,8 +1063,9 @@ int parrot_moe_forward_deferred_bf16(const parrot_moe_dims* dims,
   if (rc) return rc;
   if (dims->tokens == 0) return PARROT_OK;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if ((rc = run_route(dims, weights, x, outputs, workspace, L, s))) return rc;
-  return run_experts(dims, weights, x, outputs, workspace, L, s, false);
+  const bool slots = slot_mode(dims, L);
+  if ((rc = run_route(dims, weights, x, outputs, workspace, L, s, nullptr, slots))) return rc;
+  return run_experts(dims, weights, x, outputs, workspace, L, s, false, slots);
 }
 
 int parrot_depthmix_route_bf16(void* out, const void* const* sources, int n_sources,
@@ -1082,14 +1097,7 @@ int parrot_depthmix_route_bf16(void* out, const void* const* sources, int n_sour
   parrot::DepthRouteArgs r{};
   r.router_w = static_cast<const __nv_bfloat16*>(weights->router);
   r.r = route_args(dims, weights, outputs, workspace, L);
-  if (slot_mode(dims, L)) {
-    r.slot_counts = slot_counters(workspace, L);
-    r.slot_stride = L.capacity;
-    r.grouped = at<__nv_bfloat16>(workspace, L.grouped);
-    r.positions = at<int>(workspace, L.positions);
-    r.row_dst = at<int>(workspace, L.row_dst);
-    r.row_w = at<float>(workspace, L.row_w);
-  }
+  if (slot_mode(dims, L)) set_slots(&r.r, workspace, L);
   return depthmix_launch(out, sources, n_sources, query, key_norm_weight, key_eps,
                          out_norm_weight, out_eps, mix_out, a, rows, dim, stream, &r);
 }
@@ -1189,8 +1197,9 @@ int parrot_moe_forward_static_bf16(const parrot_moe_dims* dims,
   // start at zero, so clear it first.
   if (cudaMemsetAsync(ws, 0, L.indices, s) != cudaSuccess)
     return check_launch("static workspace clear");
-  if ((rc = run_route(dims, weights, x, outputs, ws, L, s))) return rc;
-  return run_experts(dims, weights, x, outputs, ws, L, s);
+  const bool slots = slot_mode(dims, L);
+  if ((rc = run_route(dims, weights, x, outputs, ws, L, s, nullptr, slots))) return rc;
+  return run_experts(dims, weights, x, outputs, ws, L, s, true, slots);
 }
 
 int parrot_moe_ep_dispatch_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,

@@ -62,25 +62,25 @@ struct RouteArgs {
   MoeTables tab;
   int tokens, dim, n_experts;
   int* status;
+  // Slot mode (slot_counts != null; the routers up to 4096 tokens): the
+  // grouping done by the router too.  Each assignment takes the next slot of
+  // its expert from a per-expert counter (zero before the call), its row goes
+  // to grouped row e * slot_stride + slot with the position, contribution
+  // slot and route weight; the GEMMs read the counters as segment sizes.
+  // Rows keep no order within an expert (the products do not depend on it).
+  int* slot_counts;           // [E]
+  int slot_stride;            // rows per expert region (>= 2T: no overflow)
+  __nv_bfloat16* grouped;
+  int* positions;             // [2T]
+  int* row_dst;               // [E * slot_stride]
+  float* row_w;
 };
 
 // The router folded into a depth mix whose normalised output is the MoE
 // block's input (norm.cu): the router weight and the router's outputs.
 struct DepthRouteArgs {
   const __nv_bfloat16* router_w;  // [E, d]
-  RouteArgs r;                    // tokens == the depth mix's rows
-  // Slot mode (slot_counts != null): the grouping done here too.  Each
-  // assignment takes the next slot of its expert from a per-expert counter
-  // (zero before the call), its row goes to grouped row e * slot_stride +
-  // slot with the position, contribution slot and route weight; the GEMMs
-  // read the counters as segment sizes.  Rows keep no order within an expert
-  // (the products do not depend on it).
-  int* slot_counts;               // [E]
-  int slot_stride;                // rows per expert region (>= 2T: no overflow)
-  __nv_bfloat16* grouped;
-  int* positions;                 // [2T]
-  int* row_dst;                   // [E * slot_stride]
-  float* row_w;
+  RouteArgs r;                    // tokens == the depth mix's rows (slot mode included)
 };
 
 struct GroupArgs {

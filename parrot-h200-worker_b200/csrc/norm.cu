@@ -384,16 +384,16 @@ __global__ void __launch_bounds__(32 * W * R, (NS <= 8 && R == 1) ? 768 / (32 * 
         }
         atomicAdd(&hist[i1], 1);
         atomicAdd(&hist[i2], 1);
-        if (ra.slot_counts != nullptr) {
+        if (ra.r.slot_counts != nullptr) {
           // the grouping: the next free slot of each expert, then the row's
           // position, contribution slot (the lower expert id first) and weight
-          const int r1 = i1 * ra.slot_stride + atomicAdd(ra.slot_counts + i1, 1);
-          const int r2 = i2 * ra.slot_stride + atomicAdd(ra.slot_counts + i2, 1);
-          reinterpret_cast<int2*>(ra.positions)[row] = make_int2(r1, r2);
-          ra.row_dst[r1] = 2 * row + (i1 < i2 ? 0 : 1);
-          ra.row_dst[r2] = 2 * row + (i2 < i1 ? 0 : 1);
-          ra.row_w[r1] = w1;
-          ra.row_w[r2] = w2;
+          const int r1 = i1 * ra.r.slot_stride + atomicAdd(ra.r.slot_counts + i1, 1);
+          const int r2 = i2 * ra.r.slot_stride + atomicAdd(ra.r.slot_counts + i2, 1);
+          reinterpret_cast<int2*>(ra.r.positions)[row] = make_int2(r1, r2);
+          ra.r.row_dst[r1] = 2 * row + (i1 < i2 ? 0 : 1);
+          ra.r.row_dst[r2] = 2 * row + (i2 < i1 ? 0 : 1);
+          ra.r.row_w[r1] = w1;
+          ra.r.row_w[r2] = w2;
           slot_row[ty][0] = r1;
           slot_row[ty][1] = r2;
         }
@@ -403,11 +403,11 @@ __global__ void __launch_bounds__(32 * W * R, (NS <= 8 && R == 1) ? 768 / (32 * 
       if (lane < NP) psum[ty][lane] = p;
     }
     __syncthreads();
-    if (ra.slot_counts != nullptr && active && row < a.rows) {
+    if (ra.r.slot_counts != nullptr && active && row < a.rows) {
       // this thread's 16 bytes of the row, into both grouped rows
       const size_t nv = (size_t)nvec;
-      reinterpret_cast<uint4*>(ra.grouped)[(size_t)slot_row[ty][0] * nv + c] = ov;
-      reinterpret_cast<uint4*>(ra.grouped)[(size_t)slot_row[ty][1] * nv + c] = ov;
+      reinterpret_cast<uint4*>(ra.r.grouped)[(size_t)slot_row[ty][0] * nv + c] = ov;
+      reinterpret_cast<uint4*>(ra.r.grouped)[(size_t)slot_row[ty][1] * nv + c] = ov;
     }
     if (ty == 0 && c < E) {
       float sum = 0.f;

@@ -398,6 +398,36 @@ __global__ void __launch_bounds__(32 * kRouteSmallTile)
   }
   if (valid_t && valid_e && a.probs != nullptr) a.probs[(size_t)t * E + ex] = p;
   psum[warp * TW + tw][ex] = p;
+  if (a.slot_counts != nullptr) {
+    // slot mode: the grouping too.  Lane 0 of each token's group takes the
+    // next slot of both experts and writes the position, contribution slot
+    // (the lower expert id first) and weight; then the warp copies its
+    // tokens' rows (x, read again through L1) to their two grouped rows.
+    int r1 = 0, r2 = 0;
+    if (valid_t && ex == 0) {
+      const float sel = v1 + v2;
+      r1 = i1 * a.slot_stride + atomicAdd(a.slot_counts + i1, 1);
+      r2 = i2 * a.slot_stride + atomicAdd(a.slot_counts + i2, 1);
+      reinterpret_cast<int2*>(a.positions)[t] = make_int2(r1, r2);
+      a.row_dst[r1] = 2 * t + (i1 < i2 ? 0 : 1);
+      a.row_dst[r2] = 2 * t + (i2 < i1 ? 0 : 1);
+      a.row_w[r1] = v1 / sel;
+      a.row_w[r2] = v2 / sel;
+    }
+#pragma unroll
+    for (int u = 0; u < TW; ++u) {
+      const int g1 = __shfl_sync(0xffffffffu, r1, u * NP);
+      const int g2 = __shfl_sync(0xffffffffu, r2, u * NP);
+      if (t_first + u >= T) continue;
+      const uint4* src = reinterpret_cast<const uint4*>(x) + (size_t)(t_first + u) * nvec;
+      uint4* grouped = reinterpret_cast<uint4*>(a.grouped);
+      for (int c = lane; c < nvec; c += 32) {
+        const uint4 v = __ldg(src + c);
+        grouped[(size_t)g1 * nvec + c] = v;
+        grouped[(size_t)g2 * nvec + c] = v;
+      }
+    }
+  }
   __syncthreads();
   if (threadIdx.x < E) {
     const int e = threadIdx.x;

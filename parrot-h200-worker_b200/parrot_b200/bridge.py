@@ -234,11 +234,11 @@ def b200_vocab_argmax(hidden: Tensor, weight: Tensor) -> Tensor:
 FUSE_MOE_ROUTER = True
 
 
-# With the router folded in, the depth mix also groups the rows (slot mode of
-# parrot_depthmix_route_bf16: each assignment takes an atomic slot of its
-# expert and its row is written there), so the group kernel does not run.
-# It needs a capacity no expert can overflow (2 T rows per expert region),
-# taken up to SLOT_GROUPING_MAX_TOKENS.
+# The router (folded into the depth mix, or the router kernel) also groups the
+# rows (slot mode: each assignment takes an atomic slot of its expert and its
+# row is written there), so the group kernel does not run.  It needs a
+# capacity no expert can overflow (2 T rows per expert region), taken up to
+# SLOT_GROUPING_MAX_TOKENS.
 SLOT_GROUPING = True
 SLOT_GROUPING_MAX_TOKENS = 1024
 
@@ -246,7 +246,13 @@ SLOT_GROUPING_MAX_TOKENS = 1024
 def _route_dims(cfg, rows: int) -> _lib.MoeDims:
     """The MoE dims of a block whose router runs inside the depth mix."""
     slots = SLOT_GROUPING and rows <= SLOT_GROUPING_MAX_TOKENS
-    return moe_dims(cfg, rows, 2 * rows if slots else 0)
+    return moe_dims(cfg, rows, -2 if slots else 0)
+
+
+def _block_dims(cfg, rows: int) -> _lib.MoeDims:
+    """The MoE dims of a block routed by its own router kernel: slot mode too
+    (the router groups the rows) above the decode batch sizes."""
+    return _route_dims(cfg, rows) if rows > DECODE_MOE_MAX_TOKENS else moe_dims(cfg, rows)
 
 
 def _routes_in_mix(route, rows: int) -> bool:
@@ -548,7 +554,7 @@ def b200_moe(module, flat: Tensor, collect_stats: bool, addend: Tensor | None = 
     packed = pack_weights(module)
     fused = _routed_workspace(flat.device, cfg, T, flat)
     routed = fused is not None
-    dims, ws = fused if routed else (moe_dims(cfg, T), None)
+    dims, ws = fused if routed else (_block_dims(cfg, T), None)
     if ws is None:
         ws = workspace(flat.device, dims)
     out = torch.empty_like(flat)
@@ -604,7 +610,7 @@ def b200_moe_deferred(module, flat: Tensor, collect_stats: bool, addend: Tensor 
         return out.view(shape), aux, util
     packed = pack_weights(module)
     fused = _routed_workspace(flat.device, cfg, T, flat)
-    dims, ws = fused if fused is not None else (moe_dims(cfg, T), None)
+    dims, ws = fused if fused is not None else (_block_dims(cfg, T), None)
     if ws is None:
         ws = workspace(flat.device, dims)
     if addend is not None:

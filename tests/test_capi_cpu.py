@@ -102,6 +102,23 @@ def test_workspace_layout_is_aligned_and_ordered(lib):
     assert lay.shared_y + 512 * 768 * 2 <= lay.total
 
 
+def test_slot_mode_layout(lib):
+    """capacity -2 (slot mode): a 2T-row region per expert, no overflow region
+    needed; the status region grows by the E expert counters and a ticket."""
+    plain, slots = _lib.MoeLayout(), _lib.MoeLayout()
+    assert lib.parrot_moe_workspace_layout(
+        ctypes.byref(_lib.MoeDims(512, 768, 16, 2, 512, 256, 0)), ctypes.byref(plain)) == 0
+    assert lib.parrot_moe_workspace_layout(
+        ctypes.byref(_lib.MoeDims(512, 768, 16, 2, 512, 256, -2)), ctypes.byref(slots)) == 0
+    assert slots.capacity == 1024
+    assert slots.grouped_rows == 16 * 1024 + 1024
+    assert slots.status == 0 and slots.indices >= 16 + 4 * (16 + 1)
+    assert slots.indices == plain.indices
+    bad = _lib.MoeDims(512, 768, 16, 2, 512, 256, -3)
+    assert lib.parrot_moe_workspace_layout(ctypes.byref(bad), ctypes.byref(slots)) == \
+        _lib.PARROT_EINVAL
+
+
 @pytest.mark.parametrize("field,value", [("top_k", 1), ("dim", 96), ("n_experts", 33),
                                          ("expert_dim", 100), ("shared_dim", 0)])
 def test_layout_rejects_unsupported_dims(lib, field, value):

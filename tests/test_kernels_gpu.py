@@ -298,7 +298,7 @@ def test_decode_moe_matches_oracle_and_gemm_path(tokens, residual, zipf):
     res = hidden_states(tokens, cfg.dim, seed=62) if residual else None
     xd = x.cuda()
     got, _, _ = bridge.b200_moe(prod, xd, False, None if res is None else res.cuda())
-    dims = bridge.moe_dims(cfg, tokens)
+    dims = bridge._block_dims(cfg, tokens)  # the workspace the block ran in
     layout = bridge.workspace_layout(dims)
     ws = bridge.workspace(xd.device, dims)
     idx = workspace_view(ws, layout, "indices", torch.int32, (tokens, 2)).cpu().long()
@@ -541,6 +541,38 @@ def test_gemm_primary_partner_tiles(tokens, capacity, kinds):
     assert torch.equal(out, packed)
 
 
+@pytest.mark.parametrize("tokens,experts", [(37, 16), (256, 16), (512, 16), (1024, 16),
+                                            (100, 32), (130, 8)])
+def test_slot_mode_grouping_equals_the_group_kernel(tokens, experts):
+    """Slot mode (capacity -2: a 2T-row region per expert): the router takes each assignment's slot with an
+    atomic and copies the row, no group kernel runs.  Against the default
+    capacity layout (the group kernel): the block output, counts and
+    statistics are bit-identical; each expert's positions fill its region and
+    every grouped row holds its token's row; a second call (the counters were
+    left at zero) repeats the output."""
+    cfg = moe_config(n_experts=experts) if experts == 16 else \
+        moe_config(dim=256, n_experts=experts, expert_dim=128, shared_dim=128)
+    prod, _ = build_moe_pair(cfg, seed=experts + tokens)
+    x = hidden_states(tokens, cfg.dim, seed=tokens).cuda()
+    ref, ex_ref, _, _ = call_moe_forward(prod, x)
+    out, ex, ws, layout = call_moe_forward(prod, x, capacity=-2)
+    assert ex["status"][0] == 0, ex["status"]
+    assert layout.capacity == 2 * tokens
+    assert torch.equal(out, ref)
+    for k in ("indices", "weights", "counts", "stats"):
+        assert torch.equal(ex[k], ex_ref[k]), k
+    C = layout.capacity
+    cnt, pos, idx = ex["counts"].cpu(), ex["positions"].cpu().long(), ex["indices"].cpu().flatten()
+    for e in range(cfg.n_experts):
+        got = torch.sort(pos[idx == e]).values
+        assert torch.equal(got, e * C + torch.arange(int(cnt[e]))), e
+    grouped = workspace_view(ws, layout, "grouped", torch.bfloat16,
+                             (layout.grouped_rows, cfg.dim)).cpu()
+    assert torch.equal(grouped[pos], x.cpu()[torch.arange(2 * tokens) // 2])
+    again, _, _, _ = call_moe_forward(prod, x, capacity=-2)
+    assert torch.equal(again, ref)
+
+
 def test_residual_is_fused_into_combine():
     cfg = moe_config()
     prod, orc = build_moe_pair(cfg, seed=2)
@@ -695,7 +727,7 @@ def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending
     expert ids agree wherever the router's top-2 / top-3 probability margin
     exceeds 1e-5 and equal top-2 of the fused call's own probabilities; the
     block output is identical on every token routed alike.  Slot mode
-    (capacity 2T: the depth mix groups the rows itself, no group kernel):
+    (capacity -2: the depth mix groups the rows itself, no group kernel):
     each expert's positions fill its region, every grouped row holds its
     token's row, counts and statistics equal the grouping kernel's, and a
     second call (the counters were left at zero) gives the same output."""
@@ -715,7 +747,7 @@ def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending
     w = bridge._weights_struct(bridge.pack_weights(module), None)
     results = {}
     for fused in (False, True):
-        dims = bridge.moe_dims(cfg, rows, 2 * rows if (fused and slots) else 0)
+        dims = bridge.moe_dims(cfg, rows, -2 if (fused and slots) else 0)
         out = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16)
         pend_out = torch.empty_like(out) if pending else None
         layout = bridge.workspace_layout(dims)
