@@ -221,7 +221,8 @@ def time_moe_breakdown(model, tokens: int = 256, replays: int = 10) -> dict:
     """BASELINE config 2 kernel by kernel: one CUDA graph of 16 MoE blocks
     (cycling the model's 16 layers, so every launch streams its own weights
     from HBM) replayed under the torch profiler (CUPTI device timestamps, not
-    ncu).  Per kernel kind: mean device duration per block, the exposed part
+    ncu).  The block runs in slot mode: the router also groups the rows, so
+    there is no grouping kernel.  Per kernel kind: mean device duration per block, the exposed part
     (not overlapped by the previous kernel's tail: launches are programmatic
     dependent launches), algorithmic bytes, and bytes / duration against the
     measured HBM bandwidth."""
@@ -251,10 +252,10 @@ def time_moe_breakdown(model, tokens: int = 256, replays: int = 10) -> dict:
     dur, exp = collections.defaultdict(float), collections.defaultdict(float)
     prev_end, gemms = evs[0][0], 0
     for start, end, name in evs:
-        if "route_kernel" in name:
-            kind = "route"
+        if "route_kernel" in name or "route_small_kernel" in name:
+            kind, gemms = "route", 0  # each block starts at its router
         elif "group_kernel" in name:
-            kind, gemms = "group", 0
+            kind = "group"
         elif "grouped_gemm" in name:
             kind = "gate_up_swiglu" if gemms == 0 else "down"
             gemms += 1
@@ -268,7 +269,9 @@ def time_moe_breakdown(model, tokens: int = 256, replays: int = 10) -> dict:
     n = replays * len(layers)
     T, d, E, H, Hs = tokens, cfg.dim, cfg.n_experts, cfg.expert_dim, cfg.shared_expert_dim
     A = 2 * T
-    algo = {"route": 2 * T * d + 2 * E * d + 16 * T,
+    # the router groups the rows itself (slot mode): its bytes include the
+    # two grouped copies of every token row
+    algo = {"route": 2 * T * d + 2 * E * d + 16 * T + 4 * T * d,
             "group": 2 * T * d + 4 * T * d,
             "gate_up_swiglu": 2 * (E * 2 * H * d + 2 * Hs * d + A * d + T * d + A * H + T * Hs),
             "down": 2 * (E * d * H + d * Hs + A * H + T * Hs + A * d + T * d),

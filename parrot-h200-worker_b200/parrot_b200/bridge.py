@@ -240,7 +240,7 @@ FUSE_MOE_ROUTER = True
 # capacity no expert can overflow (2 T rows per expert region), taken up to
 # SLOT_GROUPING_MAX_TOKENS.
 SLOT_GROUPING = True
-SLOT_GROUPING_MAX_TOKENS = 1024
+SLOT_GROUPING_MAX_TOKENS = 4096  # the routers that can group; a 2T-row region per expert
 
 
 def _route_dims(cfg, rows: int) -> _lib.MoeDims:

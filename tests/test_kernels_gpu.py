@@ -542,7 +542,7 @@ def test_gemm_primary_partner_tiles(tokens, capacity, kinds):
 
 
 @pytest.mark.parametrize("tokens,experts", [(37, 16), (256, 16), (512, 16), (1024, 16),
-                                            (100, 32), (130, 8)])
+                                            (2048, 16), (4096, 16), (100, 32), (130, 8)])
 def test_slot_mode_grouping_equals_the_group_kernel(tokens, experts):
     """Slot mode (capacity -2: a 2T-row region per expert): the router takes each assignment's slot with an
     atomic and copies the row, no group kernel runs.  Against the default
@@ -720,7 +720,8 @@ def test_vocab_argmax_is_repeatable_and_graph_capturable():
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("rows,n_sources,pending,slots", [
     (512, 6, True, False), (37, 3, False, False), (4096, 9, True, False), (9, 1, False, False),
-    (512, 6, True, True), (37, 3, False, True), (1024, 9, True, True), (9, 1, False, True)])
+    (512, 6, True, True), (37, 3, False, True), (1024, 9, True, True), (9, 1, False, True),
+    (4096, 4, False, True)])
 def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending, slots):
     """parrot_depthmix_route_bf16 + parrot_moe_forward_routed_bf16 against
     parrot_depthmix_bf16 + parrot_moe_forward_bf16: the mix is bit-identical;
