@@ -184,9 +184,9 @@ typedef struct parrot_moe_dims {
   int shared_dim;  /* Hs, % 64 == 0 */
   int capacity;    /* slots per expert; 0 selects parrot_moe_capacity();
                       -1 packs all rows per expert, experts in id order (no capacity
-                      region: the expert-parallel send layout); -2 slot mode (up to
-                      4096 tokens): a region of 2T rows per expert that the router
-                      fills itself, see parrot_depthmix_route_bf16 */
+                      region: the expert-parallel send layout); -2 slot mode: a
+                      region of 2T rows per expert that the router fills itself,
+                      see parrot_depthmix_route_bf16 */
 } parrot_moe_dims;
 
 /* Expert weights start in torch.nn.Linear [out, in] layout and are packed

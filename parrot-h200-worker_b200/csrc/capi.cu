@@ -294,16 +294,17 @@ int run_group(const parrot_moe_dims* dims, const void* x, const parrot_moe_outpu
 // depth mix) does the grouping too (an atomic slot per assignment in a 2T-row
 // region of its expert, the rows written straight to their grouped rows), and
 // the block's GEMMs read the per-expert counters as their segments; the down
-// GEMM leaves them zero.  Up to 4096 tokens (the routers that can do it).
+// GEMM leaves them zero.
 bool slot_mode(const parrot_moe_dims* d, const parrot_moe_layout& L) {
-  return d->capacity == -2 && d->tokens <= 4096 && L.capacity == 2 * d->tokens;
+  return d->capacity == -2 && L.capacity == 2 * d->tokens;
 }
 int* slot_counters(void* ws, const parrot_moe_layout& L) {
   return reinterpret_cast<int*>(static_cast<char*>(ws) + L.status + 16);  // [E], then the ticket
 }
 
-void set_slots(parrot::RouteArgs* ra, void* ws, const parrot_moe_layout& L) {
+void set_slots(parrot::RouteArgs* ra, void* ws, const parrot_moe_layout& L, const void* x) {
   ra->slot_counts = slot_counters(ws, L);
+  ra->slot_x = static_cast<const __nv_bfloat16*>(x);
   ra->slot_stride = L.capacity;
   ra->grouped = at<__nv_bfloat16>(ws, L.grouped);
   ra->positions = at<int>(ws, L.positions);
@@ -317,7 +318,7 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
               const signed char* ep_order = nullptr, bool slots = false) {
   const int T = dims->tokens, E = dims->n_experts;
   parrot::RouteArgs ra = route_args(dims, w, o, ws, L);
-  if (slots) set_slots(&ra, ws, L);
+  if (slots) set_slots(&ra, ws, L, x);
   CUtensorMap mx, mw;
   if (parrot::route_tile(T) != parrot::kRouteSmallTile &&
       (!tensor_map(&mx, x, T, dims->dim, parrot::route_tile(T)) ||
@@ -1097,7 +1098,7 @@ int parrot_depthmix_route_bf16(void* out, const void* const* sources, int n_sour
   parrot::DepthRouteArgs r{};
   r.router_w = static_cast<const __nv_bfloat16*>(weights->router);
   r.r = route_args(dims, weights, outputs, workspace, L);
-  if (slot_mode(dims, L)) set_slots(&r.r, workspace, L);
+  if (slot_mode(dims, L)) set_slots(&r.r, workspace, L, nullptr);  // the mix has the rows
   return depthmix_launch(out, sources, n_sources, query, key_norm_weight, key_eps,
                          out_norm_weight, out_eps, mix_out, a, rows, dim, stream, &r);
 }

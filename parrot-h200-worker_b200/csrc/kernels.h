@@ -70,6 +70,7 @@ struct RouteArgs {
   // Rows keep no order within an expert (the products do not depend on it).
   int* slot_counts;           // [E]
   int slot_stride;            // rows per expert region (>= 2T: no overflow)
+  const __nv_bfloat16* slot_x;  // the token rows the router reads (its copy source)
   __nv_bfloat16* grouped;
   int* positions;             // [2T]
   int* row_dst;               // [E * slot_stride]

@@ -45,6 +45,7 @@ struct __align__(8) RouteSmem {
   int abort;
   int hist[4][kMaxExperts];
   float psum[4][kMaxExperts];
+  int slot_cur[kMaxExperts];  // slot mode: this tile's next grouped row per expert
 };
 
 // The 128-token tiles stream through a 4-slot ring: about
@@ -217,9 +218,10 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
 #pragma unroll
     for (int e = 0; e < NP; ++e) p[e] = valid_tok ? p[e] * rden : 0.f;
   }
+  int i1 = 0, i2 = -1;
+  float w1 = 0.f, w2 = 0.f;
   if (valid_tok) {
     // top-2; equal probabilities resolve to the lower expert id
-    int i1 = 0;
     float v1 = p[0];
 #pragma unroll
     for (int e = 1; e < NP; ++e)
@@ -227,7 +229,6 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
         v1 = p[e];
         i1 = e;
       }
-    int i2 = -1;
     float v2 = -1.f;  // every probability is >= 0
 #pragma unroll
     for (int e = 0; e < NP; ++e)
@@ -236,7 +237,8 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
         i2 = e;
       }
     const float sel = v1 + v2;
-    const float w1 = v1 / sel, w2 = v2 / sel;
+    w1 = v1 / sel;
+    w2 = v2 / sel;
     reinterpret_cast<int2*>(a.indices)[t] = make_int2(i1, i2);
     reinterpret_cast<float2*>(a.weights)[t] = make_float2(w1, w2);
     if (a.weights_out != nullptr) reinterpret_cast<float2*>(a.weights_out)[t] = make_float2(w1, w2);
@@ -267,6 +269,63 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
           sm.hist[0][e] + sm.hist[1][e] + sm.hist[2][e] + sm.hist[3][e];
       a.tab.tile_probsum[(size_t)tile * E + e] =
           ((sm.psum[0][e] + sm.psum[1][e]) + sm.psum[2][e]) + sm.psum[3][e];
+    }
+  }
+  if (a.slot_counts != nullptr && ok) {
+    // slot mode: the grouping too.  One atomic per expert reserves this
+    // tile's block of its region, shared-memory atomics hand out the rows in
+    // it; each assignment's position, contribution slot (the lower expert id
+    // first) and weight are written, then each warp copies its 32 token rows
+    // (x, read again) to their two grouped rows.
+    if (threadIdx.x < E) {
+      const int e = threadIdx.x;
+      const int cnt = sm.hist[0][e] + sm.hist[1][e] + sm.hist[2][e] + sm.hist[3][e];
+      sm.slot_cur[e] = e * a.slot_stride + atomicAdd(a.slot_counts + e, cnt);
+    }
+    __syncthreads();
+    int r1 = 0, r2 = 0;
+    if (valid_tok) {
+      r1 = atomicAdd(&sm.slot_cur[i1], 1);
+      r2 = atomicAdd(&sm.slot_cur[i2], 1);
+      reinterpret_cast<int2*>(a.positions)[t] = make_int2(r1, r2);
+      a.row_dst[r1] = 2 * t + (i1 < i2 ? 0 : 1);
+      a.row_dst[r2] = 2 * t + (i2 < i1 ? 0 : 1);
+      a.row_w[r1] = w1;
+      a.row_w[r2] = w2;
+    }
+    // four tokens' loads in flight before their stores (a load after a store
+    // through another pointer waits for it: one memory round trip per token)
+    const int nvec = a.dim >> 3;
+    const uint4* __restrict__ xs = reinterpret_cast<const uint4*>(a.slot_x);
+    uint4* __restrict__ grouped = reinterpret_cast<uint4*>(a.grouped);
+    constexpr int kU = 4, kV = 4;  // tokens per batch; vectors per lane (d <= 1024)
+    for (int u0 = 0; u0 < 32; u0 += kU) {
+      uint4 v[kU][kV];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int tu = tile * rows + warp * 32 + u0 + u;
+        const bool in = warp * 32 + u0 + u < rows && tu < T;
+#pragma unroll
+        for (int k = 0; k < kV; ++k) {
+          const int c = lane + 32 * k;
+          v[u][k] = in && c < nvec ? __ldg(xs + (size_t)tu * nvec + c) : make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int g1 = __shfl_sync(0xffffffffu, r1, u0 + u);
+        const int g2 = __shfl_sync(0xffffffffu, r2, u0 + u);
+        const int tu = tile * rows + warp * 32 + u0 + u;
+        if (warp * 32 + u0 + u >= rows || tu >= T) continue;  // uniform over the warp
+#pragma unroll
+        for (int k = 0; k < kV; ++k) {
+          const int c = lane + 32 * k;
+          if (c < nvec) {
+            grouped[(size_t)g1 * nvec + c] = v[u][k];
+            grouped[(size_t)g2 * nvec + c] = v[u][k];
+          }
+        }
+      }
     }
   }
   tc_fence_before();
@@ -401,8 +460,9 @@ __global__ void __launch_bounds__(32 * kRouteSmallTile)
   if (a.slot_counts != nullptr) {
     // slot mode: the grouping too.  Lane 0 of each token's group takes the
     // next slot of both experts and writes the position, contribution slot
-    // (the lower expert id first) and weight; then the warp copies its
-    // tokens' rows (x, read again through L1) to their two grouped rows.
+    // (the lower expert id first) and weight; then the warp writes its
+    // tokens' rows to their two grouped rows from the registers that hold
+    // them (exact bf16 values, packed again).
     int r1 = 0, r2 = 0;
     if (valid_t && ex == 0) {
       const float sel = v1 + v2;
@@ -414,17 +474,24 @@ __global__ void __launch_bounds__(32 * kRouteSmallTile)
       a.row_w[r1] = v1 / sel;
       a.row_w[r2] = v2 / sel;
     }
+    uint4* grouped = reinterpret_cast<uint4*>(a.grouped);
 #pragma unroll
     for (int u = 0; u < TW; ++u) {
       const int g1 = __shfl_sync(0xffffffffu, r1, u * NP);
       const int g2 = __shfl_sync(0xffffffffu, r2, u * NP);
       if (t_first + u >= T) continue;
-      const uint4* src = reinterpret_cast<const uint4*>(x) + (size_t)(t_first + u) * nvec;
-      uint4* grouped = reinterpret_cast<uint4*>(a.grouped);
-      for (int c = lane; c < nvec; c += 32) {
-        const uint4 v = __ldg(src + c);
-        grouped[(size_t)g1 * nvec + c] = v;
-        grouped[(size_t)g2 * nvec + c] = v;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int c = lane + 32 * k;
+        if (c < nvec) {
+          uint4 v;
+          v.x = pack_bf16x2(xf[u][k][0].x, xf[u][k][0].y);
+          v.y = pack_bf16x2(xf[u][k][1].x, xf[u][k][1].y);
+          v.z = pack_bf16x2(xf[u][k][2].x, xf[u][k][2].y);
+          v.w = pack_bf16x2(xf[u][k][3].x, xf[u][k][3].y);
+          grouped[(size_t)g1 * nvec + c] = v;
+          grouped[(size_t)g2 * nvec + c] = v;
+        }
       }
     }
   }

@@ -541,9 +541,10 @@ def test_gemm_primary_partner_tiles(tokens, capacity, kinds):
     assert torch.equal(out, packed)
 
 
-@pytest.mark.parametrize("tokens,experts", [(37, 16), (256, 16), (512, 16), (1024, 16),
-                                            (2048, 16), (4096, 16), (100, 32), (130, 8)])
-def test_slot_mode_grouping_equals_the_group_kernel(tokens, experts):
+@pytest.mark.parametrize("tokens,experts,zipf", [
+    (37, 16, False), (256, 16, False), (512, 16, False), (1024, 16, False), (2048, 16, False),
+    (4096, 16, False), (100, 32, False), (130, 8, False), (8192, 16, False), (16384, 16, True)])
+def test_slot_mode_grouping_equals_the_group_kernel(tokens, experts, zipf):
     """Slot mode (capacity -2: a 2T-row region per expert): the router takes each assignment's slot with an
     atomic and copies the row, no group kernel runs.  Against the default
     capacity layout (the group kernel): the block output, counts and
@@ -554,6 +555,8 @@ def test_slot_mode_grouping_equals_the_group_kernel(tokens, experts):
         moe_config(dim=256, n_experts=experts, expert_dim=128, shared_dim=128)
     prod, _ = build_moe_pair(cfg, seed=experts + tokens)
     x = hidden_states(tokens, cfg.dim, seed=tokens).cuda()
+    if zipf:  # above 4096 tokens the tensor-core router; skewed, the overflow path on the left
+        prod.router_bias = torch.tensor([3.0, 2.0, 1.0] + [0.0] * (experts - 3)).cuda()
     ref, ex_ref, _, _ = call_moe_forward(prod, x)
     out, ex, ws, layout = call_moe_forward(prod, x, capacity=-2)
     assert ex["status"][0] == 0, ex["status"]
