@@ -372,6 +372,16 @@ int parrot_moe_decode_bf16(const parrot_moe_dims* dims, const parrot_moe_weights
                            const void* x, const parrot_moe_outputs* outputs, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* parrot_moe_decode_bf16 after parrot_depthmix_route_bf16 routed its input x
+ * (rows == tokens <= 4 with a non-slot dims->capacity): the gate/up kernel
+ * reads the routing from the workspace instead of computing it, and the down
+ * kernel fetches its expert rows before its dependency wait (the routing was
+ * written two launches earlier).  outputs->probs / indices / weights must be
+ * NULL (the routing call writes them). */
+int parrot_moe_decode_routed_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                                  const void* x, const parrot_moe_outputs* outputs,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
 /* Expert GEMMs + shared expert + combine on a workspace filled by
  * parrot_moe_route_bf16 for the same x (metal_moe.py:372-416 after routing). */
 int parrot_moe_experts_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,

@@ -1119,9 +1119,9 @@ int parrot_moe_forward_routed_bf16(const parrot_moe_dims* dims, const parrot_moe
   return run_experts(dims, weights, x, outputs, workspace, L, s, !deferred, slots);
 }
 
-int parrot_moe_decode_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
-                           const void* x, const parrot_moe_outputs* outputs, void* workspace,
-                           size_t workspace_bytes, void* stream) {
+static int moe_decode(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                      const void* x, const parrot_moe_outputs* outputs, void* workspace,
+                      size_t workspace_bytes, void* stream, bool routed) {
   parrot_moe_layout L;
   int rc = prepare(dims, weights, x, outputs, workspace, workspace_bytes, &L);
   if (rc) return rc;
@@ -1131,8 +1131,13 @@ int parrot_moe_decode_bf16(const parrot_moe_dims* dims, const parrot_moe_weights
                                "both multiples of 32%s");
   if (outputs->counts != nullptr || outputs->stats != nullptr || outputs->positions != nullptr)
     return fail(PARROT_EINVAL, "moe_decode: no grouping, counts or statistics on this path%s");
+  if (routed && (outputs->probs != nullptr || outputs->indices != nullptr ||
+                 outputs->weights != nullptr))
+    return fail(PARROT_EINVAL, "moe_decode_routed: probs, indices and weights come from the "
+                               "routing call%s");
   if (dims->tokens == 0) return PARROT_OK;
   parrot::MoeDecodeArgs a{};
+  a.routed = routed ? 1 : 0;
   a.x = static_cast<const __nv_bfloat16*>(x);
   a.router = static_cast<const __nv_bfloat16*>(weights->router);
   a.router_bias = weights->router_bias;
@@ -1156,6 +1161,18 @@ int parrot_moe_decode_bf16(const parrot_moe_dims* dims, const parrot_moe_weights
   if (parrot::launch_moe_decode(a, static_cast<cudaStream_t>(stream)))
     return fail(PARROT_ECUDA, "moe_decode: launch failed%s");
   return check_launch("moe_decode kernels");
+}
+
+int parrot_moe_decode_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                           const void* x, const parrot_moe_outputs* outputs, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  return moe_decode(dims, weights, x, outputs, workspace, workspace_bytes, stream, false);
+}
+
+int parrot_moe_decode_routed_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,
+                                  const void* x, const parrot_moe_outputs* outputs,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  return moe_decode(dims, weights, x, outputs, workspace, workspace_bytes, stream, true);
 }
 
 int parrot_moe_gemm_bf16(const parrot_moe_dims* dims, const parrot_moe_weights* weights,

@@ -269,6 +269,10 @@ struct MoeDecodeArgs {
   const __nv_bfloat16* residual;     // [T, d] or null
   __nv_bfloat16* out;                // [T, d]
   int tokens, dim, n_experts, expert_dim, shared_dim;
+  // 1: the routing depth mix (two launches before the down projection) wrote
+  // indices and weights; the gate/up CTAs read them instead of routing, and
+  // the down CTAs fetch their expert rows before their dependency wait
+  int routed;
 };
 int launch_moe_decode(const MoeDecodeArgs& args, cudaStream_t stream);
 

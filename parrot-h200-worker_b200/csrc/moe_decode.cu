@@ -209,16 +209,19 @@ __global__ void __launch_bounds__(128) moe_decode_up_kernel(MoeDecodeArgs a) {
   }
   __shared__ int ids_s[2 * kDecodeMoeMaxTokens];
   if constexpr (NT <= 4) {
-    // routed CTAs route the (at most 4) tokens themselves: the router weight
-    // is a parameter, so it is in flight before the wait
-    if (!shared)
+    // routed CTAs route the (at most 4) tokens themselves, unless the depth
+    // mix before did: the router weight is a parameter, so it is in flight
+    // before the wait
+    if (!shared && !a.routed)
       for (int i = threadIdx.x; i < E * nvec; i += blockDim.x)
         cp_async16(r_s + i, reinterpret_cast<const uint4*>(a.router) + i);
     griddep_wait();
     griddep_launch();
     for (int i = threadIdx.x; i < T * nvec; i += blockDim.x)
       cp_async16(x_s + i, reinterpret_cast<const uint4*>(a.x) + i);
-    if (!shared) {
+    if (a.routed) {
+      if (threadIdx.x < 2 * T) ids_s[threadIdx.x] = a.indices[threadIdx.x];
+    } else if (!shared) {
       __shared__ float red_s[4 * 4 * 32];
       cp_async_wait_all();
       __syncthreads();
@@ -381,15 +384,30 @@ __global__ void __launch_bounds__(128) moe_decode_down_kernel(MoeDecodeArgs a) {
     const int r = i / hsv, c = i - r * hsv;
     cp_async16(rows[2] + i, a.shared_down + tiled_index(0, o0 + r, c * 8, d, Hs));
   }
+  auto fetch_routed = [&](int e0, int e1) {
+    for (int i = threadIdx.x; i < 2 * kColsPerCta * hv; i += blockDim.x) {
+      const int k = i / (kColsPerCta * hv), rem = i - k * (kColsPerCta * hv);
+      const int r = rem / hv, c = rem - r * hv;
+      cp_async16(rows[k] + rem, a.down + tiled_index(k == 0 ? e0 : e1, o0 + r, c * 8, d, H));
+    }
+  };
+  // routed by the depth mix two launches back: its ids are complete before
+  // the gate/up kernel this one follows could start, so the expert rows come
+  // before the wait too
+  int e0 = 0, e1 = 0;
+  if (a.routed) {
+    e0 = a.indices[2 * t];
+    e1 = a.indices[2 * t + 1];
+    fetch_routed(e0, e1);
+  }
   griddep_wait();
   griddep_launch();
-  const int e0 = a.indices[2 * t], e1 = a.indices[2 * t + 1];
-  const float w0 = round_bf16(a.weights[2 * t]), w1 = round_bf16(a.weights[2 * t + 1]);
-  for (int i = threadIdx.x; i < 2 * kColsPerCta * hv; i += blockDim.x) {
-    const int k = i / (kColsPerCta * hv), rem = i - k * (kColsPerCta * hv);
-    const int r = rem / hv, c = rem - r * hv;
-    cp_async16(rows[k] + rem, a.down + tiled_index(k == 0 ? e0 : e1, o0 + r, c * 8, d, H));
+  if (!a.routed) {
+    e0 = a.indices[2 * t];
+    e1 = a.indices[2 * t + 1];
+    fetch_routed(e0, e1);
   }
+  const float w0 = round_bf16(a.weights[2 * t]), w1 = round_bf16(a.weights[2 * t + 1]);
   for (int i = threadIdx.x; i < (2 * H + Hs) / 8; i += blockDim.x) {
     const int k = i < H / 4 ? i / (H / 8) : 2;
     const int c = k < 2 ? i - k * (H / 8) : i - H / 4;
@@ -467,8 +485,9 @@ int launch_moe_decode(const MoeDecodeArgs& a, cudaStream_t stream) {
   const int max_chosen = a.n_experts < 2 * a.tokens ? a.n_experts : 2 * a.tokens;
   const int up_ctas = max_chosen * (a.expert_dim / kFeatPerCta) + a.shared_dim / kFeatPerCta;
   const size_t route_smem = (size_t)(a.n_experts + 4) * a.dim * 2;
-  // up to 4 tokens the gate/up CTAs route the tokens themselves
-  if ((a.tokens > 4 && launch_pdl(moe_decode_route_kernel, dim3((a.tokens + 3) / 4), dim3(128),
+  // up to 4 tokens the gate/up CTAs route the tokens themselves (or read the
+  // routing the depth mix did)
+  if ((a.tokens > 4 && !a.routed && launch_pdl(moe_decode_route_kernel, dim3((a.tokens + 3) / 4), dim3(128),
                                   route_smem, stream, a) != cudaSuccess) ||
       (a.tokens <= 4
            ? launch_pdl(moe_decode_up_kernel<4>, dim3(up_ctas), dim3(128), up_smem, stream, a)

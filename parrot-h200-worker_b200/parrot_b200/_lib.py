@@ -119,6 +119,8 @@ _SIGNATURES = {
                                                c_void_p]),
     "parrot_moe_decode_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                        POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
+    "parrot_moe_decode_routed_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
+                                       POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
     "parrot_moe_route_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,
                                       POINTER(MoeOutputs), c_void_p, c_size_t, c_void_p]),
     "parrot_moe_experts_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights), c_void_p,

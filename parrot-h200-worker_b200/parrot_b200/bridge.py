@@ -248,8 +248,9 @@ SLOT_GROUPING_MAX_TOKENS = 4096
 
 
 def _route_dims(cfg, rows: int) -> _lib.MoeDims:
-    """The MoE dims of a block whose router runs inside the depth mix."""
-    slots = SLOT_GROUPING and rows <= SLOT_GROUPING_MAX_TOKENS
+    """The MoE dims of a block whose router runs inside the depth mix (slot
+    mode above the decode batch sizes, whose kernels do not group)."""
+    slots = SLOT_GROUPING and DECODE_MOE_MAX_TOKENS < rows <= SLOT_GROUPING_MAX_TOKENS
     return moe_dims(cfg, rows, -2 if slots else 0)
 
 
@@ -259,13 +260,17 @@ def _block_dims(cfg, rows: int) -> _lib.MoeDims:
     return _route_dims(cfg, rows) if rows > DECODE_MOE_MAX_TOKENS else moe_dims(cfg, rows)
 
 
+# At decode batch sizes too (the small-batch kernels then read the routing
+# instead of computing it).  False: they route themselves.
+ROUTE_DECODE_IN_MIX = True
+
+
 def _routes_in_mix(route, rows: int) -> bool:
     """Whether the mix producing ``route``'s (an MoE module's, or None) input of
-    ``rows`` tokens also routes it: the grouped-GEMM path up to 4096 tokens
-    (at most DECODE_MOE_MAX_TOKENS rows usually take the small-batch kernels,
-    which route themselves)."""
-    return (route is not None and FUSE_MOE_ROUTER and
-            DECODE_MOE_MAX_TOKENS < rows <= 4096)
+    ``rows`` tokens also routes it: up to 4096 tokens (the grouped-GEMM path,
+    and at decode batch sizes the small-batch kernels)."""
+    low = 0 if ROUTE_DECODE_IN_MIX else DECODE_MOE_MAX_TOKENS
+    return route is not None and FUSE_MOE_ROUTER and low < rows <= 4096
 
 
 def _depth_call(module, sources: Sequence[Tensor], output_norm, pending_delta: Tensor | None,
@@ -572,11 +577,12 @@ def b200_moe(module, flat: Tensor, collect_stats: bool, addend: Tensor | None = 
                               None, None, None, None, None,
                               None if stats is None else stats.data_ptr())
     weights = _weights_struct(packed, bias)
-    if stats is None and 0 < T <= DECODE_MOE_MAX_TOKENS and cfg.expert_dim <= 1024 and not routed:
+    if stats is None and 0 < T <= DECODE_MOE_MAX_TOKENS and cfg.expert_dim <= 1024:
         # decode batch sizes: the two-kernel small-batch path
-        _lib.check(_lib.load().parrot_moe_decode_bf16(
+        fn = "parrot_moe_decode_routed_bf16" if routed else "parrot_moe_decode_bf16"
+        _lib.check(getattr(_lib.load(), fn)(
             ctypes.byref(dims), ctypes.byref(weights), _p(flat), ctypes.byref(outputs),
-            _p(ws), ws.numel(), _stream()), "parrot_moe_decode_bf16")
+            _p(ws), ws.numel(), _stream()), fn)
     elif routed:
         _lib.check(_lib.load().parrot_moe_forward_routed_bf16(
             ctypes.byref(dims), ctypes.byref(weights), _p(flat), ctypes.byref(outputs), 0,

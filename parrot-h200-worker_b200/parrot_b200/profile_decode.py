@@ -1,4 +1,5 @@
-"""Per-kernel timeline of a graph-replayed Parrot XL decode step.
+"""Per-kernel timeline of a graph-replayed Parrot XL decode step (or, with
+``--forward``, of the graph-replayed 1 x 512 forward the bench times).
 
 Builds Parrot XL (seed 0, bf16), prefills 128 random ids per batch row,
 captures one decode step (``Parrot.capture_decode``) and replays it under the
@@ -31,7 +32,7 @@ def timeline(prof, steps: int, top: int) -> list[str]:
         collections.Counter()
     prev_end = ks[0][0]
     for s, e, n in ks:
-        short = n.split("(")[0].replace("void ", "")[:56]
+        short = n.replace("(anonymous namespace)::", "").split("(")[0].replace("void ", "")[:56]
         exposed[short] += max(0.0, e - max(s, prev_end))
         dur[short] += e - s
         cnt[short] += 1
@@ -50,9 +51,23 @@ def main() -> None:
     p.add_argument("--batches", type=int, nargs="+", default=[1, 8, 64])
     p.add_argument("--steps", type=int, default=4)
     p.add_argument("--top", type=int, default=14)
+    p.add_argument("--forward", action="store_true", help="the 1 x 512 forward instead")
     a = p.parse_args()
     torch.manual_seed(0)
     model = Parrot(ModelConfig()).to("cuda", torch.bfloat16).eval()
+    if a.forward:
+        with torch.inference_mode():
+            ids = random_token_ids(1, 512, 32768, 0).cuda()
+            graphed = model.capture(1, 512)
+            for _ in range(3):
+                graphed(ids)
+            torch.cuda.synchronize()
+            with profile(activities=[ProfilerActivity.CUDA], acc_events=True) as prof:
+                for _ in range(a.steps):
+                    graphed.replay()
+                torch.cuda.synchronize()
+        print("== graphed forward 1 x 512: " + "\n".join(timeline(prof, a.steps, a.top)))
+        return
     with torch.inference_mode():
         for b in a.batches:
             ids = random_token_ids(b, 128, 32768, seed=b).cuda()

@@ -833,3 +833,64 @@ def test_depth_mix_with_router_matches_separate_kernels(rows, n_sources, pending
     same = (i0 == i1).all(-1).cuda()
     assert torch.equal(y0[same], y1[same]) or \
         float((y0[same].float() - y1[same].float()).abs().max()) <= 2 ** -6 * float(y0.float().abs().max())
+
+
+@pytest.mark.parametrize("rows,n_sources", [(1, 5), (3, 8), (4, 2)])
+def test_decode_moe_routed_by_the_depth_mix(rows, n_sources):
+    """Decode batch sizes: parrot_depthmix_route_bf16 + parrot_moe_decode_routed_bf16
+    (the gate/up kernel reads the routing, the down kernel fetches its expert
+    rows before its dependency wait) against parrot_depthmix_bf16 +
+    parrot_moe_decode_bf16 (the kernels route themselves): the mix is
+    bit-identical and the block output identical on every token routed alike."""
+    cfg = moe_config()
+    module, _ = build_moe_pair(cfg, seed=41 + rows)
+    dim = cfg.dim
+    g = torch.Generator().manual_seed(100 + rows)
+    srcs = [(torch.randn(rows, dim, generator=g) * (1 + i)).to(torch.bfloat16).cuda()
+            for i in range(n_sources)]
+    query = (0.3 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    key_w = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    out_w = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    res = torch.randn(rows, dim, generator=g).to(torch.bfloat16).cuda()
+    lib = _lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    ptrs = (ctypes.c_void_p * n_sources)(*[s.data_ptr() for s in srcs])
+    dims = bridge.moe_dims(cfg, rows)
+    w = bridge._weights_struct(bridge.pack_weights(module), None)
+    results = {}
+    for fused in (False, True):
+        out = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16)
+        ws = torch.zeros(int(bridge.workspace_layout(dims).total), device="cuda",
+                         dtype=torch.uint8)
+        idx = torch.empty(rows, 2, device="cuda", dtype=torch.int64)
+        y = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16)
+        args = (ctypes.c_void_p(out.data_ptr()), ptrs, n_sources,
+                ctypes.c_void_p(query.data_ptr()), ctypes.c_void_p(key_w.data_ptr()), 1e-6,
+                ctypes.c_void_p(out_w.data_ptr()), 1e-6, None, None, None, None, rows, dim)
+        if fused:
+            ro = _lib.MoeOutputs(None, None, None, idx.data_ptr(), None, None, None, None)
+            _lib.check(lib.parrot_depthmix_route_bf16(
+                *args, ctypes.byref(dims), ctypes.byref(w), ctypes.byref(ro),
+                ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream), "depthmix_route")
+            mo = _lib.MoeOutputs(y.data_ptr(), res.data_ptr(), None, None, None, None, None, None)
+            _lib.check(lib.parrot_moe_decode_routed_bf16(
+                ctypes.byref(dims), ctypes.byref(w), ctypes.c_void_p(out.data_ptr()),
+                ctypes.byref(mo), ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream),
+                "moe_decode_routed")
+        else:
+            _lib.check(lib.parrot_depthmix_bf16(*args, stream), "depthmix")
+            mo = _lib.MoeOutputs(y.data_ptr(), res.data_ptr(), None, idx.data_ptr(), None, None,
+                                 None, None)
+            _lib.check(lib.parrot_moe_decode_bf16(
+                ctypes.byref(dims), ctypes.byref(w), ctypes.c_void_p(out.data_ptr()),
+                ctypes.byref(mo), ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream),
+                "moe_decode")
+        torch.cuda.synchronize()
+        results[fused] = (out.clone(), idx.cpu(), y.clone())
+    (o0, i0, y0), (o1, i1, y1) = results[False], results[True]
+    assert torch.equal(o0, o1)
+    same = (i0 == i1).all(-1)
+    assert bool(same.any())
+    assert torch.equal(y0[same.cuda()], y1[same.cuda()]) or \
+        float((y0[same.cuda()].float() - y1[same.cuda()].float()).abs().max()) <= \
+        2 ** -6 * float(y0.float().abs().max())
