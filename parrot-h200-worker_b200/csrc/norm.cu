@@ -419,12 +419,166 @@ __global__ void __launch_bounds__(32 * W * R, (NS <= 8 && R == 1) ? 768 / (32 * 
   }
 }
 
+// The plain depth mix at large row counts (no deferred source, no router):
+// each thread takes its 16-byte vector of two rows, so the per-CTA work that
+// does not depend on the row (the query and norm weights, their products,
+// the launch and the block barriers) is shared by two rows and the two rows'
+// chains interleave.  Every row's arithmetic is the one-row kernel's, in the
+// same order (bit-identical outputs).
+template <int W, int NS>
+__global__ void __launch_bounds__(32 * W, 4)
+    depthmix2_kernel(DepthMixArgs a) {
+  __shared__ float red_sr[2][W][2 * NS], red_sq[2][W];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = threadIdx.x;
+  const int dim = a.dim, nvec = dim >> 3, S = a.n_sources;
+  const int row0 = 2 * blockIdx.x;
+  bool active[2];
+  size_t off[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    active[u] = c < nvec && row0 + u < a.rows;
+    off[u] = (size_t)(row0 + u) * dim;
+  }
+  float q[8], kw[8];
+  uint4 owv = make_uint4(0, 0, 0, 0);
+  if (c < nvec) {
+    bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.query) + c), q);
+    bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(a.key_w) + c), kw);
+    if (a.out_w != nullptr) owv = __ldg(reinterpret_cast<const uint4*>(a.out_w) + c);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = kw[j] = 0.f;
+  }
+  griddep_wait();
+  griddep_launch();
+
+  uint4 v[2][NS];
+#pragma unroll
+  for (int u = 0; u < 2; ++u)
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      v[u][s] = make_uint4(0, 0, 0, 0);
+      if (s < S && active[u]) v[u][s] = __ldg(reinterpret_cast<const uint4*>(a.sources[s] + off[u]) + c);
+    }
+  float2 kq[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) kq[p] = make_float2(kw[2 * p] * q[2 * p], kw[2 * p + 1] * q[2 * p + 1]);
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    float sr[2 * NS];
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      sr[s] = 0.f;
+      sr[NS + s] = 0.f;
+      if (s < S) {
+        const uint32_t w[4] = {v[u][s].x, v[u][s].y, v[u][s].z, v[u][s].w};
+        float2 ss2 = make_float2(0.f, 0.f), raw2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float2 f2 = bf16x2_to_float2(w[p]);
+          ss2 = __ffma2_rn(f2, f2, ss2);
+          raw2 = __ffma2_rn(f2, kq[p], raw2);
+        }
+        sr[s] = ss2.x + ss2.y;
+        sr[NS + s] = raw2.x + raw2.y;
+      }
+    }
+    const float sr_l = warp_reduce_many<2 * NS>(sr, lane);
+    if (lane < 2 * NS) red_sr[u][warp][lane] = sr_l;
+  }
+  __syncthreads();
+  const float inv_dim = 1.0f / (float)dim;
+  float h[2][8], sq[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    float score = -INFINITY;
+    if (lane < S) {
+      float tss = 0.f, traw = 0.f;
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        tss += red_sr[u][w][lane];
+        traw += red_sr[u][w][NS + lane];
+      }
+      score = rsqrtf(tss * inv_dim + a.key_eps) * traw;
+    }
+    const float m = warp_max(score);
+    const float e_l = lane < S ? __expf(score - m) : 0.f;
+    float alpha[NS];
+    float den = 0.f;
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      alpha[s] = __shfl_sync(0xffffffffu, e_l, s);
+      den += alpha[s];
+    }
+    const float rden = 1.0f / den;
+    float2 h2[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) h2[p] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      if (s < S) {
+        const float al = alpha[s] * rden;
+        const float2 al2 = make_float2(al, al);
+        const uint32_t w[4] = {v[u][s].x, v[u][s].y, v[u][s].z, v[u][s].w};
+#pragma unroll
+        for (int p = 0; p < 4; ++p) h2[p] = __ffma2_rn(al2, bf16x2_to_float2(w[p]), h2[p]);
+      }
+    }
+    sq[u] = 0.f;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      h[u][2 * p] = round_bf16(h2[p].x);
+      h[u][2 * p + 1] = round_bf16(h2[p].y);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sq[u] = fmaf(h[u][j], h[u][j], sq[u]);
+    if (active[u] && a.mix_out != nullptr)
+      reinterpret_cast<uint4*>(a.mix_out + off[u])[c] = float_to_bf16x8(h[u]);
+    if (a.out_w == nullptr) {
+      if (active[u]) reinterpret_cast<uint4*>(a.out + off[u])[c] = float_to_bf16x8(h[u]);
+    } else {
+      sq[u] = warp_sum(sq[u]);
+      if (lane == 0) red_sq[u][warp] = sq[u];
+    }
+  }
+  if (a.out_w == nullptr) return;
+  __syncthreads();
+  float g[8];
+  bf16x8_to_float(owv, g);
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    float total = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) total += red_sq[u][w];
+    const float inv = rsqrtf(total / (float)dim + a.out_eps);
+    if (active[u]) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (h[u][j] * inv) * g[j];
+      reinterpret_cast<uint4*>(a.out + off[u])[c] = float_to_bf16x8(o);
+    }
+  }
+}
+
+// rows from which the two-row kernel takes the plain mix, up to 4 sources (at
+// 32768 rows: 4 sources 69.2 -> 61.8 us; 8 sources measured 109.0 against
+// 102.9 us, its 118 registers leaving too few warps per SM)
+constexpr int kDepthMixTwoRowsFrom = 8192;
+
 template <int W>
 static int launch_depthmix_w(const DepthMixArgs& args, cudaStream_t stream) {
   const dim3 grid(args.rows), block(32 * W);
   const int S = args.n_sources;
   const DepthRouteArgs none{};
   cudaError_t e;
+  const bool plain = args.pending_delta == nullptr && args.pending_contrib == nullptr;
+  if (plain && args.rows >= kDepthMixTwoRowsFrom && S <= 4) {
+    const dim3 grid2((args.rows + 1) / 2);
+    if (S <= 2) e = launch_pdl(depthmix2_kernel<W, 2>, grid2, block, 0, stream, args);
+    else e = launch_pdl(depthmix2_kernel<W, 4>, grid2, block, 0, stream, args);
+    return e == cudaSuccess ? 0 : -2;
+  }
   if (S <= 2) e = launch_pdl(depthmix_kernel<W, 2, 1, 0>, grid, block, 0, stream, args, none);
   else if (S <= 4) e = launch_pdl(depthmix_kernel<W, 4, 1, 0>, grid, block, 0, stream, args, none);
   else if (S <= 8) e = launch_pdl(depthmix_kernel<W, 8, 1, 0>, grid, block, 0, stream, args, none);

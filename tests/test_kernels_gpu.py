@@ -894,3 +894,51 @@ def test_decode_moe_routed_by_the_depth_mix(rows, n_sources):
     assert torch.equal(y0[same.cuda()], y1[same.cuda()]) or \
         float((y0[same.cuda()].float() - y1[same.cuda()].float()).abs().max()) <= \
         2 ** -6 * float(y0.float().abs().max())
+
+
+@pytest.mark.parametrize("rows,n_sources,norm", [(8192, 4, True), (8193, 4, True),
+                                                 (9000, 3, False), (8192, 2, True),
+                                                 (8192, 8, True)])
+def test_two_row_depth_mix_is_bit_identical(rows, n_sources, norm):
+    """From 8192 rows the plain depth mix with up to 4 sources runs two rows per
+    thread (8 sources: the one-row kernel either way); every
+    row's arithmetic is the one-row kernel's, so the output equals the same
+    rows mixed in calls below that size (one-row kernel) bit for bit, and
+    stays within the bf16 contract of the oracle."""
+    dim = 768
+    g = torch.Generator().manual_seed(rows + n_sources)
+    srcs = [(torch.randn(rows, dim, generator=g) * (1 + i)).to(torch.bfloat16).cuda()
+            for i in range(n_sources)]
+    q = (0.3 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    kw = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    ow = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    lib = _lib.load()
+
+    def mix(lo, hi):
+        n = hi - lo
+        out = torch.empty(n, dim, device="cuda", dtype=torch.bfloat16)
+        mix_out = torch.empty_like(out)
+        parts = [s[lo:hi] for s in srcs]
+        ptrs = (ctypes.c_void_p * n_sources)(*[p.data_ptr() for p in parts])
+        _lib.check(lib.parrot_depthmix_bf16(
+            out.data_ptr(), ptrs, n_sources, q.data_ptr(), kw.data_ptr(), 1e-6,
+            ow.data_ptr() if norm else None, 1e-6, mix_out.data_ptr(), None, None, None, n, dim,
+            bridge._stream()), "parrot_depthmix_bf16")
+        return out, mix_out
+
+    whole, whole_mix = mix(0, rows)
+    half = rows // 2  # each part below the two-row threshold
+    a, am = mix(0, half)
+    b, bm = mix(half, rows)
+    torch.cuda.synchronize()
+    assert torch.equal(whole, torch.cat([a, b]))
+    assert torch.equal(whole_mix, torch.cat([am, bm]))
+    _, orc, onorm, _ = _depth_modules(dim, 1)
+    orc.query.data.copy_(q.float().cpu())
+    orc.norm.weight.data.copy_(kw.float().cpu())
+    onorm.weight.data.copy_(ow.float().cpu())
+    sample = torch.arange(0, rows, 97)
+    exp_mix = orc([s.float().cpu()[sample] for s in srcs])
+    assert_bf16_close(whole_mix.cpu()[sample], exp_mix, "two-row mix")
+    if norm:
+        assert_bf16_close(whole.cpu()[sample], onorm(exp_mix), "two-row mix + norm")
