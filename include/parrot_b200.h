@@ -306,7 +306,10 @@ int parrot_moe_forward_deferred_bf16(const parrot_moe_dims* dims,
  * run.  Rows of one expert are in no particular order within its region
  * (positions say where each went; the block output does not depend on it).
  * The call must be followed by parrot_moe_forward_routed_bf16 on the same
- * workspace, which reads the counters and leaves them zero. */
+ * workspace, which reads the counters and leaves them zero.  Counters left
+ * set by a routing call whose block never ran are caught: a slot past the
+ * expert's region is reported in the status word (PARROT code 2) and nothing
+ * is written there; parrot_moe_workspace_init zeroes the counters again. */
 int parrot_depthmix_route_bf16(void* out, const void* const* sources, int n_sources,
                                const void* query, const void* key_norm_weight, float key_eps,
                                const void* out_norm_weight, float out_eps, void* mix_out,

@@ -403,6 +403,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     int rows = 0;
     if (s < n_seg) {
       rows = g.seg_rows[s];
+      if (g.seg_stride > 0 && rows > g.seg_stride) {
+        // slot mode: a counter beyond its region (left over from a routing
+        // call whose block never ran) is reported and read no further
+        report_status(g.status, kStatusBadIndex, 53, rows);
+        rows = g.seg_stride;
+      }
       t.seg_rows[s] = rows;
       t.seg_base[s] = g.seg_stride > 0 ? s * g.seg_stride : g.seg_base[s];
       t.seg_expert[s] = g.seg_expert != nullptr ? g.seg_expert[s] : s % g.n_experts;

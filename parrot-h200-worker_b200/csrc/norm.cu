@@ -387,13 +387,21 @@ __global__ void __launch_bounds__(32 * W * R, (NS <= 8 && R == 1) ? 768 / (32 * 
         if (ra.r.slot_counts != nullptr) {
           // the grouping: the next free slot of each expert, then the row's
           // position, contribution slot (the lower expert id first) and weight
-          const int r1 = i1 * ra.r.slot_stride + atomicAdd(ra.r.slot_counts + i1, 1);
-          const int r2 = i2 * ra.r.slot_stride + atomicAdd(ra.r.slot_counts + i2, 1);
-          reinterpret_cast<int2*>(ra.r.positions)[row] = make_int2(r1, r2);
-          ra.r.row_dst[r1] = 2 * row + (i1 < i2 ? 0 : 1);
-          ra.r.row_dst[r2] = 2 * row + (i2 < i1 ? 0 : 1);
-          ra.r.row_w[r1] = w1;
-          ra.r.row_w[r2] = w2;
+          const int s1 = atomicAdd(ra.r.slot_counts + i1, 1);
+          const int s2 = atomicAdd(ra.r.slot_counts + i2, 1);
+          int r1 = i1 * ra.r.slot_stride + s1, r2 = i2 * ra.r.slot_stride + s2;
+          if (s1 >= ra.r.slot_stride || s2 >= ra.r.slot_stride) {
+            // counters left over from a routing call whose block never ran:
+            // nothing is written past the expert's region
+            report_status(ra.r.status, kStatusBadIndex, 50, max(s1, s2));
+            r1 = r2 = -1;
+          } else {
+            reinterpret_cast<int2*>(ra.r.positions)[row] = make_int2(r1, r2);
+            ra.r.row_dst[r1] = 2 * row + (i1 < i2 ? 0 : 1);
+            ra.r.row_dst[r2] = 2 * row + (i2 < i1 ? 0 : 1);
+            ra.r.row_w[r1] = w1;
+            ra.r.row_w[r2] = w2;
+          }
           slot_row[ty][0] = r1;
           slot_row[ty][1] = r2;
         }
@@ -403,7 +411,7 @@ __global__ void __launch_bounds__(32 * W * R, (NS <= 8 && R == 1) ? 768 / (32 * 
       if (lane < NP) psum[ty][lane] = p;
     }
     __syncthreads();
-    if (ra.r.slot_counts != nullptr && active && row < a.rows) {
+    if (ra.r.slot_counts != nullptr && active && row < a.rows && slot_row[ty][0] >= 0) {
       // this thread's 16 bytes of the row, into both grouped rows
       const size_t nv = (size_t)nvec;
       reinterpret_cast<uint4*>(ra.r.grouped)[(size_t)slot_row[ty][0] * nv + c] = ov;

@@ -280,18 +280,30 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
     if (threadIdx.x < E) {
       const int e = threadIdx.x;
       const int cnt = sm.hist[0][e] + sm.hist[1][e] + sm.hist[2][e] + sm.hist[3][e];
-      sm.slot_cur[e] = e * a.slot_stride + atomicAdd(a.slot_counts + e, cnt);
+      const int base = atomicAdd(a.slot_counts + e, cnt);
+      if (base + cnt > a.slot_stride) {
+        // counters left over from a call whose block never ran: nothing is
+        // written past the expert's region (negative rows are skipped)
+        report_status(a.status, kStatusBadIndex, 52, base + cnt);
+        sm.slot_cur[e] = -(1 << 30);
+      } else {
+        sm.slot_cur[e] = e * a.slot_stride + base;
+      }
     }
     __syncthreads();
-    int r1 = 0, r2 = 0;
+    int r1 = -1, r2 = -1;
     if (valid_tok) {
       r1 = atomicAdd(&sm.slot_cur[i1], 1);
       r2 = atomicAdd(&sm.slot_cur[i2], 1);
-      reinterpret_cast<int2*>(a.positions)[t] = make_int2(r1, r2);
-      a.row_dst[r1] = 2 * t + (i1 < i2 ? 0 : 1);
-      a.row_dst[r2] = 2 * t + (i2 < i1 ? 0 : 1);
-      a.row_w[r1] = w1;
-      a.row_w[r2] = w2;
+      if (r1 < 0 || r2 < 0) {
+        r1 = r2 = -1;
+      } else {
+        reinterpret_cast<int2*>(a.positions)[t] = make_int2(r1, r2);
+        a.row_dst[r1] = 2 * t + (i1 < i2 ? 0 : 1);
+        a.row_dst[r2] = 2 * t + (i2 < i1 ? 0 : 1);
+        a.row_w[r1] = w1;
+        a.row_w[r2] = w2;
+      }
     }
     // four tokens' loads in flight before their stores (a load after a store
     // through another pointer waits for it: one memory round trip per token)
@@ -316,7 +328,7 @@ __global__ void __launch_bounds__(128) route_kernel(const __grid_constant__ CUte
         const int g1 = __shfl_sync(0xffffffffu, r1, u0 + u);
         const int g2 = __shfl_sync(0xffffffffu, r2, u0 + u);
         const int tu = tile * rows + warp * 32 + u0 + u;
-        if (warp * 32 + u0 + u >= rows || tu >= T) continue;  // uniform over the warp
+        if (warp * 32 + u0 + u >= rows || tu >= T || g1 < 0) continue;  // uniform over the warp
 #pragma unroll
         for (int k = 0; k < kV; ++k) {
           const int c = lane + 32 * k;
@@ -463,23 +475,30 @@ __global__ void __launch_bounds__(32 * kRouteSmallTile)
     // (the lower expert id first) and weight; then the warp writes its
     // tokens' rows to their two grouped rows from the registers that hold
     // them (exact bf16 values, packed again).
-    int r1 = 0, r2 = 0;
+    int r1 = -1, r2 = -1;
     if (valid_t && ex == 0) {
       const float sel = v1 + v2;
-      r1 = i1 * a.slot_stride + atomicAdd(a.slot_counts + i1, 1);
-      r2 = i2 * a.slot_stride + atomicAdd(a.slot_counts + i2, 1);
-      reinterpret_cast<int2*>(a.positions)[t] = make_int2(r1, r2);
-      a.row_dst[r1] = 2 * t + (i1 < i2 ? 0 : 1);
-      a.row_dst[r2] = 2 * t + (i2 < i1 ? 0 : 1);
-      a.row_w[r1] = v1 / sel;
-      a.row_w[r2] = v2 / sel;
+      const int s1 = atomicAdd(a.slot_counts + i1, 1), s2 = atomicAdd(a.slot_counts + i2, 1);
+      if (s1 >= a.slot_stride || s2 >= a.slot_stride) {
+        // counters left over from a call whose block never ran: nothing is
+        // written past the expert's region
+        report_status(a.status, kStatusBadIndex, 51, max(s1, s2));
+      } else {
+        r1 = i1 * a.slot_stride + s1;
+        r2 = i2 * a.slot_stride + s2;
+        reinterpret_cast<int2*>(a.positions)[t] = make_int2(r1, r2);
+        a.row_dst[r1] = 2 * t + (i1 < i2 ? 0 : 1);
+        a.row_dst[r2] = 2 * t + (i2 < i1 ? 0 : 1);
+        a.row_w[r1] = v1 / sel;
+        a.row_w[r2] = v2 / sel;
+      }
     }
     uint4* grouped = reinterpret_cast<uint4*>(a.grouped);
 #pragma unroll
     for (int u = 0; u < TW; ++u) {
       const int g1 = __shfl_sync(0xffffffffu, r1, u * NP);
       const int g2 = __shfl_sync(0xffffffffu, r2, u * NP);
-      if (t_first + u >= T) continue;
+      if (t_first + u >= T || g1 < 0) continue;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int c = lane + 32 * k;

@@ -942,3 +942,69 @@ def test_two_row_depth_mix_is_bit_identical(rows, n_sources, norm):
     assert_bf16_close(whole_mix.cpu()[sample], exp_mix, "two-row mix")
     if norm:
         assert_bf16_close(whole.cpu()[sample], onorm(exp_mix), "two-row mix + norm")
+
+
+def test_slot_mode_left_over_counters_are_reported_not_written_past():
+    """Slot mode keeps per-expert counters in the workspace; a routing call
+    whose block never runs leaves them set.  Routing again and again with
+    every token on one expert must report the overflow in the status word and
+    write nothing past the expert's region; parrot_moe_workspace_init clears
+    the counters and the block then runs as usual."""
+    cfg = moe_config()
+    module, _ = build_moe_pair(cfg, seed=77)
+    rows, dim = 256, cfg.dim
+    g = torch.Generator().manual_seed(5)
+    src = torch.randn(rows, dim, generator=g).to(torch.bfloat16).cuda()
+    q = (0.3 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    kw = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    ow = (1 + 0.2 * torch.randn(dim, generator=g)).to(torch.bfloat16).cuda()
+    bias = torch.tensor([30.0] + [0.0] * (cfg.n_experts - 1), device="cuda")
+    lib = _lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    ptrs = (ctypes.c_void_p * 1)(src.data_ptr())
+    dims = bridge.moe_dims(cfg, rows, -2)
+    layout = bridge.workspace_layout(dims)
+    # room past the workspace to see that nothing lands there
+    guard = 1 << 20
+    buf = torch.zeros(int(layout.total) + guard, device="cuda", dtype=torch.uint8)
+    ws = buf[:int(layout.total)]
+    w = bridge._weights_struct(bridge.pack_weights(module), bias)
+    out = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16)
+    ro = _lib.MoeOutputs()
+
+    def route():
+        _lib.check(lib.parrot_depthmix_route_bf16(
+            ctypes.c_void_p(out.data_ptr()), ptrs, 1, ctypes.c_void_p(q.data_ptr()),
+            ctypes.c_void_p(kw.data_ptr()), 1e-6, ctypes.c_void_p(ow.data_ptr()), 1e-6, None,
+            None, None, None, rows, dim, ctypes.byref(dims), ctypes.byref(w), ctypes.byref(ro),
+            ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream), "depthmix_route")
+
+    def status():
+        st = (ctypes.c_int * 4)()
+        _lib.check(lib.parrot_moe_read_status(ctypes.c_void_p(ws.data_ptr()), ctypes.byref(dims),
+                                              st, stream), "status")
+        return list(st)
+
+    def block():
+        y = torch.empty(rows, dim, device="cuda", dtype=torch.bfloat16)
+        mo = _lib.MoeOutputs(y.data_ptr(), None, None, None, None, None, None, None)
+        _lib.check(lib.parrot_moe_forward_routed_bf16(
+            ctypes.byref(dims), ctypes.byref(w), ctypes.c_void_p(out.data_ptr()),
+            ctypes.byref(mo), 0, ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream), "routed")
+        torch.cuda.synchronize()
+        return y
+
+    route()
+    first = block()  # a clean pair leaves the counters at zero
+    assert status() == [0, 0, 0, 0]
+    for _ in range(3):  # every token's first expert is 0: T slots of its 2T per call
+        route()
+    torch.cuda.synchronize()
+    st = status()
+    assert st[0] == 2 and st[1] == 50, st  # a bad index, reported by the routing depth mix
+    assert int(buf[int(layout.total):].count_nonzero()) == 0
+    _lib.check(lib.parrot_moe_workspace_init(ctypes.c_void_p(ws.data_ptr()), ctypes.byref(dims),
+                                             stream), "workspace_init")
+    route()
+    assert torch.equal(block(), first)
+    assert status() == [0, 0, 0, 0]
