@@ -459,13 +459,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     t.n_secondary = t.prefix[n_seg] +
                     ((g.shared_rows + BN - 1) / BN) * (g.m_tiles_shared / Cfg::kMPerUnit);
     griddep_launch();
-    // slot mode: this CTA has copied the counters; the last CTA to do so
-    // zeroes them for the next block (the kernels after this one start once
-    // it has completed)
-    if (g.slot_ticket != nullptr && atomicAdd(g.slot_ticket, 1) == (int)gridDim.x - 1) {
-      for (int e = 0; e < g.n_experts; ++e) g.slot_counts[e] = 0;
-      *g.slot_ticket = 0;
-    }
   }
   __syncthreads();
 
@@ -582,6 +575,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
+    // slot mode: this CTA has copied the counters (the barrier above); the
+    // last CTA to get here zeroes them for the next block (the kernels after
+    // this one start once it has completed).  Taken by an epilogue warp,
+    // idle until its first accumulator, so the round trip delays no load.
+    if (g.slot_ticket != nullptr && warp == 2 && lane == 0 &&
+        atomicAdd(g.slot_ticket, 1) == (int)gridDim.x - 1) {
+      for (int e = 0; e < g.n_experts; ++e) g.slot_counts[e] = 0;
+      *g.slot_ticket = 0;
+    }
     if (g.st.stats != nullptr && blockIdx.x == gridDim.x - 1)
       slot_stats(g, t, reinterpret_cast<float*>(epi_tiles), threadIdx.x - 64);
     const int q = warp & 3;                 // TMEM lane quarter of this warp
