@@ -425,8 +425,10 @@ def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 
     16384 tokens split evenly over the ranks.  The product path exchanges rows
     and outputs through the other ranks' memory (``ep.PeerExpertParallelMoE``,
     CUDA IPC over NVLink) with no host synchronisation; it is captured once as
-    a CUDA graph and replayed, with a load-balanced placement and with
-    round-robin placement.  Per-phase times come from CUDA events between the
+    a CUDA graph and replayed, with a load-balanced placement (rows stored
+    into the peers by the grouping kernel and the down GEMM, and, beside it,
+    by separate copy kernels) and with round-robin placement.  Per-phase
+    times come from CUDA events between the
     phases of one eager call; the NCCL all-to-all path with its host read of
     the split sizes (``ep.ExpertParallelMoE``, round-robin) is timed beside it.
     Every number is the max over ranks."""
@@ -467,15 +469,19 @@ def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 
         # load-balanced placement replicates the experts above 1 / world of them
         _, _, util = bridge.b200_moe(moe, x.to("cuda", torch.bfloat16), True)
         counts = (util.float() * 2 * total).round().int().tolist()
-    placements = {"balanced": ep.Placement.balanced(counts, world),
-                  "round_robin": ep.Placement.round_robin(world, cfg.n_experts)}
+    balanced = ep.Placement.balanced(counts, world)
+    # (placement, rows stored by the grouping kernel and the down GEMM
+    # themselves, or moved by separate copy kernels)
+    variants = {"balanced": (balanced, True),
+                "balanced_copy_kernels": (balanced, False),
+                "round_robin": (ep.Placement.round_robin(world, cfg.n_experts), True)}
     res = {}
-    for name, placement in placements.items():
+    for name, (placement, fused) in variants.items():
         shape = ep.EpShape(world, per, cfg.dim, cfg.n_experts, cfg.expert_dim,
                            placement=placement)
         peers = ep.PeerSet.connect(shape)
         with torch.inference_mode():
-            layer = ep.PeerExpertParallelMoE(moe, peers)
+            layer = ep.PeerExpertParallelMoE(moe, peers, fused=fused)
             for _ in range(warmup):
                 layer(xs)
             eager_us = timed(lambda: layer(xs), iters)
@@ -530,8 +536,12 @@ def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 
             "placement": "load-balanced from the batch's routing counts: experts above 1/ranks "
                          "of the rows replicated (each source computes its own rows of them), "
                          "the rest largest first onto the least-loaded rank",
-            "exchange": "peer memory (CUDA IPC over NVLink): stores + epoch flags, no host read",
-            "balanced": best, "round_robin": res["round_robin"],
+            "exchange": "peer memory (CUDA IPC over NVLink): the grouping kernel stores each "
+                        "row into its destination's receive region and the down GEMM each "
+                        "output into its source's return region; epoch flags, no host read "
+                        "(balanced_copy_kernels: separate send / return copy kernels instead)",
+            "balanced": best, "balanced_copy_kernels": res["balanced_copy_kernels"],
+            "round_robin": res["round_robin"],
             "nccl_all_to_all_host_read_us": nccl_us,
             "timing": "CUDA-graph replay of the whole layer, CUDA events, max over ranks; "
                       "phase_us: one eager call behind a GPU sleep, events between phases, "

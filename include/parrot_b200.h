@@ -491,6 +491,15 @@ int parrot_argmax_rows_bf16(long long* out, const void* logits, int rows, int co
  *   parrot_moe_ep_experts_bf16       local experts on the received rows
  *   parrot_moe_ep_return_bf16        outputs back into every source's buffer
  *   parrot_moe_ep_combine_peer_bf16  wait for every return; combine (+ residual)
+ * or, with the copies folded into the kernels that produce the rows:
+ *   parrot_moe_ep_dispatch_send_bf16   router + grouping storing each row into
+ *                                      its destination's receive region; counts
+ *   parrot_moe_shared_ffn_bf16, parrot_moe_ep_receive
+ *   parrot_moe_ep_experts_return_bf16  local experts, the down GEMM storing each
+ *                                      output into its source's return region
+ *   parrot_moe_ep_combine_peer_bf16
+ * Both sequences leave the same bytes in every buffer the combine reads and
+ * may be mixed from call to call.
  * Nothing is read back to the host and every size is fixed by max_tokens, so
  * the sequence can be captured in a CUDA graph.  Every rank must make the
  * same calls in the same order (a rank with no tokens still calls them).
@@ -572,6 +581,19 @@ int parrot_moe_ep_send_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* e
                             const parrot_ep_peers* peers, const void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* parrot_moe_ep_dispatch_planned_bf16 then parrot_moe_ep_send_bf16 without
+ * the copy: the grouping kernel stores every dispatched row straight into
+ * its destination's receive region (peer memory, 16-byte stores) and fences
+ * them at system scope; the send kernel then writes the counts and row base
+ * and raises the arrival flags.  The workspace's grouped rows are not
+ * written.  dims as parrot_moe_ep_send_bf16 (capacity -1); with no tokens
+ * only the counts and flags are sent. */
+int parrot_moe_ep_dispatch_send_bf16(const parrot_moe_dims* dims,
+                                     const parrot_moe_weights* weights, const void* x,
+                                     const parrot_moe_outputs* outputs, const parrot_ep_dims* ep,
+                                     const parrot_ep_peers* peers, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
 /* Waits for every source's arrival flag, then writes the segment table of the
  * received rows (one segment per (source, local slot)) into the buffer. */
 int parrot_moe_ep_receive(const parrot_ep_dims* ep, void* buffer, void* stream);
@@ -586,6 +608,14 @@ int parrot_moe_ep_experts_bf16(const parrot_ep_dims* ep, void* buffer, const voi
  * dispatch order, then raises this rank's return flag there. */
 int parrot_moe_ep_return_bf16(const parrot_ep_dims* ep, const parrot_ep_peers* peers,
                               void* stream);
+
+/* parrot_moe_ep_experts_bf16 then parrot_moe_ep_return_bf16 without the
+ * copy: the down GEMM's epilogue stores each output row straight into its
+ * source's return region (peer memory, 16-byte stores, at the row base the
+ * source sent) and fences at system scope; a one-block kernel then raises
+ * the return flags.  The buffer's y is not written. */
+int parrot_moe_ep_experts_return_bf16(const parrot_ep_dims* ep, const parrot_ep_peers* peers,
+                                      const void* gate_up, const void* down, void* stream);
 
 /* Waits for every expert rank's return flag, then parrot_moe_ep_combine_bf16
  * on the returned rows (buffer's back_rows). */

@@ -256,9 +256,17 @@ parrot::RouteArgs route_args(const parrot_moe_dims* dims, const parrot_moe_weigh
 // x_from_upstream: x was written by the kernel just before this one on the
 // stream (the depth mix with the router folded in), so the grouping may only
 // read it after its dependency wait.
+// Expert parallelism: the dispatched rows go straight into each destination's
+// receive region for this source (peer memory) instead of the workspace.
+struct EpRowsTo {
+  __nv_bfloat16* recv[parrot::kEpMaxRanks];
+  signed char dest[parrot::kMaxExperts];  // destination rank of each expert
+  int region;                             // rows of one receive region
+};
+
 int run_group(const parrot_moe_dims* dims, const void* x, const parrot_moe_outputs* o, void* ws,
               const parrot_moe_layout& L, cudaStream_t s, const signed char* ep_order = nullptr,
-              bool x_from_upstream = false) {
+              bool x_from_upstream = false, const EpRowsTo* to = nullptr) {
   const int T = dims->tokens, E = dims->n_experts;
   parrot::GroupArgs ga{};
   ga.x = static_cast<const __nv_bfloat16*>(x);
@@ -279,6 +287,11 @@ int run_group(const parrot_moe_dims* dims, const void* x, const parrot_moe_outpu
   ga.ep_packed = ep_order != nullptr;
   if (ep_order != nullptr)
     for (int q = 0; q < E; ++q) ga.ep_order[q] = ep_order[q];
+  if (to != nullptr) {
+    for (int q = 0; q < parrot::kEpMaxRanks; ++q) ga.ep_recv[q] = to->recv[q];
+    for (int e = 0; e < parrot::kMaxExperts; ++e) ga.ep_dest[e] = to->dest[e];
+    ga.ep_region = to->region;
+  }
   const int ng = parrot::group_blocks(T);
   const int want = (2 * sm_count() + ng - 1) / ng;  // about two blocks per SM
   int split = 1;
@@ -315,7 +328,8 @@ void set_slots(parrot::RouteArgs* ra, void* ws, const parrot_moe_layout& L, cons
 // Router + grouping (slots: the router groups the rows itself, slot mode).
 int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const void* x,
               const parrot_moe_outputs* o, void* ws, const parrot_moe_layout& L, cudaStream_t s,
-              const signed char* ep_order = nullptr, bool slots = false) {
+              const signed char* ep_order = nullptr, bool slots = false,
+              const EpRowsTo* to = nullptr) {
   const int T = dims->tokens, E = dims->n_experts;
   parrot::RouteArgs ra = route_args(dims, w, o, ws, L);
   if (slots) set_slots(&ra, ws, L, x);
@@ -328,7 +342,7 @@ int run_route(const parrot_moe_dims* dims, const parrot_moe_weights* w, const vo
     return fail(PARROT_ECUDA, "route: unsupported dim or shared-memory setup failed%s");
   int rc = check_launch("route_kernel");
   if (rc || slots) return rc;
-  return run_group(dims, x, o, ws, L, s, ep_order);
+  return run_group(dims, x, o, ws, L, s, ep_order, false, to);
 }
 
 int run_gemm(bool swiglu, const parrot_moe_dims* dims, const parrot_moe_weights* w,
@@ -469,9 +483,19 @@ int ws_ok(const void* ws, size_t ws_bytes, const parrot_moe_layout& L) {
 
 // Grouped SwiGLU FFN over caller-described row segments: hidden = SwiGLU
 // halves of x @ gate_up, y = hidden @ down, rows in the order of x.
+// Expert parallelism: the down GEMM stores source q's rows straight into q's
+// return region (peer memory), at the row base q sent, instead of into y.
+struct EpRowsBack {
+  __nv_bfloat16* back[parrot::kEpMaxRanks];  // each source's return region
+  const int* base;                           // [ranks] device table: each source's row base
+  int segs_per_source;                       // segment s belongs to source s / segs_per_source
+  int region;                                // rows of one receive region
+};
+
 int run_ffn(int rows, int dim, int expert_dim, int n_mats, int n_seg, const int* seg_rows,
             const int* seg_base, const int* seg_expert, const void* gate_up, const void* down,
-            const void* x, void* hidden, void* y, int* status, cudaStream_t s) {
+            const void* x, void* hidden, void* y, int* status, cudaStream_t s,
+            const EpRowsBack* back = nullptr) {
   CUtensorMap mw, mx;
   const int sms = sm_count();
   for (int stage = 0; stage < 2; ++stage) {
@@ -501,6 +525,12 @@ int run_ffn(int rows, int dim, int expert_dim, int n_mats, int n_seg, const int*
       g.out_routed = static_cast<__nv_bfloat16*>(y);
       g.ld_out_routed = dim;
       g.mode = parrot::kGemmPlain;
+      if (back != nullptr) {
+        g.out_peer_segs = back->segs_per_source;
+        g.out_peer_region = back->region;
+        g.out_peer_base = back->base;
+        for (int q = 0; q < parrot::kEpMaxRanks; ++q) g.out_peer[q] = back->back[q];
+      }
       ok = tensor_map(&mw, down, (long long)n_mats * dim * expert_dim / kGemmBlockK, kGemmBlockK,
                       128) &&
            tensor_map(&mx, hidden, rows, expert_dim, kGemmSubRows);
@@ -1412,26 +1442,22 @@ int parrot_ipc_close(void* base) {
   return PARROT_OK;
 }
 
-int parrot_moe_ep_send_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* ep,
-                            const parrot_ep_peers* peers, const void* workspace,
-                            size_t workspace_bytes, void* stream) {
-  parrot_moe_layout L;
-  parrot_ep_layout P;
-  int rc = layout_of(dims, &L);
-  if (rc || (rc = ep_layout_of(ep, &P)) || (rc = ep_peers_ok(ep, peers))) return rc;
-  if (dims->capacity != -1 || dims->dim != ep->dim || dims->n_experts != ep->n_experts)
-    return fail(PARROT_EINVAL, "ep_send: dims must be the packed dispatch dims of this EP set%s");
-  if (dims->tokens > ep->max_tokens)
-    return fail(PARROT_EINVAL, "ep_send: more tokens than ep->max_tokens%s");
-  if (dims->tokens > 0 && (rc = ws_ok(workspace, workspace_bytes, L))) return rc;
+// The send kernel over a checked dispatch (rows_sent: the grouping kernel
+// already stored the rows; counts, row base and arrival flags only).
+static int ep_send(const parrot_moe_dims* dims, const parrot_ep_dims* ep,
+                   const parrot_ep_peers* peers, const void* workspace,
+                   const parrot_moe_layout& L, const parrot_ep_layout& P, bool rows_sent,
+                   cudaStream_t stream) {
   char* own = static_cast<char*>(peers->buffers[ep->rank]);
   parrot::EpSendArgs a{};
-  if ((rc = ep_plan(ep, a.plan))) return rc;
+  int rc = ep_plan(ep, a.plan);
+  if (rc) return rc;
   if (dims->tokens > 0) {
     void* ws = const_cast<void*>(workspace);
     a.rows = at<__nv_bfloat16>(ws, L.grouped);
     a.counts = at<int>(ws, L.counts);
   }
+  a.rows_sent = rows_sent ? 1 : 0;
   a.tokens = dims->tokens;
   a.dim = ep->dim;
   a.n_experts = ep->n_experts;
@@ -1445,8 +1471,62 @@ int parrot_moe_ep_send_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* e
   a.epoch = reinterpret_cast<unsigned*>(own + P.epoch);
   a.counter = reinterpret_cast<unsigned*>(own + P.counters);
   a.status = reinterpret_cast<int*>(own + P.status);
-  parrot::launch_ep_send(a, sm_count(), static_cast<cudaStream_t>(stream));
+  parrot::launch_ep_send(a, sm_count(), stream);
   return check_launch("ep_send_kernel");
+}
+
+static int ep_send_checks(const parrot_moe_dims* dims, const parrot_ep_dims* ep,
+                          const parrot_ep_peers* peers, parrot_moe_layout* L,
+                          parrot_ep_layout* P) {
+  int rc = layout_of(dims, L);
+  if (rc || (rc = ep_layout_of(ep, P)) || (rc = ep_peers_ok(ep, peers))) return rc;
+  if (dims->capacity != -1 || dims->dim != ep->dim || dims->n_experts != ep->n_experts)
+    return fail(PARROT_EINVAL, "ep_send: dims must be the packed dispatch dims of this EP set%s");
+  if (dims->tokens > ep->max_tokens)
+    return fail(PARROT_EINVAL, "ep_send: more tokens than ep->max_tokens%s");
+  return PARROT_OK;
+}
+
+int parrot_moe_ep_send_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* ep,
+                            const parrot_ep_peers* peers, const void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  parrot_ep_layout P;
+  int rc = ep_send_checks(dims, ep, peers, &L, &P);
+  if (rc) return rc;
+  if (dims->tokens > 0 && (rc = ws_ok(workspace, workspace_bytes, L))) return rc;
+  return ep_send(dims, ep, peers, workspace, L, P, false, static_cast<cudaStream_t>(stream));
+}
+
+int parrot_moe_ep_dispatch_send_bf16(const parrot_moe_dims* dims,
+                                     const parrot_moe_weights* weights, const void* x,
+                                     const parrot_moe_outputs* outputs, const parrot_ep_dims* ep,
+                                     const parrot_ep_peers* peers, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  parrot_moe_layout L;
+  parrot_ep_layout P;
+  int rc = ep_send_checks(dims, ep, peers, &L, &P);
+  if (rc) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dims->tokens == 0) return ep_send(dims, ep, peers, workspace, L, P, true, s);
+  signed char plan[parrot::kEpMaxRanks][parrot::kMaxExperts];
+  if ((rc = ep_plan(ep, plan))) return rc;
+  if ((rc = check_router(weights)) || (rc = ws_ok(workspace, workspace_bytes, L))) return rc;
+  if (outputs == nullptr) return fail(PARROT_EINVAL, "ep_dispatch_send: outputs is NULL%s");
+  if (x == nullptr || !aligned16(x)) return fail(PARROT_EINVAL, "x must be 16-byte aligned%s");
+  signed char order[parrot::kMaxExperts];
+  ep_order(plan, ep->ranks, order);
+  EpRowsTo to{};
+  for (int q = 0; q < ep->ranks; ++q) {
+    to.recv[q] = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(peers->buffers[q]) +
+                                                   P.recv_rows) +
+                 (size_t)ep->rank * P.region_rows * ep->dim;
+    for (int j = 0; j < parrot::kMaxExperts; ++j)
+      if (plan[q][j] >= 0) to.dest[plan[q][j]] = (signed char)q;
+  }
+  to.region = P.region_rows;
+  if ((rc = run_route(dims, weights, x, outputs, workspace, L, s, order, false, &to))) return rc;
+  return ep_send(dims, ep, peers, workspace, L, P, true, s);
 }
 
 int parrot_moe_ep_receive(const parrot_ep_dims* ep, void* buffer, void* stream) {
@@ -1491,13 +1571,13 @@ int parrot_moe_ep_experts_bf16(const parrot_ep_dims* ep, void* buffer, const voi
                  static_cast<cudaStream_t>(stream));
 }
 
-int parrot_moe_ep_return_bf16(const parrot_ep_dims* ep, const parrot_ep_peers* peers,
-                              void* stream) {
-  parrot_ep_layout P;
-  int rc = ep_layout_of(ep, &P);
-  if (rc || (rc = ep_peers_ok(ep, peers))) return rc;
+// The return kernel (rows_sent: the down GEMM already stored the outputs;
+// the return flags only).
+static int ep_return(const parrot_ep_dims* ep, const parrot_ep_peers* peers,
+                     const parrot_ep_layout& P, bool rows_sent, void* stream) {
   char* own = static_cast<char*>(peers->buffers[ep->rank]);
   parrot::EpReturnArgs a{};
+  a.rows_sent = rows_sent ? 1 : 0;
   a.y = reinterpret_cast<const __nv_bfloat16*>(own + P.y);
   a.back_n = reinterpret_cast<const int*>(own + P.back_n);
   a.back_base = reinterpret_cast<const int*>(own + P.back_base);
@@ -1512,6 +1592,40 @@ int parrot_moe_ep_return_bf16(const parrot_ep_dims* ep, const parrot_ep_peers* p
   a.counter = reinterpret_cast<unsigned*>(own + P.counters) + 1;
   parrot::launch_ep_return(a, sm_count(), static_cast<cudaStream_t>(stream));
   return check_launch("ep_return_kernel");
+}
+
+int parrot_moe_ep_return_bf16(const parrot_ep_dims* ep, const parrot_ep_peers* peers,
+                              void* stream) {
+  parrot_ep_layout P;
+  int rc = ep_layout_of(ep, &P);
+  if (rc || (rc = ep_peers_ok(ep, peers))) return rc;
+  return ep_return(ep, peers, P, false, stream);
+}
+
+int parrot_moe_ep_experts_return_bf16(const parrot_ep_dims* ep, const parrot_ep_peers* peers,
+                                      const void* gate_up, const void* down, void* stream) {
+  parrot_ep_layout P;
+  int rc = ep_layout_of(ep, &P);
+  if (rc || (rc = ep_peers_ok(ep, peers))) return rc;
+  if (gate_up == nullptr || down == nullptr || !aligned16(gate_up) || !aligned16(down))
+    return fail(PARROT_EINVAL, "ep_experts_return: 16-byte aligned weights required%s");
+  char* b = static_cast<char*>(peers->buffers[ep->rank]);
+  const int slots = ep_slots(ep);
+  EpRowsBack back{};
+  for (int q = 0; q < ep->ranks; ++q)
+    back.back[q] = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(peers->buffers[q]) +
+                                                    P.back_rows);
+  back.base = reinterpret_cast<const int*>(b + P.back_base);
+  back.segs_per_source = slots;
+  back.region = P.region_rows;
+  rc = run_ffn(ep->ranks * P.region_rows, ep->dim, ep->expert_dim, slots, ep->ranks * slots,
+               reinterpret_cast<const int*>(b + P.seg_rows),
+               reinterpret_cast<const int*>(b + P.seg_base),
+               reinterpret_cast<const int*>(b + P.seg_expert), gate_up, down, b + P.recv_rows,
+               b + P.hidden, b + P.y, reinterpret_cast<int*>(b + P.status),
+               static_cast<cudaStream_t>(stream), &back);
+  if (rc) return rc;
+  return ep_return(ep, peers, P, true, stream);
 }
 
 int parrot_moe_ep_combine_peer_bf16(const parrot_moe_dims* dims, const parrot_ep_dims* ep,

@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpSendArgs a) {
   __syncthreads();
   const int nvec = a.dim >> 3;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
-  const int total = 2 * a.tokens;
+  const int total = a.rows_sent ? 0 : 2 * a.tokens;
   const size_t region = (size_t)2 * a.max_tokens;
   const uint4* rows = reinterpret_cast<const uint4*>(a.rows);
   for (int i = (blockIdx.x * warps + (threadIdx.x >> 5)) * kRowBatch; i < total;
@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(256) ep_return_kernel(EpReturnArgs a) {
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const size_t region = (size_t)2 * a.max_tokens;
   const uint4* y = reinterpret_cast<const uint4*>(a.y);
-  const int total = start_s[G];
+  const int total = a.rows_sent ? 0 : start_s[G];
   auto source_of = [&](int r) {
     int s = 0;
     while (s + 1 < G && r >= start_s[s + 1]) ++s;
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(256) ep_return_kernel(EpReturnArgs a) {
 }
 
 int launch_ep_send(const EpSendArgs& a, int sms, cudaStream_t stream) {
-  const int rows = 2 * a.tokens;
+  const int rows = a.rows_sent ? 0 : 2 * a.tokens;
   int grid = (rows + 8 * kRowBatch - 1) / (8 * kRowBatch);
   if (grid > 2 * sms) grid = 2 * sms;
   if (grid < 1) grid = 1;
@@ -257,7 +257,8 @@ int launch_ep_receive(const EpReceiveArgs& a, cudaStream_t stream) {
 
 int launch_ep_return(const EpReturnArgs& a, int sms, cudaStream_t stream) {
   // the row count is only known on the device: a fixed grid strides over it
-  return launch_pdl(ep_return_kernel, dim3(2 * sms), dim3(256), 0, stream, a) == cudaSuccess
+  return launch_pdl(ep_return_kernel, dim3(a.rows_sent ? 1 : 2 * sms), dim3(256), 0, stream, a) ==
+                 cudaSuccess
              ? 0
              : -1;
 }

@@ -103,6 +103,7 @@ struct __align__(16) SmemTail {
   int seg_rows[kSegMax];
   int seg_base[kSegMax];
   int seg_expert[kSegMax];
+  int seg_shift[kSegMax];  // output row - input row (rows sent back to their source)
 };
 
 template <int BN, bool PAIR>
@@ -122,6 +123,7 @@ struct Unit {
   int valid;      // token rows present (<= BN)
   int k_blocks;
   int out_col;    // first output feature
+  int out_row;    // output row of the tile's first token row
   __nv_bfloat16* out;
   int ld;
 };
@@ -148,7 +150,13 @@ __device__ __forceinline__ Unit routed_unit(const GemmArgs& g, const SmemTail<BN
   r.x_row = t.seg_base[s] + nt * BN;
   r.valid = max(0, min(BN, t.seg_rows[s] - nt * BN));
   r.k_blocks = g.k_blocks_routed;
-  r.out = g.out_routed;
+  if (g.out_peer_segs > 0) {
+    r.out = g.out_peer[s / g.out_peer_segs];
+    r.out_row = r.x_row + t.seg_shift[s];
+  } else {
+    r.out = g.out_routed;
+    r.out_row = r.x_row;
+  }
   r.ld = g.ld_out_routed;
   r.out_col = mt * (g.mode == kGemmSwiGLU ? BM / 2 : BM);
   return r;
@@ -200,6 +208,7 @@ __device__ __forceinline__ bool cta_unit(int k, const GemmArgs& g, const SmemTai
   r.routed = false;
   r.w_row = mt * g.k_blocks_shared * BM;
   r.x_row = nt * BN;
+  r.out_row = r.x_row;
   r.valid = min(BN, g.shared_rows - nt * BN);
   r.k_blocks = g.k_blocks_shared;
   r.out = g.out_shared;
@@ -412,6 +421,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       t.seg_rows[s] = rows;
       t.seg_base[s] = g.seg_stride > 0 ? s * g.seg_stride : g.seg_base[s];
       t.seg_expert[s] = g.seg_expert != nullptr ? g.seg_expert[s] : s % g.n_experts;
+      if (g.out_peer_segs > 0) {
+        // the receive kernel checked that base + rows stays in the return region
+        const int q = s / g.out_peer_segs;
+        t.seg_shift[s] = __ldg(g.out_peer_base + q) - q * g.out_peer_region;
+      }
     }
     int incl =
         s < n_seg ? secondary_tiles<BN>(s, rows, prim, g.n_experts) * (g.m_tiles_routed / MD) : 0;
@@ -647,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 2; ++i) {
             const int v = lane + 32 * i, tok = v >> 1, cc = v & 1;
             if (tok < rows_here)
-              *reinterpret_cast<uint4*>(un.out + (size_t)(un.x_row + c * kChunk + tok) * un.ld +
+              *reinterpret_cast<uint4*>(un.out + (size_t)(un.out_row + c * kChunk + tok) * un.ld +
                                         un.out_col + q * 16 + cc * 8) =
                   *reinterpret_cast<const uint4*>(tile_p + tok * 32 +
                                                   ((cc ^ ((tok >> 2) & 1)) << 4));
@@ -687,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int v = lane + 32 * i, tok = v >> 2, cc = v & 3;
             if (tok < rows_here) {
               const size_t row = scatter ? (size_t)t.unit_dst[c * kChunk + tok]
-                                         : (size_t)(un.x_row + c * kChunk + tok);
+                                         : (size_t)(un.out_row + c * kChunk + tok);
               *reinterpret_cast<uint4*>(un.out + row * un.ld + un.out_col + q * 32 + cc * 8) =
                   *reinterpret_cast<const uint4*>(tile_p + tok * 64 +
                                                   ((cc ^ ((tok >> 1) & 3)) << 4));
@@ -727,6 +741,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    // rows stored into another GPU's memory are visible there before this
+    // kernel completes, so the kernel after it may raise the return flags
+    if (g.out_peer_segs > 0) __threadfence_system();
   }
 
   tc_fence_before();

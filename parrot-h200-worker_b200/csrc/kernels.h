@@ -11,6 +11,7 @@ namespace parrot {
 
 constexpr int kMaxDepthSources = 16;
 constexpr int kMaxExperts = 32;
+constexpr int kEpMaxRanks = 8;             // expert-parallel ranks (ep_peer.cu)
 constexpr int kGroupTokensPerBlock = 32;   // grouping block / histogram chunk: 64 assignments
 constexpr int kGemmSubRows = 64;           // token rows per activation TMA box
 constexpr int kGemmBlockK = 64;            // 128-byte swizzled K slab
@@ -106,6 +107,14 @@ struct GroupArgs {
   int x_from_upstream;  // x is written by the kernel this one waits for (router fused into it)
   int copy_split;
   int* status;
+  // ep_packed, rows sent from here: a row of an expert whose destination is
+  // rank q is stored at row (grouped row - q's first grouped row) of
+  // ep_recv[q] (q's receive region for this source, in q's memory) instead
+  // of into `grouped`; ep_dest[e] is expert e's destination rank, and no row
+  // may land at or past ep_region.  Off when ep_recv[0] is null.
+  __nv_bfloat16* ep_recv[kEpMaxRanks];
+  signed char ep_dest[kMaxExperts];
+  int ep_region;
 };
 
 struct CombineArgs {
@@ -157,7 +166,6 @@ struct ArgmaxRowsArgs {
 };
 
 // ---- expert-parallel exchange over peer memory (ep_peer.cu) ----------------
-constexpr int kEpMaxRanks = 8;
 constexpr int kEpMetaStride = kMaxExperts + 1;  // per source: counts [El], then its row base
 
 struct EpSendArgs {
@@ -172,6 +180,7 @@ struct EpSendArgs {
   unsigned* epoch;            // this rank's send count (own buffer)
   unsigned* counter;          // last-CTA counter (own buffer)
   int* status;                // own buffer's status word
+  int rows_sent;              // 1: the grouping kernel stored the rows; counts and flags only
 };
 
 struct EpReceiveArgs {
@@ -197,6 +206,7 @@ struct EpReturnArgs {
   int ranks, rank, dim, max_tokens;
   const unsigned* epoch;
   unsigned* counter;
+  int rows_sent;              // 1: the expert GEMM stored the outputs; flags only
 };
 
 enum GemmMode : int { kGemmSwiGLU = 0, kGemmPlain = 1 };
@@ -248,6 +258,15 @@ struct GemmArgs {
     const int* positions;       // [2T]
     int* positions_out;         // or null
   } st;
+  // expert parallelism, plain mode, rows sent back from here: segment s
+  // holds rows of source q = s / out_peer_segs (rows [q * out_peer_region,
+  // ...) of the receive regions); its row r is stored to row
+  // r - q * out_peer_region + out_peer_base[q] of out_peer[q] (the source's
+  // return region, in its memory) instead of out_routed.  Off when 0.
+  int out_peer_segs;
+  int out_peer_region;
+  const int* out_peer_base;   // [ranks] device table (the receive kernel's back_base)
+  __nv_bfloat16* out_peer[kEpMaxRanks];
 };
 
 // The MoE block at decode batch sizes (moe_decode.cu).

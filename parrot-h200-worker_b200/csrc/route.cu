@@ -599,7 +599,8 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
   __shared__ int prefix_s[kMaxExperts];
   __shared__ int count_s[kMaxExperts];
   __shared__ int obase_s[kMaxExperts];
-  __shared__ int row_s[kAssign];
+  __shared__ uint4* dst_s[kAssign];  // where each assignment's row goes
+  __shared__ int dbase_s[kEpMaxRanks];
   __shared__ int red_before[128], red_total[128];
   __shared__ float red_psum[128];
   const int E = a.n_experts, C = a.capacity, T = a.tokens, d = a.dim;
@@ -700,9 +701,12 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
     }
   } else if (tid == 0) {
     // destination-major for expert parallelism: experts in the send order
+    // (and each destination's first grouped row, for rows sent from here)
     int base = E * C;
+    for (int q = 0; q < kEpMaxRanks; ++q) dbase_s[q] = 0;
     for (int q = 0; q < E; ++q) {
       const int ex = a.ep_order[q];
+      if (q == 0 || a.ep_dest[ex] != a.ep_dest[a.ep_order[q - 1]]) dbase_s[a.ep_dest[ex]] = base;
       obase_s[ex] = base;
       base += max(count_s[ex] - C, 0);
     }
@@ -755,6 +759,7 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
   if (warp < 2) {
     const int partner = __shfl_xor_sync(0xffffffffu, e, 1);  // the token's other expert
     int row = -1;
+    uint4* dst = nullptr;
     if (e >= 0) {
       const int slot = prefix_s[e] + (warp == 1 ? warp_cnt[0][e] : 0) + rank;
       row = slot < C ? e * C + slot : obase_s[e] + (slot - C);
@@ -764,20 +769,32 @@ __global__ void __launch_bounds__(128) group_kernel(GroupArgs a) {
         a.row_dst[row] = (a_idx & ~1) + (e < partner ? 0 : 1);
         a.row_w[row] = __ldg(a.weights + a_idx);
       }
+      if (a.ep_recv[0] == nullptr) {
+        dst = reinterpret_cast<uint4*>(a.grouped + (size_t)row * d);
+      } else {
+        // straight into the destination's receive region (peer memory)
+        const int q = a.ep_dest[e], k = row - dbase_s[q];
+        if (k >= 0 && k < a.ep_region)
+          dst = reinterpret_cast<uint4*>(a.ep_recv[q] + (size_t)k * d);
+        else if (split == 0)
+          report_status(a.status, kStatusBadIndex, 2, row);
+      }
     }
-    row_s[tid] = row;
+    dst_s[tid] = dst;
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
 
   // scatter this split's rows from shared memory
   for (int j = lo + warp; j < hi; j += 4) {
-    const int row = row_s[j];
+    uint4* dst = dst_s[j];
     const int lt = (j - lo) >> 1;
-    if (row < 0 || lt >= n_tok) continue;
-    uint4* dst = reinterpret_cast<uint4*>(a.grouped + (size_t)row * d);
+    if (dst == nullptr || lt >= n_tok) continue;
     for (int c = lane; c < nvec; c += 32) dst[c] = x_s[lt * nvec + c];
   }
+  // rows stored into another GPU's memory are visible there before this
+  // kernel completes, so the send kernel after it may raise the arrival flags
+  if (a.ep_recv[0] != nullptr) __threadfence_system();
 }
 
 int launch_group(const GroupArgs& args, cudaStream_t stream) {

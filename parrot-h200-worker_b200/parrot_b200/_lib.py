@@ -158,6 +158,12 @@ _SIGNATURES = {
     "parrot_moe_ep_experts_bf16": (c_int, [POINTER(EpDims), c_void_p, c_void_p, c_void_p,
                                            c_void_p]),
     "parrot_moe_ep_return_bf16": (c_int, [POINTER(EpDims), POINTER(EpPeers), c_void_p]),
+    "parrot_moe_ep_dispatch_send_bf16": (c_int, [POINTER(MoeDims), POINTER(MoeWeights),
+                                                 c_void_p, POINTER(MoeOutputs), POINTER(EpDims),
+                                                 POINTER(EpPeers), c_void_p, c_size_t,
+                                                 c_void_p]),
+    "parrot_moe_ep_experts_return_bf16": (c_int, [POINTER(EpDims), POINTER(EpPeers), c_void_p,
+                                                  c_void_p, c_void_p]),
     "parrot_moe_ep_combine_peer_bf16": (c_int, [POINTER(MoeDims), POINTER(EpDims), c_void_p,
                                                 c_void_p, c_size_t, c_void_p, c_void_p,
                                                 c_void_p]),

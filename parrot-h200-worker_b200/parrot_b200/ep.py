@@ -33,6 +33,12 @@ other ranks' memory (CUDA IPC mappings over NVLink / NVSwitch) instead of
 NCCL, with the split sizes kept on the device — no host read, fixed-size
 regions sized by the largest token count, so a layer can be captured in a
 CUDA graph (``parrot_moe_ep_send_bf16`` … ``parrot_moe_ep_combine_peer_bf16``).
+By default the two row exchanges have no copy kernel of their own: the
+grouping kernel stores each dispatched row straight into its destination's
+receive region, and the expert down GEMM stores each output straight into
+its source's return region (``parrot_moe_ep_dispatch_send_bf16``,
+``parrot_moe_ep_experts_return_bf16``), so the NVLink traffic overlaps the
+grouping and the GEMM instead of following them.
 """
 from __future__ import annotations
 
@@ -44,6 +50,10 @@ import torch
 from torch import Tensor
 
 from . import _lib, bridge
+
+# PeerExpertParallelMoE default: rows stored into the peers' regions by the
+# grouping kernel and the down GEMM (True) or by separate copy kernels.
+FUSED_EXCHANGE = True
 
 
 def owner(expert: int, ranks: int) -> int:
@@ -471,9 +481,14 @@ class PeerExpertParallelMoE:
     stream with no host synchronisation; every rank must call it the same
     number of times (with zero tokens if it has none).  The three phases are
     also callable on their own (``send``, ``experts``, ``finish``) so that
-    ranks sharing one GPU can run one after another in tests."""
+    ranks sharing one GPU can run one after another in tests.
 
-    def __init__(self, module, peers: PeerSet):
+    ``fused`` (default ``FUSED_EXCHANGE``): the grouping kernel and the down
+    GEMM store the rows into the peers' regions themselves; otherwise
+    separate send and return copy kernels move them.  Both leave the same
+    bytes in every region, so ranks may differ in this setting."""
+
+    def __init__(self, module, peers: PeerSet, fused: bool | None = None):
         cfg = module.cfg
         shape = peers.shape
         if (shape.dim, shape.n_experts, shape.expert_dim) != (cfg.dim, cfg.n_experts,
@@ -482,6 +497,7 @@ class PeerExpertParallelMoE:
         self.peers = peers
         self.ops = B200EpOps(module, peers.rank, shape.ranks, shape.slots(peers.rank))
         self.cfg = cfg
+        self.fused = FUSED_EXCHANGE if fused is None else bool(fused)
         self._pending: tuple | None = None
         # (name, event) after each phase when a list is set (instrumentation only)
         self.marks: list | None = None
@@ -506,6 +522,15 @@ class PeerExpertParallelMoE:
         w = bridge._weights_struct(ops.packed, ops.bias)
         lib, stream = _lib.load(), bridge._stream()
         outputs = _lib.MoeOutputs(None, None, None, None, None, None, None, None)
+        if self.fused:
+            _lib.check(lib.parrot_moe_ep_dispatch_send_bf16(
+                ctypes.byref(dims), ctypes.byref(w), bridge._p(x), ctypes.byref(outputs),
+                ctypes.byref(peers.dims), ctypes.byref(peers.peers), bridge._p(ws), ws.numel(),
+                stream), "parrot_moe_ep_dispatch_send_bf16")
+            self._mark("dispatch")
+            self._mark("send")
+            self._pending = (x, dims, ws, w)
+            return
         _lib.check(lib.parrot_moe_ep_dispatch_planned_bf16(
             ctypes.byref(dims), ctypes.byref(w), bridge._p(x), ctypes.byref(outputs),
             ctypes.byref(peers.dims), bridge._p(ws), ws.numel(), stream),
@@ -530,6 +555,13 @@ class PeerExpertParallelMoE:
         _lib.check(lib.parrot_moe_ep_receive(ctypes.byref(peers.dims), own, stream),
                    "parrot_moe_ep_receive")
         self._mark("receive")
+        if self.fused:
+            _lib.check(lib.parrot_moe_ep_experts_return_bf16(
+                ctypes.byref(peers.dims), ctypes.byref(peers.peers), bridge._p(ops.gate_up),
+                bridge._p(ops.down), stream), "parrot_moe_ep_experts_return_bf16")
+            self._mark("experts")
+            self._mark("return")
+            return
         _lib.check(lib.parrot_moe_ep_experts_bf16(
             ctypes.byref(peers.dims), own, bridge._p(ops.gate_up), bridge._p(ops.down), stream),
             "parrot_moe_ep_experts_bf16")

@@ -156,12 +156,20 @@ def test_expert_parallel_over_nccl_equals_single_device_block():
 
 # ---- the peer-memory exchange -------------------------------------------------
 
-def _peer_layers(module, sizes, wait_ns=200_000_000, placement=None):
+def _fused(exchange: str, rank: int) -> bool:
+    """The row exchange a rank uses: the grouping kernel and the down GEMM
+    store into the peers' regions ("fused"), separate copy kernels do
+    ("copies"), or the ranks alternate ("mixed": even ranks fused)."""
+    return exchange == "fused" or (exchange == "mixed" and rank % 2 == 0)
+
+
+def _peer_layers(module, sizes, wait_ns=200_000_000, placement=None, exchange="fused"):
     cfg = module.cfg
     shape = ep.EpShape(len(sizes), max(1, max(sizes)), cfg.dim, cfg.n_experts, cfg.expert_dim,
                        wait_ns, placement)
     peers = ep.PeerSet.local(shape, torch.device("cuda"))
-    return peers, [ep.PeerExpertParallelMoE(module, p) for p in peers]
+    return peers, [ep.PeerExpertParallelMoE(module, p, fused=_fused(exchange, r))
+                   for r, p in enumerate(peers)]
 
 
 def _balanced(module, x, ranks):
@@ -171,17 +179,22 @@ def _balanced(module, x, ranks):
     return ep.Placement.balanced(counts, ranks)
 
 
-@pytest.mark.parametrize("ranks,zipf,placement", [(1, False, "rr"), (2, False, "rr"),
-                                                  (4, True, "rr"), (8, True, "rr"),
-                                                  (2, True, "balanced"), (4, True, "balanced"),
-                                                  (8, True, "balanced")])
-def test_peer_exchange_ranks_in_turn_equal_single_device_block(ranks, zipf, placement):
+_IN_TURN = [(1, False, "rr"), (2, False, "rr"), (4, True, "rr"), (8, True, "rr"),
+            (2, True, "balanced"), (4, True, "balanced"), (8, True, "balanced")]
+
+
+@pytest.mark.parametrize("ranks,zipf,placement,exchange",
+                         [c + (x,) for x in ("fused", "copies") for c in _IN_TURN] +
+                         [(2, True, "balanced", "mixed"), (4, False, "rr", "mixed")])
+def test_peer_exchange_ranks_in_turn_equal_single_device_block(ranks, zipf, placement, exchange):
     """All ranks' buffers on one GPU, the ranks' phases issued in turn on one
     stream: every send before any receive, every return before any combine, so
     each flag a kernel waits for was raised by a kernel that already finished.
     Two calls in a row (the epoch advances, the regions are reused).  Round-
     robin placement, and load-balanced placements whose hot experts are
-    replicated (each source computes its own rows of them)."""
+    replicated (each source computes its own rows of them).  The rows move
+    by the grouping kernel and the down GEMM themselves, by the copy kernels,
+    or by both (ranks alternating)."""
     tokens = 3000
     with torch.inference_mode():
         if zipf:
@@ -196,7 +209,7 @@ def test_peer_exchange_ranks_in_turn_equal_single_device_block(ranks, zipf, plac
         plan = _balanced(module, x, ranks) if placement == "balanced" else None
         if plan is not None and ranks >= 4:
             assert plan.replicated  # the Zipf head is computed where its rows are
-        peers, layers = _peer_layers(module, sizes, placement=plan)
+        peers, layers = _peer_layers(module, sizes, placement=plan, exchange=exchange)
         for call in range(2):
             xs = [x[starts[r]:starts[r] + sizes[r]] * (1 + call) for r in range(ranks)]
             rs = [residual[starts[r]:starts[r] + sizes[r]] for r in range(ranks)]
@@ -236,7 +249,7 @@ def test_peer_exchange_wait_for_a_missing_rank_times_out_with_status():
         assert torch.isfinite(want).all()
 
 
-def _peer_rank(rank, ranks, port, seed, tokens, balanced):
+def _peer_rank(rank, ranks, port, seed, tokens, balanced, exchange):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=ranks,
@@ -255,7 +268,7 @@ def _peer_rank(rank, ranks, port, seed, tokens, balanced):
             shape = ep.EpShape(ranks, max(sizes), cfg.dim, cfg.n_experts, cfg.expert_dim,
                                1_000_000_000, plan)
             peers = ep.PeerSet.connect(shape)
-            layer = ep.PeerExpertParallelMoE(module, peers)
+            layer = ep.PeerExpertParallelMoE(module, peers, fused=_fused(exchange, rank))
             want = bridge.b200_moe(module, xs, True, rs)[0] if sizes[rank] else None
             for _ in range(3):
                 got = layer(xs, rs)
@@ -284,7 +297,9 @@ def _peer_rank(rank, ranks, port, seed, tokens, balanced):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
-@pytest.mark.parametrize("balanced", [False, True])
-def test_peer_exchange_over_nvlink_equals_single_device_block(balanced):
+@pytest.mark.parametrize("balanced,exchange", [(False, "fused"), (True, "fused"),
+                                               (False, "copies"), (True, "mixed")])
+def test_peer_exchange_over_nvlink_equals_single_device_block(balanced, exchange):
     ranks = min(torch.cuda.device_count(), 8)
-    mp.spawn(_peer_rank, args=(ranks, _free_port(), 31, 4096, balanced), nprocs=ranks, join=True)
+    mp.spawn(_peer_rank, args=(ranks, _free_port(), 31, 4096, balanced, exchange), nprocs=ranks,
+             join=True)
