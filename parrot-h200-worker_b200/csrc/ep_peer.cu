@@ -22,6 +22,13 @@
 //   combine  (route.cu) waits for every expert rank's return flag, then adds
 //            the weighted outputs to the shared expert's in expert-id order.
 //
+// The row copies of send and return can also be left to the kernels that
+// produce the rows: the grouping kernel (route.cu) stores each dispatched
+// row into its destination's receive region, the down GEMM's epilogue
+// (gemm.cu) each output into its source's return region, and both fence at
+// system scope before they complete; send and return then run as one block
+// that writes the counts and raises the flags (rows_sent).
+//
 // No host synchronisation and no size known only on the device reaches the
 // host, so the layer can be captured in a CUDA graph.  Flags carry an epoch
 // (the number of sends this rank has made, kept in its own buffer); every
