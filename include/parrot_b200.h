@@ -629,6 +629,16 @@ int parrot_moe_ep_combine_peer_bf16(const parrot_moe_dims* dims, const parrot_ep
 int parrot_ep_read_status(const parrot_ep_dims* ep, const void* buffer, int* host_status4,
                           void* stream);
 
+/* ---- self-test --------------------------------------------------------------
+ * The failure path of the kernels' bounded mbarrier waits, without a fault: a
+ * one-warp kernel waits on an mbarrier nobody arrives at through the same wait
+ * loop the grouped GEMM and the router use, limited to limit_ns (1 us .. 1 s)
+ * instead of their 2 s.  device_out8 (8 int32, 16-byte aligned, device memory)
+ * receives the status word the wait writes {1 (timeout), 90 (site), 0 (block),
+ * 0}, the wait's result (0: it gave up), the CTA abort flag it set (1) and the
+ * microseconds it waited.  No reference counterpart. */
+int parrot_selftest_wait_timeout(unsigned long long limit_ns, int* device_out8, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

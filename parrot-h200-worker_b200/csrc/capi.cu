@@ -565,7 +565,7 @@ int ep_layout_of(const parrot_ep_dims* e, parrot_ep_layout* L) {
   if (e->max_tokens < 1 || (long long)e->ranks * 2 * e->max_tokens > (1ll << 30))
     return fail(PARROT_EINVAL, "ep: max_tokens out of range%s");
   std::memset(L, 0, sizeof(*L));
-  const size_t G = e->ranks, R = 2 * (size_t)e->max_tokens, D = e->dim, E = e->n_experts;
+  const size_t G = e->ranks, R = 2 * (size_t)e->max_tokens, D = e->dim;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t at = off;
@@ -1693,6 +1693,18 @@ int parrot_moe_read_status(const void* workspace, const parrot_moe_dims* dims, i
       cudaStreamSynchronize(s) != cudaSuccess)
     return check_launch("read status");
   return PARROT_OK;
+}
+
+int parrot_selftest_wait_timeout(unsigned long long limit_ns, int* device_out8, void* stream) {
+  if (limit_ns < 1000 || limit_ns > 1000000000ull)
+    return fail(PARROT_EINVAL, "selftest_wait_timeout: 1 us <= limit_ns <= 1 s required%s");
+  if (device_out8 == nullptr || (reinterpret_cast<uintptr_t>(device_out8) & 15))
+    return fail(PARROT_EINVAL, "selftest_wait_timeout: 16-byte aligned output required%s");
+  if (cudaMemsetAsync(device_out8, 0, 8 * sizeof(int), static_cast<cudaStream_t>(stream)) !=
+      cudaSuccess)
+    return check_launch("selftest clear");
+  parrot::launch_mbar_timeout_selftest(limit_ns, device_out8, static_cast<cudaStream_t>(stream));
+  return check_launch("mbar_timeout_selftest_kernel");
 }
 
 }  // extern "C"

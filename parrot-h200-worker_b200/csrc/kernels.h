@@ -354,6 +354,12 @@ int launch_vocab_argmax(const VocabArgmaxArgs& args, int sms, cudaStream_t strea
 int launch_argmax_rows(const ArgmaxRowsArgs& args, cudaStream_t stream);
 int launch_ep_receive(const EpReceiveArgs& args, cudaStream_t stream);
 int launch_ep_return(const EpReturnArgs& args, int sms, cudaStream_t stream);
+
+// selftest.cu: a bounded mbarrier wait on a barrier nobody arrives at.
+// out[0..3] = the status word it writes, out[4] = the wait's result (0: gave
+// up), out[5] = the abort flag, out[6] = microseconds waited.
+constexpr int kSelftestSite = 90;
+int launch_mbar_timeout_selftest(unsigned long long limit_ns, int* out, cudaStream_t stream);
 int launch_grouped_gemm(const GemmArgs& args, const CUtensorMap* tm_w_routed,
                         const CUtensorMap* tm_x_routed, const CUtensorMap* tm_w_shared,
                         const CUtensorMap* tm_x_shared, int grid, int token_tile,

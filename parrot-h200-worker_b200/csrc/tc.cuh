@@ -39,21 +39,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait.  Returns false if the CTA is aborting or the limit ran out.
-static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                       int* status, int site) {
+// Bounded wait.  Returns false if the CTA is aborting or the limit ran out;
+// on a timeout it sets the abort flag and records {timeout, site, block}.
+__device__ __forceinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity,
+                                                volatile int* abort_flag, int* status, int site,
+                                                uint64_t limit_ns) {
   for (int i = 0; i < 128; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       report_status(status, kStatusWaitTimeout, site, (int)blockIdx.x);
       return false;
     }
   }
+}
+
+// The kernels' wait: the loop above with the 2 s limit.
+static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                       int* status, int site) {
+  return mbar_wait_until(bar, parity, abort_flag, status, site, kWaitLimitNs);
 }
 
 // The common case inline (one try_wait), the bounded loop (a call) only when

@@ -168,6 +168,7 @@ _SIGNATURES = {
                                                 c_void_p, c_size_t, c_void_p, c_void_p,
                                                 c_void_p]),
     "parrot_ep_read_status": (c_int, [POINTER(EpDims), c_void_p, POINTER(c_int), c_void_p]),
+    "parrot_selftest_wait_timeout": (c_int, [ctypes.c_ulonglong, c_void_p, c_void_p]),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -944,6 +944,34 @@ def test_two_row_depth_mix_is_bit_identical(rows, n_sources, norm):
         assert_bf16_close(whole.cpu()[sample], onorm(exp_mix), "two-row mix + norm")
 
 
+def test_bounded_mbarrier_wait_runs_out_with_status_and_the_device_stays_usable():
+    """An mbarrier nobody arrives at, waited on through the tensor-core
+    kernels' own bounded wait loop with a 20 ms limit: the wait gives up after
+    the limit (not before, and well before the kernels' 2 s), sets the abort
+    flag and records {timeout, site 90, block 0}; afterwards a MoE block runs
+    on the same context and matches the oracle-checked path."""
+    lib = _lib.load()
+    out = torch.full((8,), -1, dtype=torch.int32, device="cuda")
+    limit_ns = 20_000_000
+    _lib.check(lib.parrot_selftest_wait_timeout(limit_ns, ctypes.c_void_p(out.data_ptr()),
+                                                bridge._stream()), "selftest")
+    torch.cuda.synchronize()
+    code, site, block, spare, ok, aborted, waited_us, _ = out.tolist()
+    assert (code, site, block, spare) == (1, 90, 0, 0)
+    assert (ok, aborted) == (0, 1)
+    assert limit_ns // 1000 <= waited_us < 1_000_000
+    bad = ctypes.c_void_p(out.data_ptr())
+    assert lib.parrot_selftest_wait_timeout(2_000_000_000, bad, bridge._stream()) != 0
+    cfg = moe_config()
+    with torch.inference_mode():
+        module, _ = build_moe_pair(cfg, seed=21)
+        x = hidden_states(64, cfg.dim, seed=22).cuda()
+        first, _, _ = bridge.b200_moe(module, x, True)
+        second, _, _ = bridge.b200_moe(module, x, True)
+        torch.cuda.synchronize()
+    assert torch.isfinite(first).all() and torch.equal(first, second)
+
+
 def test_slot_mode_left_over_counters_are_reported_not_written_past():
     """Slot mode keeps per-expert counters in the workspace; a routing call
     whose block never runs leaves them set.  Routing again and again with
