@@ -282,3 +282,45 @@ def test_ep_calls_reject_bad_arguments_before_any_launch(lib):
     assert lib.parrot_moe_ep_experts_bf16(ctypes.byref(ep), None, None, None,
                                           None) == _lib.PARROT_EINVAL
     assert lib.parrot_ipc_export(None, None, None) == _lib.PARROT_EINVAL
+
+
+def test_fused_ep_calls_reject_bad_arguments_before_any_launch(lib):
+    """The dispatch + send and experts + return entry points check the same
+    things as the pairs they replace, before anything is launched."""
+    E = _lib.PARROT_EINVAL
+    ep = _ep_dims(ranks=2, rank=1, max_tokens=64)
+    unmapped = _lib.EpPeers()
+    dims = _lib.MoeDims(64, 768, 16, 2, 512, 256, -1)
+    w = _lib.MoeWeights()
+    out = _lib.MoeOutputs(None, None, None, None, None, None, None, None)
+
+    def dispatch_send(d, peers, weights=w, x=None):
+        return lib.parrot_moe_ep_dispatch_send_bf16(
+            ctypes.byref(d), ctypes.byref(weights), x, ctypes.byref(out), ctypes.byref(ep),
+            ctypes.byref(peers), None, 0, None)
+
+    assert dispatch_send(dims, unmapped) == E
+    assert b"mapped" in lib.parrot_b200_last_error()
+    peers = _lib.EpPeers()
+    peers.buffers[0] = peers.buffers[1] = 256
+    assert dispatch_send(_lib.MoeDims(65, 768, 16, 2, 512, 256, -1), peers) == E
+    assert b"max_tokens" in lib.parrot_b200_last_error()
+    assert dispatch_send(_lib.MoeDims(64, 768, 16, 2, 512, 256, 0), peers) == E
+    assert dispatch_send(_lib.MoeDims(64, 768, 8, 2, 512, 256, -1), peers) == E
+    assert dispatch_send(dims, peers) == E  # no router weight
+    assert b"router" in lib.parrot_b200_last_error()
+    assert lib.parrot_moe_ep_experts_return_bf16(ctypes.byref(ep), ctypes.byref(unmapped),
+                                                 None, None, None) == E
+    assert lib.parrot_moe_ep_experts_return_bf16(ctypes.byref(ep), ctypes.byref(peers), None,
+                                                 None, None) == E
+    assert b"aligned weights" in lib.parrot_b200_last_error()
+    assert lib.parrot_moe_ep_experts_return_bf16(ctypes.byref(ep), ctypes.byref(peers), 8, 16,
+                                                 None) == E
+
+
+def test_wait_selftest_rejects_bad_arguments_before_launch(lib):
+    E = _lib.PARROT_EINVAL
+    assert lib.parrot_selftest_wait_timeout(0, 256, None) == E
+    assert lib.parrot_selftest_wait_timeout(2_000_000_000, 256, None) == E
+    assert lib.parrot_selftest_wait_timeout(1_000_000, None, None) == E
+    assert lib.parrot_selftest_wait_timeout(1_000_000, 8, None) == E  # not 16-byte aligned
