@@ -471,17 +471,19 @@ def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 
         counts = (util.float() * 2 * total).round().int().tolist()
     balanced = ep.Placement.balanced(counts, world)
     # (placement, rows stored by the grouping kernel and the down GEMM
-    # themselves, or moved by separate copy kernels)
-    variants = {"balanced": (balanced, True),
-                "balanced_copy_kernels": (balanced, False),
-                "round_robin": (ep.Placement.round_robin(world, cfg.n_experts), True)}
+    # themselves or moved by separate copy kernels, shared expert on a side
+    # stream or in line)
+    variants = {"balanced": (balanced, True, True),
+                "balanced_shared_in_line": (balanced, True, False),
+                "balanced_copy_kernels": (balanced, False, False),
+                "round_robin": (ep.Placement.round_robin(world, cfg.n_experts), True, True)}
     res = {}
-    for name, (placement, fused) in variants.items():
+    for name, (placement, fused, overlap) in variants.items():
         shape = ep.EpShape(world, per, cfg.dim, cfg.n_experts, cfg.expert_dim,
                            placement=placement)
         peers = ep.PeerSet.connect(shape)
         with torch.inference_mode():
-            layer = ep.PeerExpertParallelMoE(moe, peers, fused=fused)
+            layer = ep.PeerExpertParallelMoE(moe, peers, fused=fused, overlap_shared=overlap)
             for _ in range(warmup):
                 layer(xs)
             eager_us = timed(lambda: layer(xs), iters)
@@ -538,9 +540,12 @@ def time_ep_layer(dist, rank: int, world: int, total: int = 16384, iters: int = 
                          "the rest largest first onto the least-loaded rank",
             "exchange": "peer memory (CUDA IPC over NVLink): the grouping kernel stores each "
                         "row into its destination's receive region and the down GEMM each "
-                        "output into its source's return region; epoch flags, no host read "
-                        "(balanced_copy_kernels: separate send / return copy kernels instead)",
-            "balanced": best, "balanced_copy_kernels": res["balanced_copy_kernels"],
+                        "output into its source's return region; epoch flags, no host read; "
+                        "the shared expert on a side stream beside them "
+                        "(balanced_shared_in_line: the shared expert after the send; "
+                        "balanced_copy_kernels: that and separate send / return copy kernels)",
+            "balanced": best, "balanced_shared_in_line": res["balanced_shared_in_line"],
+            "balanced_copy_kernels": res["balanced_copy_kernels"],
             "round_robin": res["round_robin"],
             "nccl_all_to_all_host_read_us": nccl_us,
             "timing": "CUDA-graph replay of the whole layer, CUDA events, max over ranks; "

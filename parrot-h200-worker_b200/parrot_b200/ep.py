@@ -51,9 +51,12 @@ from torch import Tensor
 
 from . import _lib, bridge
 
-# PeerExpertParallelMoE default: rows stored into the peers' regions by the
-# grouping kernel and the down GEMM (True) or by separate copy kernels.
+# PeerExpertParallelMoE defaults: rows stored into the peers' regions by the
+# grouping kernel and the down GEMM (True) or by separate copy kernels; the
+# shared expert on a side stream beside the dispatch and exchange (True) or
+# on the layer's stream after the send.
 FUSED_EXCHANGE = True
+OVERLAP_SHARED = True
 
 
 def owner(expert: int, ranks: int) -> int:
@@ -486,9 +489,16 @@ class PeerExpertParallelMoE:
     ``fused`` (default ``FUSED_EXCHANGE``): the grouping kernel and the down
     GEMM store the rows into the peers' regions themselves; otherwise
     separate send and return copy kernels move them.  Both leave the same
-    bytes in every region, so ranks may differ in this setting."""
+    bytes in every region, so ranks may differ in this setting.
 
-    def __init__(self, module, peers: PeerSet, fused: bool | None = None):
+    ``overlap_shared`` (default ``OVERLAP_SHARED``): the shared expert, which
+    needs only the layer input, runs on a side stream forked when the layer
+    starts and joined before the combine, so it overlaps the dispatch and the
+    exchange instead of following them; otherwise it runs on the layer's
+    stream between the send and the receive.  Both capture in a CUDA graph."""
+
+    def __init__(self, module, peers: PeerSet, fused: bool | None = None,
+                 overlap_shared: bool | None = None):
         cfg = module.cfg
         shape = peers.shape
         if (shape.dim, shape.n_experts, shape.expert_dim) != (cfg.dim, cfg.n_experts,
@@ -498,6 +508,9 @@ class PeerExpertParallelMoE:
         self.ops = B200EpOps(module, peers.rank, shape.ranks, shape.slots(peers.rank))
         self.cfg = cfg
         self.fused = FUSED_EXCHANGE if fused is None else bool(fused)
+        self.overlap_shared = OVERLAP_SHARED if overlap_shared is None else bool(overlap_shared)
+        self._side: torch.cuda.Stream | None = None
+        self._shared_on_side = False
         self._pending: tuple | None = None
         # (name, event) after each phase when a list is set (instrumentation only)
         self.marks: list | None = None
@@ -522,6 +535,18 @@ class PeerExpertParallelMoE:
         w = bridge._weights_struct(ops.packed, ops.bias)
         lib, stream = _lib.load(), bridge._stream()
         outputs = _lib.MoeOutputs(None, None, None, None, None, None, None, None)
+        self._shared_on_side = self.overlap_shared
+        if self.overlap_shared:
+            # the shared expert writes only its own workspace regions (its
+            # hidden rows and output), disjoint from what the router, the
+            # grouping and the exchange touch
+            main = torch.cuda.current_stream()
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=x.device)
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                self._shared(x, dims, ws, w)
+            x.record_stream(self._side)
         if self.fused:
             _lib.check(lib.parrot_moe_ep_dispatch_send_bf16(
                 ctypes.byref(dims), ctypes.byref(w), bridge._p(x), ctypes.byref(outputs),
@@ -547,10 +572,9 @@ class PeerExpertParallelMoE:
         ops, peers = self.ops, self.peers
         lib, stream = _lib.load(), bridge._stream()
         own = ctypes.c_void_p(peers.own.data_ptr())
-        # the shared expert runs while the other ranks' rows arrive
-        _lib.check(lib.parrot_moe_shared_ffn_bf16(
-            ctypes.byref(dims), ctypes.byref(w), bridge._p(x), bridge._p(ws), ws.numel(),
-            stream), "parrot_moe_shared_ffn_bf16")
+        if not self._shared_on_side:
+            # the shared expert runs while the other ranks' rows arrive
+            self._shared(x, dims, ws, w)
         self._mark("shared")
         _lib.check(lib.parrot_moe_ep_receive(ctypes.byref(peers.dims), own, stream),
                    "parrot_moe_ep_receive")
@@ -571,9 +595,17 @@ class PeerExpertParallelMoE:
                    "parrot_moe_ep_return_bf16")
         self._mark("return")
 
+    def _shared(self, x: Tensor, dims, ws: Tensor, w) -> None:
+        _lib.check(_lib.load().parrot_moe_shared_ffn_bf16(
+            ctypes.byref(dims), ctypes.byref(w), bridge._p(x), bridge._p(ws), ws.numel(),
+            bridge._stream()), "parrot_moe_shared_ffn_bf16")
+
     def finish(self, residual: Tensor | None = None) -> Tensor:
         x, dims, ws, _ = self._pending
         self._pending = None
+        if self._shared_on_side:
+            torch.cuda.current_stream().wait_stream(self._side)  # the shared output is ready
+            self._shared_on_side = False
         out = torch.empty_like(x)
         if residual is not None:
             residual = residual.reshape(out.shape).contiguous()

@@ -158,9 +158,15 @@ def test_expert_parallel_over_nccl_equals_single_device_block():
 
 def _fused(exchange: str, rank: int) -> bool:
     """The row exchange a rank uses: the grouping kernel and the down GEMM
-    store into the peers' regions ("fused"), separate copy kernels do
-    ("copies"), or the ranks alternate ("mixed": even ranks fused)."""
+    store into the peers' regions and the shared expert runs on a side stream
+    ("fused"), separate copy kernels move the rows and the shared expert runs
+    in line ("copies"), or the ranks alternate ("mixed": even ranks fused)."""
     return exchange == "fused" or (exchange == "mixed" and rank % 2 == 0)
+
+
+def _layer(module, peers, exchange, rank):
+    on = _fused(exchange, rank)
+    return ep.PeerExpertParallelMoE(module, peers, fused=on, overlap_shared=on)
 
 
 def _peer_layers(module, sizes, wait_ns=200_000_000, placement=None, exchange="fused"):
@@ -168,8 +174,7 @@ def _peer_layers(module, sizes, wait_ns=200_000_000, placement=None, exchange="f
     shape = ep.EpShape(len(sizes), max(1, max(sizes)), cfg.dim, cfg.n_experts, cfg.expert_dim,
                        wait_ns, placement)
     peers = ep.PeerSet.local(shape, torch.device("cuda"))
-    return peers, [ep.PeerExpertParallelMoE(module, p, fused=_fused(exchange, r))
-                   for r, p in enumerate(peers)]
+    return peers, [_layer(module, p, exchange, r) for r, p in enumerate(peers)]
 
 
 def _balanced(module, x, ranks):
@@ -229,6 +234,35 @@ def test_peer_exchange_ranks_in_turn_equal_single_device_block(ranks, zipf, plac
                 assert torch.equal(outs[r], want), f"call {call}, rank {r}"
 
 
+@pytest.mark.parametrize("exchange", ["fused", "copies"])
+def test_peer_exchange_single_rank_captured_in_a_graph(exchange):
+    """A one-rank set runs the whole layer on one GPU (its own flags are
+    raised earlier on the same stream), so the layer can be captured in a
+    CUDA graph here: with the shared expert forked onto a side stream and
+    joined before the combine, and with it in line.  Replays with new inputs
+    equal the single-device block."""
+    tokens = 1500
+    with torch.inference_mode():
+        module, x = zipf_module(seed=41, tokens=tokens)
+        residual = hidden_states(tokens, module.cfg.dim, seed=42).cuda()
+        peers, (layer,) = _peer_layers(module, [tokens], exchange=exchange)
+        static_x = x.clone()
+        layer(static_x, residual)  # first call outside the capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_out = layer(static_x, residual)
+        for scale in (1.0, 0.5, 2.0):
+            static_x.copy_(x * scale)
+            graph.replay()
+            torch.cuda.synchronize()
+            want, _, _ = bridge.b200_moe(module, static_x, True, residual)
+            torch.cuda.synchronize()
+            assert peers[0].status() == [0, 0, 0, 0]
+            assert torch.equal(static_out, want), f"scale {scale}"
+        del graph
+
+
 def test_peer_exchange_wait_for_a_missing_rank_times_out_with_status():
     """A two-rank set whose second rank never runs: rank 0's wait for its rows
     (and later for its returned outputs) runs out after the short limit, the
@@ -268,7 +302,7 @@ def _peer_rank(rank, ranks, port, seed, tokens, balanced, exchange):
             shape = ep.EpShape(ranks, max(sizes), cfg.dim, cfg.n_experts, cfg.expert_dim,
                                1_000_000_000, plan)
             peers = ep.PeerSet.connect(shape)
-            layer = ep.PeerExpertParallelMoE(module, peers, fused=_fused(exchange, rank))
+            layer = _layer(module, peers, exchange, rank)
             want = bridge.b200_moe(module, xs, True, rs)[0] if sizes[rank] else None
             for _ in range(3):
                 got = layer(xs, rs)
